@@ -1,0 +1,510 @@
+"""bench.py — Q4_0 prefill GEMM throughput on B200, driver contract.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the hot path over one ubatch: the two prefill projections of BASELINE
+config 2 — 512 tokens x K 1536 -> 8960 features (up/gate shape) and 512 tokens x K 8960 -> 1536
+(down shape), f16 activations, Q4_0 weights (d = f16(|N(0,1)|*0.02), nibbles U{0..15}), fp32
+accumulation, f16 outputs.  2 * 14,092,861,440 FLOP per step.
+
+value: whole-job TFLOP/s with inputs resident in HBM, CUDA events on the launch stream, max over
+ranks; a pool of input sets larger than L2 is rotated between steps.  e2e: the same metric through
+the C ABI with host buffers (pinned host -> device copies of the step's activations, device ->
+host copies of its outputs, inside the timed region).  --gpus N > 1: one process per GPU, each rank
+prefilling its own ubatches (independent prompts, no collective: weak scaling).
+--impl reference: the reference's own CPU implementation of the path (the C restatement of
+sulimo-cpu's AVX2 prefill: per token quantize_f32_to_q8_0 + matvec_q4_0_q8_0_avx2), all host threads.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+T, K_UP, F_UP = 512, 1536, 8960          # up/gate projection
+K_DN, F_DN = 8960, 1536                   # down projection
+FLOP_PER_GEMM = 2 * T * K_UP * F_UP       # == 2 * T * K_DN * F_DN
+FLOP_PER_STEP = 2 * FLOP_PER_GEMM
+METRIC = "Q4_0 prefill GEMM TFLOP/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def ncu_traffic(kernel):
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(kernel)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self, t0, t1):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(2)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for ts, line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            rows.append((ts, parts))
+        inside = [r for ts, r in rows if t0 - 0.15 <= ts <= t1 + 0.15] or [r for _, r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        mhz, maxmhz = [], []
+        for r in inside:
+            try:
+                mhz.append(float(r[0]))
+                maxmhz.append(float(r[1]))
+            except ValueError:
+                pass
+            for i, n in enumerate(names):
+                if r[3 + i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": max(maxmhz) if maxmhz else None,
+                "reasons": sorted(reasons), "samples": len(inside)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def make_inputs(seed):
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(seed)
+
+    def q4(rows, cols):
+        nb = rows * cols // 32
+        d = (np.abs(rng.standard_normal(nb, dtype=np.float32)) * np.float32(0.02)).astype(np.float16)
+        q = rng.integers(0, 256, nb * 16, dtype=np.uint8)
+        return (torch.from_numpy(d.view(np.int16).copy()).cuda(), torch.from_numpy(q).cuda())
+
+    up = q4(F_UP, K_UP)
+    dn = q4(F_DN, K_DN)
+    x_up = torch.randn(T * K_UP, device="cuda", dtype=torch.float16, generator=None)
+    x_dn = torch.randn(T * K_DN, device="cuda", dtype=torch.float16)
+    y_up = torch.empty(T * F_UP, device="cuda", dtype=torch.float16)
+    y_dn = torch.empty(T * F_DN, device="cuda", dtype=torch.float16)
+    return dict(up=up, dn=dn, x_up=x_up, x_dn=x_dn, y_up=y_up, y_dn=y_dn)
+
+
+def set_bytes(s):
+    b = 0
+    for k in ("x_up", "x_dn", "y_up", "y_dn"):
+        b += s[k].numel() * s[k].element_size()
+    for k in ("up", "dn"):
+        b += sum(t.numel() * t.element_size() for t in s[k])
+    return b
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import sulimo_b200 as sb
+
+    torch.manual_seed(1234 + rank)
+    ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
+    sets = [make_inputs(seed=rank * 100 + i) for i in range(1)]
+    per_set = set_bytes(sets[0])
+    n_sets = max(2, -(-int(1.5 * L2_BYTES) // per_set))
+    sets += [make_inputs(seed=rank * 100 + i) for i in range(1, n_sets)]
+
+    def step(s):
+        sb.gemm_q4_0_f16(ctx, s["up"][0], s["up"][1], s["x_up"], s["y_up"], F_UP, K_UP, T)
+        sb.gemm_q4_0_f16(ctx, s["dn"][0], s["dn"][1], s["x_dn"], s["y_dn"], F_DN, K_DN, T)
+
+    # eager warm-up steps (first calls set kernel attributes, outside any capture)
+    for i in range(args.warmup):
+        step(sets[i % n_sets])
+    ctx.finish()
+
+    # The timed steps are one CUDA graph (the launches are ~10 us of device work each, so a
+    # host-side launch loop would time Python, not the GPU).
+    launches0 = ctx.launch_count
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.set_stream(torch.cuda.current_stream())
+        for j in range(args.steps):
+            step(sets[j % n_sets])
+    ctx.set_stream(torch.cuda.current_stream())
+    launches = ctx.launch_count - launches0
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_w = time.time()
+    while time.time() - t_w < 1.0:   # keep the GPU under the same load until the timed region
+        graph.replay()
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop(t0, t1)
+    clocks["window"] = "1 s of identical graph replays before the timed replay + the timed replay"
+    ctx.finish()
+    del graph
+    ms_max = max_over_ranks(ms, world)
+    value = FLOP_PER_STEP * args.steps * world / (ms_max / 1e3) / 1e12
+
+    # ---- e2e through the C ABI with host buffers ----
+    e2e = run_e2e(args, ctx, sets[0], world)
+
+    # ---- roofline of the dominant kernel (the tcgen05 GEMM: both launches of a step) ----
+    hbm, tf_burst, tf_sust, src = peaks()
+    per_launch_ms = ms / (2 * args.steps)
+    achieved = FLOP_PER_GEMM / (per_launch_ms / 1e3) / 1e12
+    roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tf_burst,
+            "unit": "TFLOP/s", "frac": round(achieved / tf_burst, 4),
+            "traffic": ncu_traffic("gemm_q4_0_tc_kernel"),
+            "peak_source": f"{src} bf16 dense burst (MEASURED_PEAKS.json)"
+            if src == "measured" else "fallback 1.59 PFLOP/s"}
+
+    secondary = None
+    if rank == 0 and not args.no_secondary:
+        secondary = run_secondary(ctx, hbm)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(time_budget_s=args.cpu_seconds)
+
+    return dict(value=value, ms=ms_max, launches=launches, clocks=clocks, e2e=e2e, roof=roof,
+                secondary=secondary, cpu=cpu, n_sets=n_sets, set_bytes=per_set)
+
+
+def run_e2e(args, ctx, s, world):
+    """Host buffers in, host buffers out, through the C-ABI buffer + GEMM entry points."""
+    import ctypes as C
+    import torch
+    from sulimo_b200 import capi
+    import sulimo_b200 as sb
+
+    hx_up = torch.randn(T * K_UP, dtype=torch.float16).pin_memory()
+    hx_dn = torch.randn(T * K_DN, dtype=torch.float16).pin_memory()
+    hy_up = torch.empty(T * F_UP, dtype=torch.float16).pin_memory()
+    hy_dn = torch.empty(T * F_DN, dtype=torch.float16).pin_memory()
+    bufs = {}
+    for name, n in (("x_up", hx_up.numel() * 2), ("x_dn", hx_dn.numel() * 2),
+                    ("y_up", hy_up.numel() * 2), ("y_dn", hy_dn.numel() * 2)):
+        h = C.c_void_p()
+        capi.call("sulimo_cuda_buffer_alloc", ctx.handle, n, C.byref(h))
+        bufs[name] = h
+    L = capi.load()
+    ptr = {k: L.sulimo_cuda_buffer_device_ptr(v) for k, v in bufs.items()}
+
+    def step():
+        capi.call("sulimo_cuda_buffer_write", bufs["x_up"], 0, hx_up.data_ptr(), hx_up.numel() * 2)
+        capi.call("sulimo_cuda_buffer_write", bufs["x_dn"], 0, hx_dn.data_ptr(), hx_dn.numel() * 2)
+        sb.gemm_q4_0_f16(ctx, s["up"][0], s["up"][1], ptr["x_up"], ptr["y_up"], F_UP, K_UP, T)
+        sb.gemm_q4_0_f16(ctx, s["dn"][0], s["dn"][1], ptr["x_dn"], ptr["y_dn"], F_DN, K_DN, T)
+        capi.call("sulimo_cuda_buffer_read", bufs["y_up"], 0, hy_up.data_ptr(), hy_up.numel() * 2)
+        capi.call("sulimo_cuda_buffer_read", bufs["y_dn"], 0, hy_dn.data_ptr(), hy_dn.numel() * 2)
+
+    for _ in range(max(3, args.warmup // 10)):
+        step()
+    ctx.finish()
+    n = max(10, args.steps // 10)
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(n):
+        step()
+    ctx.finish()
+    dt = time.perf_counter() - t0
+    dt = max_over_ranks(dt, world)
+    for h in bufs.values():
+        capi.call("sulimo_cuda_buffer_free", h)
+    return {"value": round(FLOP_PER_STEP * n * world / dt / 1e12, 3), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": (hx_up.numel() + hx_dn.numel()) * 2,
+            "d2h_bytes_per_step": (hy_up.numel() + hy_dn.numel()) * 2, "steps": n,
+            "how": "C-ABI sulimo_cuda_buffer_write -> 2x sulimo_cuda_gemm_q4_0_f16 -> "
+                   "sulimo_cuda_buffer_read, pinned host memory, wall clock, max over ranks"}
+
+
+def run_secondary(ctx, hbm):
+    """Decode-side kernels (configs 1/4 shapes), HBM GB/s against the measured copy peak."""
+    import numpy as np
+    import torch
+    import sulimo_b200 as sb
+
+    out = {}
+    rng = np.random.default_rng(7)
+
+    def gemv_case(rows, cols, batch, name):
+        nbytes_w = rows * cols // 32 * 18
+        copies = max(2, -(-int(1.5 * L2_BYTES) // nbytes_w))
+        ws = [torch.randint(0, 1 << 14, (rows * cols // 32,), dtype=torch.int16, device="cuda")
+              .bitwise_and_(0x3fff) for _ in range(copies)]
+        wq = [torch.randint(0, 256, (rows * cols // 32 * 16,), dtype=torch.uint8, device="cuda")
+              for _ in range(copies)]
+        xq = torch.randint(-100, 100, (batch * cols // 32 * 34,), dtype=torch.int8,
+                           device="cuda").view(torch.uint8)
+        xq.view(-1, 34)[:, :2] = 0x2C  # sane f16 scales
+        y = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
+        for i in range(5):
+            sb.dispatch_matvec_q4_0_q8_0(ctx, ws[i % copies], wq[i % copies], xq, rows, cols, y, batch)
+        iters = max(20, copies * 4)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(iters):
+            sb.dispatch_matvec_q4_0_q8_0(ctx, ws[i % copies], wq[i % copies], xq, rows, cols, y, batch)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / iters
+        alg = nbytes_w + batch * cols // 32 * 34 + batch * rows * 4
+        out[name] = {"us_per_launch": round(us, 2), "GBps": round(alg / us / 1e3, 1),
+                     "frac_of_measured_hbm": round(alg / us / 1e3 / hbm, 3),
+                     "alg_bytes": alg, "l2": f"{copies} rotated weight copies"}
+
+    gemv_case(8960, 1536, 1, "gemv_config1_8960x1536_b1")
+    gemv_case(151936, 1536, 1, "gemv_lm_head_151936x1536_b1")
+    gemv_case(8192, 3072, 8, "gemv_ffn_8192x3072_b8")
+
+    # decode attention, Llama-3.2-3B geometry at ctx 4096, batch 1
+    H, Hkv, hd, cap = 24, 8, 128, 4096
+    ring_bytes = cap * Hkv * hd // 32 * 34
+    copies = max(2, -(-int(1.5 * L2_BYTES) // (2 * ring_bytes)))
+    ks = [torch.randint(-127, 127, (ring_bytes,), dtype=torch.int8, device="cuda").view(torch.uint8)
+          for _ in range(copies)]
+    vs = [torch.randint(-127, 127, (ring_bytes,), dtype=torch.int8, device="cuda").view(torch.uint8)
+          for _ in range(copies)]
+    for r in ks + vs:
+        r.view(-1, 34)[:, 0] = 0x00
+        r.view(-1, 34)[:, 1] = 0x20
+    q = torch.randn(H * hd, device="cuda")
+    o = torch.empty(H * hd, device="cuda")
+    for i in range(5):
+        sb.causal_gqa_decode(ctx, q, ks[i % copies], vs[i % copies], cap, cap, H, Hkv, hd, o)
+    iters = max(20, copies * 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(iters):
+        sb.causal_gqa_decode(ctx, q, ks[i % copies], vs[i % copies], cap, cap, H, Hkv, hd, o)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    alg = 2 * ring_bytes + 2 * H * hd * 4
+    out["attn_decode_llama3b_ctx4096_b1"] = {"us_per_call": round(us, 2),
+                                             "GBps": round(alg / us / 1e3, 1),
+                                             "frac_of_measured_hbm": round(alg / us / 1e3 / hbm, 3),
+                                             "alg_bytes": alg}
+    return out
+
+
+def cpu_baseline(time_budget_s=10.0, steps=None):
+    """The reference's CPU prefill of the two projections (C restatement), all host threads,
+    on a bounded token sample; returns TFLOP/s scaled to the full-step FLOP count."""
+    import numpy as np
+    import oracle.ffi as O
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+
+    def q4(rows, cols):
+        nb = rows * cols // 32
+        d = (np.abs(rng.standard_normal(nb, dtype=np.float32)) * np.float32(0.02)).astype(np.float16)
+        return d.view(np.uint16).copy(), rng.integers(0, 256, nb * 16, dtype=np.uint8)
+
+    ws_u, wq_u = q4(F_UP, K_UP)
+    ws_d, wq_d = q4(F_DN, K_DN)
+
+    def run(tokens):
+        x_u = rng.standard_normal((tokens, K_UP)).astype(np.float32)
+        x_d = rng.standard_normal((tokens, K_DN)).astype(np.float32)
+        t0 = time.perf_counter()
+        O.cpu_prefill_projection(ws_u, wq_u, x_u, F_UP, K_UP, tokens, threads)
+        O.cpu_prefill_projection(ws_d, wq_d, x_d, F_DN, K_DN, tokens, threads)
+        return time.perf_counter() - t0
+
+    t1 = run(threads)  # calibration: one token per thread
+    per_tok = t1 / threads
+    tokens = int(max(threads, min(T, time_budget_s / max(per_tok, 1e-9))))
+    tokens = max(threads, (tokens // threads) * threads)
+    dt = run(tokens)
+    tf = 2 * 2 * tokens * K_UP * F_UP / dt / 1e12
+    return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{tokens} of the {T} tokens of both projections (per token: "
+                      f"quantize_f32_to_q8_0 + matvec_q4_0_q8_0_avx2, {threads} threads), "
+                      f"{dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's own CPU implementation of the path, all host threads."""
+    if rank != 0:
+        return None
+    import numpy as np
+    import oracle.ffi as O
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+
+    def q4(rows, cols):
+        nb = rows * cols // 32
+        d = (np.abs(rng.standard_normal(nb, dtype=np.float32)) * np.float32(0.02)).astype(np.float16)
+        return d.view(np.uint16).copy(), rng.integers(0, 256, nb * 16, dtype=np.uint8)
+
+    ws_u, wq_u = q4(F_UP, K_UP)
+    ws_d, wq_d = q4(F_DN, K_DN)
+    x_u = rng.standard_normal((T, K_UP)).astype(np.float32)
+    x_d = rng.standard_normal((T, K_DN)).astype(np.float32)
+
+    def step(tokens, off):
+        O.cpu_prefill_projection(ws_u, wq_u, x_u[off:off + tokens], F_UP, K_UP, tokens, threads)
+        O.cpu_prefill_projection(ws_d, wq_d, x_d[off:off + tokens], F_DN, K_DN, tokens, threads)
+
+    t0 = time.perf_counter()
+    step(threads, 0)
+    per_tok = (time.perf_counter() - t0) / threads
+    budget = 90.0 / max(1, args.steps + args.warmup)   # whole run ~1.5 min
+    tokens = int(max(1, min(T, budget / max(per_tok, 1e-9))))
+    for i in range(args.warmup):
+        step(tokens, 0)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(tokens, (i * tokens) % max(1, T - tokens + 1))
+    dt = time.perf_counter() - t0
+    value = 2 * 2 * tokens * K_UP * F_UP * args.steps / dt / 1e12
+    return {"metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / int8+fp32 CPU math",
+            "data": "synthetic",
+            "config": {"workload": "config2 prefill GEMM pair, bounded token sample per step",
+                       "tokens_per_step": tokens, "of_tokens": T,
+                       "shapes": "512x1536->8960 and 512x8960->1536"},
+            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads,
+                             "kind": "port",
+                             "sample": f"{tokens} tokens of both projections per step"},
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    rank, world, local = dist_setup(args.gpus)
+    r = run_ours(args, rank, world, local)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(r["value"], 3), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(r["ms"] / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded Q4_0 weights d=f16(|N|*0.02), nibbles U{0..15}; x f16 N(0,1))",
+            "config": {"workload": "BASELINE config 2: Q4_0 prefill GEMM, 512 tokens x K1536 -> "
+                                   "N8960 and 512 x K8960 -> N1536 per step",
+                       "global_batch": T * world, "seq_len": T,
+                       "parallelism": f"dp{world} (independent ubatches per rank)",
+                       "l2": f"inputs rotated over {r['n_sets']} sets of "
+                             f"{r['set_bytes'] / 2**20:.0f} MiB (> 126 MB L2)"},
+            "e2e": r["e2e"], "gpu_launches": r["launches"], "roofline": r["roof"],
+            "clocks": r["clocks"],
+        }
+        if r["cpu"] is not None:
+            line["cpu_baseline"] = r["cpu"]
+        if r["secondary"] is not None:
+            line["secondary"] = r["secondary"]
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,189 @@
+/*
+ * sulimo_cuda.h — C ABI of the B200 (sm_100a) backend for Sulimo's quantized-matmul hot path.
+ *
+ * This is the drop-in boundary a `sulimo-cuda` Rust crate binds through FFI in place of the
+ * `sulimo-ocl` (OpenCL prefill) and `sulimo-cpu` (AVX2 decode) backends.  Every entry point
+ * names the reference interface it replaces (paths relative to the reference repository).
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Tensor pointers are DEVICE pointers (cudaMalloc'd or
+ *     obtained from sulimo_cuda_buffer_device_ptr) unless a parameter says "host".
+ *   - Weight format is the reference's Q4_0 SoA arena layout (crates/sulimo-core/src/repack.rs:
+ *     45-81): `scales` = rows*(cols/32) little-endian f16, `quants` = rows*(cols/32)*16 bytes,
+ *     row r / block b at index r*(cols/32)+b; weight i<16 is the low nibble of qs[i], i>=16 the
+ *     high nibble of qs[i-16]; value (nibble-8)*d.
+ *   - Activation / KV format is Q8_0 (crates/sulimo-core/src/kv_cache.rs:11-15): 34-byte blocks
+ *     [f16 d][32 x i8].
+ *   - Every call returns an int status (SULIMO_OK == 0).  Shape violations that the reference
+ *     turns into a panic (assert!) return SULIMO_EINVAL here; nothing aborts the process.
+ *     sulimo_cuda_last_error() returns a thread-local message for the last failure.
+ *   - Kernels are enqueued on the context's stream and return without waiting, like the
+ *     reference's enqueue_* functions; sulimo_cuda_ctx_synchronize / sulimo_cuda_event_wait
+ *     are the waits.  A kernel whose bounded internal wait ran out records a device error that
+ *     the next synchronize returns as SULIMO_EDEVICE.
+ */
+#ifndef SULIMO_CUDA_H
+#define SULIMO_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Status codes — map the variants of OclError (crates/sulimo-ocl/src/program.rs:26-40). */
+enum {
+    SULIMO_OK = 0,
+    SULIMO_EINVAL = 1,   /* bad shape / argument (reference: assert! panics)            */
+    SULIMO_ENODEV = 2,   /* no usable sm_100 device (OclError::DeviceNotFound)          */
+    SULIMO_EOOM = 3,     /* device allocation failed                                    */
+    SULIMO_ELAUNCH = 4,  /* CUDA launch / driver error (OclError::Driver)               */
+    SULIMO_ETIMEOUT = 5, /* host wait deadline passed                                   */
+    SULIMO_ENCCL = 6,    /* NCCL error in a sharded call                                */
+    SULIMO_EALIGN = 7,   /* pointer / size alignment violated (OclError::ZeroCopyViolation) */
+    SULIMO_EDEVICE = 8   /* a kernel reported a device-side error (OclError::ExecutionFailed) */
+};
+
+/* Output element types for the prefill GEMM. */
+enum { SULIMO_OUT_F16 = 0, SULIMO_OUT_F32 = 1 };
+/* Activation element types. */
+enum { SULIMO_ACT_F16 = 0, SULIMO_ACT_F32 = 1 };
+
+typedef struct sulimo_ctx sulimo_ctx;
+typedef struct sulimo_buf sulimo_buf;
+typedef struct sulimo_event sulimo_event;
+
+/* ---------------------------------------------------------------------------------------- */
+/* Errors / version                                                                          */
+/* ---------------------------------------------------------------------------------------- */
+const char* sulimo_cuda_last_error(void);
+const char* sulimo_cuda_version(void);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Context — replaces OclContext::new / get_or_init / finish                                 */
+/* (crates/sulimo-ocl/src/program.rs:79-94).  One context = one device + one stream.          */
+/* ---------------------------------------------------------------------------------------- */
+int sulimo_cuda_ctx_create(int device, sulimo_ctx** out);
+int sulimo_cuda_ctx_destroy(sulimo_ctx* ctx);
+/* Wait for all work on the context stream; returns SULIMO_EDEVICE if a kernel flagged an error. */
+int sulimo_cuda_ctx_synchronize(sulimo_ctx* ctx);
+/* Use the caller's cudaStream_t (e.g. a framework's current stream) instead of the own one. */
+int sulimo_cuda_ctx_set_stream(sulimo_ctx* ctx, void* cuda_stream);
+void* sulimo_cuda_ctx_get_stream(sulimo_ctx* ctx);
+int sulimo_cuda_ctx_device(sulimo_ctx* ctx);
+/* Launches issued by this library since the context was created (a kernel-count probe). */
+uint64_t sulimo_cuda_ctx_launch_count(sulimo_ctx* ctx);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Buffers — replace OclBuffer::from_host_ptr / map_read / Drop / active_cl_mem_count        */
+/* (crates/sulimo-ocl/src/buffer.rs:21-161).  The reference wraps host arena memory          */
+/* zero-copy; a B200 is discrete, so a buffer owns device memory and from_host copies the    */
+/* host bytes in.  The host alignment contract is kept: host_ptr 4096-aligned and size a     */
+/* multiple of 64 when `strict_arena` is set (else SULIMO_EALIGN).                           */
+/* ---------------------------------------------------------------------------------------- */
+int sulimo_cuda_buffer_from_host(sulimo_ctx* ctx, const void* host_ptr, size_t size,
+                                 int read_only, int strict_arena, sulimo_buf** out);
+int sulimo_cuda_buffer_alloc(sulimo_ctx* ctx, size_t size, sulimo_buf** out);
+int sulimo_cuda_buffer_write(sulimo_buf* buf, size_t offset, const void* host_src, size_t n);
+int sulimo_cuda_buffer_read(sulimo_buf* buf, size_t offset, void* host_dst, size_t n);
+void* sulimo_cuda_buffer_device_ptr(sulimo_buf* buf);
+size_t sulimo_cuda_buffer_size(sulimo_buf* buf);
+int sulimo_cuda_buffer_free(sulimo_buf* buf);
+/* Number of live buffers (active_cl_mem_count, buffer.rs:21-23). */
+size_t sulimo_cuda_live_buffer_count(void);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Events — replace wait_event_zero_spin (crates/sulimo-ocl/src/waiter.rs:39-82).            */
+/* The wait blocks in the driver (cudaEventBlockingSync, no spinning) up to timeout_ns       */
+/* (0 = no deadline) and returns SULIMO_ETIMEOUT instead of hanging.                         */
+/* ---------------------------------------------------------------------------------------- */
+int sulimo_cuda_event_record(sulimo_ctx* ctx, sulimo_event** out);
+int sulimo_cuda_event_wait(sulimo_event* ev, uint64_t timeout_ns);
+int sulimo_cuda_event_free(sulimo_event* ev);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Prefill GEMM — replaces enqueue_gemm_q4_0_f16 (crates/sulimo-ocl/src/prefill.rs:69-105)   */
+/* and gemm_q4_0_f16 (crates/sulimo-ocl/src/gemm.rs:28-102), kernels                          */
+/* gemm_q4_0_f16_{portable,intel} (kernels/gemm_q4_0.cl:13-130).                             */
+/*   out[t][r] = sum_b d[r][b] * sum_i x[t][32b+i] * (q[r][b][i]-8),  t < n, r < m            */
+/* m = output features (rows of W), k = input channels, n = tokens; x is [n][k] f16 row-major,*/
+/* out is [n][m] f16 (SULIMO_OUT_F16, as the reference) or f32 (SULIMO_OUT_F32, the          */
+/* logits_f16_output form, kernels/prefill.cl:269-308).  Requires k % 32 == 0 and            */
+/* m % 8 == 0 (the reference's asserts, gemm.rs:39-40); x, out and quants 16-byte aligned.    */
+/* Tensor cores compute with B operand f16(d*(q-8)) (one RNE rounding per weight) and fp32   */
+/* accumulation.                                                                             */
+/* ---------------------------------------------------------------------------------------- */
+int sulimo_cuda_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants,
+                              const void* x, void* out, int m, int k, int n, int out_dtype);
+
+/* Last-token logits — replaces enqueue_logits_final (prefill.rs:300-330): fp32 logits of    */
+/* token row `token_idx` of x_all [*, embd] against a [vocab][embd] Q4_0 matrix.             */
+int sulimo_cuda_logits_final(sulimo_ctx* ctx, const void* x_all, const void* scales,
+                             const void* quants, float* logits, int vocab, int embd,
+                             int token_idx);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Decode GEMV — replaces dispatch_matvec_q4_0_q8_0 (crates/sulimo-cpu/src/avx2.rs:17-37)     */
+/* with matvec_q4_0_q8_0_avx2 / vec_dot_q4_0_q8_0_avx2 (avx2.rs:113-189).                    */
+/* x_q8 holds `batch` Q8_0 vectors of cols/32 blocks each; out is [batch][rows] f32.         */
+/* The result is bit-identical to the AVX2 kernel: eight fp32 lanes per row accumulate       */
+/* fma(float(lane_sum), d_w*d_x, acc) over blocks in order and are reduced with hsum_256's   */
+/* add tree (avx2.rs:333-342).  Requires cols % 32 == 0.                                     */
+/* ---------------------------------------------------------------------------------------- */
+int sulimo_cuda_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
+                               const void* x_q8, int rows, int cols, int batch, float* out);
+
+/* Integer per-block sums (debug / parity entry): out[b][r*(cols/32)+j] = sum_i (w_i-8)*x_i, */
+/* the i32 `block_sum` of vec_dot_q4_0_q8_0_scalar (crates/sulimo-cpu/src/scalar.rs:189-199). */
+int sulimo_cuda_block_sums_q4_0_q8_0(sulimo_ctx* ctx, const void* w_quants, const void* x_q8,
+                                     int rows, int cols, int32_t* out);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Q8_0 quantize — replaces quantize_f32_to_q8_0 (crates/sulimo-core/src/kv_cache.rs:162-192).*/
+/* n % 32 == 0; byte-identical output.                                                        */
+/* ---------------------------------------------------------------------------------------- */
+int sulimo_cuda_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst_q8, size_t n);
+
+/* Q8_0 ring store — replaces enqueue_kv_store (crates/sulimo-ocl/src/prefill.rs:176-205,     */
+/* kernel kv_store_q8_0, kernels/prefill.cl:72-116) and KvCache::store_key/store_value        */
+/* (kv_cache.rs:93-110).  act is [n][blocks_per_pos*32] (f16 or f32); token t goes to ring    */
+/* slot (start_pos+t) % capacity.  Bytes are identical to quantize_f32_to_q8_0 of the         */
+/* activations widened to f32.                                                               */
+int sulimo_cuda_kv_store_q8_0(sulimo_ctx* ctx, const void* act, int act_dtype, void* kv_ring,
+                              size_t start_pos, size_t capacity, size_t blocks_per_pos,
+                              size_t n);
+
+/* Q4_0 row dequant — dequantize_q4_0_soa (crates/sulimo-core/src/repack.rs:107-131) for      */
+/* `count` rows starting at `row0` of a [rows][cols] tensor; f32 out (bit-exact) or f16 out   */
+/* (lookup_token_embedding_f16, crates/sulimo-engine/src/scheduler.rs:329-357).              */
+int sulimo_cuda_dequantize_q4_0_rows(sulimo_ctx* ctx, const void* scales, const void* quants,
+                                     int cols, const int32_t* row_ids, int count, void* out,
+                                     int out_dtype);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Decode attention — replaces causal_gqa_decode_scalar_ext                                   */
+/* (crates/sulimo-cpu/src/scalar.rs:287-359) over the KvCache ring (kv_cache.rs:114-128).     */
+/* q: [batch][head_count][head_dim] f32; out: same shape.  Sequence s reads its K/V rings at  */
+/* k_ring + s*seq_stride_bytes (v likewise); position p reads slot p % capacity; positions    */
+/* 0..context_len-1 are attended.  softcap <= 0 disables soft-capping.  Split-K over the      */
+/* context (partial max/sum/output in the context workspace, combined by a second kernel).    */
+/* ---------------------------------------------------------------------------------------- */
+int sulimo_cuda_attn_decode_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                                 const void* v_ring, size_t seq_stride_bytes, size_t capacity,
+                                 size_t context_len, int head_count, int head_count_kv,
+                                 int head_dim, int batch, float softcap, float* out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SULIMO_CUDA_H */

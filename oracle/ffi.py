@@ -1,0 +1,229 @@
+"""numpy bindings of liboracle (the CPU restatement of the reference's hot path).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline leg as the checker.  The product library (libsulimo_cuda.so) never uses it.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.build()
+        L = C.CDLL(path)
+        vp, sz, i32, f32 = C.c_void_p, C.c_size_t, C.c_int, C.c_float
+        sig = {
+            "oracle_f32_to_f16": (C.c_uint16, [f32]),
+            "oracle_f16_to_f32": (f32, [C.c_uint16]),
+            "oracle_f32_to_f16_array": (None, [vp, vp, sz]),
+            "oracle_f16_to_f32_array": (None, [vp, vp, sz]),
+            "oracle_repack_q4_0_aos_to_soa": (C.c_long, [vp, sz, vp, sz, vp, sz]),
+            "oracle_dequantize_q4_0_aos": (None, [vp, sz, vp]),
+            "oracle_dequantize_q4_0_soa": (None, [vp, vp, sz, vp]),
+            "oracle_lookup_token_embedding_f16": (None, [vp, vp, sz, C.c_uint32, vp]),
+            "oracle_quantize_f32_to_q8_0": (None, [vp, sz, vp]),
+            "oracle_dequantize_q8_0_to_f32": (None, [vp, sz, vp]),
+            "oracle_kv_store_q8_0": (None, [vp, vp, sz, sz, sz, sz]),
+            "oracle_kv_store_f32": (None, [vp, vp, sz, sz, sz]),
+            "oracle_vec_dot_q4_0_q8_0_scalar": (f32, [vp, vp, vp, sz]),
+            "oracle_matvec_q4_0_q8_0_scalar": (None, [vp, vp, vp, sz, sz, vp]),
+            "oracle_vec_dot_q4_0_q8_0_avx2": (f32, [vp, vp, vp, sz]),
+            "oracle_matvec_q4_0_q8_0_avx2": (None, [vp, vp, vp, sz, sz, vp]),
+            "oracle_matvec_q4_0_q8_0_avx2_mt": (None, [vp, vp, vp, sz, sz, vp, i32]),
+            "oracle_block_sums_q4_0_q8_0": (None, [vp, vp, vp, sz, sz, vp]),
+            "oracle_gemm_q4_0_f16_scalar_reference": (None, [vp, vp, vp, sz, sz, sz, vp]),
+            "oracle_gemm_q4_0_f16_scalar_f32out": (None, [vp, vp, vp, sz, sz, sz, vp, i32]),
+            "oracle_cpu_prefill_projection": (None, [vp, vp, vp, sz, sz, sz, vp, i32]),
+            "oracle_rmsnorm_scalar": (None, [vp, vp, sz, f32, vp]),
+            "oracle_rmsnorm_avx2": (None, [vp, vp, sz, f32, vp]),
+            "oracle_rope_head_scalar": (None, [vp, sz, sz, f32, i32]),
+            "oracle_softmax_scalar": (None, [vp, sz]),
+            "oracle_swiglu_scalar": (None, [vp, vp, vp, sz]),
+            "oracle_causal_gqa_decode": (None, [vp, vp, vp, sz, sz, sz, sz, sz, vp, vp, f32]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    assert a.flags["C_CONTIGUOUS"], "arrays passed to the oracle must be C-contiguous"
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def f32_to_f16(x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().oracle_f32_to_f16_array(_p(x), _p(out), x.size)
+    return out
+
+
+def f16_to_f32(h):
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    out = np.empty(h.shape, np.float32)
+    lib().oracle_f16_to_f32_array(_p(h), _p(out), h.size)
+    return out
+
+
+def repack_q4_0_aos_to_soa(aos, scales_len=None, quants_len=None):
+    aos = np.ascontiguousarray(aos, dtype=np.uint8)
+    nb = aos.size // 18
+    sc = np.zeros(scales_len if scales_len is not None else nb * 2, np.uint8)
+    qu = np.zeros(quants_len if quants_len is not None else nb * 16, np.uint8)
+    r = lib().oracle_repack_q4_0_aos_to_soa(_p(aos), aos.size, _p(sc), sc.size, _p(qu), qu.size)
+    return r, sc, qu
+
+
+def dequantize_q4_0_aos(aos):
+    aos = np.ascontiguousarray(aos, dtype=np.uint8)
+    nb = aos.size // 18
+    out = np.empty(nb * 32, np.float32)
+    lib().oracle_dequantize_q4_0_aos(_p(aos), nb, _p(out))
+    return out
+
+
+def dequantize_q4_0_soa(scales_u8, quants, num_blocks):
+    scales_u8 = np.ascontiguousarray(scales_u8).view(np.uint8)
+    quants = np.ascontiguousarray(quants, dtype=np.uint8)
+    out = np.empty(num_blocks * 32, np.float32)
+    lib().oracle_dequantize_q4_0_soa(_p(scales_u8), _p(quants), num_blocks, _p(out))
+    return out
+
+
+def lookup_token_embedding_f16(scales, quants, embd, token_id):
+    scales = np.ascontiguousarray(scales).view(np.uint8)
+    quants = np.ascontiguousarray(quants, dtype=np.uint8)
+    out = np.empty(embd, np.uint16)
+    lib().oracle_lookup_token_embedding_f16(_p(scales), _p(quants), embd, token_id, _p(out))
+    return out
+
+
+def quantize_f32_to_q8_0(x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    assert x.size % 32 == 0
+    out = np.empty(x.size // 32 * 34, np.uint8)
+    lib().oracle_quantize_f32_to_q8_0(_p(x), x.size, _p(out))
+    return out
+
+
+def dequantize_q8_0_to_f32(q8, num_blocks):
+    q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+    out = np.empty(num_blocks * 32, np.float32)
+    lib().oracle_dequantize_q8_0_to_f32(_p(q8), num_blocks, _p(out))
+    return out
+
+
+def kv_store_q8_0(act_f16, kv, start_pos, capacity, blocks_per_pos, n):
+    act_f16 = np.ascontiguousarray(act_f16, dtype=np.uint16)
+    assert kv.flags["C_CONTIGUOUS"] and kv.dtype == np.uint8
+    lib().oracle_kv_store_q8_0(_p(act_f16), _p(kv), start_pos, capacity, blocks_per_pos, n)
+
+
+def kv_store_f32(vec, kv, pos, capacity, blocks_per_pos):
+    vec = np.ascontiguousarray(vec, dtype=np.float32)
+    lib().oracle_kv_store_f32(_p(vec), _p(kv), pos, capacity, blocks_per_pos)
+
+
+def vec_dot_q4_0_q8_0_scalar(ws, wq, xq8, nb):
+    return lib().oracle_vec_dot_q4_0_q8_0_scalar(_p(ws), _p(wq), _p(xq8), nb)
+
+
+def vec_dot_q4_0_q8_0_avx2(ws, wq, xq8, nb):
+    return lib().oracle_vec_dot_q4_0_q8_0_avx2(_p(ws), _p(wq), _p(xq8), nb)
+
+
+def matvec_q4_0_q8_0_avx2(ws, wq, xq8, rows, cols, threads=1):
+    out = np.empty(rows, np.float32)
+    lib().oracle_matvec_q4_0_q8_0_avx2_mt(_p(ws), _p(wq), _p(xq8), rows, cols, _p(out), threads)
+    return out
+
+
+def matvec_q4_0_q8_0_scalar(ws, wq, xq8, rows, cols):
+    out = np.empty(rows, np.float32)
+    lib().oracle_matvec_q4_0_q8_0_scalar(_p(ws), _p(wq), _p(xq8), rows, cols, _p(out))
+    return out
+
+
+def block_sums_q4_0_q8_0(ws, wq, xq8, rows, cols):
+    out = np.empty(rows * (cols // 32), np.int32)
+    lib().oracle_block_sums_q4_0_q8_0(_p(ws), _p(wq), _p(xq8), rows, cols, _p(out))
+    return out
+
+
+def gemm_q4_0_f16_scalar_reference(scales_f16, quants, x_f16, m, k, n):
+    out = np.empty(n * m, np.uint16)
+    lib().oracle_gemm_q4_0_f16_scalar_reference(_p(scales_f16), _p(quants), _p(x_f16), m, k, n,
+                                                _p(out))
+    return out
+
+
+def gemm_q4_0_f16_f32out(scales_f16, quants, x_f16, m, k, n, threads=1):
+    out = np.empty(n * m, np.float32)
+    lib().oracle_gemm_q4_0_f16_scalar_f32out(_p(scales_f16), _p(quants), _p(x_f16), m, k, n,
+                                             _p(out), threads)
+    return out
+
+
+def cpu_prefill_projection(ws, wq, x_f32, m, k, n, threads=1):
+    out = np.empty(n * m, np.float32)
+    lib().oracle_cpu_prefill_projection(_p(ws), _p(wq), _p(x_f32), m, k, n, _p(out), threads)
+    return out
+
+
+def rmsnorm_scalar(x, w, eps):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm_scalar(_p(x), _p(w), x.size, eps, _p(out))
+    return out
+
+
+def rmsnorm_avx2(x, w, eps):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm_avx2(_p(x), _p(w), x.size, eps, _p(out))
+    return out
+
+
+def rope_head(vec, pos, rope_dim, freq_base, mode):
+    v = np.array(vec, dtype=np.float32, copy=True)
+    lib().oracle_rope_head_scalar(_p(v), pos, rope_dim, freq_base, mode)
+    return v
+
+
+def softmax(x):
+    v = np.array(x, dtype=np.float32, copy=True)
+    lib().oracle_softmax_scalar(_p(v), v.size)
+    return v
+
+
+def swiglu(gate, up):
+    gate = np.ascontiguousarray(gate, np.float32)
+    up = np.ascontiguousarray(up, np.float32)
+    out = np.empty_like(gate)
+    lib().oracle_swiglu_scalar(_p(gate), _p(up), _p(out), gate.size)
+    return out
+
+
+def causal_gqa_decode(q, k_ring, v_ring, capacity, context_len, head_count, head_count_kv,
+                      head_dim, softcap=0.0):
+    q = np.ascontiguousarray(q, np.float32)
+    k_ring = np.ascontiguousarray(k_ring, np.uint8)
+    v_ring = np.ascontiguousarray(v_ring, np.uint8)
+    scores = np.empty(max(context_len, 1), np.float32)
+    out = np.empty(head_count * head_dim, np.float32)
+    lib().oracle_causal_gqa_decode(_p(q), _p(k_ring), _p(v_ring), capacity, context_len,
+                                   head_count, head_count_kv, head_dim, _p(scores), _p(out),
+                                   softcap)
+    return out

@@ -1,0 +1,113 @@
+/*
+ * sulimo_oracle.h — CPU restatement of Sulimo's quantized-matmul hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker that the CUDA
+ * kernels of sulimo_b200 are compared against, and the CPU baseline that
+ * bench.py times beside them.  Nothing in the product path (the C-ABI
+ * library libsulimo_cuda.so and the sulimo_b200 package) links or calls it.
+ *
+ * Every function restates one function of the reference (a Rust workspace;
+ * paths below are relative to the reference repository root) and cites the
+ * lines it follows.  The reference cannot be built in this environment (no
+ * Rust toolchain), so the restatement is pinned by re-running the
+ * reference's own unit tests against it (tests/test_oracle.py) rather than
+ * by reference-produced values.
+ *
+ * Numeric conventions carried over from Rust:
+ *   - no FMA contraction (the library is built with -ffp-contract=off);
+ *   - f32 -> f16 is IEEE round-to-nearest-even (the `half` crate 2.7.1),
+ *     done here with the F16C instruction VCVTPS2PH;
+ *   - f32::round is roundf (half away from zero); `as i8` after clamp;
+ *   - f32::exp/powf/sin/cos/sqrt are glibc's expf/powf/sinf/cosf/sqrtf.
+ */
+#ifndef SULIMO_ORACLE_H
+#define SULIMO_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- f16 helpers (half 2.7.1 semantics) ---- */
+uint16_t oracle_f32_to_f16(float x);
+float oracle_f16_to_f32(uint16_t h);
+void oracle_f32_to_f16_array(const float* src, uint16_t* dst, size_t n);
+void oracle_f16_to_f32_array(const uint16_t* src, float* dst, size_t n);
+
+/* ---- Q4_0 repack / dequant (crates/sulimo-core/src/repack.rs) ---- */
+/* returns number of blocks, or -1 (InvalidAosLength) / -2 / -3 (buffer too small) */
+long oracle_repack_q4_0_aos_to_soa(const uint8_t* src_aos, size_t src_len,
+                                   uint8_t* dst_scales, size_t scales_len,
+                                   uint8_t* dst_quants, size_t quants_len);
+void oracle_dequantize_q4_0_aos(const uint8_t* src_aos, size_t num_blocks, float* dst);
+void oracle_dequantize_q4_0_soa(const uint8_t* scales, const uint8_t* quants,
+                                size_t num_blocks, float* dst);
+/* f16 dequant of one embedding row (crates/sulimo-engine/src/scheduler.rs:329-374) */
+void oracle_lookup_token_embedding_f16(const uint8_t* scales, const uint8_t* quants,
+                                       size_t embd_dim, uint32_t token_id, uint16_t* out_f16);
+
+/* ---- Q8_0 (crates/sulimo-core/src/kv_cache.rs) ---- */
+void oracle_quantize_f32_to_q8_0(const float* src, size_t n, uint8_t* dst_q8);
+void oracle_dequantize_q8_0_to_f32(const uint8_t* src_q8, size_t num_blocks, float* dst);
+/* kv_store_q8_0 (kernels/prefill.cl:72-116) fed by the CPU quantizer: f16 activations
+ * [n][blocks_per_pos*32] into ring slots (start_pos+t) % capacity. */
+void oracle_kv_store_q8_0(const uint16_t* act_f16, uint8_t* kv, size_t start_pos,
+                          size_t capacity, size_t blocks_per_pos, size_t n);
+/* KvCache::store_key/store_value (kv_cache.rs:93-110): f32 vector into slot pos % capacity */
+void oracle_kv_store_f32(const float* vec, uint8_t* kv, size_t pos, size_t capacity,
+                         size_t blocks_per_pos);
+
+/* ---- Q4_0 x Q8_0 dot / matvec (crates/sulimo-cpu/src/{scalar,avx2}.rs) ---- */
+float oracle_vec_dot_q4_0_q8_0_scalar(const uint8_t* w_scales, const uint8_t* w_quants,
+                                      const uint8_t* x_q8, size_t num_blocks);
+void oracle_matvec_q4_0_q8_0_scalar(const uint8_t* w_scales, const uint8_t* w_quants,
+                                    const uint8_t* x_q8, size_t rows, size_t cols, float* out);
+float oracle_vec_dot_q4_0_q8_0_avx2(const uint8_t* w_scales, const uint8_t* w_quants,
+                                    const uint8_t* x_q8, size_t num_blocks);
+void oracle_matvec_q4_0_q8_0_avx2(const uint8_t* w_scales, const uint8_t* w_quants,
+                                  const uint8_t* x_q8, size_t rows, size_t cols, float* out);
+/* Same as above over a contiguous row range, on `threads` POSIX threads (harness
+ * partitioning for the CPU baseline; each row is computed exactly as above). */
+void oracle_matvec_q4_0_q8_0_avx2_mt(const uint8_t* w_scales, const uint8_t* w_quants,
+                                     const uint8_t* x_q8, size_t rows, size_t cols, float* out,
+                                     int threads);
+/* Integer per-block sums: out[r*nb+b] = sum_i (w_i-8)*x_i (exact i32). */
+void oracle_block_sums_q4_0_q8_0(const uint8_t* w_scales, const uint8_t* w_quants,
+                                 const uint8_t* x_q8, size_t rows, size_t cols, int32_t* out);
+
+/* ---- Prefill GEMM (crates/sulimo-ocl/src/gemm.rs:106-147) ---- */
+void oracle_gemm_q4_0_f16_scalar_reference(const uint16_t* scales, const uint8_t* quants,
+                                           const uint16_t* x, size_t m, size_t k, size_t n,
+                                           uint16_t* out);
+/* same arithmetic, fp32 result (logits_f16_output, kernels/prefill.cl:269-308) */
+void oracle_gemm_q4_0_f16_scalar_f32out(const uint16_t* scales, const uint8_t* quants,
+                                        const uint16_t* x, size_t m, size_t k, size_t n,
+                                        float* out, int threads);
+/* Reference CPU prefill of n tokens through one Q4_0 projection (engine.rs:287-318 ->
+ * forward_token -> quantize_f32_to_q8_0 + matvec_q4_0_q8_0_avx2), fp32 activations in. */
+void oracle_cpu_prefill_projection(const uint8_t* w_scales, const uint8_t* w_quants,
+                                   const float* x, size_t m, size_t k, size_t n, float* out,
+                                   int threads);
+
+/* ---- small ops (crates/sulimo-cpu/src/{scalar,avx2}.rs) ---- */
+void oracle_rmsnorm_scalar(const float* x, const float* w, size_t len, float eps, float* out);
+void oracle_rmsnorm_avx2(const float* x, const float* w, size_t len, float eps, float* out);
+void oracle_rope_head_scalar(float* vec, size_t pos, size_t rope_dim, float freq_base, int mode);
+void oracle_softmax_scalar(float* x, size_t n);
+void oracle_swiglu_scalar(const float* gate, const float* up, float* out, size_t n);
+
+/* ---- decode attention (crates/sulimo-cpu/src/scalar.rs:287-359) ----
+ * k_ring / v_ring: one layer's ring, capacity slots of (head_count_kv*head_dim/32)*34 bytes.
+ * Position p reads slot p % capacity (KvCache::key_ptr, kv_cache.rs:114-119).
+ * scores_buf must hold context_len floats.  softcap <= 0 means none. */
+void oracle_causal_gqa_decode(const float* q, const uint8_t* k_ring, const uint8_t* v_ring,
+                              size_t capacity, size_t context_len, size_t head_count,
+                              size_t head_count_kv, size_t head_dim, float* scores_buf,
+                              float* out, float softcap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,467 @@
+// capi.cu — the extern "C" boundary of libsulimo_cuda: context, buffers, events, argument
+// checks and dispatch to the sm_100a kernels.  Mirrors the host runtime of the reference's
+// sulimo-ocl crate (program.rs, buffer.rs, waiter.rs, gemm.rs, prefill.rs) with CUDA objects.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+#include <time.h>
+
+#include <atomic>
+#include <mutex>
+#include <string>
+
+#include "sulimo_internal.h"
+
+namespace {
+thread_local std::string g_last_error;
+std::atomic<size_t> g_live_buffers{0};
+}  // namespace
+
+struct sulimo_buf {
+    sulimo_ctx* ctx = nullptr;
+    void* dev = nullptr;
+    size_t size = 0;
+    int read_only = 0;
+};
+
+struct sulimo_event {
+    cudaEvent_t ev = nullptr;
+    sulimo_ctx* ctx = nullptr;
+};
+
+namespace sulimo {
+
+int set_error(int status, const std::string& msg) {
+    g_last_error = msg;
+    return status;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return SULIMO_OK;
+    int st = (e == cudaErrorMemoryAllocation) ? SULIMO_EOOM : SULIMO_ELAUNCH;
+    return set_error(st, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int ensure_workspace(sulimo_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->workspace_bytes) return SULIMO_OK;
+    // Growing frees the old block, which in-flight work may still read: drain first.
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return check_cuda(e, "workspace sync");
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    ctx->workspace = nullptr;
+    ctx->workspace_bytes = 0;
+    size_t want = bytes < (size_t)(1 << 20) ? (size_t)(1 << 20) : bytes;
+    e = cudaMalloc(&ctx->workspace, want);
+    if (e != cudaSuccess) return check_cuda(e, "workspace cudaMalloc");
+    ctx->workspace_bytes = want;
+    return SULIMO_OK;
+}
+
+EncodeTiledFn get_encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+}  // namespace sulimo
+
+using sulimo::set_error;
+
+static int check_ctx(sulimo_ctx* ctx) {
+    if (!ctx) return set_error(SULIMO_EINVAL, "null context");
+    return SULIMO_OK;
+}
+
+static int bind_device(sulimo_ctx* ctx) {
+    cudaError_t e = cudaSetDevice(ctx->device);
+    return sulimo::check_cuda(e, "cudaSetDevice");
+}
+
+static bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+extern "C" {
+
+const char* sulimo_cuda_last_error(void) { return g_last_error.c_str(); }
+
+const char* sulimo_cuda_version(void) { return "sulimo_cuda 0.1.0 sm_100a"; }
+
+// ---- context ------------------------------------------------------------------------------
+
+int sulimo_cuda_ctx_create(int device, sulimo_ctx** out) {
+    if (!out) return set_error(SULIMO_EINVAL, "out is null");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+        return set_error(SULIMO_ENODEV, "no CUDA device");
+    if (device < 0 || device >= n) return set_error(SULIMO_ENODEV, "device index out of range");
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+        return set_error(SULIMO_ENODEV, "cudaGetDeviceProperties failed");
+    if (prop.major != 10)
+        return set_error(SULIMO_ENODEV, std::string("device is not sm_100 class: ") + prop.name);
+    if (cudaSetDevice(device) != cudaSuccess) return set_error(SULIMO_ENODEV, "cudaSetDevice");
+    sulimo_ctx* ctx = new sulimo_ctx();
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    cudaError_t e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return sulimo::check_cuda(e, "cudaStreamCreate");
+    }
+    ctx->stream = ctx->own_stream;
+    e = cudaMalloc(&ctx->d_error, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_error, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(ctx->own_stream);
+        delete ctx;
+        return sulimo::check_cuda(e, "error word");
+    }
+    if (!sulimo::get_encode_tiled()) {
+        cudaFree(ctx->d_error);
+        cudaStreamDestroy(ctx->own_stream);
+        delete ctx;
+        return set_error(SULIMO_ENODEV, "cuTensorMapEncodeTiled unavailable");
+    }
+    *out = ctx;
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_ctx_destroy(sulimo_ctx* ctx) {
+    if (!ctx) return SULIMO_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    if (ctx->d_error) cudaFree(ctx->d_error);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_ctx_synchronize(sulimo_ctx* ctx) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if ((st = bind_device(ctx))) return st;
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return sulimo::check_cuda(e, "cudaStreamSynchronize");
+    int flag = 0;
+    e = cudaMemcpy(&flag, ctx->d_error, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return sulimo::check_cuda(e, "read error word");
+    if (flag != 0) {
+        cudaMemset(ctx->d_error, 0, sizeof(int));
+        return set_error(SULIMO_EDEVICE, std::string("device-side error code ") +
+                                             std::to_string(flag) +
+                                             (flag == 1 ? " (bounded wait ran out)" : ""));
+    }
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_ctx_set_stream(sulimo_ctx* ctx, void* cuda_stream) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    ctx->stream = cuda_stream ? (cudaStream_t)cuda_stream : ctx->own_stream;
+    return SULIMO_OK;
+}
+
+void* sulimo_cuda_ctx_get_stream(sulimo_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int sulimo_cuda_ctx_device(sulimo_ctx* ctx) { return ctx ? ctx->device : -1; }
+
+uint64_t sulimo_cuda_ctx_launch_count(sulimo_ctx* ctx) { return ctx ? ctx->launches.load() : 0; }
+
+// ---- buffers ------------------------------------------------------------------------------
+
+int sulimo_cuda_buffer_alloc(sulimo_ctx* ctx, size_t size, sulimo_buf** out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (!out) return set_error(SULIMO_EINVAL, "out is null");
+    *out = nullptr;
+    if ((st = bind_device(ctx))) return st;
+    sulimo_buf* b = new sulimo_buf();
+    b->ctx = ctx;
+    b->size = size;
+    if (size) {
+        cudaError_t e = cudaMalloc(&b->dev, size);
+        if (e != cudaSuccess) {
+            delete b;
+            return sulimo::check_cuda(e, "buffer cudaMalloc");
+        }
+    }
+    g_live_buffers.fetch_add(1);
+    *out = b;
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_buffer_from_host(sulimo_ctx* ctx, const void* host_ptr, size_t size,
+                                 int read_only, int strict_arena, sulimo_buf** out) {
+    if (!out) return set_error(SULIMO_EINVAL, "out is null");
+    *out = nullptr;
+    if (size && !host_ptr) return set_error(SULIMO_EINVAL, "host_ptr is null");
+    if (strict_arena && (!aligned(host_ptr, 4096) || size % 64 != 0))
+        return set_error(SULIMO_EALIGN,
+                         "host_ptr must be 4096-byte aligned and size a multiple of 64");
+    sulimo_buf* b = nullptr;
+    int st = sulimo_cuda_buffer_alloc(ctx, size, &b);
+    if (st) return st;
+    b->read_only = read_only;
+    if (size) {
+        cudaError_t e = cudaMemcpy(b->dev, host_ptr, size, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            sulimo_cuda_buffer_free(b);
+            return sulimo::check_cuda(e, "buffer upload");
+        }
+    }
+    *out = b;
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_buffer_write(sulimo_buf* buf, size_t offset, const void* host_src, size_t n) {
+    if (!buf) return set_error(SULIMO_EINVAL, "null buffer");
+    if (offset > buf->size || n > buf->size - offset)
+        return set_error(SULIMO_EINVAL, "write out of buffer bounds");
+    if (n == 0) return SULIMO_OK;
+    int st = bind_device(buf->ctx);
+    if (st) return st;
+    cudaError_t e = cudaMemcpyAsync((char*)buf->dev + offset, host_src, n, cudaMemcpyHostToDevice,
+                                    buf->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(buf->ctx->stream);
+    return sulimo::check_cuda(e, "buffer write");
+}
+
+int sulimo_cuda_buffer_read(sulimo_buf* buf, size_t offset, void* host_dst, size_t n) {
+    if (!buf) return set_error(SULIMO_EINVAL, "null buffer");
+    if (offset > buf->size || n > buf->size - offset)
+        return set_error(SULIMO_EINVAL, "read out of buffer bounds");
+    if (n == 0) return SULIMO_OK;
+    int st = bind_device(buf->ctx);
+    if (st) return st;
+    cudaError_t e = cudaMemcpyAsync(host_dst, (const char*)buf->dev + offset, n,
+                                    cudaMemcpyDeviceToHost, buf->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(buf->ctx->stream);
+    return sulimo::check_cuda(e, "buffer read");
+}
+
+void* sulimo_cuda_buffer_device_ptr(sulimo_buf* buf) { return buf ? buf->dev : nullptr; }
+
+size_t sulimo_cuda_buffer_size(sulimo_buf* buf) { return buf ? buf->size : 0; }
+
+int sulimo_cuda_buffer_free(sulimo_buf* buf) {
+    if (!buf) return SULIMO_OK;
+    if (buf->dev) {
+        cudaSetDevice(buf->ctx->device);
+        cudaFree(buf->dev);
+    }
+    delete buf;
+    g_live_buffers.fetch_sub(1);
+    return SULIMO_OK;
+}
+
+size_t sulimo_cuda_live_buffer_count(void) { return g_live_buffers.load(); }
+
+// ---- events -------------------------------------------------------------------------------
+
+int sulimo_cuda_event_record(sulimo_ctx* ctx, sulimo_event** out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (!out) return set_error(SULIMO_EINVAL, "out is null");
+    *out = nullptr;
+    if ((st = bind_device(ctx))) return st;
+    sulimo_event* ev = new sulimo_event();
+    ev->ctx = ctx;
+    cudaError_t e = cudaEventCreateWithFlags(&ev->ev, cudaEventBlockingSync | cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ev->ev, ctx->stream);
+    if (e != cudaSuccess) {
+        if (ev->ev) cudaEventDestroy(ev->ev);
+        delete ev;
+        return sulimo::check_cuda(e, "event record");
+    }
+    *out = ev;
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_event_wait(sulimo_event* ev, uint64_t timeout_ns) {
+    if (!ev) return set_error(SULIMO_EINVAL, "null event");
+    int st = bind_device(ev->ctx);
+    if (st) return st;
+    if (timeout_ns == 0) {
+        cudaError_t e = cudaEventSynchronize(ev->ev);  // blocking sync: the thread sleeps
+        if (e != cudaSuccess) return sulimo::check_cuda(e, "cudaEventSynchronize");
+    } else {
+        struct timespec t0, t1;
+        clock_gettime(CLOCK_MONOTONIC, &t0);
+        uint64_t sleep_ns = 2000;
+        while (true) {
+            cudaError_t e = cudaEventQuery(ev->ev);
+            if (e == cudaSuccess) break;
+            if (e != cudaErrorNotReady) return sulimo::check_cuda(e, "cudaEventQuery");
+            clock_gettime(CLOCK_MONOTONIC, &t1);
+            uint64_t el = (uint64_t)(t1.tv_sec - t0.tv_sec) * 1000000000ull +
+                          (uint64_t)(t1.tv_nsec - t0.tv_nsec);
+            if (el >= timeout_ns) return set_error(SULIMO_ETIMEOUT, "event wait deadline passed");
+            struct timespec ts = {0, (long)sleep_ns};
+            nanosleep(&ts, nullptr);
+            if (sleep_ns < 200000) sleep_ns *= 2;
+        }
+    }
+    int flag = 0;
+    cudaError_t e = cudaMemcpy(&flag, ev->ctx->d_error, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return sulimo::check_cuda(e, "read error word");
+    if (flag) {
+        cudaMemset(ev->ctx->d_error, 0, sizeof(int));
+        return set_error(SULIMO_EDEVICE, "device-side error code " + std::to_string(flag));
+    }
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_event_free(sulimo_event* ev) {
+    if (!ev) return SULIMO_OK;
+    if (ev->ev) cudaEventDestroy(ev->ev);
+    delete ev;
+    return SULIMO_OK;
+}
+
+// ---- kernels ------------------------------------------------------------------------------
+
+int sulimo_cuda_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants,
+                              const void* x, void* out, int m, int k, int n, int out_dtype) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (m <= 0 || k <= 0 || n < 0) return set_error(SULIMO_EINVAL, "m, k must be > 0, n >= 0");
+    if (k % 32 != 0) return set_error(SULIMO_EINVAL, "K must be a multiple of 32 (Q4_0 block size)");
+    if (m % 8 != 0) return set_error(SULIMO_EINVAL, "M must be a multiple of 8");
+    if (out_dtype != SULIMO_OUT_F16 && out_dtype != SULIMO_OUT_F32)
+        return set_error(SULIMO_EINVAL, "out_dtype must be SULIMO_OUT_F16 or SULIMO_OUT_F32");
+    if (n == 0) return SULIMO_OK;
+    if (!scales || !quants || !x || !out) return set_error(SULIMO_EINVAL, "null tensor pointer");
+    if (!aligned(x, 16) || !aligned(quants, 16) || !aligned(out, 16) || !aligned(scales, 2))
+        return set_error(SULIMO_EALIGN, "x, quants, out must be 16-byte aligned, scales 2-byte");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_gemm_q4_0_f16(ctx, scales, quants, x, out, m, k, n, out_dtype, k, 0);
+}
+
+int sulimo_cuda_logits_final(sulimo_ctx* ctx, const void* x_all, const void* scales,
+                             const void* quants, float* logits, int vocab, int embd,
+                             int token_idx) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (vocab <= 0 || embd <= 0 || token_idx < 0)
+        return set_error(SULIMO_EINVAL, "vocab, embd must be > 0 and token_idx >= 0");
+    if (embd % 32 != 0) return set_error(SULIMO_EINVAL, "embd must be a multiple of 32");
+    if (vocab % 8 != 0) return set_error(SULIMO_EINVAL, "vocab must be a multiple of 8");
+    if (!x_all || !scales || !quants || !logits) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(x_all, 16) || !aligned(quants, 16) || !aligned(logits, 16))
+        return set_error(SULIMO_EALIGN, "x_all, quants, logits must be 16-byte aligned");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_gemm_q4_0_f16(ctx, scales, quants, x_all, logits, vocab, embd, 1,
+                                        SULIMO_OUT_F32, embd, token_idx);
+}
+
+int sulimo_cuda_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
+                               const void* x_q8, int rows, int cols, int batch, float* out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (rows < 0 || cols <= 0 || batch < 0) return set_error(SULIMO_EINVAL, "bad shape");
+    if (cols % 32 != 0) return set_error(SULIMO_EINVAL, "cols must be a multiple of 32");
+    if (rows == 0 || batch == 0) return SULIMO_OK;
+    if (!w_scales || !w_quants || !x_q8 || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(w_quants, 16) || !aligned(w_scales, 2) || !aligned(x_q8, 2) || !aligned(out, 4))
+        return set_error(SULIMO_EALIGN, "w_quants must be 16-byte aligned, scales/x_q8 2-byte");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_gemv_q4_0_q8_0(ctx, w_scales, w_quants, x_q8, rows, cols, batch, out);
+}
+
+int sulimo_cuda_block_sums_q4_0_q8_0(sulimo_ctx* ctx, const void* w_quants, const void* x_q8,
+                                     int rows, int cols, int32_t* out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (rows < 0 || cols <= 0 || cols % 32 != 0) return set_error(SULIMO_EINVAL, "bad shape");
+    if (rows == 0) return SULIMO_OK;
+    if (!w_quants || !x_q8 || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(w_quants, 16) || !aligned(x_q8, 2))
+        return set_error(SULIMO_EALIGN, "w_quants must be 16-byte aligned, x_q8 2-byte");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_block_sums(ctx, w_quants, x_q8, rows, cols, out);
+}
+
+int sulimo_cuda_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst_q8, size_t n) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (n % 32 != 0) return set_error(SULIMO_EINVAL, "n must be a multiple of 32");
+    if (n == 0) return SULIMO_OK;
+    if (!src || !dst_q8) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(src, 4) || !aligned(dst_q8, 2)) return set_error(SULIMO_EALIGN, "misaligned");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_quantize_q8_0(ctx, src, dst_q8, n);
+}
+
+int sulimo_cuda_kv_store_q8_0(sulimo_ctx* ctx, const void* act, int act_dtype, void* kv_ring,
+                              size_t start_pos, size_t capacity, size_t blocks_per_pos,
+                              size_t n) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (act_dtype != SULIMO_ACT_F16 && act_dtype != SULIMO_ACT_F32)
+        return set_error(SULIMO_EINVAL, "act_dtype must be SULIMO_ACT_F16 or SULIMO_ACT_F32");
+    if (capacity == 0 || blocks_per_pos == 0)
+        return set_error(SULIMO_EINVAL, "capacity and blocks_per_pos must be > 0");
+    if (n == 0) return SULIMO_OK;
+    if (!act || !kv_ring) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(act, act_dtype == SULIMO_ACT_F16 ? 2 : 4) || !aligned(kv_ring, 2))
+        return set_error(SULIMO_EALIGN, "misaligned");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_kv_store_q8_0(ctx, act, act_dtype, kv_ring, start_pos, capacity,
+                                        blocks_per_pos, n);
+}
+
+int sulimo_cuda_dequantize_q4_0_rows(sulimo_ctx* ctx, const void* scales, const void* quants,
+                                     int cols, const int32_t* row_ids, int count, void* out,
+                                     int out_dtype) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (cols <= 0 || cols % 32 != 0 || count < 0)
+        return set_error(SULIMO_EINVAL, "cols must be a positive multiple of 32");
+    if (out_dtype != SULIMO_OUT_F16 && out_dtype != SULIMO_OUT_F32)
+        return set_error(SULIMO_EINVAL, "bad out_dtype");
+    if (count == 0) return SULIMO_OK;
+    if (!scales || !quants || !row_ids || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(quants, 16) || !aligned(scales, 2)) return set_error(SULIMO_EALIGN, "misaligned");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_dequant_rows(ctx, scales, quants, cols, row_ids, count, out, out_dtype);
+}
+
+int sulimo_cuda_attn_decode_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                                 const void* v_ring, size_t seq_stride_bytes, size_t capacity,
+                                 size_t context_len, int head_count, int head_count_kv,
+                                 int head_dim, int batch, float softcap, float* out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (head_count <= 0 || head_count_kv <= 0 || head_count % head_count_kv != 0)
+        return set_error(SULIMO_EINVAL, "head_count must be a positive multiple of head_count_kv");
+    if (head_dim <= 0 || head_dim % 32 != 0 || head_dim > 256)
+        return set_error(SULIMO_EINVAL, "head_dim must be a multiple of 32 in [32, 256]");
+    if (head_count / head_count_kv > 8)
+        return set_error(SULIMO_EINVAL, "at most 8 query heads per KV head");
+    if (batch < 0 || capacity == 0) return set_error(SULIMO_EINVAL, "bad batch / capacity");
+    if (batch == 0) return SULIMO_OK;
+    if (!q || !k_ring || !v_ring || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(q, 16) || !aligned(out, 16) || !aligned(k_ring, 2) || !aligned(v_ring, 2) ||
+        seq_stride_bytes % 2 != 0)
+        return set_error(SULIMO_EALIGN, "q/out 16-byte aligned, rings 2-byte aligned");
+    if ((st = bind_device(ctx))) return st;
+    int splits = 0;
+    size_t pbytes = sulimo::attn_decode_partial_bytes(context_len, head_count, head_dim, batch,
+                                                      ctx->num_sms, &splits);
+    if ((st = sulimo::ensure_workspace(ctx, pbytes))) return st;
+    return sulimo::launch_attn_decode(ctx, q, k_ring, v_ring, seq_stride_bytes, capacity,
+                                      context_len, head_count, head_count_kv, head_dim, batch,
+                                      softcap, out, (float*)ctx->workspace, ctx->workspace_bytes);
+}
+
+}  // extern "C"

@@ -1,0 +1,378 @@
+// gemm_q4_0_tc.cu — Q4_0-weight prefill GEMM on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// Computes the reference's gemm_q4_0_f16 (kernels/gemm_q4_0.cl:13-130, host crates/sulimo-ocl/
+// src/gemm.rs:28-102, CPU form gemm.rs:106-147):
+//     out[t][r] = sum_b d[r][b] * sum_i x[t][32b+i] * (q[r][b][i] - 8)
+// for m weight rows ("features") r, k input channels and n tokens t, f16 activations, fp32
+// accumulation, f16 (or f32) results.
+//
+// Data flow per CTA (128 features x up to 256 tokens, K streamed in 64-wide stages):
+//   warp 0   TMA: activations x[n0.., k0..k0+63] -> smem (128B-swizzled, K-major) and the raw
+//            Q4_0 nibbles of the 128 feature rows (32 bytes per row) -> smem.
+//   warps 2-5 dequant: each thread owns one feature row (= one TMEM lane), turns its 2 Q4_0
+//            blocks of the stage into 64 f16 weights f16(d*(q-8)) (exact (q-8) via the
+//            0x6400 magic, one RNE multiply by d; the rounding of the reference's f16 embedding
+//            path, crates/sulimo-engine/src/scheduler.rs:345-357) and writes them to the
+//            stage's TMEM columns with tcgen05.st.  The weights never touch shared memory.
+//   warp 1   one thread issues tcgen05.mma kind::f16, A = weights from TMEM (M = 128 features),
+//            B = activations from smem (N = tokens), D = fp32 accumulators in TMEM; each stage
+//            is released with tcgen05.commit.
+//   warps 2-5 epilogue: tcgen05.ld of the accumulators (lane = feature), convert, store
+//            out[t][r] (32 consecutive features per warp store: 64-byte coalesced rows).
+// Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records a device error,
+// drains its in-flight copies / MMAs (again bounded), frees TMEM and returns.
+// No TMA multicast: each CTA loads its own tiles.
+#include "sulimo_common.cuh"
+#include "sulimo_internal.h"
+
+namespace sulimo {
+namespace {
+
+constexpr int BM = 128;           // features per CTA = MMA M = TMEM lanes
+constexpr int BK = 64;            // k per stage: 2 Q4_0 blocks, one 128-byte swizzle row of f16
+constexpr int BN_MAX = 256;       // tokens per CTA = MMA N (max)
+constexpr int STAGES = 4;
+constexpr int THREADS = 192;      // 6 warps
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t A_COL = 0;     // A stages: columns [32*s, 32*s+32)
+constexpr uint32_t ACC_COL = 128; // accumulators: columns [128, 128+bn)
+constexpr uint32_t X_STAGE = BN_MAX * 128;  // bytes
+constexpr uint32_t Q_STAGE = BM * 32;       // bytes
+constexpr uint32_t SMEM_BYTES = STAGES * (X_STAGE + Q_STAGE) + 256 + 1024;
+
+// ---- tcgen05 / TMA wrappers ----------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
+    d |= (uint64_t)1 << 16;                    // leading byte offset (unused for SW128 K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset
+    d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Loads 32 columns of this warp's 32 TMEM lanes and waits for them; the wait carries the
+// registers as operands so no use can be scheduled before it.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+          "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]),
+                   "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]),
+                   "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]),
+                   "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]),
+                   "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]),
+                   "+r"(v[30]), "+r"(v[31])
+                 :
+                 : "memory");
+}
+
+// 16 quant bytes of one Q4_0 block -> 16 packed f16x2 words (TMEM columns of the block):
+// column c holds weights k = 2c, 2c+1 of the block; weights 0..15 are the low nibbles of
+// bytes 0..15, weights 16..31 the high nibbles (repack.rs:122-129).
+__device__ __forceinline__ void dequant_block(const uint4 q, uint32_t dbits, uint32_t* col) {
+    const __half2 d2 = __halves2half2(__ushort_as_half((uint16_t)dbits),
+                                      __ushort_as_half((uint16_t)dbits));
+    const __half2 k1032 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+        const uint32_t lo = words[w] & 0x0F0F0F0Fu;
+        const uint32_t hi = (words[w] >> 4) & 0x0F0F0F0Fu;
+        // {0x6400 | nibble} is the f16 value 1024 + nibble; minus 1032 gives nibble - 8 exactly.
+        const uint32_t p[4] = {prmt(lo, 0x64646464u, 0x4140), prmt(lo, 0x64646464u, 0x4342),
+                               prmt(hi, 0x64646464u, 0x4140), prmt(hi, 0x64646464u, 0x4342)};
+        __half2 h[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            h[e] = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p[e]), k1032), d2);
+        }
+        col[2 * w] = *reinterpret_cast<uint32_t*>(&h[0]);
+        col[2 * w + 1] = *reinterpret_cast<uint32_t*>(&h[1]);
+        col[8 + 2 * w] = *reinterpret_cast<uint32_t*>(&h[2]);
+        col[8 + 2 * w + 1] = *reinterpret_cast<uint32_t*>(&h[3]);
+    }
+}
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_q4_0_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                        const __grid_constant__ CUtensorMap tmap_q,
+                        const uint16_t* __restrict__ scales, void* __restrict__ out, int m, int k,
+                        int n, int bn, int nb, int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    uint8_t* sx = smem;
+    uint8_t* sq = smem + STAGES * X_STAGE;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sq + STAGES * Q_STAGE);
+    uint64_t* empty = full + STAGES;
+    uint64_t* afull = empty + STAGES;
+    uint64_t* done = afull + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * bn;
+    const int num_k = (k + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&afull[s], 128);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < num_k; i++) {
+                const int s = i % STAGES;
+                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
+                mbar_arrive_expect_tx(&full[s], (uint32_t)bn * 128u + Q_STAGE);
+                tma_load_2d(sx + s * X_STAGE, &tmap_x, i * BK, n0, &full[s]);
+                tma_load_2d(sq + s * Q_STAGE, &tmap_q, i * 32, m0, &full[s]);
+                issued = i + 1;
+            }
+            if (*abort_flag) {
+                // drain: the copies already issued must land before the CTA's smem is released
+                for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
+                    mbar_wait_bounded(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, err,
+                                      nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ------------------------------
+        if (lane == 0) {
+            // kind::f16: D f32 (bits 4-5 = 1), A = B = f16, both K-major, N>>3 at 17, M>>4 at 24
+            const uint32_t idesc =
+                (1u << 4) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+            for (int i = 0; i < num_k; i++) {
+                const int s = i % STAGES;
+                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+                if (!mbar_wait_bounded(&afull[s], ph, err, abort_flag)) break;
+                tc_fence_after();
+                const uint64_t bdesc = sw128_desc(smem_u32(sx + s * X_STAGE));
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++) {
+                    // +32 bytes per 16-element K step inside the swizzled 128-byte rows
+                    mma_ts(tmem + ACC_COL, tmem + A_COL + (uint32_t)s * 32u + (uint32_t)kk * 8u,
+                           bdesc + (uint64_t)(kk * 2), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(done);
+            if (*abort_flag) mbar_wait_bounded(done, 0, err, nullptr);  // MMAs drained
+        }
+    } else {
+        // --------------------------- dequant, then epilogue ---------------------------
+        const uint32_t quarter = (uint32_t)(warp & 3);
+        const int r = (int)quarter * 32 + lane;  // feature row within the tile == TMEM lane
+        const int grow = m0 + r;
+        const bool row_ok = grow < m;
+        const uint16_t* srow = scales + (size_t)(row_ok ? grow : 0) * nb;
+        const uint32_t lane_base = (quarter * 32u) << 16;
+        uint32_t s0n = 0, s1n = 0;
+        if (row_ok) {
+            s0n = __ldg(srow + 0);
+            s1n = (1 < nb) ? __ldg(srow + 1) : 0u;
+        }
+        bool ok = true;
+        for (int i = 0; i < num_k; i++) {
+            const int s = i % STAGES;
+            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            const uint32_t s0 = s0n, s1 = s1n;
+            if (row_ok) {  // prefetch the next stage's two block scales
+                const int kb = 2 * (i + 1);
+                s0n = (kb < nb) ? __ldg(srow + kb) : 0u;
+                s1n = (kb + 1 < nb) ? __ldg(srow + kb + 1) : 0u;
+            }
+            if (!mbar_wait_bounded(&full[s], ph, err, abort_flag)) {
+                ok = false;
+                break;
+            }
+            const uint4* qp = reinterpret_cast<const uint4*>(sq + s * Q_STAGE + r * 32);
+            const uint4 qa = qp[0], qb = qp[1];
+            uint32_t cols[32];
+            dequant_block(qa, row_ok ? s0 : 0u, cols);
+            dequant_block(qb, row_ok ? s1 : 0u, cols + 16);
+            tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * 32u, cols);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(&afull[s]);
+        }
+        if (ok && mbar_wait_bounded(done, 0, err, abort_flag)) {
+            tc_fence_after();
+            for (int c0 = 0; c0 < bn; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_base + ACC_COL + (uint32_t)c0, v);
+                if (row_ok) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int t = n0 + c0 + j;
+                        if (c0 + j < bn && t < n) {
+                            const float f = __uint_as_float(v[j]);
+                            if (OUT_F32)
+                                reinterpret_cast<float*>(out)[(size_t)t * m + grow] = f;
+                            else
+                                reinterpret_cast<__half*>(out)[(size_t)t * m + grow] =
+                                    __float2half_rn(f);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swz) {
+    EncodeTiledFn enc = get_encode_tiled();
+    if (!enc) return set_error(SULIMO_ENODEV, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(SULIMO_ELAUNCH, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return SULIMO_OK;
+}
+
+}  // namespace
+
+int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
+                         void* out, int m, int k, int n, int out_dtype, int x_row_stride,
+                         int x_row_offset) {
+    const int nb = k / 32;
+    int bn = ((n + 15) / 16) * 16;
+    if (bn > BN_MAX) bn = BN_MAX;
+    const uint8_t* xb = reinterpret_cast<const uint8_t*>(x) + (size_t)x_row_offset * x_row_stride * 2;
+    CUtensorMap tx, tq;
+    int st = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, (uint64_t)k, (uint64_t)n,
+                       (uint64_t)x_row_stride * 2, BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16, (uint64_t)m,
+                   (uint64_t)nb * 16, 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+
+    static uint64_t attr_mask = 0;  // per device
+    const uint64_t bit = 1ull << (ctx->device & 63);
+    if (!(attr_mask & bit)) {
+        st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)SMEM_BYTES),
+                        "gemm smem attribute");
+        if (st) return st;
+        st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)SMEM_BYTES),
+                        "gemm smem attribute");
+        if (st) return st;
+        attr_mask |= bit;
+    }
+    dim3 grid((m + BM - 1) / BM, (n + bn - 1) / bn);
+    if (grid.y > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
+    if (out_dtype == SULIMO_OUT_F32)
+        gemm_q4_0_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
+            tx, tq, reinterpret_cast<const uint16_t*>(scales), out, m, k, n, bn, nb, ctx->d_error);
+    else
+        gemm_q4_0_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
+            tx, tq, reinterpret_cast<const uint16_t*>(scales), out, m, k, n, bn, nb, ctx->d_error);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
+}
+
+}  // namespace sulimo

@@ -1,0 +1,176 @@
+// q8_0.cu — Q8_0 quantization, Q8_0 KV-ring store, Q4_0 row dequant and integer block sums.
+//
+// All of these are byte/bit-exact restatements of the reference's CPU functions:
+//   quantize_f32_to_q8_0      crates/sulimo-core/src/kv_cache.rs:162-192
+//   KvCache::store_key/value  kv_cache.rs:93-110, GPU writer kv_store_q8_0 kernels/prefill.cl:72-116
+//   dequantize_q4_0_soa       crates/sulimo-core/src/repack.rs:107-131
+//   lookup_token_embedding_f16 crates/sulimo-engine/src/scheduler.rs:329-357
+//   block_sum of vec_dot_q4_0_q8_0_scalar crates/sulimo-cpu/src/scalar.rs:189-199
+// One warp quantizes one 32-value block: lane i owns value i, the block's max|x| is a warp max.
+#include "sulimo_common.cuh"
+#include "sulimo_internal.h"
+
+namespace sulimo {
+namespace {
+
+// Quantizes the 32 values of a block held one per lane and writes the 34-byte Q8_0 block.
+// d = max|x|/127 (IEEE f32), stored as f16 RNE; id = 1/d from the f32 d; q = clamp(roundf(x*id)).
+__device__ __forceinline__ void quantize_block_warp(float v, uint8_t* dst, int lane) {
+    float a = fabsf(v);  // fmaxf drops NaN like the reference's `a > max_abs` test
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+    float d = __fdiv_rn(a, 127.0f);
+    float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    float q = roundf(__fmul_rn(v, id));
+    if (q != q) q = 0.0f;  // f32 NaN `as i8` == 0
+    q = fminf(fmaxf(q, -128.0f), 127.0f);
+    dst[2 + lane] = (uint8_t)(int8_t)(int)q;
+    if (lane == 0) {
+        uint16_t dh = __half_as_ushort(__float2half_rn(d));
+        dst[0] = (uint8_t)(dh & 0xFF);
+        dst[1] = (uint8_t)(dh >> 8);
+    }
+}
+
+__global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restrict__ src,
+                                                            uint8_t* __restrict__ dst,
+                                                            size_t nblocks) {
+    const int lane = threadIdx.x & 31;
+    size_t w = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const size_t stride = (size_t)gridDim.x * (blockDim.x / 32);
+    for (; w < nblocks; w += stride) quantize_block_warp(__ldg(src + w * 32 + lane), dst + w * 34, lane);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+// act [n][bpp*32]; token t, block b -> ring slot (start_pos+t) % capacity, byte b*34.
+template <typename T>
+__global__ void __launch_bounds__(256) kv_store_q8_0_kernel(const T* __restrict__ act,
+                                                            uint8_t* __restrict__ kv,
+                                                            size_t start_pos, size_t capacity,
+                                                            size_t bpp, size_t n) {
+    const int lane = threadIdx.x & 31;
+    size_t w = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const size_t stride = (size_t)gridDim.x * (blockDim.x / 32);
+    const size_t total = n * bpp;
+    for (; w < total; w += stride) {
+        size_t t = w / bpp, b = w % bpp;
+        size_t slot = (start_pos + t) % capacity;
+        float v = to_f32<T>(act[w * 32 + lane]);
+        quantize_block_warp(v, kv + slot * bpp * 34 + b * 34, lane);
+    }
+}
+
+// One thread per (row, block, byte i): writes weights i and i+16 of the block.
+template <bool F16OUT>
+__global__ void __launch_bounds__(256) dequant_rows_kernel(const uint16_t* __restrict__ scales,
+                                                           const uint8_t* __restrict__ quants,
+                                                           int nb, const int32_t* __restrict__ rows,
+                                                           int count, void* __restrict__ out) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t total = (size_t)count * nb * 16;
+    if (idx >= total) return;
+    int i = (int)(idx % 16);
+    size_t rb = idx / 16;
+    int b = (int)(rb % nb);
+    int c = (int)(rb / nb);
+    size_t r = (size_t)rows[c];
+    size_t blk = r * nb + b;
+    float d = f16_bits_to_f32(scales[blk]);
+    uint8_t byte = quants[blk * 16 + i];
+    float w0 = __fmul_rn((float)((int)(byte & 0x0F) - 8), d);
+    float w1 = __fmul_rn((float)((int)(byte >> 4) - 8), d);
+    size_t o = (size_t)c * nb * 32 + (size_t)b * 32 + i;
+    if (F16OUT) {
+        __half* oh = reinterpret_cast<__half*>(out);
+        oh[o] = __float2half_rn(w0);
+        oh[o + 16] = __float2half_rn(w1);
+    } else {
+        float* of = reinterpret_cast<float*>(out);
+        of[o] = w0;
+        of[o + 16] = w1;
+    }
+}
+
+// out[r*nb+b] = sum_i (w_i-8)*x_i as i32.
+__global__ void __launch_bounds__(256) block_sums_kernel(const uint8_t* __restrict__ wq,
+                                                         const uint8_t* __restrict__ xq8, int rows,
+                                                         int nb, int32_t* __restrict__ out) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)rows * nb) return;
+    int b = (int)(idx % nb);
+    const uint8_t* w = wq + idx * 16;
+    const int8_t* x = reinterpret_cast<const int8_t*>(xq8 + (size_t)b * 34 + 2);
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 16; i++) s += ((int)(w[i] & 0x0F) - 8) * x[i] + ((int)(w[i] >> 4) - 8) * x[i + 16];
+    out[idx] = s;
+}
+
+int grid_for(size_t warps_needed, int num_sms) {
+    size_t ctas = (warps_needed + 7) / 8;
+    size_t cap = (size_t)num_sms * 16;
+    if (ctas > cap) ctas = cap;
+    if (ctas < 1) ctas = 1;
+    return (int)ctas;
+}
+
+}  // namespace
+
+int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n) {
+    size_t nb = n / 32;
+    quantize_q8_0_kernel<<<grid_for(nb, ctx->num_sms), 256, 0, ctx->stream>>>(
+        src, reinterpret_cast<uint8_t*>(dst), nb);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "quantize_q8_0 launch");
+}
+
+int launch_kv_store_q8_0(sulimo_ctx* ctx, const void* act, int act_dtype, void* kv,
+                         size_t start_pos, size_t capacity, size_t bpp, size_t n) {
+    int g = grid_for(n * bpp, ctx->num_sms);
+    if (act_dtype == SULIMO_ACT_F16)
+        kv_store_q8_0_kernel<__half><<<g, 256, 0, ctx->stream>>>(
+            reinterpret_cast<const __half*>(act), reinterpret_cast<uint8_t*>(kv), start_pos,
+            capacity, bpp, n);
+    else
+        kv_store_q8_0_kernel<float><<<g, 256, 0, ctx->stream>>>(
+            reinterpret_cast<const float*>(act), reinterpret_cast<uint8_t*>(kv), start_pos,
+            capacity, bpp, n);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "kv_store_q8_0 launch");
+}
+
+int launch_dequant_rows(sulimo_ctx* ctx, const void* scales, const void* quants, int cols,
+                        const int32_t* row_ids, int count, void* out, int out_dtype) {
+    int nb = cols / 32;
+    size_t total = (size_t)count * nb * 16;
+    int g = (int)((total + 255) / 256);
+    if (out_dtype == SULIMO_OUT_F16)
+        dequant_rows_kernel<true><<<g, 256, 0, ctx->stream>>>(
+            reinterpret_cast<const uint16_t*>(scales), reinterpret_cast<const uint8_t*>(quants),
+            nb, row_ids, count, out);
+    else
+        dequant_rows_kernel<false><<<g, 256, 0, ctx->stream>>>(
+            reinterpret_cast<const uint16_t*>(scales), reinterpret_cast<const uint8_t*>(quants),
+            nb, row_ids, count, out);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "dequant_rows launch");
+}
+
+int launch_block_sums(sulimo_ctx* ctx, const void* w_quants, const void* x_q8, int rows, int cols,
+                      int32_t* out) {
+    int nb = cols / 32;
+    size_t total = (size_t)rows * nb;
+    block_sums_kernel<<<(int)((total + 255) / 256), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const uint8_t*>(w_quants), reinterpret_cast<const uint8_t*>(x_q8), rows,
+        nb, out);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "block_sums launch");
+}
+
+}  // namespace sulimo

@@ -1,0 +1,60 @@
+// sulimo_internal.h — host-side context and kernel launchers shared by the .cu files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/sulimo_cuda.h"
+
+struct sulimo_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;  // the stream launches go to (own or caller's)
+    int* d_error = nullptr;         // device error word (0 = none)
+    void* workspace = nullptr;      // split-K / attention partials
+    size_t workspace_bytes = 0;
+    std::atomic<uint64_t> launches{0};
+};
+
+namespace sulimo {
+
+// Thread-local error message + status helper.
+int set_error(int status, const std::string& msg);
+int check_cuda(cudaError_t e, const char* what);
+// Grows ctx->workspace to at least `bytes` (synchronizes the stream first if it must grow).
+int ensure_workspace(sulimo_ctx* ctx, size_t bytes);
+
+// cuTensorMapEncodeTiled resolved through the runtime's driver entry point.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn get_encode_tiled();
+
+// Launchers (return SULIMO_* status; argument checks done by the C-ABI layer).
+int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
+                         void* out, int m, int k, int n, int out_dtype, int x_row_stride,
+                         int x_row_offset);
+int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
+                          const void* x_q8, int rows, int cols, int batch, float* out);
+int launch_block_sums(sulimo_ctx* ctx, const void* w_quants, const void* x_q8, int rows, int cols,
+                      int32_t* out);
+int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n);
+int launch_kv_store_q8_0(sulimo_ctx* ctx, const void* act, int act_dtype, void* kv,
+                         size_t start_pos, size_t capacity, size_t blocks_per_pos, size_t n);
+int launch_dequant_rows(sulimo_ctx* ctx, const void* scales, const void* quants, int cols,
+                        const int32_t* row_ids, int count, void* out, int out_dtype);
+int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
+                       size_t seq_stride, size_t capacity, size_t context_len, int head_count,
+                       int head_count_kv, int head_dim, int batch, float softcap, float* out,
+                       float* partials, size_t partial_bytes);
+size_t attn_decode_partial_bytes(size_t context_len, int head_count, int head_dim, int batch,
+                                 int num_sms, int* splits_out);
+
+}  // namespace sulimo
