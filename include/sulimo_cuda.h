@@ -73,7 +73,9 @@ int sulimo_cuda_ctx_create(int device, sulimo_ctx** out);
 int sulimo_cuda_ctx_destroy(sulimo_ctx* ctx);
 /* Wait for all work on the context stream; returns SULIMO_EDEVICE if a kernel flagged an error. */
 int sulimo_cuda_ctx_synchronize(sulimo_ctx* ctx);
-/* Use the caller's cudaStream_t (e.g. a framework's current stream) instead of the own one. */
+/* Launch on the caller's cudaStream_t (e.g. a framework's current stream) instead of the
+ * context's own non-blocking stream.  NULL selects the CUDA legacy default stream; keep the
+ * value of sulimo_cuda_ctx_get_stream() from before the switch to return to the own stream. */
 int sulimo_cuda_ctx_set_stream(sulimo_ctx* ctx, void* cuda_stream);
 void* sulimo_cuda_ctx_get_stream(sulimo_ctx* ctx);
 int sulimo_cuda_ctx_device(sulimo_ctx* ctx);

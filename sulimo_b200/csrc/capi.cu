@@ -167,7 +167,7 @@ int sulimo_cuda_ctx_synchronize(sulimo_ctx* ctx) {
 int sulimo_cuda_ctx_set_stream(sulimo_ctx* ctx, void* cuda_stream) {
     int st = check_ctx(ctx);
     if (st) return st;
-    ctx->stream = cuda_stream ? (cudaStream_t)cuda_stream : ctx->own_stream;
+    ctx->stream = (cudaStream_t)cuda_stream;  // NULL is the legacy default stream
     return SULIMO_OK;
 }
 

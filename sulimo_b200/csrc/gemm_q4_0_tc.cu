@@ -9,16 +9,18 @@
 // Data flow per CTA (128 features x up to 256 tokens, K streamed in 64-wide stages):
 //   warp 0   TMA: activations x[n0.., k0..k0+63] -> smem (128B-swizzled, K-major) and the raw
 //            Q4_0 nibbles of the 128 feature rows (32 bytes per row) -> smem.
-//   warps 2-5 dequant: each thread owns one feature row (= one TMEM lane), turns its 2 Q4_0
-//            blocks of the stage into 64 f16 weights f16(d*(q-8)) (exact (q-8) via the
-//            0x6400 magic, one RNE multiply by d; the rounding of the reference's f16 embedding
-//            path, crates/sulimo-engine/src/scheduler.rs:345-357) and writes them to the
-//            stage's TMEM columns with tcgen05.st.  The weights never touch shared memory.
+//   warps 2-9 dequant: each thread owns one feature row (= one TMEM lane) and one of the
+//            stage's 2 Q4_0 blocks, turns it into 32 f16 weights f16(d*(q-8)) (exact (q-8) via
+//            the 0x6400 magic, one RNE multiply by d; the rounding of the reference's f16
+//            embedding path, crates/sulimo-engine/src/scheduler.rs:345-357) and writes them to
+//            the stage's TMEM columns with tcgen05.st.  The weights never touch shared memory.
 //   warp 1   one thread issues tcgen05.mma kind::f16, A = weights from TMEM (M = 128 features),
 //            B = activations from smem (N = tokens), D = fp32 accumulators in TMEM; each stage
 //            is released with tcgen05.commit.
-//   warps 2-5 epilogue: tcgen05.ld of the accumulators (lane = feature), convert, store
+//   warps 2-9 epilogue: tcgen05.ld of the accumulators (lane = feature), convert, store
 //            out[t][r] (32 consecutive features per warp store: 64-byte coalesced rows).
+// Outputs with few tiles (the down projection: 1536 features) split K across CTAs; the fp32
+// partials are added in split order by splitk_reduce_kernel (deterministic).
 // Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records a device error,
 // drains its in-flight copies / MMAs (again bounded), frees TMEM and returns.
 // No TMA multicast: each CTA loads its own tiles.
@@ -32,7 +34,8 @@ constexpr int BM = 128;           // features per CTA = MMA M = TMEM lanes
 constexpr int BK = 64;            // k per stage: 2 Q4_0 blocks, one 128-byte swizzle row of f16
 constexpr int BN_MAX = 256;       // tokens per CTA = MMA N (max)
 constexpr int STAGES = 4;
-constexpr int THREADS = 192;      // 6 warps
+constexpr int DEQ_WARPS = 8;      // two per TMEM lane quarter, one Q4_0 block of the stage each
+constexpr int THREADS = 64 + 32 * DEQ_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t A_COL = 0;     // A stages: columns [32*s, 32*s+32)
 constexpr uint32_t ACC_COL = 128; // accumulators: columns [128, 128+bn)
@@ -85,16 +88,13 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31, %32};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
         "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
-        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
-        "r"(v[29]), "r"(v[30]), "r"(v[31])
+        "r"(v[15])
         : "memory");
 }
 
@@ -155,12 +155,38 @@ __device__ __forceinline__ void dequant_block(const uint4 q, uint32_t dbits, uin
     }
 }
 
+// Partial sums of split-K CTAs go to an fp32 workspace [split][n][m]; this kernel adds the
+// splits in index order (deterministic) and writes f16 or f32 results.
 template <bool OUT_F32>
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ out, size_t nm,
+                         int splits) {
+    const size_t i4 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i4 >= nm) return;
+    float4 acc = *reinterpret_cast<const float4*>(ws + i4);
+    for (int z = 1; z < splits; z++) {
+        const float4 p = *reinterpret_cast<const float4*>(ws + (size_t)z * nm + i4);
+        acc.x += p.x;
+        acc.y += p.y;
+        acc.z += p.z;
+        acc.w += p.w;
+    }
+    if (OUT_F32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + i4) = acc;
+    } else {
+        __half2 a = __floats2half2_rn(acc.x, acc.y), b = __floats2half2_rn(acc.z, acc.w);
+        uint2 v = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(out) + i4) = v;
+    }
+}
+
+// OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to out + split*n*m
+template <int OUT_MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q4_0_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_q,
                         const uint16_t* __restrict__ scales, void* __restrict__ out, int m, int k,
-                        int n, int bn, int nb, int* __restrict__ err) {
+                        int n, int bn, int nb, int iters_per_split, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -175,13 +201,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * bn;
-    const int num_k = (k + BK - 1) / BK;
+    const int num_k_total = (k + BK - 1) / BK;
+    const int i_begin = blockIdx.z * iters_per_split;
+    const int i_end = min(num_k_total, i_begin + iters_per_split);
+    const int num_k = max(0, i_end - i_begin);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 128);
+            mbar_init(&afull[s], 32 * DEQ_WARPS);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -205,19 +234,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
             int issued = 0;
-            for (int i = 0; i < num_k; i++) {
-                const int s = i % STAGES;
-                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            for (int j = 0; j < num_k; j++) {
+                const int s = j % STAGES;
+                const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
                 mbar_arrive_expect_tx(&full[s], (uint32_t)bn * 128u + Q_STAGE);
-                tma_load_2d(sx + s * X_STAGE, &tmap_x, i * BK, n0, &full[s]);
-                tma_load_2d(sq + s * Q_STAGE, &tmap_q, i * 32, m0, &full[s]);
-                issued = i + 1;
+                tma_load_2d(sx + s * X_STAGE, &tmap_x, (i_begin + j) * BK, n0, &full[s]);
+                tma_load_2d(sq + s * Q_STAGE, &tmap_q, (i_begin + j) * 32, m0, &full[s]);
+                issued = j + 1;
             }
             if (*abort_flag) {
                 // drain: the copies already issued must land before the CTA's smem is released
-                for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
-                    mbar_wait_bounded(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, err,
+                for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; j++)
+                    mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, err,
                                       nullptr);
             }
         }
@@ -227,9 +256,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             // kind::f16: D f32 (bits 4-5 = 1), A = B = f16, both K-major, N>>3 at 17, M>>4 at 24
             const uint32_t idesc =
                 (1u << 4) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-            for (int i = 0; i < num_k; i++) {
-                const int s = i % STAGES;
-                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            for (int j = 0; j < num_k; j++) {
+                const int s = j % STAGES;
+                const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
                 if (!mbar_wait_bounded(&afull[s], ph, err, abort_flag)) break;
                 tc_fence_after();
                 const uint64_t bdesc = sw128_desc(smem_u32(sx + s * X_STAGE));
@@ -237,7 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int kk = 0; kk < BK / 16; kk++) {
                     // +32 bytes per 16-element K step inside the swizzled 128-byte rows
                     mma_ts(tmem + ACC_COL, tmem + A_COL + (uint32_t)s * 32u + (uint32_t)kk * 8u,
-                           bdesc + (uint64_t)(kk * 2), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                           bdesc + (uint64_t)(kk * 2), idesc, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 mma_commit(&empty[s]);
             }
@@ -246,54 +275,57 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // --------------------------- dequant, then epilogue ---------------------------
+        // warp w in 2..9: TMEM lane quarter (w % 4), Q4_0 block `half` of each stage
         const uint32_t quarter = (uint32_t)(warp & 3);
+        const int half = (warp - 2) >> 2;
         const int r = (int)quarter * 32 + lane;  // feature row within the tile == TMEM lane
         const int grow = m0 + r;
         const bool row_ok = grow < m;
         const uint16_t* srow = scales + (size_t)(row_ok ? grow : 0) * nb;
         const uint32_t lane_base = (quarter * 32u) << 16;
-        uint32_t s0n = 0, s1n = 0;
-        if (row_ok) {
-            s0n = __ldg(srow + 0);
-            s1n = (1 < nb) ? __ldg(srow + 1) : 0u;
+        uint32_t sc_next = 0;
+        {
+            const int kb = 2 * i_begin + half;
+            if (row_ok && num_k > 0 && kb < nb) sc_next = __ldg(srow + kb);
         }
         bool ok = true;
-        for (int i = 0; i < num_k; i++) {
-            const int s = i % STAGES;
-            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-            const uint32_t s0 = s0n, s1 = s1n;
-            if (row_ok) {  // prefetch the next stage's two block scales
-                const int kb = 2 * (i + 1);
-                s0n = (kb < nb) ? __ldg(srow + kb) : 0u;
-                s1n = (kb + 1 < nb) ? __ldg(srow + kb + 1) : 0u;
+        for (int j = 0; j < num_k; j++) {
+            const int s = j % STAGES;
+            const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+            const uint32_t sc = sc_next;
+            {  // prefetch the next stage's block scale
+                const int kb = 2 * (i_begin + j + 1) + half;
+                sc_next = (row_ok && j + 1 < num_k && kb < nb) ? __ldg(srow + kb) : 0u;
             }
             if (!mbar_wait_bounded(&full[s], ph, err, abort_flag)) {
                 ok = false;
                 break;
             }
-            const uint4* qp = reinterpret_cast<const uint4*>(sq + s * Q_STAGE + r * 32);
-            const uint4 qa = qp[0], qb = qp[1];
-            uint32_t cols[32];
-            dequant_block(qa, row_ok ? s0 : 0u, cols);
-            dequant_block(qb, row_ok ? s1 : 0u, cols + 16);
-            tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * 32u, cols);
+            const uint4 qv = *reinterpret_cast<const uint4*>(sq + s * Q_STAGE + r * 32 + half * 16);
+            uint32_t cols[16];
+            dequant_block(qv, row_ok ? sc : 0u, cols);
+            tmem_st16(tmem + lane_base + A_COL + (uint32_t)s * 32u + (uint32_t)half * 16u, cols);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&afull[s]);
         }
-        if (ok && mbar_wait_bounded(done, 0, err, abort_flag)) {
+        if (ok && num_k > 0 && mbar_wait_bounded(done, 0, err, abort_flag)) {
             tc_fence_after();
-            for (int c0 = 0; c0 < bn; c0 += 32) {
+            // the two warps of a lane quarter take alternate 32-token column chunks
+            for (int c0 = half * 32; c0 < bn; c0 += 64) {
                 uint32_t v[32];
                 tmem_ld32(tmem + lane_base + ACC_COL + (uint32_t)c0, v);
                 if (row_ok) {
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const int t = n0 + c0 + j;
-                        if (c0 + j < bn && t < n) {
-                            const float f = __uint_as_float(v[j]);
-                            if (OUT_F32)
+                    for (int jj = 0; jj < 32; jj++) {
+                        const int t = n0 + c0 + jj;
+                        if (c0 + jj < bn && t < n) {
+                            const float f = __uint_as_float(v[jj]);
+                            if (OUT_MODE == 1)
                                 reinterpret_cast<float*>(out)[(size_t)t * m + grow] = f;
+                            else if (OUT_MODE == 2)
+                                reinterpret_cast<float*>(out)[((size_t)blockIdx.z * n + t) * m +
+                                                              grow] = f;
                             else
                                 reinterpret_cast<__half*>(out)[(size_t)t * m + grow] =
                                     __float2half_rn(f);
@@ -301,6 +333,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
+        } else if (ok && num_k == 0 && OUT_MODE == 2) {
+            // an empty split contributes zeros
+            for (int c0 = half * 32; c0 < bn; c0 += 64)
+                if (row_ok)
+                    for (int jj = 0; jj < 32; jj++) {
+                        const int t = n0 + c0 + jj;
+                        if (c0 + jj < bn && t < n)
+                            reinterpret_cast<float*>(out)[((size_t)blockIdx.z * n + t) * m + grow] = 0.0f;
+                    }
         }
     }
 
@@ -331,7 +372,30 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
     return SULIMO_OK;
 }
 
+template <int MODE>
+int set_smem_attr(int device) {
+    static uint64_t mask = 0;  // the attribute is per device
+    const uint64_t bit = 1ull << (device & 63);
+    if (mask & bit) return SULIMO_OK;
+    int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<MODE>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)SMEM_BYTES),
+                        "gemm smem attribute");
+    if (!st) mask |= bit;
+    return st;
+}
+
 }  // namespace
+
+// Split count: enough CTAs to fill the SMs when the output has few tiles (the down projection
+// 512 x 8960 -> 1536 has 24 tiles of 128 x 256), each split keeping >= 8 k-stages.
+int gemm_splits(int tiles, int num_k, int num_sms) {
+    if (tiles * 2 > num_sms) return 1;
+    int s = num_sms / tiles;
+    int by_k = num_k / 8;
+    if (s > by_k) s = by_k;
+    return s < 1 ? 1 : s;
+}
 
 int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                          void* out, int m, int k, int n, int out_dtype, int x_row_stride,
@@ -347,32 +411,42 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
     st = encode_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16, (uint64_t)m,
                    (uint64_t)nb * 16, 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
+    if ((st = set_smem_attr<0>(ctx->device)) || (st = set_smem_attr<1>(ctx->device)) ||
+        (st = set_smem_attr<2>(ctx->device)))
+        return st;
 
-    static uint64_t attr_mask = 0;  // per device
-    const uint64_t bit = 1ull << (ctx->device & 63);
-    if (!(attr_mask & bit)) {
-        st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<false>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)SMEM_BYTES),
-                        "gemm smem attribute");
-        if (st) return st;
-        st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<true>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)SMEM_BYTES),
-                        "gemm smem attribute");
-        if (st) return st;
-        attr_mask |= bit;
+    const int mt = (m + BM - 1) / BM, nt = (n + bn - 1) / bn;
+    const int num_k = (k + BK - 1) / BK;
+    const int splits = gemm_splits(mt * nt, num_k, ctx->num_sms);
+    const int ips = (num_k + splits - 1) / splits;
+    if (nt > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(scales);
+    if (splits == 1) {
+        dim3 grid(mt, nt, 1);
+        if (out_dtype == SULIMO_OUT_F32)
+            gemm_q4_0_tc_kernel<1><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
+                tx, tq, sc, out, m, k, n, bn, nb, ips, ctx->d_error);
+        else
+            gemm_q4_0_tc_kernel<0><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
+                tx, tq, sc, out, m, k, n, bn, nb, ips, ctx->d_error);
+        ctx->launches++;
+        return check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
     }
-    dim3 grid((m + BM - 1) / BM, (n + bn - 1) / bn);
-    if (grid.y > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
+    const size_t nm = (size_t)n * m;
+    if ((st = ensure_workspace(ctx, nm * splits * sizeof(float)))) return st;
+    float* ws = reinterpret_cast<float*>(ctx->workspace);
+    dim3 grid(mt, nt, splits);
+    gemm_q4_0_tc_kernel<2><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
+        tx, tq, sc, ws, m, k, n, bn, nb, ips, ctx->d_error);
+    st = check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
+    if (st) return st;
+    const unsigned rb = (unsigned)((nm / 4 + 255) / 256);  // m % 8 == 0, so nm % 4 == 0
     if (out_dtype == SULIMO_OUT_F32)
-        gemm_q4_0_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-            tx, tq, reinterpret_cast<const uint16_t*>(scales), out, m, k, n, bn, nb, ctx->d_error);
+        splitk_reduce_kernel<true><<<rb, 256, 0, ctx->stream>>>(ws, out, nm, splits);
     else
-        gemm_q4_0_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-            tx, tq, reinterpret_cast<const uint16_t*>(scales), out, m, k, n, bn, nb, ctx->d_error);
-    ctx->launches++;
-    return check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
+        splitk_reduce_kernel<false><<<rb, 256, 0, ctx->stream>>>(ws, out, nm, splits);
+    ctx->launches += 2;
+    return check_cuda(cudaGetLastError(), "splitk_reduce launch");
 }
 
 }  // namespace sulimo

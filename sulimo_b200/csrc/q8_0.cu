@@ -25,11 +25,8 @@ __device__ __forceinline__ void quantize_block_warp(float v, uint8_t* dst, int l
     if (q != q) q = 0.0f;  // f32 NaN `as i8` == 0
     q = fminf(fmaxf(q, -128.0f), 127.0f);
     dst[2 + lane] = (uint8_t)(int8_t)(int)q;
-    if (lane == 0) {
-        uint16_t dh = __half_as_ushort(__float2half_rn(d));
-        dst[0] = (uint8_t)(dh & 0xFF);
-        dst[1] = (uint8_t)(dh >> 8);
-    }
+    // the f16 scale as one 2-byte store (blocks are 34 bytes, so dst is 2-byte aligned)
+    if (lane == 0) *reinterpret_cast<__half*>(dst) = __float2half_rn(d);
 }
 
 __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restrict__ src,
