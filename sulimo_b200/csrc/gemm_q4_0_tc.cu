@@ -33,15 +33,20 @@ namespace {
 constexpr int BM = 128;           // features per CTA = MMA M = TMEM lanes
 constexpr int BK = 64;            // k per stage: 2 Q4_0 blocks, one 128-byte swizzle row of f16
 constexpr int BN_MAX = 256;       // tokens per CTA = MMA N (max)
-constexpr int STAGES = 4;
+// 6 stages: one ring slot turns over in ~1.5 us (MMA, commit, TMA issue, L2 latency, dequant),
+// so 6 slots keep ~4 MMA stages of work queued at the tensor-core rate.
+constexpr int STAGES = 6;
 constexpr int DEQ_WARPS = 8;      // two per TMEM lane quarter, one Q4_0 block of the stage each
 constexpr int THREADS = 64 + 32 * DEQ_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t A_COL = 0;     // A stages: columns [32*s, 32*s+32)
-constexpr uint32_t ACC_COL = 128; // accumulators: columns [128, 128+bn)
+constexpr uint32_t A_COL = 0;                 // A stages: columns [32*s, 32*s+32)
+constexpr uint32_t ACC_COL = STAGES * 32;     // accumulators: columns [ACC_COL, ACC_COL+bn)
 constexpr uint32_t X_STAGE = BN_MAX * 128;  // bytes
 constexpr uint32_t Q_STAGE = BM * 32;       // bytes
 constexpr uint32_t SMEM_BYTES = STAGES * (X_STAGE + Q_STAGE) + 256 + 1024;
+static_assert(ACC_COL + BN_MAX <= TMEM_COLS, "TMEM budget");
+static_assert(STAGES * X_STAGE >= BN_MAX * BM * 4, "epilogue staging tile must fit the X ring");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 // ---- tcgen05 / TMA wrappers ----------------------------------------------------------------
 __device__ __forceinline__ void tc_fence_before() {
@@ -58,6 +63,35 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1,
+                                             const void* src) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(smem_u32(src))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int c0, int c1, int c2,
+                                             const void* src) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::
+            "l"(reinterpret_cast<uint64_t>(map)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+        : "memory");
+}
+
+// Commits the issued bulk stores and waits until their global writes are complete (the
+// shared-memory source must stay valid until then; the CTA exits right after).
+__device__ __forceinline__ void bulk_commit_and_wait_all() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
@@ -185,8 +219,9 @@ template <int OUT_MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q4_0_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_q,
-                        const uint16_t* __restrict__ scales, void* __restrict__ out, int m, int k,
-                        int n, int bn, int nb, int iters_per_split, int* __restrict__ err) {
+                        const __grid_constant__ CUtensorMap tmap_out,
+                        const uint16_t* __restrict__ scales, int m, int k, int n, int bn, int nb,
+                        int iters_per_split, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -217,6 +252,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_barrier_init();
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_out)) : "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -309,39 +345,40 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_before();
             mbar_arrive(&afull[s]);
         }
-        if (ok && num_k > 0 && mbar_wait_bounded(done, 0, err, abort_flag)) {
+        // Epilogue: accumulators -> [token][feature] tile in shared memory (the X stages are
+        // free once `done` fired) -> one TMA tensor store; the tensor map clips ragged edges.
+        const bool have = ok && (num_k == 0 || mbar_wait_bounded(done, 0, err, abort_flag));
+        if (have) {
             tc_fence_after();
+            constexpr int ES = (OUT_MODE == 0) ? 2 : 4;
             // the two warps of a lane quarter take alternate 32-token column chunks
             for (int c0 = half * 32; c0 < bn; c0 += 64) {
                 uint32_t v[32];
-                tmem_ld32(tmem + lane_base + ACC_COL + (uint32_t)c0, v);
-                if (row_ok) {
+                if (num_k > 0) {
+                    tmem_ld32(tmem + lane_base + ACC_COL + (uint32_t)c0, v);
+                } else {
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj++) {
-                        const int t = n0 + c0 + jj;
-                        if (c0 + jj < bn && t < n) {
-                            const float f = __uint_as_float(v[jj]);
-                            if (OUT_MODE == 1)
-                                reinterpret_cast<float*>(out)[(size_t)t * m + grow] = f;
-                            else if (OUT_MODE == 2)
-                                reinterpret_cast<float*>(out)[((size_t)blockIdx.z * n + t) * m +
-                                                              grow] = f;
-                            else
-                                reinterpret_cast<__half*>(out)[(size_t)t * m + grow] =
-                                    __float2half_rn(f);
-                        }
-                    }
+                    for (int jj = 0; jj < 32; jj++) v[jj] = 0u;  // an empty split adds zeros
+                }
+                uint8_t* col = sx + ((size_t)c0 * BM + r) * ES;
+#pragma unroll
+                for (int jj = 0; jj < 32; jj++) {
+                    const float f = __uint_as_float(v[jj]);
+                    if (ES == 2)
+                        *reinterpret_cast<__half*>(col + (size_t)jj * BM * ES) = __float2half_rn(f);
+                    else
+                        *reinterpret_cast<float*>(col + (size_t)jj * BM * ES) = f;
                 }
             }
-        } else if (ok && num_k == 0 && OUT_MODE == 2) {
-            // an empty split contributes zeros
-            for (int c0 = half * 32; c0 < bn; c0 += 64)
-                if (row_ok)
-                    for (int jj = 0; jj < 32; jj++) {
-                        const int t = n0 + c0 + jj;
-                        if (c0 + jj < bn && t < n)
-                            reinterpret_cast<float*>(out)[((size_t)blockIdx.z * n + t) * m + grow] = 0.0f;
-                    }
+            fence_proxy_async_smem();
+        }
+        named_barrier_sync(1, 32 * DEQ_WARPS);
+        if (warp == 2 && lane == 0 && have && !*abort_flag) {
+            if (OUT_MODE == 2)
+                tma_store_3d(&tmap_out, m0, n0, (int)blockIdx.z, sx);
+            else
+                tma_store_2d(&tmap_out, m0, n0, sx);
+            bulk_commit_and_wait_all();
         }
     }
 
@@ -355,21 +392,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
-              uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle swz) {
+// Encodes a tiled tensor map of rank 2 or 3; dims/box innermost first, strides in bytes for
+// dims 1.. (rank-1 entries).
+int encode_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int rank,
+               const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+               CUtensorMapSwizzle swz) {
     EncodeTiledFn enc = get_encode_tiled();
     if (!enc) return set_error(SULIMO_ENODEV, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {row_bytes};
-    cuuint32_t box[2] = {box_inner, box_outer};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+    cuuint64_t d[3], st[2];
+    cuuint32_t bx[3], estr[3] = {1, 1, 1};
+    for (int i = 0; i < rank; i++) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+    }
+    for (int i = 0; i + 1 < rank; i++) st[i] = strides[i];
+    CUresult r = enc(map, dt, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return set_error(SULIMO_ELAUNCH, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
     return SULIMO_OK;
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swz) {
+    const uint64_t dims[2] = {inner, outer};
+    const uint32_t box[2] = {box_inner, box_outer};
+    return encode_map(map, dt, base, 2, dims, &row_bytes, box, swz);
 }
 
 template <int MODE>
@@ -421,23 +471,37 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
     const int ips = (num_k + splits - 1) / splits;
     if (nt > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
     const uint16_t* sc = reinterpret_cast<const uint16_t*>(scales);
+    CUtensorMap to;
     if (splits == 1) {
+        const bool f32 = out_dtype == SULIMO_OUT_F32;
+        st = encode_2d(&to, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                       out, (uint64_t)m, (uint64_t)n, (uint64_t)m * (f32 ? 4 : 2), BM,
+                       (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
         dim3 grid(mt, nt, 1);
-        if (out_dtype == SULIMO_OUT_F32)
+        if (f32)
             gemm_q4_0_tc_kernel<1><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-                tx, tq, sc, out, m, k, n, bn, nb, ips, ctx->d_error);
+                tx, tq, to, sc, m, k, n, bn, nb, ips, ctx->d_error);
         else
             gemm_q4_0_tc_kernel<0><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-                tx, tq, sc, out, m, k, n, bn, nb, ips, ctx->d_error);
+                tx, tq, to, sc, m, k, n, bn, nb, ips, ctx->d_error);
         ctx->launches++;
         return check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
     }
     const size_t nm = (size_t)n * m;
     if ((st = ensure_workspace(ctx, nm * splits * sizeof(float)))) return st;
     float* ws = reinterpret_cast<float*>(ctx->workspace);
+    {  // partials [split][n][m]: rank 3 so a ragged token tile cannot spill into the next split
+        const uint64_t dims[3] = {(uint64_t)m, (uint64_t)n, (uint64_t)splits};
+        const uint64_t strides[2] = {(uint64_t)m * 4, (uint64_t)nm * 4};
+        const uint32_t box[3] = {BM, (uint32_t)bn, 1};
+        st = encode_map(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, 3, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
     dim3 grid(mt, nt, splits);
     gemm_q4_0_tc_kernel<2><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-        tx, tq, sc, ws, m, k, n, bn, nb, ips, ctx->d_error);
+        tx, tq, to, sc, m, k, n, bn, nb, ips, ctx->d_error);
     st = check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
     if (st) return st;
     const unsigned rb = (unsigned)((nm / 4 + 255) / 256);  // m % 8 == 0, so nm % 4 == 0
