@@ -181,6 +181,25 @@ int sulimo_cuda_attn_decode_q8_0(sulimo_ctx* ctx, const float* q, const void* k_
                                  size_t context_len, int head_count, int head_count_kv,
                                  int head_dim, int batch, float softcap, float* out);
 
+/* Decode attention that allocates nothing.  No counterpart in the reference: it exists for
+ * callers that must not allocate device memory — a decode loop held to a no-allocation rule
+ * per token (the reference's CPU decode makes zero heap allocations), or a host that plans all
+ * device memory up front from a fixed budget.  Same arguments and results as
+ * sulimo_cuda_attn_decode_q8_0, but the split-K partials live in a fixed 2 MiB array compiled
+ * into the library (reserved on every GPU that loads it, until the process exits) instead of
+ * the context workspace.  Limit: batch * head_count * ceil(context_len / 256) * (head_dim + 2)
+ * <= 524288 floats, else SULIMO_EINVAL; within the limit the split count is reduced to fit.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
+ * caches it; make that first call before any stream capture.  All calls share the array and it
+ * keeps the last call's contents (every call overwrites the part it reads, so nothing needs
+ * clearing); calls that overlap on the GPU — different streams or contexts of one device —
+ * race on it and must be serialized by the caller. */
+int sulimo_cuda_attn_decode_q8_0_noalloc(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                                         const void* v_ring, size_t seq_stride_bytes,
+                                         size_t capacity, size_t context_len, int head_count,
+                                         int head_count_kv, int head_dim, int batch,
+                                         float softcap, float* out);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

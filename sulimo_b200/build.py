@@ -19,6 +19,7 @@ SOURCES = [
     "q8_0.cu",
     "gemv_q4_0_q8_0.cu",
     "attn_decode_q8_0.cu",
+    "attn_decode_noalloc.cu",
     "gemm_q4_0_tc.cu",
 ]
 

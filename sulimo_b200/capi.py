@@ -52,6 +52,8 @@ SIGNATURES = {
     "sulimo_cuda_dequantize_q4_0_rows": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i]),
     "sulimo_cuda_attn_decode_q8_0": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _i, _i,
                                           _f, _vp]),
+    "sulimo_cuda_attn_decode_q8_0_noalloc": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _i,
+                                                  _i, _f, _vp]),
 }
 
 _lib = None

@@ -296,6 +296,30 @@ int launch_hd(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* 
 
 }  // namespace
 
+void attn_decode_split_range(size_t context_len, int head_count_kv, int batch, int num_sms,
+                             int* min_splits, int* default_splits) {
+    size_t mn = (context_len + ATT_PMAX - 1) / ATT_PMAX;
+    *min_splits = (int)(mn < 1 ? 1 : mn);
+    *default_splits = pick_splits(context_len, head_count_kv, batch, num_sms);
+}
+
+int launch_attn_decode_with_splits(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                                   const void* v_ring, size_t seq_stride, size_t capacity,
+                                   size_t context_len, int head_count, int head_count_kv,
+                                   int head_dim, int batch, float softcap, float* out,
+                                   float* partials, int splits) {
+    const uint8_t* k = reinterpret_cast<const uint8_t*>(k_ring);
+    const uint8_t* v = reinterpret_cast<const uint8_t*>(v_ring);
+    switch (head_dim) {
+        case 32: return launch_hd<32>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
+        case 64: return launch_hd<64>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
+        case 96: return launch_hd<96>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
+        case 128: return launch_hd<128>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
+        case 256: return launch_hd<256>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
+        default: return set_error(SULIMO_EINVAL, "head_dim must be one of 32, 64, 96, 128, 256");
+    }
+}
+
 size_t attn_decode_partial_bytes(size_t context_len, int head_count, int head_dim, int batch,
                                  int num_sms, int* splits_out) {
     // head_count_kv only steers the split count; the byte bound uses the worst case (Hkv = 1)

@@ -56,5 +56,16 @@ int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, cons
                        float* partials, size_t partial_bytes);
 size_t attn_decode_partial_bytes(size_t context_len, int head_count, int head_dim, int batch,
                                  int num_sms, int* splits_out);
+// Smallest split count the partial kernel accepts (<= 256 positions per split) and the count
+// the workspace path would pick.
+void attn_decode_split_range(size_t context_len, int head_count_kv, int batch, int num_sms,
+                             int* min_splits, int* default_splits);
+// Decode attention with a caller-chosen split count and partials buffer (which must hold
+// batch * head_count * splits * (head_dim + 2) floats).
+int launch_attn_decode_with_splits(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                                   const void* v_ring, size_t seq_stride, size_t capacity,
+                                   size_t context_len, int head_count, int head_count_kv,
+                                   int head_dim, int batch, float softcap, float* out,
+                                   float* partials, int splits);
 
 }  // namespace sulimo
