@@ -54,15 +54,21 @@ def build(force=False, verbose=False, extra_flags=()):
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
     nvcc = nvcc_path()
-    objs = []
+    jobs = []
     for s in SOURCES:
         src = os.path.join(CSRC, s)
         obj = os.path.join(objdir, s.replace(".cu", ".o"))
-        cmd = [nvcc, *NVCC_FLAGS, *extra_flags, "-c", src, "-o", obj]
+        jobs.append(([nvcc, *NVCC_FLAGS, *extra_flags, "-c", src, "-o", obj], obj))
+    from concurrent.futures import ThreadPoolExecutor
+
+    def run(job):
         if verbose:
-            print(" ".join(cmd))
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+            print(" ".join(job[0]), flush=True)
+        subprocess.run(job[0], check=True)
+        return job[1]
+
+    with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(run, jobs))
     tmp = LIB + ".tmp"
     cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs,
            "-Xcompiler", "-fPIC", "-cudart", "static"]

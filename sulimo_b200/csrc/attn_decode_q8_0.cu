@@ -15,6 +15,8 @@
 //   kernel 2 merges the splits: out = sum_s o_s e^{m_s-M} / sum_s l_s e^{m_s-M}.
 // Reordered fp32 sums: the result matches the reference within fp32 rounding (the parity
 // tests bound the relative L2 error at 2e-3).
+#include <string.h>
+
 #include "sulimo_common.cuh"
 #include "sulimo_internal.h"
 
@@ -24,6 +26,7 @@ namespace {
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_PMAX = 256;  // positions per split
 constexpr int ATT_GMAX = 8;    // query heads per kv head
+constexpr int ATT_SMEM_SLACK = 128;  // room to align the dynamic region to 128 bytes
 
 // Shared memory per CTA (dynamic): q[G][HD] f32 | sc[PMAX][NB] f32 | qs[PMAX][NB*32 + 16] i8 |
 // e[G][PMAX] f32
@@ -36,6 +39,13 @@ struct AttnLayout {
     static constexpr size_t qs_off = sc_off + sizeof(float) * ATT_PMAX * NB;
     static constexpr size_t e_off = qs_off + (size_t)QS_STRIDE * ATT_PMAX;
     static constexpr size_t bytes = e_off + sizeof(float) * ATT_GMAX * ATT_PMAX;
+    // TMA staging: the head row of NB*34 bytes starts at a 2-byte aligned offset; the copy
+    // starts at the 16-byte boundary below it and is BOXW bytes wide (<= 14 bytes of lead-in).
+    static constexpr int HB = NB * 34;
+    static constexpr int BOXW = ((HB + 14 + 15) / 16) * 16;
+    static constexpr size_t raw_off = (bytes + 127) / 128 * 128;
+    __host__ __device__ static size_t raw_bytes(int chunk) { return ((size_t)chunk * BOXW + 127) / 128 * 128; }
+    __host__ __device__ static size_t tma_bytes(int chunk) { return raw_off + 2 * raw_bytes(chunk) + 16; }
 };
 
 // Copies the head rows of positions [p0, p0+np) of one kv head into shared memory:
@@ -61,23 +71,59 @@ __device__ __forceinline__ void stage_rows(const uint8_t* __restrict__ ring, siz
     }
 }
 
+// Same repacking as stage_rows, from a TMA tile in shared memory: position pos of the tile is
+// the raw row at raw + pos*BOXW, the head's bytes start `off` bytes into it.
 template <int HD>
+__device__ __forceinline__ void repack_rows(const uint8_t* raw, int off, int np, float* sc,
+                                            uint8_t* qs) {
+    using L = AttnLayout<HD>;
+    constexpr int W = L::NB * 17;
+    for (int it = threadIdx.x; it < np * W; it += ATT_THREADS) {
+        const int pos = it / W, w = it - pos * W;
+        const int b = w / 17, k = w - b * 17;
+        const uint16_t v =
+            *reinterpret_cast<const uint16_t*>(raw + (size_t)pos * L::BOXW + off + b * 34 + 2 * k);
+        if (k == 0)
+            sc[pos * L::NB + b] = f16_bits_to_f32(v);
+        else
+            *reinterpret_cast<uint16_t*>(qs + pos * L::QS_STRIDE + b * 32 + 2 * (k - 1)) = v;
+    }
+}
+
+// Sign-extended byte I of w as an exact float: prmt replicates the byte's sign into the upper
+// bytes, and 1.5*2^23 + v (|v| < 2^22) has an integer ulp, so one add/subtract converts exactly.
+template <int I>
+__device__ __forceinline__ float s8_to_f32(uint32_t w) {
+    constexpr uint32_t sel = (uint32_t)I | ((0x8u | I) << 4) | ((0x8u | I) << 8) | ((0x8u | I) << 12);
+    const int v = (int)prmt(w, 0u, sel);
+    return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
+}
+
+__device__ __forceinline__ float int_to_f32_exact(int v) {
+    return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
+}
+
+template <int HD, int G, bool TMA>
 __global__ void __launch_bounds__(ATT_THREADS)
     attn_decode_partial_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kring,
                                const uint8_t* __restrict__ vring, size_t seq_stride,
                                size_t capacity, size_t ctx_len, int H, int Hkv, int chunk,
-                               float sm_scale, float softcap, float* __restrict__ part) {
+                               float sm_scale, float softcap, float* __restrict__ part,
+                               const __grid_constant__ CUtensorMap tmap_k,
+                               const __grid_constant__ CUtensorMap tmap_v, int* __restrict__ err) {
     using L = AttnLayout<HD>;
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    // The dynamic region follows the static `red` array, so its base is only 16-byte aligned;
+    // TMA destinations need 128 bytes: align explicitly (the launch adds ATT_SMEM_SLACK).
+    uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
     float* sq = reinterpret_cast<float*>(smem + L::q_off);
     float* sc = reinterpret_cast<float*>(smem + L::sc_off);
     uint8_t* qs = smem + L::qs_off;
     float* se = reinterpret_cast<float*>(smem + L::e_off);
-    __shared__ float red[ATT_THREADS / 32][ATT_GMAX];
+    __shared__ float red[ATT_THREADS / 32][G];
 
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
     const int splits = gridDim.x;
-    const int G = H / Hkv;
     const size_t p0 = (size_t)split * chunk;
     const int np = (int)min((size_t)chunk, ctx_len > p0 ? ctx_len - p0 : (size_t)0);
     const size_t hb = (size_t)L::NB * 34;
@@ -85,21 +131,47 @@ __global__ void __launch_bounds__(ATT_THREADS)
     const size_t head_off = (size_t)kvh * hb;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+    uint8_t* raw_k = smem + L::raw_off;
+    uint8_t* raw_v = raw_k + L::raw_bytes(chunk);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(raw_v + L::raw_bytes(chunk));
+    const int x0 = (int)(head_off & ~(size_t)15), off = (int)(head_off & 15);
+    if (TMA) {
+        // both tiles are requested up front; V lands while the scores are computed
+        if (tid == 0) {
+            mbar_init(&bar[0], 1);
+            mbar_init(&bar[1], 1);
+            fence_barrier_init();
+        }
+        __syncthreads();
+        if (tid == 0) {
+            mbar_arrive_expect_tx(&bar[0], (uint32_t)(chunk * L::BOXW));
+            tma_load_3d(raw_k, &tmap_k, x0, (int)p0, seq, &bar[0]);
+            mbar_arrive_expect_tx(&bar[1], (uint32_t)(chunk * L::BOXW));
+            tma_load_3d(raw_v, &tmap_v, x0, (int)p0, seq, &bar[1]);
+        }
+    }
     // query heads of this group
     for (int i = tid; i < G * HD; i += ATT_THREADS)
         sq[i] = q[((size_t)seq * H + (size_t)kvh * G) * HD + i];
-    stage_rows<HD>(kring + (size_t)seq * seq_stride, capacity, bpp, head_off, p0, np, sc, qs);
+    if (TMA) {
+        const bool ok = mbar_wait_bounded(&bar[0], 0, err, nullptr);
+        repack_rows<HD>(raw_k, off, ok ? np : 0, sc, qs);
+    } else {
+        stage_rows<HD>(kring + (size_t)seq * seq_stride, capacity, bpp, head_off, p0, np, sc, qs);
+    }
     __syncthreads();
 
-    // ---- scores: one thread per position ----
+    // ---- scores: one thread per position; the block scale is applied to each block's sum ----
     for (int pos = tid; pos < np; pos += ATT_THREADS) {
-        float dot[ATT_GMAX];
+        float dot[G];
 #pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++) dot[g] = 0.0f;
+        for (int g = 0; g < G; g++) dot[g] = 0.0f;
         const uint8_t* row = qs + pos * L::QS_STRIDE;
 #pragma unroll
         for (int b = 0; b < L::NB; b++) {
-            const float s = sc[pos * L::NB + b];
+            float blk[G];
+#pragma unroll
+            for (int g = 0; g < G; g++) blk[g] = 0.0f;
 #pragma unroll
             for (int i16 = 0; i16 < 2; i16++) {
                 // 16-byte loads: with the 16-byte row skew, 8 lanes hit 8 distinct bank groups
@@ -107,52 +179,52 @@ __global__ void __launch_bounds__(ATT_THREADS)
                 const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
                 for (int i4 = 0; i4 < 4; i4++) {
+                    const float k0 = s8_to_f32<0>(ws[i4]), k1 = s8_to_f32<1>(ws[i4]);
+                    const float k2 = s8_to_f32<2>(ws[i4]), k3 = s8_to_f32<3>(ws[i4]);
+                    const int d = b * 32 + i16 * 16 + i4 * 4;
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float kv =
-                            __fmul_rn((float)(int8_t)((ws[i4] >> (8 * e)) & 0xFF), s);
-                        const int d = b * 32 + i16 * 16 + i4 * 4 + e;
-#pragma unroll
-                        for (int g = 0; g < ATT_GMAX; g++)
-                            if (g < G) dot[g] = __fmaf_rn(sq[g * HD + d], kv, dot[g]);
+                    for (int g = 0; g < G; g++) {
+                        const float4 qv = *reinterpret_cast<const float4*>(sq + g * HD + d);
+                        blk[g] = __fmaf_rn(qv.x, k0, blk[g]);
+                        blk[g] = __fmaf_rn(qv.y, k1, blk[g]);
+                        blk[g] = __fmaf_rn(qv.z, k2, blk[g]);
+                        blk[g] = __fmaf_rn(qv.w, k3, blk[g]);
                     }
                 }
             }
+            const float s = sc[pos * L::NB + b];
+#pragma unroll
+            for (int g = 0; g < G; g++) dot[g] = __fmaf_rn(blk[g], s, dot[g]);
         }
 #pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++) {
-            if (g < G) {
-                float score = __fmul_rn(dot[g], sm_scale);
-                if (softcap > 0.0f) score = tanhf(score / softcap) * softcap;
-                se[g * ATT_PMAX + pos] = score;
-            }
+        for (int g = 0; g < G; g++) {
+            float score = __fmul_rn(dot[g], sm_scale);
+            if (softcap > 0.0f) score = tanhf(score / softcap) * softcap;
+            se[g * ATT_PMAX + pos] = score;
         }
     }
     __syncthreads();
 
     // ---- split max and sum of exp, per query head ----
-    float mloc[ATT_GMAX], lloc[ATT_GMAX];
+    float mloc[G], lloc[G];
 #pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++) {
-        if (g >= G) break;
+    for (int g = 0; g < G; g++) {
         float m = -INFINITY;
         for (int pos = tid; pos < np; pos += ATT_THREADS) m = fmaxf(m, se[g * ATT_PMAX + pos]);
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) red[warp][g] = m;
     }
     __syncthreads();
 #pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++) {
-        if (g >= G) break;
+    for (int g = 0; g < G; g++) {
         float m = red[0][g];
         for (int w = 1; w < ATT_THREADS / 32; w++) m = fmaxf(m, red[w][g]);
         mloc[g] = m;
     }
     __syncthreads();
 #pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++) {
-        if (g >= G) break;
+    for (int g = 0; g < G; g++) {
         float l = 0.0f;
         for (int pos = tid; pos < np; pos += ATT_THREADS) {
             const float e = expf(se[g * ATT_PMAX + pos] - mloc[g]);
@@ -160,28 +232,32 @@ __global__ void __launch_bounds__(ATT_THREADS)
             l += e;
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         if (lane == 0) red[warp][g] = l;
     }
     __syncthreads();
 #pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++) {
-        if (g >= G) break;
+    for (int g = 0; g < G; g++) {
         float l = 0.0f;
         for (int w = 0; w < ATT_THREADS / 32; w++) l += red[w][g];
         lloc[g] = l;
     }
 
     // ---- V: stage, then one thread per head dimension (groups of threads split positions) ----
-    stage_rows<HD>(vring + (size_t)seq * seq_stride, capacity, bpp, head_off, p0, np, sc, qs);
+    if (TMA) {
+        const bool ok = mbar_wait_bounded(&bar[1], 0, err, nullptr);
+        repack_rows<HD>(raw_v, off, ok ? np : 0, sc, qs);
+    } else {
+        stage_rows<HD>(vring + (size_t)seq * seq_stride, capacity, bpp, head_off, p0, np, sc, qs);
+    }
     __syncthreads();
     constexpr int DPT = (HD + ATT_THREADS - 1) / ATT_THREADS;  // dims per thread
     constexpr int GROUPS = (HD >= ATT_THREADS) ? 1 : ATT_THREADS / HD;
     const int grp = tid / (ATT_THREADS / GROUPS);
     const int dt = tid % (ATT_THREADS / GROUPS);
-    float o[ATT_GMAX][DPT];
+    float o[G][DPT];
 #pragma unroll
-    for (int g = 0; g < ATT_GMAX; g++)
+    for (int g = 0; g < G; g++)
 #pragma unroll
         for (int k = 0; k < DPT; k++) o[g][k] = 0.0f;
     for (int pos = grp; pos < np; pos += GROUPS) {
@@ -190,10 +266,11 @@ __global__ void __launch_bounds__(ATT_THREADS)
             const int d = dt + k * ATT_THREADS;
             if (d < HD) {
                 const int b = d / 32;
-                const float v = __fmul_rn((float)(int8_t)qs[pos * L::QS_STRIDE + d], sc[pos * L::NB + b]);
+                const float v = __fmul_rn(
+                    int_to_f32_exact((int)*reinterpret_cast<const int8_t*>(qs + pos * L::QS_STRIDE + d)),
+                    sc[pos * L::NB + b]);
 #pragma unroll
-                for (int g = 0; g < ATT_GMAX; g++)
-                    if (g < G) o[g][k] = __fmaf_rn(se[g * ATT_PMAX + pos], v, o[g][k]);
+                for (int g = 0; g < G; g++) o[g][k] = __fmaf_rn(se[g * ATT_PMAX + pos], v, o[g][k]);
             }
         }
     }
@@ -202,20 +279,18 @@ __global__ void __launch_bounds__(ATT_THREADS)
     float* ored = se;  // [GROUPS][G][HD] <= GMAX*PMAX floats
     if (GROUPS > 1) {
 #pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++)
-            if (g < G)
+        for (int g = 0; g < G; g++)
 #pragma unroll
-                for (int k = 0; k < DPT; k++) {
-                    const int d = dt + k * ATT_THREADS;
-                    if (d < HD) ored[(grp * G + g) * HD + d] = o[g][k];
-                }
+            for (int k = 0; k < DPT; k++) {
+                const int d = dt + k * ATT_THREADS;
+                if (d < HD) ored[(grp * G + g) * HD + d] = o[g][k];
+            }
         __syncthreads();
     }
     const size_t base = (((size_t)seq * H + (size_t)kvh * G) * splits + split);
     if (grp == 0) {
 #pragma unroll
-        for (int g = 0; g < ATT_GMAX; g++) {
-            if (g >= G) break;
+        for (int g = 0; g < G; g++) {
             float* dst = part + (base + (size_t)g * splits) * (HD + 2);
 #pragma unroll
             for (int k = 0; k < DPT; k++) {
@@ -266,8 +341,8 @@ int pick_splits(size_t ctx_len, int Hkv, int batch, int num_sms) {
     return (int)s;
 }
 
-template <int HD>
-int launch_hd(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* v,
+template <int HD, int G>
+int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* v,
               size_t seq_stride, size_t capacity, size_t ctx_len, int H, int Hkv, int batch,
               float softcap, float* out, float* part, int splits) {
     using L = AttnLayout<HD>;
@@ -276,22 +351,75 @@ int launch_hd(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* 
     static uint64_t attr_set_mask = 0;  // one bit per device: the attribute is per device
     const uint64_t bit = 1ull << (ctx->device & 63);
     if (!(attr_set_mask & bit)) {
-        int st = check_cuda(cudaFuncSetAttribute(attn_decode_partial_kernel<HD>,
+        const int max_bytes =
+            (int)(L::BOXW <= 256 ? L::tma_bytes(ATT_PMAX) : L::bytes) + ATT_SMEM_SLACK;
+        int st = check_cuda(cudaFuncSetAttribute(attn_decode_partial_kernel<HD, G, false>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)L::bytes),
+                                                 (int)L::bytes + ATT_SMEM_SLACK),
+                            "attn smem attribute");
+        if (!st)
+            st = check_cuda(cudaFuncSetAttribute(attn_decode_partial_kernel<HD, G, true>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 max_bytes),
                             "attn smem attribute");
         if (st) return st;
         attr_set_mask |= bit;
     }
+    // TMA staging when the ring geometry allows 16-byte aligned tensor-map copies and the
+    // context does not wrap the ring (positions 0..ctx-1 are slots 0..ctx-1)
+    const size_t bpp = (size_t)Hkv * L::HB;
+    const size_t stride = batch > 1 ? seq_stride : bpp * capacity;
+    const bool tma = L::BOXW <= 256 && ctx_len <= capacity && bpp % 16 == 0 &&
+                     stride % 16 == 0 && ((uintptr_t)k % 16) == 0 && ((uintptr_t)v % 16) == 0 &&
+                     capacity <= 0x7fffffffu && batch <= 65535;
+    CUtensorMap tk, tv;
+    memset(&tk, 0, sizeof(tk));
+    memset(&tv, 0, sizeof(tv));
+    if (tma) {
+        const uint64_t dims[3] = {(uint64_t)bpp, (uint64_t)capacity, (uint64_t)batch};
+        const uint64_t strides[2] = {(uint64_t)bpp, (uint64_t)stride};
+        const uint32_t box[3] = {(uint32_t)L::BOXW, (uint32_t)chunk, 1};
+        int st = encode_tensor_map(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k, 3, dims, strides, box,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!st)
+            st = encode_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, v, 3, dims, strides, box,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
     dim3 g1(splits, Hkv, batch);
-    attn_decode_partial_kernel<HD><<<g1, ATT_THREADS, L::bytes, ctx->stream>>>(
-        q, k, v, seq_stride, capacity, ctx_len, H, Hkv, chunk, sm_scale, softcap, part);
+    if (tma)
+        attn_decode_partial_kernel<HD, G, true>
+            <<<g1, ATT_THREADS, L::tma_bytes(chunk) + ATT_SMEM_SLACK, ctx->stream>>>(
+                q, k, v, seq_stride, capacity, ctx_len, H, Hkv, chunk, sm_scale, softcap, part,
+                tk, tv, ctx->d_error);
+    else
+        attn_decode_partial_kernel<HD, G, false><<<g1, ATT_THREADS, L::bytes + ATT_SMEM_SLACK,
+                                                   ctx->stream>>>(
+            q, k, v, seq_stride, capacity, ctx_len, H, Hkv, chunk, sm_scale, softcap, part, tk, tv,
+            ctx->d_error);
     int st = check_cuda(cudaGetLastError(), "attn_decode_partial launch");
     if (st) return st;
     dim3 g2(H, batch);
     attn_decode_combine_kernel<HD><<<g2, HD, 0, ctx->stream>>>(part, H, splits, out);
     ctx->launches += 2;
     return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
+}
+
+
+// The query-group size is a template parameter so that the inner loops carry no predicated
+// lanes for the heads a group does not have.
+template <int HD>
+int launch_hd(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* v,
+              size_t seq_stride, size_t capacity, size_t ctx_len, int H, int Hkv, int batch,
+              float softcap, float* out, float* part, int splits) {
+    switch (H / Hkv) {
+#define SULIMO_ATTN_G(g) \
+    case g: return launch_hdg<HD, g>(ctx, q, k, v, seq_stride, capacity, ctx_len, H, Hkv, batch, softcap, out, part, splits);
+        SULIMO_ATTN_G(1) SULIMO_ATTN_G(2) SULIMO_ATTN_G(3) SULIMO_ATTN_G(4)
+        SULIMO_ATTN_G(5) SULIMO_ATTN_G(6) SULIMO_ATTN_G(7) SULIMO_ATTN_G(8)
+#undef SULIMO_ATTN_G
+        default: return set_error(SULIMO_EINVAL, "at most 8 query heads per KV head");
+    }
 }
 
 }  // namespace

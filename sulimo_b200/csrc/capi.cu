@@ -72,6 +72,27 @@ EncodeTiledFn get_encode_tiled() {
     return fn;
 }
 
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int rank,
+                      const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                      CUtensorMapSwizzle swz) {
+    EncodeTiledFn enc = get_encode_tiled();
+    if (!enc) return set_error(SULIMO_ENODEV, "cuTensorMapEncodeTiled unavailable");
+    if (rank < 1 || rank > 3) return set_error(SULIMO_EINVAL, "tensor map rank must be 1..3");
+    cuuint64_t d[3], st[2];
+    cuuint32_t bx[3], estr[3] = {1, 1, 1};
+    for (int i = 0; i < rank; i++) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+    }
+    for (int i = 0; i + 1 < rank; i++) st[i] = strides[i];
+    CUresult r = enc(map, dt, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(SULIMO_ELAUNCH, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return SULIMO_OK;
+}
+
 }  // namespace sulimo
 
 using sulimo::set_error;

@@ -56,15 +56,6 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
-}
-
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1,
                                              const void* src) {
     asm volatile(
@@ -397,21 +388,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 int encode_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int rank,
                const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
                CUtensorMapSwizzle swz) {
-    EncodeTiledFn enc = get_encode_tiled();
-    if (!enc) return set_error(SULIMO_ENODEV, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t d[3], st[2];
-    cuuint32_t bx[3], estr[3] = {1, 1, 1};
-    for (int i = 0; i < rank; i++) {
-        d[i] = dims[i];
-        bx[i] = box[i];
-    }
-    for (int i = 0; i + 1 < rank; i++) st[i] = strides[i];
-    CUresult r = enc(map, dt, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return set_error(SULIMO_ELAUNCH, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
-    return SULIMO_OK;
+    return encode_tensor_map(map, dt, base, rank, dims, strides, box, swz);
 }
 
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,

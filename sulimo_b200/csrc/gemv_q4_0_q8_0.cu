@@ -129,11 +129,215 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Streaming form for K a multiple of 256 and 16-byte aligned scales (every BASELINE shape).
+//
+// CTA: 64 rows x 4 threads per row (thread p of a row owns AVX2 lanes 2p and 2p+1, i.e. quant
+// word p of every block) + 1 producer warp.  The producer streams the rows' quants and scales
+// through a ring of TS stages of 8 blocks with TMA (quants 128-byte swizzled, so the 4 word reads
+// of 8 rows hit 32 distinct banks); the activations of NV vectors are packed into per-lane words
+// in shared memory once per CTA.  Each thread keeps 2 x NV fp32 lane accumulators and applies
+// exactly the AVX2 FMA sequence; the row's 8 lanes are combined with hsum_256's tree through
+// shuffles inside the 4-thread group.
+constexpr int TS_ROWS = 64;
+constexpr int TS_BLOCKS = 8;                     // Q4_0 blocks per stage (K = 256)
+constexpr int TS_STAGES = 8;
+constexpr int TS_THREADS = TS_ROWS * 4 + 32;     // + producer warp
+constexpr uint32_t TS_Q_BYTES = TS_ROWS * TS_BLOCKS * 16;  // 8 KB
+constexpr uint32_t TS_S_BYTES = TS_ROWS * TS_BLOCKS * 2;   // 1 KB
+constexpr uint32_t TS_STAGE_BYTES = TS_Q_BYTES + TS_S_BYTES;
+
+// exact int -> float for |s| < 2^22: 1.5*2^23 + s has an integer ulp
+__device__ __forceinline__ float small_int_to_float(int s) {
+    return __fsub_rn(__int_as_float(0x4B400000 + s), 12582912.0f);
+}
+
+template <int NV>
+__global__ void __launch_bounds__(TS_THREADS, 1)
+    gemv_q4_0_q8_0_tma_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                              const __grid_constant__ CUtensorMap tmap_s,
+                              const uint8_t* __restrict__ xq8, int rows, int nb, int batch,
+                              float* __restrict__ out, int* __restrict__ err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    uint8_t* stages = sm;                                            // TS_STAGES x stage
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + TS_STAGES * TS_STAGE_BYTES);
+    uint64_t* empty = full + TS_STAGES;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + TS_STAGES);
+    int* xw = reinterpret_cast<int*>(empty + TS_STAGES + 1);        // [NV][nb][8]
+    int* xc = xw + NV * nb * 8;                                      // [NV][nb][8]
+    float* xs = reinterpret_cast<float*>(xc + NV * nb * 8);          // [NV][nb]
+
+    const int tid = threadIdx.x;
+    const int row0 = blockIdx.x * TS_ROWS;
+    const int v0 = blockIdx.y * NV;
+    const int nchunks = nb / TS_BLOCKS;
+
+    if (tid == 0) {
+        for (int s = 0; s < TS_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], TS_ROWS * 4);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (tid >= TS_ROWS * 4) {
+        // ------------------------------ producer warp ------------------------------
+        if (tid == TS_ROWS * 4) {
+            prefetch_tensormap(&tmap_q);
+            prefetch_tensormap(&tmap_s);
+            int issued = 0;
+            for (int c = 0; c < nchunks; c++) {
+                const int s = c % TS_STAGES;
+                const uint32_t ph = (uint32_t)(c / TS_STAGES) & 1u;
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
+                uint8_t* st = stages + s * TS_STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[s], TS_STAGE_BYTES);
+                tma_load_2d(st, &tmap_q, c * TS_BLOCKS * 16, row0, &full[s]);
+                tma_load_2d(st + TS_Q_BYTES, &tmap_s, c * TS_BLOCKS, row0, &full[s]);
+                issued = c + 1;
+            }
+            if (*abort_flag)  // the issued copies must land before the CTA releases its smem
+                for (int c = (issued > TS_STAGES ? issued - TS_STAGES : 0); c < issued; c++)
+                    mbar_wait_bounded(&full[c % TS_STAGES], (uint32_t)(c / TS_STAGES) & 1u, err,
+                                      nullptr);
+        }
+        return;  // the consumers synchronize among themselves (named barrier 1) from here on
+    }
+
+    // ---- pack the activations: lane j of block b -> {x[2j],x[2j+1],x[16+2j],x[17+2j]} ----
+    for (int it = tid; it < NV * nb * 8; it += TS_ROWS * 4) {
+        const int v = it / (nb * 8), rem = it - v * nb * 8;
+        const int b = rem >> 3, j = rem & 7;
+        uint32_t w = 0;
+        float d = 0.0f;
+        if (v0 + v < batch) {
+            const uint16_t* blk =
+                reinterpret_cast<const uint16_t*>(xq8 + ((size_t)(v0 + v) * nb + b) * 34);
+            w = (uint32_t)__ldg(blk + 1 + j) | ((uint32_t)__ldg(blk + 9 + j) << 16);
+            if (j == 0) d = f16_bits_to_f32(__ldg(blk));
+        }
+        const int sum = (int)(int8_t)(w & 0xFF) + (int)(int8_t)((w >> 8) & 0xFF) +
+                        (int)(int8_t)((w >> 16) & 0xFF) + (int)(int8_t)(w >> 24);
+        xw[it] = (int)w;
+        xc[it] = -8 * sum;
+        if (j == 0) xs[v * nb + b] = d;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(TS_ROWS * 4) : "memory");  // consumers only
+
+    const int rl = tid >> 2, p = tid & 3;
+    float acc[NV][2];
+#pragma unroll
+    for (int v = 0; v < NV; v++) acc[v][0] = acc[v][1] = 0.0f;
+
+    for (int c = 0; c < nchunks; c++) {
+        const int s = c % TS_STAGES;
+        const uint32_t ph = (uint32_t)(c / TS_STAGES) & 1u;
+        if (!mbar_wait_bounded(&full[s], ph, err, abort_flag)) break;
+        const uint8_t* qst = stages + s * TS_STAGE_BYTES + rl * 128;
+        const uint16_t* sst =
+            reinterpret_cast<const uint16_t*>(stages + s * TS_STAGE_BYTES + TS_Q_BYTES) + rl * 8;
+#pragma unroll
+        for (int b = 0; b < TS_BLOCKS; b++) {
+            const int kb = c * TS_BLOCKS + b;
+            // 128-byte swizzle: the 16-byte chunk b of row rl sits at chunk b ^ (rl & 7)
+            const uint32_t word =
+                *reinterpret_cast<const uint32_t*>(qst + ((b ^ (rl & 7)) << 4) + p * 4);
+            const float dw = f16_bits_to_f32(sst[b]);
+            const uint32_t lo = word & 0x0F0F0F0Fu;
+            const uint32_t hi = (word >> 4) & 0x0F0F0F0Fu;
+            const uint32_t l0 = prmt(lo, hi, 0x5410);  // lane 2p
+            const uint32_t l1 = prmt(lo, hi, 0x7632);  // lane 2p+1
+#pragma unroll
+            for (int v = 0; v < NV; v++) {
+                const int2 xv = *reinterpret_cast<const int2*>(xw + (v * nb + kb) * 8 + 2 * p);
+                const int2 cv = *reinterpret_cast<const int2*>(xc + (v * nb + kb) * 8 + 2 * p);
+                const float d = __fmul_rn(dw, xs[v * nb + kb]);
+                acc[v][0] = __fmaf_rn(small_int_to_float(dp4a_us(l0, (uint32_t)xv.x, cv.x)), d,
+                                      acc[v][0]);
+                acc[v][1] = __fmaf_rn(small_int_to_float(dp4a_us(l1, (uint32_t)xv.y, cv.y)), d,
+                                      acc[v][1]);
+            }
+        }
+        mbar_arrive(&empty[s]);
+    }
+
+    // hsum_256: ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)); thread p holds lanes 2p, 2p+1
+    const int row = row0 + rl;
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const float u0 = __fadd_rn(acc[v][0], __shfl_xor_sync(0xffffffffu, acc[v][0], 2));
+        const float u1 = __fadd_rn(acc[v][1], __shfl_xor_sync(0xffffffffu, acc[v][1], 2));
+        const float w = __fadd_rn(u0, u1);
+        const float r = __fadd_rn(w, __shfl_xor_sync(0xffffffffu, w, 1));
+        if (p == 0 && row < rows && v0 + v < batch && !*abort_flag)
+            out[(size_t)(v0 + v) * rows + row] = r;
+    }
+}
+
+template <int NV>
+size_t gemv_tma_smem(int nb) {
+    return 1024 + (size_t)TS_STAGES * TS_STAGE_BYTES + 8 * (2 * TS_STAGES + 1) +
+           (size_t)NV * nb * (8 * 4 * 2 + 4);
+}
+
+template <int NV>
+int launch_gemv_tma(sulimo_ctx* ctx, const CUtensorMap& tq, const CUtensorMap& ts,
+                    const uint8_t* xq8, int rows, int nb, int batch, float* out) {
+    const size_t smem = gemv_tma_smem<NV>(nb);
+    static uint64_t attr_mask = 0;  // per device
+    const uint64_t bit = 1ull << (ctx->device & 63);
+    if (!(attr_mask & bit)) {
+        int st = check_cuda(cudaFuncSetAttribute(gemv_q4_0_q8_0_tma_kernel<NV>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 227 * 1024),
+                            "gemv smem attribute");
+        if (st) return st;
+        attr_mask |= bit;
+    }
+    dim3 grid((rows + TS_ROWS - 1) / TS_ROWS, (batch + NV - 1) / NV);
+    gemv_q4_0_q8_0_tma_kernel<NV><<<grid, TS_THREADS, smem, ctx->stream>>>(
+        tq, ts, xq8, rows, nb, batch, out, ctx->d_error);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "gemv_q4_0_q8_0_tma launch");
+}
+
 }  // namespace
 
 int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                           const void* x_q8, int rows, int cols, int batch, float* out) {
     const int nb = cols / 32;
+    // streaming form: K multiple of 256, 16-byte aligned scales, activations of up to 8 vectors
+    // packed in <= 96 KB of shared memory
+    if (nb % TS_BLOCKS == 0 && ((uintptr_t)w_scales % 16) == 0 && rows > 0) {
+        int nv = 8;  // vectors per weight pass: <= batch, packed activations <= 96 KB
+        while (nv > 1 && (nv > batch || (size_t)nv * nb * 68 > 96 * 1024)) nv >>= 1;
+        if ((size_t)nv * nb * 68 <= 96 * 1024) {
+            CUtensorMap tq, ts;
+            const uint64_t qd[2] = {(uint64_t)nb * 16, (uint64_t)rows};
+            const uint64_t qs[1] = {(uint64_t)nb * 16};
+            const uint32_t qb[2] = {TS_BLOCKS * 16, TS_ROWS};
+            int st = encode_tensor_map(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_quants, 2, qd, qs, qb,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+            if (st) return st;
+            const uint64_t sd[2] = {(uint64_t)nb, (uint64_t)rows};
+            const uint64_t ss[1] = {(uint64_t)nb * 2};
+            const uint32_t sbx[2] = {TS_BLOCKS, TS_ROWS};
+            st = encode_tensor_map(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, w_scales, 2, sd, ss, sbx,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (st) return st;
+            const uint8_t* x = reinterpret_cast<const uint8_t*>(x_q8);
+            switch (nv) {
+                case 8: return launch_gemv_tma<8>(ctx, tq, ts, x, rows, nb, batch, out);
+                case 4: return launch_gemv_tma<4>(ctx, tq, ts, x, rows, nb, batch, out);
+                case 2: return launch_gemv_tma<2>(ctx, tq, ts, x, rows, nb, batch, out);
+                default: return launch_gemv_tma<1>(ctx, tq, ts, x, rows, nb, batch, out);
+            }
+        }
+    }
     const size_t tiles = ((size_t)rows + GEMV_ROWS - 1) / GEMV_ROWS;
     const size_t grid = tiles * (size_t)batch;
     if (grid > 0x7fffffffu) return set_error(SULIMO_EINVAL, "gemv grid too large");

@@ -36,6 +36,11 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn get_encode_tiled();
+// Encodes a tiled tensor map of rank 2 or 3: dims and box innermost first, `strides` = byte
+// strides of dims 1.. (rank-1 entries); interleave none, L2 promotion 256B, zero OOB fill.
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int rank,
+                      const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                      CUtensorMapSwizzle swz);
 
 // Launchers (return SULIMO_* status; argument checks done by the C-ABI layer).
 int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,

@@ -161,7 +161,7 @@ def test_gemv_reference_avx2_case(ctx):
 
 @pytest.mark.parametrize("rows,cols,batch", [
     (1, 32, 1), (17, 64, 1), (300, 8960, 1), (8192, 3072, 2), (100, 96, 3), (33, 2080, 1),
-    (1536, 8960, 1), (256, 3072, 8),
+    (1536, 8960, 1), (256, 3072, 8), (1000, 2048, 5), (512, 3072, 32), (65, 256, 9),
 ])
 def test_gemv_shapes_bit_exact(ctx, rows, cols, batch):
     ws, wq = make_q4_0(rows, cols, seed=rows + cols)
@@ -172,6 +172,22 @@ def test_gemv_shapes_bit_exact(ctx, rows, cols, batch):
         ref = O.matvec_q4_0_q8_0_avx2(ws, wq, xq8[b * cols // 32 * 34:(b + 1) * cols // 32 * 34],
                                       rows, cols, threads=8)
         assert np.array_equal(got[b].view(np.uint32), ref.view(np.uint32)), f"batch {b}"
+
+
+def test_gemv_unaligned_scales_take_the_general_kernel(ctx):
+    """Scales that are only 2-byte aligned cannot be streamed with TMA; the general kernel
+    must give the same bits."""
+    import torch
+    rows, cols = 700, 1536
+    ws, wq = make_q4_0(rows, cols, seed=21)
+    x = np.random.default_rng(22).standard_normal(cols).astype(np.float32)
+    xq8 = O.quantize_f32_to_q8_0(x)
+    big = dev(np.concatenate([np.zeros(1, np.uint16), ws]))      # scales start 2 bytes in
+    out = empty(rows, torch.float32)
+    sb.dispatch_matvec_q4_0_q8_0(ctx, big.data_ptr() + 2, dev(wq), dev(xq8), rows, cols, out)
+    ctx.finish()
+    ref = O.matvec_q4_0_q8_0_avx2(ws, wq, xq8, rows, cols, threads=8)
+    assert np.array_equal(host(out).view(np.uint32), ref.view(np.uint32))
 
 
 def test_gemv_rejects_bad_cols(ctx):
