@@ -309,25 +309,306 @@ __global__ void __launch_bounds__(ATT_THREADS)
     }
 }
 
-// One CTA per (query head, sequence); thread d owns output dimension d.
+// ---------------------------------------------------------------------------------------------
+// Slot form: one CTA per (context split, sequence) covering ALL kv heads.  Positions
+// p0..p0+np-1 of a ring are np contiguous slots, so K and V arrive with one bulk copy each
+// (exactly the algorithmic bytes, no tensor map).  Used when the context does not wrap the
+// ring and the slot size is a multiple of 16 bytes (Qwen2.5-1.5B: 272 B, Llama-3.2-3B: 1088 B).
+//   scores : item (position, kv head), G dot products over the head's Q8_0 blocks read in place
+//            (2-byte loads: 34-byte blocks are 2-byte aligned), block scale applied per block;
+//   softmax: one warp per (kv head, query head) row over the split's positions;
+//   V      : weights pre-multiplied by V's block scales, item (kv head, dim) accumulates
+//            sum_pos w[g][pos][b] * v_int[pos][d] for the G query heads.
+constexpr int SLOT_THREADS = 256;
+constexpr size_t SLOT_SMEM_MAX = 200 * 1024;
+
+template <int HD, int G>
+struct SlotLayout {
+    static constexpr int NB = HD / 32;
+    static constexpr int HB = NB * 34;
+    static constexpr int QROW = G * HD + 4;  // padded: kv heads' query rows hit distinct banks
+    __host__ __device__ static size_t raw_bytes(int chunk, int Hkv) {
+        return ((size_t)chunk * Hkv * HB + 127) / 128 * 128;
+    }
+    __host__ __device__ static size_t q_off(int chunk, int Hkv) { return 2 * raw_bytes(chunk, Hkv); }
+    __host__ __device__ static size_t e_off(int chunk, int Hkv) {
+        return q_off(chunk, Hkv) + (size_t)Hkv * QROW * 4;
+    }
+    __host__ __device__ static size_t w_off(int chunk, int Hkv) {  // [Hkv][G][chunk][NB]
+        return e_off(chunk, Hkv) + (size_t)Hkv * G * chunk * 4;
+    }
+    __host__ __device__ static size_t stat_off(int chunk, int Hkv) {  // m, l per row
+        return w_off(chunk, Hkv) + (size_t)Hkv * G * chunk * NB * 4;
+    }
+    __host__ __device__ static size_t bar_off(int chunk, int Hkv) {
+        return (stat_off(chunk, Hkv) + (size_t)Hkv * G * 8 + 15) / 16 * 16;
+    }
+    static size_t bytes(int chunk, int Hkv) { return bar_off(chunk, Hkv) + 16 + 128; }
+};
+
+// two sign-extended bytes of a little-endian 16-bit word, as exact floats
+__device__ __forceinline__ void s8x2_to_f32(uint32_t w, float& lo, float& hi) {
+    lo = __fsub_rn(__int_as_float(0x4B400000 + (int)prmt(w, 0u, 0x8880)), 12582912.0f);
+    hi = __fsub_rn(__int_as_float(0x4B400000 + (int)prmt(w, 0u, 0x9991)), 12582912.0f);
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(SLOT_THREADS)
+    attn_decode_slots_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kring,
+                             const uint8_t* __restrict__ vring, size_t seq_stride,
+                             size_t ctx_len, int H, int Hkv, int chunk, float sm_scale,
+                             float softcap, float* __restrict__ part, int* __restrict__ err) {
+    using L = SlotLayout<HD, G>;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+    uint8_t* raw_k = smem;
+    uint8_t* raw_v = smem + L::raw_bytes(chunk, Hkv);
+    float* sq = reinterpret_cast<float*>(smem + L::q_off(chunk, Hkv));
+    float* se = reinterpret_cast<float*>(smem + L::e_off(chunk, Hkv));
+    float* sw = reinterpret_cast<float*>(smem + L::w_off(chunk, Hkv));
+    float* stat = reinterpret_cast<float*>(smem + L::stat_off(chunk, Hkv));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::bar_off(chunk, Hkv));
+
+    const int split = blockIdx.x, seq = blockIdx.y, splits = gridDim.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t bpp = (size_t)Hkv * L::HB;
+    const size_t p0 = (size_t)split * chunk;
+    const int np = (int)min((size_t)chunk, ctx_len > p0 ? ctx_len - p0 : (size_t)0);
+    const int rows = Hkv * G;
+
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0 && np > 0) {
+        const uint32_t bytes = (uint32_t)(np * bpp);
+        mbar_arrive_expect_tx(&bar[0], bytes);
+        bulk_load(raw_k, kring + (size_t)seq * seq_stride + p0 * bpp, bytes, &bar[0]);
+        mbar_arrive_expect_tx(&bar[1], bytes);
+        bulk_load(raw_v, vring + (size_t)seq * seq_stride + p0 * bpp, bytes, &bar[1]);
+    }
+    // query rows, kv head major, padded
+    for (int i = tid; i < H * HD; i += SLOT_THREADS) {
+        const int h = i / HD, d = i - h * HD;
+        sq[(h / G) * L::QROW + (h % G) * HD + d] = q[(size_t)seq * H * HD + i];
+    }
+    bool ok = np > 0 && mbar_wait_bounded(&bar[0], 0, err, nullptr);
+    __syncthreads();
+
+    // ---- scores ----
+    if (ok) {
+        for (int item = tid; item < np * Hkv; item += SLOT_THREADS) {
+            const int kvh = item % Hkv, pos = item / Hkv;
+            const uint8_t* row = raw_k + (size_t)pos * bpp + kvh * L::HB;
+            const float* qh = sq + kvh * L::QROW;
+            float dot[G];
+#pragma unroll
+            for (int g = 0; g < G; g++) dot[g] = 0.0f;
+#pragma unroll
+            for (int b = 0; b < L::NB; b++) {
+                const uint16_t* blk = reinterpret_cast<const uint16_t*>(row + b * 34);
+                float acc[G];
+#pragma unroll
+                for (int g = 0; g < G; g++) acc[g] = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    float k0, k1;
+                    s8x2_to_f32(blk[1 + i], k0, k1);
+                    const int d = b * 32 + 2 * i;
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        const float2 qv = *reinterpret_cast<const float2*>(qh + g * HD + d);
+                        acc[g] = __fmaf_rn(qv.x, k0, acc[g]);
+                        acc[g] = __fmaf_rn(qv.y, k1, acc[g]);
+                    }
+                }
+                const float s = f16_bits_to_f32(blk[0]);
+#pragma unroll
+                for (int g = 0; g < G; g++) dot[g] = __fmaf_rn(acc[g], s, dot[g]);
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float score = __fmul_rn(dot[g], sm_scale);
+                if (softcap > 0.0f) score = tanhf(score / softcap) * softcap;
+                se[(kvh * G + g) * chunk + pos] = score;
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- softmax over the split: one warp per (kv head, query head) row ----
+    for (int r = warp; r < rows; r += SLOT_THREADS / 32) {
+        float* e = se + r * chunk;
+        float m = -INFINITY;
+        for (int pos = lane; pos < np; pos += 32) m = fmaxf(m, e[pos]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int pos = lane; pos < np; pos += 32) {
+            const float x = expf(e[pos] - m);
+            e[pos] = x;
+            l += x;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) {
+            stat[2 * r] = m;
+            stat[2 * r + 1] = l;
+        }
+    }
+    // always wait for V when it was requested: the copy must land before the CTA exits
+    if (np > 0) ok = mbar_wait_bounded(&bar[1], 0, err, nullptr) && ok;
+    __syncthreads();
+
+    // ---- weights times V's block scales: w[kvh][g][pos][b] ----
+    if (ok) {
+        for (int it = tid; it < rows * np * L::NB; it += SLOT_THREADS) {
+            const int b = it % L::NB, rp = it / L::NB;
+            const int pos = rp % np, r = rp / np;
+            const int kvh = r / G;
+            const float s = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
+                raw_v + (size_t)pos * bpp + kvh * L::HB + b * 34));
+            sw[(r * chunk + pos) * L::NB + b] = __fmul_rn(se[r * chunk + pos], s);
+        }
+    }
+    __syncthreads();
+
+    // ---- V: item (kv head, dim) ----
+    const size_t base = (size_t)seq * H;
+    for (int item = tid; item < Hkv * HD; item += SLOT_THREADS) {
+        const int kvh = item / HD, d = item - kvh * HD;
+        const int b = d >> 5;
+        float acc[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) acc[g] = 0.0f;
+        if (ok) {
+            const int8_t* col =
+                reinterpret_cast<const int8_t*>(raw_v + kvh * L::HB + b * 34 + 2 + (d & 31));
+            const float* wr = sw + ((size_t)kvh * G * chunk) * L::NB + b;
+#pragma unroll 4
+            for (int pos = 0; pos < np; pos++) {
+                const float v = __fsub_rn(
+                    __int_as_float(0x4B400000 + (int)col[(size_t)pos * bpp]), 12582912.0f);
+#pragma unroll
+                for (int g = 0; g < G; g++)
+                    acc[g] = __fmaf_rn(wr[((size_t)g * chunk + pos) * L::NB], v, acc[g]);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const int h = kvh * G + g;
+            float* dst = part + ((base + h) * splits + split) * (HD + 2);
+            dst[d] = acc[g];
+            if (d == 0) {
+                dst[HD] = ok ? stat[2 * h] : -INFINITY;
+                dst[HD + 1] = ok ? stat[2 * h + 1] : 0.0f;
+            }
+        }
+    }
+}
+
+// Shared-memory bytes of the slot form (must equal SlotLayout<HD, G>::bytes; checked at launch).
+size_t slot_bytes_generic(int chunk, int Hkv, int G, int HD) {
+    const int NB = HD / 32, HB = NB * 34;
+    const size_t raw = ((size_t)chunk * Hkv * HB + 127) / 128 * 128;
+    size_t off = 2 * raw + (size_t)Hkv * (G * HD + 4) * 4 + (size_t)Hkv * G * chunk * 4 +
+                 (size_t)Hkv * G * chunk * NB * 4;
+    off = (off + (size_t)Hkv * G * 8 + 15) / 16 * 16;
+    return off + 16 + 128;
+}
+
+// Whether the slot form can run this launch: no ring wrap, 16-byte slots, aligned rings, and
+// the split's tiles fit the shared-memory budget.
+bool slot_form_ok(size_t ctx_len, size_t capacity, int Hkv, int G, int HD, int batch,
+                  size_t seq_stride, const void* k, const void* v, int chunk) {
+    const size_t bpp = (size_t)Hkv * (HD / 32) * 34;
+    const size_t stride = batch > 1 ? seq_stride : 0;
+    return ctx_len >= 1 && ctx_len <= capacity && bpp % 16 == 0 && stride % 16 == 0 &&
+           ((uintptr_t)k % 16) == 0 && ((uintptr_t)v % 16) == 0 && chunk >= 1 &&
+           slot_bytes_generic(chunk, Hkv, G, HD) <= SLOT_SMEM_MAX &&
+           (size_t)chunk * bpp < (1u << 30) && batch <= 65535 && G >= 1 && G <= 8;
+}
+
+// Split count for the slot form, or 0 when the ring does not allow it: one CTA per SM (the
+// merge reads every split's partial row, so more splits cost more than they hide), at least 8
+// positions per split, and a chunk whose tiles fit two CTAs per SM.
+int slot_splits(size_t ctx_len, size_t capacity, int H, int Hkv, int HD, int batch, int num_sms,
+                size_t seq_stride, const void* k, const void* v) {
+    const int G = H / Hkv;
+    if (G < 1 || G > 8) return 0;
+    int max_chunk = 256;
+    while (max_chunk > 1 && slot_bytes_generic(max_chunk, Hkv, G, HD) > SLOT_SMEM_MAX / 2)
+        max_chunk--;
+    if (!slot_form_ok(ctx_len, capacity, Hkv, G, HD, batch, seq_stride, k, v, max_chunk))
+        return 0;
+    const size_t min_splits = (ctx_len + max_chunk - 1) / max_chunk;
+    size_t want = ((size_t)num_sms + batch - 1) / batch;
+    const size_t cap8 = (ctx_len + 7) / 8;
+    if (want > cap8) want = cap8;
+    const size_t s = want > min_splits ? want : min_splits;
+    return s > 0x7fffffffu ? 0 : (int)(s < 1 ? 1 : s);
+}
+
+// One CTA per (query head, sequence) merges that head's splits:
+//   M = max_s m_s,  out = sum_s o_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
+// The splits are shared out over 8 warps (lane owns HD/32 consecutive dimensions of each o_s
+// row, so a warp reads a row coalesced); the warps' sums are added in a fixed order through
+// shared memory.  A per-thread serial walk over the splits would be a chain of dependent
+// global loads.
+constexpr int COMBINE_THREADS = 256;
+
 template <int HD>
-__global__ void __launch_bounds__(HD < 32 ? 32 : HD)
+__global__ void __launch_bounds__(COMBINE_THREADS)
     attn_decode_combine_kernel(const float* __restrict__ part, int H, int splits,
                                float* __restrict__ out) {
-    const int h = blockIdx.x, seq = blockIdx.y, d = threadIdx.x;
+    constexpr int W = COMBINE_THREADS / 32;
+    constexpr int DPL = HD / 32;  // dimensions per lane
+    __shared__ float red[W];
+    __shared__ float so[W][HD];
+    __shared__ float sl[W];
+    const int h = blockIdx.x, seq = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* p = part + ((size_t)seq * H + h) * splits * (HD + 2);
+
     float M = -INFINITY;
-    for (int s = 0; s < splits; s++) M = fmaxf(M, p[(size_t)s * (HD + 2) + HD]);
-    float Lsum = 0.0f, O = 0.0f;
-    for (int s = 0; s < splits; s++) {
+    for (int s = tid; s < splits; s += COMBINE_THREADS)
+        M = fmaxf(M, p[(size_t)s * (HD + 2) + HD]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red[warp] = M;
+    __syncthreads();
+    M = red[0];
+#pragma unroll
+    for (int w = 1; w < W; w++) M = fmaxf(M, red[w]);
+
+    float acc[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; j++) acc[j] = 0.0f;
+    float L = 0.0f;
+#pragma unroll 4
+    for (int s = warp; s < splits; s += W) {
         const float* ps = p + (size_t)s * (HD + 2);
         const float m = ps[HD];
-        if (m == -INFINITY) continue;
-        const float f = expf(m - M);
-        Lsum = __fmaf_rn(ps[HD + 1], f, Lsum);
-        O = __fmaf_rn(ps[d], f, O);
+        const float f = (m == -INFINITY) ? 0.0f : expf(m - M);
+        L = __fmaf_rn(ps[HD + 1], f, L);
+#pragma unroll
+        for (int j = 0; j < DPL; j++) acc[j] = __fmaf_rn(ps[lane * DPL + j], f, acc[j]);
     }
-    out[((size_t)seq * H + h) * HD + d] = Lsum > 0.0f ? O / Lsum : 0.0f;
+#pragma unroll
+    for (int j = 0; j < DPL; j++) so[warp][lane * DPL + j] = acc[j];
+    if (lane == 0) sl[warp] = L;
+    __syncthreads();
+    for (int d = tid; d < HD; d += COMBINE_THREADS) {
+        float O = 0.0f, Ls = 0.0f;
+#pragma unroll
+        for (int w = 0; w < W; w++) {
+            O += so[w][d];
+            Ls += sl[w];
+        }
+        out[((size_t)seq * H + h) * HD + d] = Ls > 0.0f ? O / Ls : 0.0f;
+    }
 }
 
 int pick_splits(size_t ctx_len, int Hkv, int batch, int num_sms) {
@@ -348,6 +629,32 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
     using L = AttnLayout<HD>;
     const int chunk = (int)((ctx_len + splits - 1) / splits);
     const float sm_scale = 1.0f / sqrtf((float)HD);
+    if (slot_form_ok(ctx_len, capacity, Hkv, G, HD, batch, seq_stride, k, v, chunk)) {
+        using SL = SlotLayout<HD, G>;
+        const size_t bytes = SL::bytes(chunk, Hkv);
+        if (bytes != slot_bytes_generic(chunk, Hkv, G, HD))
+            return set_error(SULIMO_ELAUNCH, "slot layout size mismatch");
+        static uint64_t slot_attr_mask = 0;  // per device
+        const uint64_t sbit = 1ull << (ctx->device & 63);
+        if (!(slot_attr_mask & sbit)) {
+            int st = check_cuda(cudaFuncSetAttribute(attn_decode_slots_kernel<HD, G>,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int)SLOT_SMEM_MAX),
+                                "attn slot smem attribute");
+            if (st) return st;
+            slot_attr_mask |= sbit;
+        }
+        dim3 g1(splits, batch);
+        attn_decode_slots_kernel<HD, G><<<g1, SLOT_THREADS, bytes, ctx->stream>>>(
+            q, k, v, seq_stride, ctx_len, H, Hkv, chunk, sm_scale, softcap, part, ctx->d_error);
+        int st = check_cuda(cudaGetLastError(), "attn_decode_slots launch");
+        if (st) return st;
+        dim3 g2(H, batch);
+        attn_decode_combine_kernel<HD><<<g2, COMBINE_THREADS, 0, ctx->stream>>>(part, H, splits,
+                                                                                out);
+        ctx->launches += 2;
+        return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
+    }
     static uint64_t attr_set_mask = 0;  // one bit per device: the attribute is per device
     const uint64_t bit = 1ull << (ctx->device & 63);
     if (!(attr_set_mask & bit)) {
@@ -400,7 +707,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
     int st = check_cuda(cudaGetLastError(), "attn_decode_partial launch");
     if (st) return st;
     dim3 g2(H, batch);
-    attn_decode_combine_kernel<HD><<<g2, HD, 0, ctx->stream>>>(part, H, splits, out);
+    attn_decode_combine_kernel<HD><<<g2, COMBINE_THREADS, 0, ctx->stream>>>(part, H, splits, out);
     ctx->launches += 2;
     return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
 }
@@ -448,10 +755,20 @@ int launch_attn_decode_with_splits(sulimo_ctx* ctx, const float* q, const void* 
     }
 }
 
-size_t attn_decode_partial_bytes(size_t context_len, int head_count, int head_dim, int batch,
-                                 int num_sms, int* splits_out) {
-    // head_count_kv only steers the split count; the byte bound uses the worst case (Hkv = 1)
-    int splits = pick_splits(context_len, 1, batch, num_sms);
+int attn_decode_splits(size_t context_len, size_t capacity, int head_count, int head_count_kv,
+                       int head_dim, int batch, int num_sms, size_t seq_stride, const void* k,
+                       const void* v) {
+    const int s = slot_splits(context_len, capacity, head_count, head_count_kv, head_dim, batch,
+                              num_sms, seq_stride, k, v);
+    return s > 0 ? s : pick_splits(context_len, head_count_kv, batch, num_sms);
+}
+
+size_t attn_decode_partial_bytes(size_t context_len, size_t capacity, int head_count,
+                                 int head_count_kv, int head_dim, int batch, int num_sms,
+                                 size_t seq_stride, const void* k, const void* v,
+                                 int* splits_out) {
+    const int splits = attn_decode_splits(context_len, capacity, head_count, head_count_kv,
+                                          head_dim, batch, num_sms, seq_stride, k, v);
     if (splits_out) *splits_out = splits;
     return (size_t)batch * head_count * splits * (head_dim + 2) * sizeof(float);
 }
@@ -460,7 +777,9 @@ int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, cons
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
                        float* partials, size_t partial_bytes) {
-    const int splits = pick_splits(context_len, head_count_kv, batch, ctx->num_sms);
+    const int splits = attn_decode_splits(context_len, capacity, head_count, head_count_kv,
+                                          head_dim, batch, ctx->num_sms, seq_stride, k_ring,
+                                          v_ring);
     const size_t need = (size_t)batch * head_count * splits * (head_dim + 2) * sizeof(float);
     if (need > partial_bytes) return set_error(SULIMO_EINVAL, "attention workspace too small");
     const uint8_t* k = reinterpret_cast<const uint8_t*>(k_ring);

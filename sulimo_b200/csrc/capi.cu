@@ -477,8 +477,10 @@ int sulimo_cuda_attn_decode_q8_0(sulimo_ctx* ctx, const float* q, const void* k_
         return set_error(SULIMO_EALIGN, "q/out 16-byte aligned, rings 2-byte aligned");
     if ((st = bind_device(ctx))) return st;
     int splits = 0;
-    size_t pbytes = sulimo::attn_decode_partial_bytes(context_len, head_count, head_dim, batch,
-                                                      ctx->num_sms, &splits);
+    size_t pbytes = sulimo::attn_decode_partial_bytes(context_len, capacity, head_count,
+                                                      head_count_kv, head_dim, batch,
+                                                      ctx->num_sms, seq_stride_bytes, k_ring,
+                                                      v_ring, &splits);
     if ((st = sulimo::ensure_workspace(ctx, pbytes))) return st;
     return sulimo::launch_attn_decode(ctx, q, k_ring, v_ring, seq_stride_bytes, capacity,
                                       context_len, head_count, head_count_kv, head_dim, batch,

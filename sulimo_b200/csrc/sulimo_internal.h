@@ -59,10 +59,13 @@ int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, cons
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
                        float* partials, size_t partial_bytes);
-size_t attn_decode_partial_bytes(size_t context_len, int head_count, int head_dim, int batch,
-                                 int num_sms, int* splits_out);
-// Smallest split count the partial kernel accepts (<= 256 positions per split) and the count
-// the workspace path would pick.
+// Workspace bytes (and split count) the attention entry point will use for this geometry.
+size_t attn_decode_partial_bytes(size_t context_len, size_t capacity, int head_count,
+                                 int head_count_kv, int head_dim, int batch, int num_sms,
+                                 size_t seq_stride, const void* k, const void* v,
+                                 int* splits_out);
+// Smallest split count the per-head partial kernel accepts (<= 256 positions per split) and
+// that kernel's own preferred count.
 void attn_decode_split_range(size_t context_len, int head_count_kv, int batch, int num_sms,
                              int* min_splits, int* default_splits);
 // Decode attention with a caller-chosen split count and partials buffer (which must hold
