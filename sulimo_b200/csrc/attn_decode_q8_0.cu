@@ -6,12 +6,16 @@
 //     score[p] = (q_h . dequant(K[p % cap])) * 1/sqrt(hd)   [optionally tanh soft-capped]
 //     w = softmax(score[0..ctx]);  out_h = sum_p w[p] * dequant(V[p % cap])
 //
-// B200 form (split-K over the context, "flash-decoding"):
-//   kernel 1, one CTA per (context split, kv head, sequence): stages the split's K head-rows
-//   into shared memory once for all H/Hkv query heads of the group (the scalar reference
-//   re-reads them per query head), computes the scores, the split's max m and sum l of
-//   exp(score - m), stages V the same way and accumulates sum exp(score-m) * v.  It writes
-//   (o[hd], m, l) per (sequence, query head, split) to a workspace.
+// B200 form (split-K over the context, "flash-decoding"), two kernels:
+//   kernel 1 computes, per (sequence, query head, context split), the split's max score m, the
+//   sum l of exp(score - m) and o = sum exp(score - m) * v, into a workspace.  K/V are read once
+//   for all H/Hkv query heads of a kv head (the scalar reference re-reads them per query head).
+//   Two forms:
+//     slot form (default): one CTA per (split, sequence) covering all kv heads; its positions
+//       are contiguous ring slots fetched with two bulk copies (exact bytes);
+//     per-head form (ring wrap, unaligned rings, too few splits for the slot form's shared
+//       memory): one CTA per (split, kv head, sequence), K/V rows staged by TMA tensor copies
+//       or, when the rows are not 16-byte aligned, by 2-byte loads.
 //   kernel 2 merges the splits: out = sum_s o_s e^{m_s-M} / sum_s l_s e^{m_s-M}.
 // Reordered fp32 sums: the result matches the reference within fp32 rounding (the parity
 // tests bound the relative L2 error at 2e-3).
@@ -551,63 +555,69 @@ int slot_splits(size_t ctx_len, size_t capacity, int H, int Hkv, int HD, int bat
     return s > 0x7fffffffu ? 0 : (int)(s < 1 ? 1 : s);
 }
 
-// One CTA per (query head, sequence) merges that head's splits:
-//   M = max_s m_s,  out = sum_s o_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
-// The splits are shared out over 8 warps (lane owns HD/32 consecutive dimensions of each o_s
-// row, so a warp reads a row coalesced); the warps' sums are added in a fixed order through
-// shared memory.  A per-thread serial walk over the splits would be a chain of dependent
-// global loads.
+// Merge of the splits: out = sum_s o_s e^{m_s - M} / sum_s l_s e^{m_s - M}, M = max_s m_s.
+// One CTA per (query head, sequence, 32-dimension slice); lane = dimension.  The 8 warps share
+// the splits; each warp keeps a running (max, sum, output) and folds in COMBINE_BATCH splits per
+// step whose loads are all issued before any is used (the partials are a few MB read once, so
+// the merge is bound by load latency, not bandwidth).  The warps' results are merged in a fixed
+// order through shared memory.
 constexpr int COMBINE_THREADS = 256;
+constexpr int COMBINE_BATCH = 8;
 
 template <int HD>
 __global__ void __launch_bounds__(COMBINE_THREADS)
     attn_decode_combine_kernel(const float* __restrict__ part, int H, int splits,
                                float* __restrict__ out) {
     constexpr int W = COMBINE_THREADS / 32;
-    constexpr int DPL = HD / 32;  // dimensions per lane
-    __shared__ float red[W];
-    __shared__ float so[W][HD];
-    __shared__ float sl[W];
-    const int h = blockIdx.x, seq = blockIdx.y;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float sm_m[W], sm_l[W], sm_o[W][32];
+    const int h = blockIdx.x, seq = blockIdx.y, d = blockIdx.z * 32 + (threadIdx.x & 31);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* p = part + ((size_t)seq * H + h) * splits * (HD + 2);
 
-    float M = -INFINITY;
-    for (int s = tid; s < splits; s += COMBINE_THREADS)
-        M = fmaxf(M, p[(size_t)s * (HD + 2) + HD]);
+    float mw = -INFINITY, lw = 0.0f, ow = 0.0f;
+    for (int s0 = warp; s0 < splits; s0 += W * COMBINE_BATCH) {
+        float m[COMBINE_BATCH], l[COMBINE_BATCH], o[COMBINE_BATCH];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if (lane == 0) red[warp] = M;
-    __syncthreads();
-    M = red[0];
+        for (int j = 0; j < COMBINE_BATCH; j++) {
+            const int s = s0 + j * W;
+            const float* ps = p + (size_t)(s < splits ? s : 0) * (HD + 2);
+            m[j] = s < splits ? ps[HD] : -INFINITY;
+            l[j] = ps[HD + 1];
+            o[j] = ps[d];
+        }
+        float mb = mw;
 #pragma unroll
-    for (int w = 1; w < W; w++) M = fmaxf(M, red[w]);
-
-    float acc[DPL];
+        for (int j = 0; j < COMBINE_BATCH; j++) mb = fmaxf(mb, m[j]);
+        if (mb == -INFINITY) continue;                  // nothing seen yet
+        const float r = (mw == -INFINITY) ? 0.0f : expf(mw - mb);
+        lw *= r;
+        ow *= r;
 #pragma unroll
-    for (int j = 0; j < DPL; j++) acc[j] = 0.0f;
-    float L = 0.0f;
-#pragma unroll 4
-    for (int s = warp; s < splits; s += W) {
-        const float* ps = p + (size_t)s * (HD + 2);
-        const float m = ps[HD];
-        const float f = (m == -INFINITY) ? 0.0f : expf(m - M);
-        L = __fmaf_rn(ps[HD + 1], f, L);
-#pragma unroll
-        for (int j = 0; j < DPL; j++) acc[j] = __fmaf_rn(ps[lane * DPL + j], f, acc[j]);
+        for (int j = 0; j < COMBINE_BATCH; j++) {
+            const float f = (m[j] == -INFINITY) ? 0.0f : expf(m[j] - mb);
+            lw = __fmaf_rn(l[j], f, lw);
+            ow = __fmaf_rn(o[j], f, ow);
+        }
+        mw = mb;
     }
-#pragma unroll
-    for (int j = 0; j < DPL; j++) so[warp][lane * DPL + j] = acc[j];
-    if (lane == 0) sl[warp] = L;
+    if (lane == 0) {
+        sm_m[warp] = mw;
+        sm_l[warp] = lw;
+    }
+    sm_o[warp][lane] = ow;
     __syncthreads();
-    for (int d = tid; d < HD; d += COMBINE_THREADS) {
-        float O = 0.0f, Ls = 0.0f;
+    if (warp == 0 && d < HD) {
+        float M = sm_m[0];
+#pragma unroll
+        for (int w = 1; w < W; w++) M = fmaxf(M, sm_m[w]);
+        float L = 0.0f, O = 0.0f;
 #pragma unroll
         for (int w = 0; w < W; w++) {
-            O += so[w][d];
-            Ls += sl[w];
+            const float f = (sm_m[w] == -INFINITY) ? 0.0f : expf(sm_m[w] - M);
+            L = __fmaf_rn(sm_l[w], f, L);
+            O = __fmaf_rn(sm_o[w][lane], f, O);
         }
-        out[((size_t)seq * H + h) * HD + d] = Ls > 0.0f ? O / Ls : 0.0f;
+        out[((size_t)seq * H + h) * HD + d] = L > 0.0f ? O / L : 0.0f;
     }
 }
 
@@ -649,7 +659,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
             q, k, v, seq_stride, ctx_len, H, Hkv, chunk, sm_scale, softcap, part, ctx->d_error);
         int st = check_cuda(cudaGetLastError(), "attn_decode_slots launch");
         if (st) return st;
-        dim3 g2(H, batch);
+        dim3 g2(H, batch, (HD + 31) / 32);
         attn_decode_combine_kernel<HD><<<g2, COMBINE_THREADS, 0, ctx->stream>>>(part, H, splits,
                                                                                 out);
         ctx->launches += 2;
@@ -706,7 +716,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
             ctx->d_error);
     int st = check_cuda(cudaGetLastError(), "attn_decode_partial launch");
     if (st) return st;
-    dim3 g2(H, batch);
+    dim3 g2(H, batch, (HD + 31) / 32);
     attn_decode_combine_kernel<HD><<<g2, COMBINE_THREADS, 0, ctx->stream>>>(part, H, splits, out);
     ctx->launches += 2;
     return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
