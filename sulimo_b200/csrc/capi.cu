@@ -97,6 +97,10 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base
 
 using sulimo::set_error;
 
+// After a kernel recorded a device error (a bounded wait ran out) clear the error word so the
+// context stays usable.
+static void clear_device_state(sulimo_ctx* ctx) { cudaMemset(ctx->d_error, 0, sizeof(int)); }
+
 static int check_ctx(sulimo_ctx* ctx) {
     if (!ctx) return set_error(SULIMO_EINVAL, "null context");
     return SULIMO_OK;
@@ -177,7 +181,7 @@ int sulimo_cuda_ctx_synchronize(sulimo_ctx* ctx) {
     e = cudaMemcpy(&flag, ctx->d_error, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return sulimo::check_cuda(e, "read error word");
     if (flag != 0) {
-        cudaMemset(ctx->d_error, 0, sizeof(int));
+        clear_device_state(ctx);
         return set_error(SULIMO_EDEVICE, std::string("device-side error code ") +
                                              std::to_string(flag) +
                                              (flag == 1 ? " (bounded wait ran out)" : ""));
@@ -336,7 +340,7 @@ int sulimo_cuda_event_wait(sulimo_event* ev, uint64_t timeout_ns) {
     cudaError_t e = cudaMemcpy(&flag, ev->ctx->d_error, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return sulimo::check_cuda(e, "read error word");
     if (flag) {
-        cudaMemset(ev->ctx->d_error, 0, sizeof(int));
+        clear_device_state(ev->ctx);
         return set_error(SULIMO_EDEVICE, "device-side error code " + std::to_string(flag));
     }
     return SULIMO_OK;

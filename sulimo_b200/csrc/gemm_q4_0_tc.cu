@@ -9,18 +9,22 @@
 // Data flow per CTA (128 features x up to 256 tokens, K streamed in 64-wide stages):
 //   warp 0   TMA: activations x[n0.., k0..k0+63] -> smem (128B-swizzled, K-major) and the raw
 //            Q4_0 nibbles of the 128 feature rows (32 bytes per row) -> smem.
-//   warps 2-9 dequant: each thread owns one feature row (= one TMEM lane) and one of the
-//            stage's 2 Q4_0 blocks, turns it into 32 f16 weights f16(d*(q-8)) (exact (q-8) via
-//            the 0x6400 magic, one RNE multiply by d; the rounding of the reference's f16
-//            embedding path, crates/sulimo-engine/src/scheduler.rs:345-357) and writes them to
-//            the stage's TMEM columns with tcgen05.st.  The weights never touch shared memory.
+//   warps 2-17 dequant, in four groups of four warps (one warp per TMEM lane quarter); group g
+//            takes the stages j = g (mod 4).  Each thread owns one feature row (= one TMEM
+//            lane), turns the stage's two Q4_0 blocks of its row into 64 f16 weights
+//            f16(d*(q-8)) (exact (q-8) via the 0x6400 magic, one RNE multiply by d; the rounding
+//            of the reference's f16 embedding path, crates/sulimo-engine/src/scheduler.rs:
+//            345-357) and writes them to the stage's TMEM columns with tcgen05.st.  The weights
+//            never touch shared memory.
 //   warp 1   one thread issues tcgen05.mma kind::f16, A = weights from TMEM (M = 128 features),
 //            B = activations from smem (N = tokens), D = fp32 accumulators in TMEM; each stage
 //            is released with tcgen05.commit.
-//   warps 2-9 epilogue: tcgen05.ld of the accumulators (lane = feature), convert, store
-//            out[t][r] (32 consecutive features per warp store: 64-byte coalesced rows).
+//   warps 2-17 epilogue: per group, 32-token chunks: tcgen05.ld of the accumulators (lane =
+//            feature), convert, stage [32 tokens][128 features] in shared memory, one TMA
+//            tensor store per chunk.
 // Outputs with few tiles (the down projection: 1536 features) split K across CTAs; the fp32
-// partials are added in split order by splitk_reduce_kernel (deterministic).
+// partials are added in split order by splitk_reduce_kernel (deterministic).  Launches use
+// programmatic dependent launch (a kernel's prologue overlaps the previous kernel's tail).
 // Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records a device error,
 // drains its in-flight copies / MMAs (again bounded), frees TMEM and returns.
 // No TMA multicast: each CTA loads its own tiles.
@@ -33,20 +37,43 @@ namespace {
 constexpr int BM = 128;           // features per CTA = MMA M = TMEM lanes
 constexpr int BK = 64;            // k per stage: 2 Q4_0 blocks, one 128-byte swizzle row of f16
 constexpr int BN_MAX = 256;       // tokens per CTA = MMA N (max)
-// 6 stages: one ring slot turns over in ~1.5 us (MMA, commit, TMA issue, L2 latency, dequant),
-// so 6 slots keep ~4 MMA stages of work queued at the tensor-core rate.
-constexpr int STAGES = 6;
-constexpr int DEQ_WARPS = 8;      // two per TMEM lane quarter, one Q4_0 block of the stage each
+// The ring depth is chosen per launch: as many stages as shared memory (bn*128 + 4096 bytes
+// each) and TMEM (32 weight columns each, next to bn accumulator columns) allow, at most
+// MAX_STAGES.  A slot turns over in ~1.5 us (MMA, commit, TMA issue, L2/DRAM latency,
+// dequant), so 256-token tiles (6 stages) keep ~4 stages of MMA work queued and narrow tiles get
+// deeper rings.
+constexpr int MAX_STAGES = 16;
+constexpr uint32_t SMEM_LIMIT = 232448;  // dynamic shared memory per CTA on sm_100
+// Dequant warps form DEQ_GROUPS groups of four (one warp per TMEM lane quarter); group g turns
+// the stages j = g (mod DEQ_GROUPS) into TMEM weights, so four stages' tcgen05.st round trips
+// are in flight at once (one group alone needs ~0.25 us per stage, the MMA ~0.27 us).
+constexpr int DEQ_GROUPS = 4;
+constexpr int DEQ_WARPS = 4 * DEQ_GROUPS;
 constexpr int THREADS = 64 + 32 * DEQ_WARPS;
+constexpr int EPI_TOKENS = 32;    // tokens per epilogue chunk (one TMA store each)
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t A_COL = 0;                 // A stages: columns [32*s, 32*s+32)
-constexpr uint32_t ACC_COL = STAGES * 32;     // accumulators: columns [ACC_COL, ACC_COL+bn)
-constexpr uint32_t X_STAGE = BN_MAX * 128;  // bytes
-constexpr uint32_t Q_STAGE = BM * 32;       // bytes
-constexpr uint32_t SMEM_BYTES = STAGES * (X_STAGE + Q_STAGE) + 256 + 1024;
-static_assert(ACC_COL + BN_MAX <= TMEM_COLS, "TMEM budget");
-static_assert(STAGES * X_STAGE >= BN_MAX * BM * 4, "epilogue staging tile must fit the X ring");
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+constexpr uint32_t A_COL = 0;               // A stages: columns [32*s, 32*s+32)
+constexpr uint32_t Q_STAGE = BM * 32;       // bytes of raw Q4_0 nibbles per stage
+constexpr uint32_t BAR_BYTES = 512;         // mbarriers + TMEM slot + flags
+static_assert((3 * MAX_STAGES + 1) * 8 + 8 <= BAR_BYTES, "barrier block");
+static_assert(THREADS * 112 <= 65536, "register budget of one CTA per SM");
+
+// Shared memory of a launch: the X and Q rings, the barrier block, 1024 bytes of alignment.
+__host__ __device__ constexpr uint32_t ring_bytes(int bn, int stages) {
+    return (uint32_t)stages * ((uint32_t)bn * 128u + Q_STAGE);
+}
+__host__ __device__ constexpr uint32_t smem_bytes(int bn, int stages) {
+    return ring_bytes(bn, stages) + BAR_BYTES + 1024;
+}
+// Deepest ring for a token-tile width (>= 2 stages for every bn <= 256).
+__host__ __device__ constexpr int ring_stages(int bn) {
+    int s = MAX_STAGES;
+    if ((int)((TMEM_COLS - (uint32_t)bn) / 32) < s) s = (int)((TMEM_COLS - (uint32_t)bn) / 32);
+    while (s > 2 && smem_bytes(bn, s) > SMEM_LIMIT) s--;
+    return s;
+}
+static_assert(ring_stages(BN_MAX) == 6 && smem_bytes(BN_MAX, 6) <= SMEM_LIMIT, "256-token ring");
+static_assert(ring_bytes(BN_MAX, 6) >= BN_MAX * BM * 4, "epilogue staging tile fits the ring");
 
 // ---- tcgen05 / TMA wrappers ----------------------------------------------------------------
 __device__ __forceinline__ void tc_fence_before() {
@@ -74,11 +101,14 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int c0, int
         : "memory");
 }
 
-// Commits the issued bulk stores and waits until their global writes are complete (the
-// shared-memory source must stay valid until then; the CTA exits right after).
-__device__ __forceinline__ void bulk_commit_and_wait_all() {
+__device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Waits until the committed bulk stores have read their shared-memory sources (the global
+// writes complete on their own before the grid is complete).
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
@@ -96,14 +126,31 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return d;
 }
 
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
+// One stage = four K=16 MMAs into the accumulators (the first one overwrites them when
+// `accumulate` is 0), issued in one instruction stream together with a non-blocking test of the
+// next stage's barrier.  An mbarrier test costs ~250 cycles even on a completed phase; reading
+// its result only after the MMAs are queued hides that latency behind the MMA issue.
+__device__ __forceinline__ uint32_t mma_stage_and_peek(uint32_t d_tmem, uint32_t a_tmem,
+                                                       uint64_t b_desc, uint32_t idesc,
+                                                       uint32_t accumulate, uint64_t* peek_bar,
+                                                       uint32_t peek_parity) {
+    uint32_t ready;
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        "{\n\t.reg .pred pa, pt, q;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%1], %2;\n\t"
+        "setp.ne.b32 pa, %7, 0;\n\t"
+        "setp.eq.u32 pt, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%4], %5, %6, pa;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%8], %9, %6, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%10], %11, %6, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%12], %13, %6, pt;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(ready)
+        : "r"(smem_u32(peek_bar)), "r"(peek_parity), "r"(d_tmem), "r"(a_tmem), "l"(b_desc),
+          "r"(idesc), "r"(accumulate), "r"(a_tmem + 8u), "l"(b_desc + 2), "r"(a_tmem + 16u),
+          "l"(b_desc + 4), "r"(a_tmem + 24u), "l"(b_desc + 6)
         : "memory");
+    return ready;
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -113,13 +160,16 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31, %32};" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
         "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-        "r"(v[15])
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 
@@ -181,16 +231,19 @@ __device__ __forceinline__ void dequant_block(const uint4 q, uint32_t dbits, uin
 }
 
 // Partial sums of split-K CTAs go to an fp32 workspace [split][n][m]; this kernel adds the
-// splits in index order (deterministic) and writes f16 or f32 results.
+// splits in index order (deterministic) and writes f16 or f32 results.  Launched as a
+// programmatic dependent of the GEMM: its CTAs wait for the partials in griddepcontrol.wait.
 template <bool OUT_F32>
 __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ out, size_t nm,
                          int splits) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     const size_t i4 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i4 >= nm) return;
-    float4 acc = *reinterpret_cast<const float4*>(ws + i4);
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(ws + i4));
     for (int z = 1; z < splits; z++) {
-        const float4 p = *reinterpret_cast<const float4*>(ws + (size_t)z * nm + i4);
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(ws + (size_t)z * nm + i4));
         acc.x += p.x;
         acc.y += p.y;
         acc.z += p.z;
@@ -205,23 +258,27 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to out + split*n*m
+// OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace
+// [split][n][m] (all by TMA tensor stores).
 template <int OUT_MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q4_0_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_q,
                         const __grid_constant__ CUtensorMap tmap_out,
+                        const __grid_constant__ CUtensorMap tmap_out16,
                         const uint16_t* __restrict__ scales, int m, int k, int n, int bn, int nb,
-                        int iters_per_split, int* __restrict__ err) {
+                        int iters_per_split, int stages, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+    const uint32_t x_stage = (uint32_t)bn * 128u;  // a multiple of 1024: SW128 atoms stay aligned
+    const uint32_t acc_col = (uint32_t)stages * 32u;  // accumulators: [acc_col, acc_col + bn)
     uint8_t* sx = smem;
-    uint8_t* sq = smem + STAGES * X_STAGE;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sq + STAGES * Q_STAGE);
-    uint64_t* empty = full + STAGES;
-    uint64_t* afull = empty + STAGES;
-    uint64_t* done = afull + STAGES;
+    uint8_t* sq = smem + stages * x_stage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sq + stages * Q_STAGE);
+    uint64_t* empty = full + MAX_STAGES;
+    uint64_t* afull = empty + MAX_STAGES;
+    uint64_t* done = afull + MAX_STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -233,10 +290,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int num_k = max(0, i_end - i_begin);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
+        for (int s = 0; s < stages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 32 * DEQ_WARPS);
+            mbar_init(&afull[s], 4 * 32);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -244,6 +301,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_q)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_out)) : "memory");
+        // Launched as a programmatic dependent: let the next kernel's CTAs start their own
+        // prologue as SMs free up, then wait until the previous kernel's writes are visible
+        // before the first global read (the __syncthreads below orders the other threads).
+        pdl_launch_dependents();
+        pdl_wait_prerequisites();
+        // The first ring pass needs no empty-slot waits: issue it before the TMEM allocation.
+        for (int j = 0; j < num_k && j < stages; j++) {
+            mbar_arrive_expect_tx(&full[j], x_stage + Q_STAGE);
+            tma_load_2d(sx + j * x_stage, &tmap_x, (i_begin + j) * BK, n0, &full[j]);
+            tma_load_2d(sq + j * Q_STAGE, &tmap_q, (i_begin + j) * 32, m0, &full[j]);
+        }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -260,20 +328,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
-            int issued = 0;
-            for (int j = 0; j < num_k; j++) {
-                const int s = j % STAGES;
-                const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+            int issued = num_k < stages ? num_k : stages;
+            for (int j = stages; j < num_k; j++) {
+                const int s = j % stages;
+                const uint32_t ph = (uint32_t)(j / stages) & 1u;
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)bn * 128u + Q_STAGE);
-                tma_load_2d(sx + s * X_STAGE, &tmap_x, (i_begin + j) * BK, n0, &full[s]);
+                mbar_arrive_expect_tx(&full[s], x_stage + Q_STAGE);
+                tma_load_2d(sx + s * x_stage, &tmap_x, (i_begin + j) * BK, n0, &full[s]);
                 tma_load_2d(sq + s * Q_STAGE, &tmap_q, (i_begin + j) * 32, m0, &full[s]);
                 issued = j + 1;
             }
             if (*abort_flag) {
                 // drain: the copies already issued must land before the CTA's smem is released
-                for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; j++)
-                    mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, err,
+                for (int j = (issued > stages ? issued - stages : 0); j < issued; j++)
+                    mbar_wait_bounded(&full[j % stages], (uint32_t)(j / stages) & 1u, err,
                                       nullptr);
             }
         }
@@ -283,93 +351,111 @@ __global__ void __launch_bounds__(THREADS, 1)
             // kind::f16: D f32 (bits 4-5 = 1), A = B = f16, both K-major, N>>3 at 17, M>>4 at 24
             const uint32_t idesc =
                 (1u << 4) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+            int s = 0;
+            uint32_t ph = 0;
+            bool ready = false;  // afull[s] already seen complete by the previous peek
             for (int j = 0; j < num_k; j++) {
-                const int s = j % STAGES;
-                const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-                if (!mbar_wait_bounded(&afull[s], ph, err, abort_flag)) break;
+                if (!ready && !mbar_wait_bounded(&afull[s], ph, err, abort_flag)) break;
                 tc_fence_after();
-                const uint64_t bdesc = sw128_desc(smem_u32(sx + s * X_STAGE));
-#pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++) {
-                    // +32 bytes per 16-element K step inside the swizzled 128-byte rows
-                    mma_ts(tmem + ACC_COL, tmem + A_COL + (uint32_t)s * 32u + (uint32_t)kk * 8u,
-                           bdesc + (uint64_t)(kk * 2), idesc, (j > 0 || kk > 0) ? 1u : 0u);
-                }
+                const int s1 = s + 1 == stages ? 0 : s + 1;
+                const uint32_t ph1 = s + 1 == stages ? ph ^ 1u : ph;
+                // K steps advance 32 bytes inside the swizzled 128-byte rows (descriptor +2) and
+                // 8 TMEM columns of the stage's weights
+                ready = mma_stage_and_peek(tmem + acc_col, tmem + A_COL + (uint32_t)s * 32u,
+                                           sw128_desc(smem_u32(sx + s * x_stage)), idesc,
+                                           j > 0 ? 1u : 0u, &afull[s1], ph1) != 0 &&
+                        j + 1 < num_k;
                 mma_commit(&empty[s]);
+                if (++s == stages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
             mma_commit(done);
             if (*abort_flag) mbar_wait_bounded(done, 0, err, nullptr);  // MMAs drained
         }
     } else {
         // --------------------------- dequant, then epilogue ---------------------------
-        // warp w in 2..9: TMEM lane quarter (w % 4), Q4_0 block `half` of each stage
+        // warp w in 2..17: TMEM lane quarter w % 4, group (w - 2) / 4
         const uint32_t quarter = (uint32_t)(warp & 3);
-        const int half = (warp - 2) >> 2;
+        const int group = (warp - 2) >> 2;
         const int r = (int)quarter * 32 + lane;  // feature row within the tile == TMEM lane
         const int grow = m0 + r;
         const bool row_ok = grow < m;
         const uint16_t* srow = scales + (size_t)(row_ok ? grow : 0) * nb;
         const uint32_t lane_base = (quarter * 32u) << 16;
-        uint32_t sc_next = 0;
-        {
-            const int kb = 2 * i_begin + half;
-            if (row_ok && num_k > 0 && kb < nb) sc_next = __ldg(srow + kb);
-        }
+        // block scales of the group's next stage (two Q4_0 blocks per stage)
+        auto load_scales = [&](int j, uint32_t& a, uint32_t& b) {
+            const int kb = 2 * (i_begin + j);
+            a = (row_ok && j < num_k && kb < nb) ? __ldg(srow + kb) : 0u;
+            b = (row_ok && j < num_k && kb + 1 < nb) ? __ldg(srow + kb + 1) : 0u;
+        };
+        uint32_t sa_next, sb_next;
+        load_scales(group, sa_next, sb_next);
         bool ok = true;
-        for (int j = 0; j < num_k; j++) {
-            const int s = j % STAGES;
-            const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-            const uint32_t sc = sc_next;
-            {  // prefetch the next stage's block scale
-                const int kb = 2 * (i_begin + j + 1) + half;
-                sc_next = (row_ok && j + 1 < num_k && kb < nb) ? __ldg(srow + kb) : 0u;
-            }
+        for (int j = group; j < num_k; j += DEQ_GROUPS) {
+            const int s = j % stages;
+            const uint32_t ph = (uint32_t)(j / stages) & 1u;
+            const uint32_t sa = sa_next, sb = sb_next;
+            load_scales(j + DEQ_GROUPS, sa_next, sb_next);
             if (!mbar_wait_bounded(&full[s], ph, err, abort_flag)) {
                 ok = false;
                 break;
             }
-            const uint4 qv = *reinterpret_cast<const uint4*>(sq + s * Q_STAGE + r * 32 + half * 16);
-            uint32_t cols[16];
-            dequant_block(qv, row_ok ? sc : 0u, cols);
-            tmem_st16(tmem + lane_base + A_COL + (uint32_t)s * 32u + (uint32_t)half * 16u, cols);
+            const uint4* qp = reinterpret_cast<const uint4*>(sq + s * Q_STAGE + r * 32);
+            const uint4 q0 = qp[0], q1 = qp[1];
+            uint32_t cols[32];
+            dequant_block(q0, sa, cols);
+            dequant_block(q1, sb, cols + 16);
+            tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * 32u, cols);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&afull[s]);
         }
-        // Epilogue: accumulators -> [token][feature] tile in shared memory (the X stages are
-        // free once `done` fired) -> one TMA tensor store; the tensor map clips ragged edges.
+        // Epilogue: each group takes 32-token chunks of the accumulators (chunk c = group,
+        // group + DEQ_GROUPS, ...), stages chunk c as a [32 tokens][128 features] tile in the
+        // X ring (free once `done` fired) and stores it with one TMA tensor store; the tensor
+        // map clips ragged edges.  The group barriers run whether or not the accumulators are
+        // valid, so a warp that gave up on a wait cannot strand the others.
         const bool have = ok && (num_k == 0 || mbar_wait_bounded(done, 0, err, abort_flag));
-        if (have) {
-            tc_fence_after();
-            constexpr int ES = (OUT_MODE == 0) ? 2 : 4;
-            // the two warps of a lane quarter take alternate 32-token column chunks
-            for (int c0 = half * 32; c0 < bn; c0 += 64) {
-                uint32_t v[32];
-                if (num_k > 0) {
-                    tmem_ld32(tmem + lane_base + ACC_COL + (uint32_t)c0, v);
-                } else {
+        if (have) tc_fence_after();
+        constexpr int ES = (OUT_MODE == 0) ? 2 : 4;
+        {
+            const bool issuer = (warp - 2) % 4 == 0 && lane == 0;
+            for (int c0 = group * EPI_TOKENS; c0 < bn; c0 += DEQ_GROUPS * EPI_TOKENS) {
+                uint8_t* tile = sx + (size_t)c0 * BM * ES;
+                if (have) {
+                    uint32_t v[32];
+                    if (num_k > 0) {
+                        tmem_ld32(tmem + lane_base + acc_col + (uint32_t)c0, v);
+                    } else {
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj++) v[jj] = 0u;  // an empty split adds zeros
+                        for (int jj = 0; jj < 32; jj++) v[jj] = 0u;
+                    }
+                    uint8_t* col = tile + (size_t)r * ES;
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) {
+                        const float f = __uint_as_float(v[jj]);
+                        if (ES == 2)
+                            *reinterpret_cast<__half*>(col + (size_t)jj * BM * ES) =
+                                __float2half_rn(f);
+                        else
+                            *reinterpret_cast<float*>(col + (size_t)jj * BM * ES) = f;
+                    }
+                    fence_proxy_async_smem();
                 }
-                uint8_t* col = sx + ((size_t)c0 * BM + r) * ES;
-#pragma unroll
-                for (int jj = 0; jj < 32; jj++) {
-                    const float f = __uint_as_float(v[jj]);
-                    if (ES == 2)
-                        *reinterpret_cast<__half*>(col + (size_t)jj * BM * ES) = __float2half_rn(f);
+                named_barrier_sync(1 + group, 128);
+                if (issuer && have && !*abort_flag && n0 + c0 < n) {
+                    // a 16-token remainder (bn % 32 == 16) must not spill into the next tile
+                    const CUtensorMap* map = c0 + EPI_TOKENS <= bn ? &tmap_out : &tmap_out16;
+                    if (OUT_MODE == 2)
+                        tma_store_3d(map, m0, n0 + c0, (int)blockIdx.z, tile);
                     else
-                        *reinterpret_cast<float*>(col + (size_t)jj * BM * ES) = f;
+                        tma_store_2d(map, m0, n0 + c0, tile);
+                    bulk_commit();
                 }
             }
-            fence_proxy_async_smem();
-        }
-        named_barrier_sync(1, 32 * DEQ_WARPS);
-        if (warp == 2 && lane == 0 && have && !*abort_flag) {
-            if (OUT_MODE == 2)
-                tma_store_3d(&tmap_out, m0, n0, (int)blockIdx.z, sx);
-            else
-                tma_store_2d(&tmap_out, m0, n0, sx);
-            bulk_commit_and_wait_all();
+            if (issuer) bulk_wait_read_all();
         }
     }
 
@@ -406,7 +492,7 @@ int set_smem_attr(int device) {
     if (mask & bit) return SULIMO_OK;
     int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<MODE>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)SMEM_BYTES),
+                                             (int)SMEM_LIMIT),
                         "gemm smem attribute");
     if (!st) mask |= bit;
     return st;
@@ -414,12 +500,17 @@ int set_smem_attr(int device) {
 
 }  // namespace
 
+// Token-tile width: all tokens up to 256 (rounded up to 16), else 256.  Narrower tiles do not
+// pay: every stage costs the MMA issuer a fixed ~0.15 us (barrier test, fence, commit, issue)
+// whatever N is, and each weight is dequantized once per token tile.
+int gemm_token_tile(int n) { return n <= BN_MAX ? ((n + 15) / 16) * 16 : BN_MAX; }
+
 // Split count: enough CTAs to fill the SMs when the output has few tiles (the down projection
 // 512 x 8960 -> 1536 has 24 tiles of 128 x 256), each split keeping >= 8 k-stages.
 int gemm_splits(int tiles, int num_k, int num_sms) {
     if (tiles * 2 > num_sms) return 1;
     int s = num_sms / tiles;
-    int by_k = num_k / 8;
+    const int by_k = num_k / 8;
     if (s > by_k) s = by_k;
     return s < 1 ? 1 : s;
 }
@@ -428,8 +519,9 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
                          void* out, int m, int k, int n, int out_dtype, int x_row_stride,
                          int x_row_offset) {
     const int nb = k / 32;
-    int bn = ((n + 15) / 16) * 16;
-    if (bn > BN_MAX) bn = BN_MAX;
+    const int bn = gemm_token_tile(n);
+    const int stages = ring_stages(bn);
+    const uint32_t smem = smem_bytes(bn, stages);
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(x) + (size_t)x_row_offset * x_row_stride * 2;
     CUtensorMap tx, tq;
     int st = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, (uint64_t)k, (uint64_t)n,
@@ -448,46 +540,59 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
     const int ips = (num_k + splits - 1) / splits;
     if (nt > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
     const uint16_t* sc = reinterpret_cast<const uint16_t*>(scales);
-    CUtensorMap to;
+    CUtensorMap to, to16;
     if (splits == 1) {
         const bool f32 = out_dtype == SULIMO_OUT_F32;
-        st = encode_2d(&to, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                       out, (uint64_t)m, (uint64_t)n, (uint64_t)m * (f32 ? 4 : 2), BM,
-                       (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+        const CUtensorMapDataType dt =
+            f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        const uint64_t rowb = (uint64_t)m * (f32 ? 4 : 2);
+        st = encode_2d(&to, dt, out, (uint64_t)m, (uint64_t)n, rowb, BM, (uint32_t)EPI_TOKENS,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+        st = encode_2d(&to16, dt, out, (uint64_t)m, (uint64_t)n, rowb, BM, 16u,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
         dim3 grid(mt, nt, 1);
-        if (f32)
-            gemm_q4_0_tc_kernel<1><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-                tx, tq, to, sc, m, k, n, bn, nb, ips, ctx->d_error);
-        else
-            gemm_q4_0_tc_kernel<0><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-                tx, tq, to, sc, m, k, n, bn, nb, ips, ctx->d_error);
+        const cudaError_t e =
+            f32 ? launch_pdl(gemm_q4_0_tc_kernel<1>, grid, dim3(THREADS), smem, ctx->stream, tx,
+                             tq, to, to16, sc, m, k, n, bn, nb, ips, stages, ctx->d_error)
+                : launch_pdl(gemm_q4_0_tc_kernel<0>, grid, dim3(THREADS), smem, ctx->stream, tx,
+                             tq, to, to16, sc, m, k, n, bn, nb, ips, stages, ctx->d_error);
         ctx->launches++;
-        return check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
+        return check_cuda(e, "gemm_q4_0_tc launch");
     }
+    // split-K: fp32 partials [split][n][m] (rank 3, so a ragged token tile cannot spill into the
+    // next split), then the ordered reduction
     const size_t nm = (size_t)n * m;
     if ((st = ensure_workspace(ctx, nm * splits * sizeof(float)))) return st;
     float* ws = reinterpret_cast<float*>(ctx->workspace);
-    {  // partials [split][n][m]: rank 3 so a ragged token tile cannot spill into the next split
+    {
         const uint64_t dims[3] = {(uint64_t)m, (uint64_t)n, (uint64_t)splits};
         const uint64_t strides[2] = {(uint64_t)m * 4, (uint64_t)nm * 4};
-        const uint32_t box[3] = {BM, (uint32_t)bn, 1};
+        const uint32_t box[3] = {BM, (uint32_t)EPI_TOKENS, 1};
+        const uint32_t box16[3] = {BM, 16u, 1};
         st = encode_map(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, 3, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+        st = encode_map(&to16, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, 3, dims, strides, box16,
                         CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
     }
     dim3 grid(mt, nt, splits);
-    gemm_q4_0_tc_kernel<2><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(
-        tx, tq, to, sc, m, k, n, bn, nb, ips, ctx->d_error);
-    st = check_cuda(cudaGetLastError(), "gemm_q4_0_tc launch");
+    st = check_cuda(launch_pdl(gemm_q4_0_tc_kernel<2>, grid, dim3(THREADS), smem, ctx->stream,
+                               tx, tq, to, to16, sc, m, k, n, bn, nb, ips, stages, ctx->d_error),
+                    "gemm_q4_0_tc split-K launch");
     if (st) return st;
     const unsigned rb = (unsigned)((nm / 4 + 255) / 256);  // m % 8 == 0, so nm % 4 == 0
-    if (out_dtype == SULIMO_OUT_F32)
-        splitk_reduce_kernel<true><<<rb, 256, 0, ctx->stream>>>(ws, out, nm, splits);
-    else
-        splitk_reduce_kernel<false><<<rb, 256, 0, ctx->stream>>>(ws, out, nm, splits);
+    const float* wsc = ws;
+    const cudaError_t e =
+        out_dtype == SULIMO_OUT_F32
+            ? launch_pdl(splitk_reduce_kernel<true>, dim3(rb), dim3(256), 0, ctx->stream, wsc, out,
+                         nm, splits)
+            : launch_pdl(splitk_reduce_kernel<false>, dim3(rb), dim3(256), 0, ctx->stream, wsc,
+                         out, nm, splits);
     ctx->launches += 2;
-    return check_cuda(cudaGetLastError(), "splitk_reduce launch");
+    return check_cuda(e, "splitk_reduce launch");
 }
 
 }  // namespace sulimo

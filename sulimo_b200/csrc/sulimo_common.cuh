@@ -118,6 +118,20 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- programmatic dependent launch ------------------------------------------------------
+// A kernel launched with the programmatic-stream-serialization attribute may start while the
+// previous kernel of the stream still runs; it must wait here before its first global read or
+// write of data that kernel touches.  Without the attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait_prerequisites() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next programmatically dependent kernel of the stream begin launching (it still
+// waits for this grid's completion in pdl_wait_prerequisites).
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- misc ------------------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <string>
+#include <utility>
 
 #include "../../include/sulimo_cuda.h"
 
@@ -17,12 +18,31 @@ struct sulimo_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;  // the stream launches go to (own or caller's)
     int* d_error = nullptr;         // device error word (0 = none)
-    void* workspace = nullptr;      // split-K / attention partials
+    void* workspace = nullptr;      // attention partials
     size_t workspace_bytes = 0;
     std::atomic<uint64_t> launches{0};
 };
 
 namespace sulimo {
+
+// Launches a kernel with programmatic stream serialization: it may begin (prologue, TMEM
+// allocation, barrier setup) while the previous kernel of the stream drains, and orders its
+// global accesses after that kernel with griddepcontrol.wait.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Thread-local error message + status helper.
 int set_error(int status, const std::string& msg);

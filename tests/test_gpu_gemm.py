@@ -105,6 +105,40 @@ def test_gemm_ragged_shapes(ctx, n, k, m):
     assert rel_l2(got, ref) <= TOL
 
 
+def test_gemm_split_k_repeatable_and_graph_safe(ctx):
+    """The down shape (512 x 8960 -> 1536) splits K over 6 CTAs per tile that meet on
+    self-resetting tile counters: back-to-back calls and CUDA-graph replays must give
+    bit-identical f16 results (partials are added in fixed split order)."""
+    import torch
+    n, k, m = 512, 8960, 1536
+    ws, wq = make_q4_0(m, k, seed=3)
+    x = np.random.default_rng(4).standard_normal(n * k).astype(np.float16)
+    dws, dwq, dx = dev(ws), dev(wq), dev(x)
+    outs = []
+    for _ in range(3):
+        out = empty(n * m, torch.float16)
+        sb.gemm_q4_0_f16(ctx, dws, dwq, dx, out, m, k, n, sb.OUT_F16)
+        ctx.finish()
+        outs.append(host(out))
+    out = empty(n * m, torch.float16)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.set_stream(torch.cuda.current_stream())
+        sb.gemm_q4_0_f16(ctx, dws, dwq, dx, out, m, k, n, sb.OUT_F16)
+    ctx.set_stream(torch.cuda.current_stream())
+    for _ in range(4):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        outs.append(host(out))
+    del graph
+    ctx.finish()
+    for o in outs[1:]:
+        assert np.array_equal(o.view(np.uint16), outs[0].view(np.uint16))
+    ref = torch_reference(ws, wq, x, m, k, n).ravel()
+    assert rel_l2(outs[0].astype(np.float32), ref) <= TOL
+
+
 def test_logits_final_last_token(ctx):
     """enqueue_logits_final (prefill.rs:300-330): fp32 logits of one token row."""
     import torch
