@@ -466,6 +466,136 @@ def run_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_sharded(args, rank, world, local):
+    """Row-sharded Q4_0 projections with one NCCL all-gather (the sharded sweep of the path's
+    measurement plan): W_lm 128256x3072 and W_ffn 8192x3072 split by rows over the ranks, X
+    [M, 3072] f16 replicated, M in {1, 16, 128, 1024, 8192}.  Per (weight, M): the local GEMM, the
+    all-gather and the whole forward (GEMM + all-gather + row-major unshard), each timed with
+    CUDA events over `steps` iterations after `warmup`, max over ranks.  One JSON line each."""
+    import torch
+    import sulimo_b200 as sb
+    from sulimo_b200.sharded import ShardedQ4Projection, shard_weight
+    ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
+    K = 3072
+    lines = []
+    for wname, F in (("lm_head 128256x3072", 128256), ("ffn 8192x3072", 8192)):
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(F)
+        nb = F * K // 32
+        d = (torch.randn(nb, device="cuda", generator=gen).abs() * 0.02).half().view(torch.int16)
+        qn = torch.randint(0, 256, (nb * 16,), device="cuda", dtype=torch.uint8, generator=gen)
+        s_r, q_r, fs = shard_weight(d, qn, F, K, rank, world)
+        del d, qn
+        proj = ShardedQ4Projection(ctx, s_r, q_r, F, K, fs)
+        for M in (1, 16, 128, 1024, 8192):
+            x = torch.randn(M * K, device="cuda", dtype=torch.float16, generator=gen)
+            g, y = proj.buffers(M, sb.OUT_F16)
+
+            def timed(fn):
+                for _ in range(args.warmup):
+                    fn()
+                barrier(world)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(args.steps):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                return max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+
+            t_gemm = timed(lambda: proj.local_gemm(x, M, g, sb.OUT_F16))
+            t_ag = timed(lambda: proj.all_gather(M, g)) if world > 1 else 0.0
+            t_e2e = timed(lambda: proj.forward(x, M, g, y, sb.OUT_F16))
+            flop = 2.0 * M * K * F
+            ag_bytes = M * F * 2 * (world - 1) / world
+            lines.append({
+                "mode": "sharded", "weight": wname, "m_tokens": M, "n_gpus": world,
+                "rows_per_gpu": fs, "dtype": "f16", "steps": args.steps, "warmup": args.warmup,
+                "gemm_ms": round(t_gemm, 4), "allgather_ms": round(t_ag, 4),
+                "e2e_ms": round(t_e2e, 4),
+                "e2e_tflops": round(flop / (t_e2e * 1e-3) / 1e12, 2),
+                "gemm_tflops_per_gpu": round(flop / world / (t_gemm * 1e-3) / 1e12, 2),
+                "allgather_GBps_per_gpu": round(ag_bytes / (t_ag * 1e-3) / 1e9, 1)
+                if t_ag > 0 else None,
+                "data": "synthetic (seeded Q4_0 d=f16(|N|*0.02), nibbles U{0..15}; x f16 N(0,1))",
+                "exchange": "NCCL all_gather_into_tensor (shard-major) + unshard_rows kernel"})
+            del x, g, y
+        del proj, s_r, q_r
+        torch.cuda.empty_cache()
+    ctx.close()
+    return lines
+
+
+def run_decode(args, rank, world, local):
+    """Config 4: Llama-3.2-3B-architecture decode at context 4096 (each sequence's ring
+    pre-filled with 4096 positions of random Q8_0 K/V), batch 1 / 8 / 32 independent sequences.
+    A step is one sulimo_cuda_forward_token (28 layers + vocab projection) plus the greedy
+    argmax, captured once as a CUDA graph and replayed `steps` times.  Decode is replicated,
+    not sharded: with N ranks each runs its own sequences and the tok/s add up."""
+    import torch
+    import sulimo_b200 as sb
+    from sulimo_b200.model import DecodeModel
+    from sulimo_b200.synthetic import LLAMA_3B, make_model_torch, weight_bytes
+    ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
+    cfg = dict(LLAMA_3B)
+    cap = 4096
+    w = make_model_torch(cfg, seed=rank, kv_capacity=cap)
+    wbytes = weight_bytes(cfg)
+    slot = cfg["head_count_kv"] * cfg["head_dim"] // 32 * 34
+    scale = torch.tensor([0.02], dtype=torch.float16).view(torch.uint8).cuda()
+    lines = []
+    for b in (1, 8, 32):
+        dm = DecodeModel(ctx, w, batch=b)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(100 + b)
+        for kr, vr in dm.rings:
+            for r in (kr, vr):
+                r.copy_(torch.randint(0, 256, r.shape, dtype=torch.uint8, device="cuda",
+                                      generator=gen))
+                r.view(-1, 34)[:, 0:2] = scale
+        tokens = torch.randint(0, cfg["vocab"], (b,), dtype=torch.int32, device="cuda",
+                               generator=gen)
+        pos = cap - 1
+        for _ in range(args.warmup):
+            dm.forward_token(tokens, pos)
+            dm.greedy()
+        ctx.finish()
+        launches0 = ctx.launch_count
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ctx.set_stream(torch.cuda.current_stream())
+            dm.forward_token(tokens, pos)
+            dm.greedy()
+        ctx.set_stream(torch.cuda.current_stream())
+        launches = ctx.launch_count - launches0
+        for _ in range(3):
+            graph.replay()
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+        step_bytes = wbytes + b * cfg["n_layers"] * 2 * cap * slot
+        hbm, _, _, src = peaks()
+        lines.append({
+            "mode": "decode", "workload": "config 4: Llama-3.2-3B-arch decode, ctx 4096",
+            "batch_per_gpu": b, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "tok_per_s": round(b * world / (ms * 1e-3), 1),
+            "bytes_per_step": step_bytes, "GBps": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+            "frac_of_measured_hbm": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 3),
+            "gpu_launches_per_step": launches, "dtype": "q4_0 weights x q8_0 activations",
+            "data": "synthetic (seeded Q4_0 weights, random Q8_0 K/V rings)"})
+        del graph, dm
+        torch.cuda.empty_cache()
+    ctx.close()
+    return lines
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -475,6 +605,10 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--mode", default="headline", choices=["headline", "sharded", "decode"],
+                    help="headline: the contract line (config 2); sharded: the row-sharded "
+                         "lm_head/FFN sweep with an NCCL all-gather; decode: config 4 "
+                         "(Llama-3B decode steps); one JSON line per case")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -487,6 +621,16 @@ def main():
         return
 
     rank, world, local = dist_setup(args.gpus)
+    if args.mode in ("sharded", "decode"):
+        run = run_sharded if args.mode == "sharded" else run_decode
+        for line in run(args, rank, world, local):
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     r = run_ours(args, rank, world, local)
     if rank == 0:
         line = {

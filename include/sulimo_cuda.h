@@ -168,6 +168,54 @@ int sulimo_cuda_dequantize_q4_0_rows(sulimo_ctx* ctx, const void* scales, const 
                                      int cols, const int32_t* row_ids, int count, void* out,
                                      int out_dtype);
 
+/* Row-sharded projection layout (multi-GPU; the reference is single-device, the sharding of  */
+/* its Q4_0 projections follows the SoA layout: rows [r*fs, r*fs+fs) of a [F][K] tensor are    */
+/* the contiguous scales/quants subranges r*fs*(K/32) .. ).  `gathered` is the shard-major     */
+/* result of an all-gather, [world][m_tokens][fs] elements of `elem_size` (2 = f16, 4 = f32)  */
+/* bytes, shard world-1 holding F - (world-1)*fs valid rows; `out` receives the row-major     */
+/* [m_tokens][F] layout of the single-device GEMM (gemm_q4_0_f16's out).                       */
+int sulimo_cuda_unshard_rows(sulimo_ctx* ctx, const void* gathered, void* out, int world,
+                             int m_tokens, size_t fs, size_t f, int elem_size);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Whole decode position — replaces forward_token                                            */
+/* (crates/sulimo-engine/src/forward_pass.rs:190-417; Llama and Qwen2 branches) for a batch   */
+/* of independent sequences at the same position.  All pointers are device pointers except    */
+/* `layers` (a host array of n_layers entries).  Weights are Q4_0 SoA (scales, quants),       */
+/* norms and biases f32 (biases may be NULL), each sequence has its own Q8_0 K and V ring per  */
+/* layer: sequence s's ring starts kv_seq_stride bytes after sequence s-1's.                   */
+typedef struct sulimo_layer_desc {
+    const void *attn_norm, *ffn_norm, *bq, *bk, *bv;
+    const void *wq_scales, *wq_quants, *wk_scales, *wk_quants, *wv_scales, *wv_quants;
+    const void *wo_scales, *wo_quants, *wg_scales, *wg_quants, *wu_scales, *wu_quants;
+    const void *wd_scales, *wd_quants;
+    void *k_ring, *v_ring;
+} sulimo_layer_desc;
+
+typedef struct sulimo_model_desc {
+    int n_layers, embd, ffn, head_count, head_count_kv, head_dim, vocab, rope_dim;
+    int rope_mode; /* 0 = Norm (Llama), 1 = Neox (Qwen2) */
+    float eps, rope_base, attn_softcap;
+    size_t kv_capacity, kv_seq_stride;
+    const void *tok_scales, *tok_quants; /* token_embd [vocab][embd] */
+    const void *out_scales, *out_quants; /* output [vocab][embd] (tied: token_embd) */
+    const float* out_norm;
+    const sulimo_layer_desc* layers;
+} sulimo_model_desc;
+
+/* Bytes of device scratch sulimo_cuda_forward_token needs for `batch` sequences (the          */
+/* reference's ScratchBuffers, forward_pass.rs:150-186: allocated once, no per-token alloc).  */
+size_t sulimo_cuda_forward_scratch_bytes(const sulimo_model_desc* model, int batch);
+
+/* logits[batch][vocab] (fp32) for tokens[batch] (device int32) at position `pos` (context     */
+/* pos+1); stores each sequence's K/V at ring slot pos % kv_capacity.                         */
+int sulimo_cuda_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                              const int32_t* tokens, int batch, size_t pos, float* logits,
+                              void* scratch, size_t scratch_bytes);
+
+/* Greedy pick: out[r] = first index of the maximum of row r of x[rows][cols].                */
+int sulimo_cuda_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out);
+
 /* ---------------------------------------------------------------------------------------- */
 /* Decode attention — replaces causal_gqa_decode_scalar_ext                                   */
 /* (crates/sulimo-cpu/src/scalar.rs:287-359) over the KvCache ring (kv_cache.rs:114-128).     */

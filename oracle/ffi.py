@@ -227,3 +227,59 @@ def causal_gqa_decode(q, k_ring, v_ring, capacity, context_len, head_count, head
                                    head_count, head_count_kv, head_dim, _p(scores), _p(out),
                                    softcap)
     return out
+
+
+# ---- forward_token (crates/sulimo-engine/src/forward_pass.rs:190-417) -----------------------
+class _OracleLayer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "attn_norm", "ffn_norm", "bq", "bk", "bv", "wq_s", "wq_q", "wk_s", "wk_q", "wv_s", "wv_q",
+        "wo_s", "wo_q", "wg_s", "wg_q", "wu_s", "wu_q", "wd_s", "wd_q", "k_ring", "v_ring")]
+
+
+class _OracleModel(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("embd", C.c_int), ("ffn", C.c_int),
+                ("head_count", C.c_int), ("head_count_kv", C.c_int), ("head_dim", C.c_int),
+                ("vocab", C.c_int), ("rope_dim", C.c_int), ("rope_mode", C.c_int),
+                ("eps", C.c_float), ("rope_base", C.c_float), ("attn_softcap", C.c_float),
+                ("kv_capacity", C.c_size_t), ("tok_s", C.c_void_p), ("tok_q", C.c_void_p),
+                ("out_s", C.c_void_p), ("out_q", C.c_void_p), ("out_norm", C.c_void_p),
+                ("layers", C.POINTER(_OracleLayer))]
+
+
+class OracleModel:
+    """A synthetic model held as numpy arrays for oracle_forward_token.  `w` is the dict made by
+    sulimo_b200.synthetic.make_model_numpy; the K/V rings live here and advance with every
+    forward_token call."""
+
+    def __init__(self, w):
+        self.w = w
+        cfg = w["cfg"]
+        self.cfg = cfg
+        kv_bytes = cfg["kv_capacity"] * cfg["head_count_kv"] * cfg["head_dim"] // 32 * 34
+        self.rings = [(np.zeros(kv_bytes, np.uint8), np.zeros(kv_bytes, np.uint8))
+                      for _ in range(cfg["n_layers"])]
+        layers = (_OracleLayer * cfg["n_layers"])()
+        for i, (L, (kr, vr)) in enumerate(zip(w["layers"], self.rings)):
+            ent = layers[i]
+            for name in ("attn_norm", "ffn_norm", "bq", "bk", "bv"):
+                setattr(ent, name, L[name].ctypes.data if L.get(name) is not None else None)
+            for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
+                setattr(ent, name + "_s", L[name][0].ctypes.data)
+                setattr(ent, name + "_q", L[name][1].ctypes.data)
+            ent.k_ring, ent.v_ring = kr.ctypes.data, vr.ctypes.data
+        self.layers = layers
+        m = _OracleModel()
+        for k in ("n_layers", "embd", "ffn", "head_count", "head_count_kv", "head_dim", "vocab",
+                  "rope_dim", "rope_mode", "eps", "rope_base", "attn_softcap", "kv_capacity"):
+            setattr(m, k, cfg[k])
+        m.tok_s, m.tok_q = w["tok"][0].ctypes.data, w["tok"][1].ctypes.data
+        m.out_s, m.out_q = w["out"][0].ctypes.data, w["out"][1].ctypes.data
+        m.out_norm = w["out_norm"].ctypes.data
+        m.layers = layers
+        self.m = m
+
+    def forward_token(self, token, pos):
+        out = np.empty(self.cfg["vocab"], np.float32)
+        lib().oracle_forward_token(C.byref(self.m), C.c_uint32(token), C.c_size_t(pos),
+                                   out.ctypes.data_as(C.POINTER(C.c_float)))
+        return out

@@ -11,6 +11,7 @@
 
 #include <immintrin.h>
 #include <math.h>
+#include <stdlib.h>
 #include <pthread.h>
 #include <string.h>
 
@@ -561,4 +562,68 @@ void oracle_causal_gqa_decode(const float* q, const uint8_t* k_ring, const uint8
             for (size_t d = 0; d < head_dim; d++) oh[d] += wgt * deq[d];
         }
     }
+}
+
+/* forward_token — crates/sulimo-engine/src/forward_pass.rs:190-417 (Llama / Qwen2 branches):
+ * lookup_token_embedding :419-450, apply_rmsnorm :493-507 (dispatch_rmsnorm -> rmsnorm_avx2),
+ * quantize_f32_to_q8_0 + apply_matvec :509-527 (dispatch_matvec_q4_0_q8_0 -> avx2), add_bias
+ * :452-465, rope_head_scalar per head, KvCache::store_key/value, causal_gqa_decode_scalar_ext
+ * with context pos+1, swiglu_scalar, residual adds, final norm + output projection. */
+void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, float* logits) {
+    const size_t E = (size_t)m->embd, F = (size_t)m->ffn, hd = (size_t)m->head_dim;
+    const size_t qd = (size_t)m->head_count * hd, kvd = (size_t)m->head_count_kv * hd;
+    const size_t nbE = E / 32;
+    const size_t ctx = pos + 1;
+    float* x = (float*)malloc(E * 4);
+    float* h = (float*)malloc(E * 4);
+    float* q = (float*)malloc(qd * 4);
+    float* k = (float*)malloc(kvd * 4);
+    float* v = (float*)malloc(kvd * 4);
+    float* att = (float*)malloc(qd * 4);
+    float* g = (float*)malloc(F * 4);
+    float* u = (float*)malloc(F * 4);
+    float* sw = (float*)malloc(F * 4);
+    float* dn = (float*)malloc(E * 4);
+    float* scores = (float*)malloc(ctx * 4);
+    size_t q8n = (qd > E ? qd : E);
+    if (F > q8n) q8n = F;
+    uint8_t* q8 = (uint8_t*)malloc(q8n / 32 * 34);
+    oracle_dequantize_q4_0_soa(m->tok_s + (size_t)token * nbE * 2, m->tok_q + (size_t)token * nbE * 16,
+                               nbE, x);
+    for (int l = 0; l < m->n_layers; l++) {
+        const oracle_layer* L = &m->layers[l];
+        oracle_rmsnorm_avx2(x, L->attn_norm, E, m->eps, h);
+        oracle_quantize_f32_to_q8_0(h, E, q8);
+        oracle_matvec_q4_0_q8_0_avx2(L->wq_s, L->wq_q, q8, qd, E, q);
+        oracle_matvec_q4_0_q8_0_avx2(L->wk_s, L->wk_q, q8, kvd, E, k);
+        oracle_matvec_q4_0_q8_0_avx2(L->wv_s, L->wv_q, q8, kvd, E, v);
+        if (L->bq) for (size_t i = 0; i < qd; i++) q[i] += L->bq[i];
+        if (L->bk) for (size_t i = 0; i < kvd; i++) k[i] += L->bk[i];
+        if (L->bv) for (size_t i = 0; i < kvd; i++) v[i] += L->bv[i];
+        for (int hh = 0; hh < m->head_count; hh++)
+            oracle_rope_head_scalar(q + hh * hd, pos, (size_t)m->rope_dim, m->rope_base, m->rope_mode);
+        for (int hh = 0; hh < m->head_count_kv; hh++)
+            oracle_rope_head_scalar(k + hh * hd, pos, (size_t)m->rope_dim, m->rope_base, m->rope_mode);
+        oracle_kv_store_f32(k, L->k_ring, pos, m->kv_capacity, kvd / 32);
+        oracle_kv_store_f32(v, L->v_ring, pos, m->kv_capacity, kvd / 32);
+        oracle_causal_gqa_decode(q, L->k_ring, L->v_ring, m->kv_capacity, ctx,
+                                 (size_t)m->head_count, (size_t)m->head_count_kv, hd, scores, att,
+                                 m->attn_softcap);
+        oracle_quantize_f32_to_q8_0(att, qd, q8);
+        oracle_matvec_q4_0_q8_0_avx2(L->wo_s, L->wo_q, q8, E, qd, h);
+        for (size_t i = 0; i < E; i++) x[i] += h[i];
+        oracle_rmsnorm_avx2(x, L->ffn_norm, E, m->eps, h);
+        oracle_quantize_f32_to_q8_0(h, E, q8);
+        oracle_matvec_q4_0_q8_0_avx2(L->wg_s, L->wg_q, q8, F, E, g);
+        oracle_matvec_q4_0_q8_0_avx2(L->wu_s, L->wu_q, q8, F, E, u);
+        oracle_swiglu_scalar(g, u, sw, F);
+        oracle_quantize_f32_to_q8_0(sw, F, q8);
+        oracle_matvec_q4_0_q8_0_avx2(L->wd_s, L->wd_q, q8, E, F, dn);
+        for (size_t i = 0; i < E; i++) x[i] += dn[i];
+    }
+    oracle_rmsnorm_avx2(x, m->out_norm, E, m->eps, h);
+    oracle_quantize_f32_to_q8_0(h, E, q8);
+    oracle_matvec_q4_0_q8_0_avx2(m->out_s, m->out_q, q8, (size_t)m->vocab, E, logits);
+    free(x); free(h); free(q); free(k); free(v); free(att); free(g); free(u); free(sw);
+    free(dn); free(scores); free(q8);
 }

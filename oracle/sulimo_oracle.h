@@ -107,6 +107,31 @@ void oracle_causal_gqa_decode(const float* q, const uint8_t* k_ring, const uint8
                               size_t head_count_kv, size_t head_dim, float* scores_buf,
                               float* out, float softcap);
 
+/* ---- one decode position through the whole model (forward_token,
+ * crates/sulimo-engine/src/forward_pass.rs:190-417), Llama / Qwen2 path: RMSNorm (AVX2),
+ * Q8_0 activations, AVX2 matvecs, optional QKV biases, RoPE (Norm / Neox), Q8_0 ring store,
+ * causal GQA decode, SwiGLU, residual adds, final norm and the vocab projection. */
+typedef struct oracle_layer {
+    const float *attn_norm, *ffn_norm;  /* [embd] */
+    const float *bq, *bk, *bv;          /* biases or NULL */
+    const uint8_t *wq_s, *wq_q, *wk_s, *wk_q, *wv_s, *wv_q, *wo_s, *wo_q;
+    const uint8_t *wg_s, *wg_q, *wu_s, *wu_q, *wd_s, *wd_q;
+    uint8_t *k_ring, *v_ring;           /* capacity slots of kv_dim/32 Q8_0 blocks */
+} oracle_layer;
+
+typedef struct oracle_model {
+    int n_layers, embd, ffn, head_count, head_count_kv, head_dim, vocab, rope_dim, rope_mode;
+    float eps, rope_base, attn_softcap;
+    size_t kv_capacity;
+    const uint8_t *tok_s, *tok_q; /* token_embd [vocab][embd] Q4_0 SoA */
+    const uint8_t *out_s, *out_q; /* output [vocab][embd] Q4_0 SoA (tied: same pointers) */
+    const float* out_norm;
+    const oracle_layer* layers;
+} oracle_model;
+
+/* logits [vocab] for `token` at position `pos` (context pos+1); stores K/V at pos. */
+void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, float* logits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,7 +12,8 @@ from .capi import ACT_F16, ACT_F32, OUT_F16, OUT_F32, SulimoError
 __all__ = [
     "CudaContext", "SulimoError", "gemm_q4_0_f16", "logits_final", "dispatch_matvec_q4_0_q8_0",
     "block_sums_q4_0_q8_0", "quantize_f32_to_q8_0", "kv_store_q8_0", "dequantize_q4_0_rows",
-    "causal_gqa_decode", "live_buffer_count", "OUT_F16", "OUT_F32", "ACT_F16", "ACT_F32",
+    "causal_gqa_decode", "live_buffer_count", "unshard_rows", "OUT_F16", "OUT_F32", "ACT_F16",
+    "ACT_F32",
 ]
 
 
@@ -118,6 +119,12 @@ def dequantize_q4_0_rows(ctx, scales, quants, cols, row_ids, out, out_dtype=OUT_
     """dequantize_q4_0_soa (repack.rs:107-131) / lookup_token_embedding_f16 (scheduler.rs:329)."""
     capi.call("sulimo_cuda_dequantize_q4_0_rows", ctx.handle, _ptr(scales), _ptr(quants), cols,
               _ptr(row_ids), row_ids.numel(), _ptr(out), out_dtype)
+
+
+def unshard_rows(ctx, gathered, out, world, m_tokens, fs, f):
+    """Shard-major all-gather result [world][m_tokens][fs] -> row-major [m_tokens][f]."""
+    capi.call("sulimo_cuda_unshard_rows", ctx.handle, _ptr(gathered), _ptr(out), world, m_tokens,
+              fs, f, gathered.element_size())
 
 
 def causal_gqa_decode(ctx, q, k_ring, v_ring, capacity, context_len, head_count, head_count_kv,

@@ -21,6 +21,8 @@ SOURCES = [
     "attn_decode_q8_0.cu",
     "attn_decode_noalloc.cu",
     "gemm_q4_0_tc.cu",
+    "shard.cu",
+    "forward.cu",
 ]
 
 NVCC_FLAGS = [

@@ -50,6 +50,10 @@ SIGNATURES = {
     "sulimo_cuda_quantize_q8_0": (_i, [_vp, _vp, _vp, _sz]),
     "sulimo_cuda_kv_store_q8_0": (_i, [_vp, _vp, _i, _vp, _sz, _sz, _sz, _sz]),
     "sulimo_cuda_dequantize_q4_0_rows": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i]),
+    "sulimo_cuda_unshard_rows": (_i, [_vp, _vp, _vp, _i, _i, _sz, _sz, _i]),
+    "sulimo_cuda_forward_scratch_bytes": (_sz, [_vp, _i]),
+    "sulimo_cuda_forward_token": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _sz]),
+    "sulimo_cuda_argmax_rows": (_i, [_vp, _vp, _i, _i, _vp]),
     "sulimo_cuda_attn_decode_q8_0": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _i, _i,
                                           _f, _vp]),
     "sulimo_cuda_attn_decode_q8_0_noalloc": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _i,

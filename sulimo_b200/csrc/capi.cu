@@ -461,6 +461,87 @@ int sulimo_cuda_dequantize_q4_0_rows(sulimo_ctx* ctx, const void* scales, const 
     return sulimo::launch_dequant_rows(ctx, scales, quants, cols, row_ids, count, out, out_dtype);
 }
 
+int sulimo_cuda_unshard_rows(sulimo_ctx* ctx, const void* gathered, void* out, int world,
+                             int m_tokens, size_t fs, size_t f, int elem_size) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (world < 1 || m_tokens < 0 || (elem_size != 2 && elem_size != 4))
+        return set_error(SULIMO_EINVAL, "bad world / m_tokens / elem_size");
+    if (fs == 0 || (size_t)(world - 1) * fs >= f || f > (size_t)world * fs)
+        return set_error(SULIMO_EINVAL, "shard rows must satisfy (world-1)*fs < F <= world*fs");
+    if (m_tokens > 2147483647 || world > 65535)
+        return set_error(SULIMO_EINVAL, "too many tokens / shards");
+    if (m_tokens == 0) return SULIMO_OK;
+    if (!gathered || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(gathered, elem_size) || !aligned(out, elem_size))
+        return set_error(SULIMO_EALIGN, "misaligned");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_unshard_rows(ctx, gathered, out, world, m_tokens, fs, f, elem_size);
+}
+
+static int check_model(const sulimo_model_desc* m) {
+    if (!m || !m->layers || m->n_layers <= 0) return set_error(SULIMO_EINVAL, "null model");
+    if (m->embd <= 0 || m->embd % 32 || m->ffn <= 0 || m->ffn % 32 || m->vocab <= 0 ||
+        m->vocab % 8)
+        return set_error(SULIMO_EINVAL, "embd / ffn multiples of 32, vocab a multiple of 8");
+    if (m->head_count <= 0 || m->head_count_kv <= 0 || m->head_count % m->head_count_kv ||
+        m->head_count / m->head_count_kv > 8)
+        return set_error(SULIMO_EINVAL, "head_count a multiple (<= 8x) of head_count_kv");
+    if (m->head_dim <= 0 || m->head_dim % 32 || m->head_dim > 256 || m->rope_dim <= 0 ||
+        m->rope_dim % 2 || m->rope_dim > m->head_dim || (m->rope_mode != 0 && m->rope_mode != 1))
+        return set_error(SULIMO_EINVAL, "bad head_dim / rope_dim / rope_mode");
+    if (m->kv_capacity == 0) return set_error(SULIMO_EINVAL, "kv_capacity must be positive");
+    if (m->embd * 4 + 33 * 4 > 227 * 1024) return set_error(SULIMO_EINVAL, "embd too large");
+    if (!m->tok_scales || !m->tok_quants || !m->out_scales || !m->out_quants || !m->out_norm)
+        return set_error(SULIMO_EINVAL, "null embedding / output tensor");
+    for (int l = 0; l < m->n_layers; l++) {
+        const sulimo_layer_desc& L = m->layers[l];
+        const void* need[] = {L.attn_norm, L.ffn_norm, L.wq_scales, L.wq_quants, L.wk_scales,
+                              L.wk_quants, L.wv_scales, L.wv_quants, L.wo_scales, L.wo_quants,
+                              L.wg_scales, L.wg_quants, L.wu_scales, L.wu_quants, L.wd_scales,
+                              L.wd_quants, L.k_ring, L.v_ring};
+        for (const void* p : need)
+            if (!p) return set_error(SULIMO_EINVAL, "null layer tensor");
+        if (!aligned(L.k_ring, 2) || !aligned(L.v_ring, 2))
+            return set_error(SULIMO_EALIGN, "rings must be 2-byte aligned");
+    }
+    if (m->kv_seq_stride % 2) return set_error(SULIMO_EALIGN, "kv_seq_stride must be even");
+    return SULIMO_OK;
+}
+
+size_t sulimo_cuda_forward_scratch_bytes(const sulimo_model_desc* model, int batch) {
+    if (check_model(model) || batch <= 0) return 0;
+    return sulimo::forward_scratch_bytes(model, batch);
+}
+
+int sulimo_cuda_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                              const int32_t* tokens, int batch, size_t pos, float* logits,
+                              void* scratch, size_t scratch_bytes) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if ((st = check_model(model))) return st;
+    if (batch <= 0 || batch > 65535) return set_error(SULIMO_EINVAL, "batch must be in [1, 65535]");
+    if (!tokens || !logits || !scratch) return set_error(SULIMO_EINVAL, "null pointer");
+    if (scratch_bytes < sulimo::forward_scratch_bytes(model, batch))
+        return set_error(SULIMO_EINVAL, "scratch smaller than sulimo_cuda_forward_scratch_bytes");
+    if (!aligned(scratch, 256) || !aligned(logits, 16) || !aligned(tokens, 4))
+        return set_error(SULIMO_EALIGN, "scratch 256-byte, logits 16-byte aligned");
+    if (pos + 1 > model->kv_capacity)
+        return set_error(SULIMO_EINVAL, "context pos+1 exceeds the ring capacity");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_forward_token(ctx, model, tokens, batch, pos, logits, scratch);
+}
+
+int sulimo_cuda_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (rows < 0 || cols <= 0) return set_error(SULIMO_EINVAL, "bad rows / cols");
+    if (rows == 0) return SULIMO_OK;
+    if (!x || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_argmax_rows(ctx, x, rows, cols, out);
+}
+
 int sulimo_cuda_attn_decode_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
                                  const void* v_ring, size_t seq_stride_bytes, size_t capacity,
                                  size_t context_len, int head_count, int head_count_kv,

@@ -1,0 +1,314 @@
+// forward.cu — one decode position through a Llama / Qwen2-architecture model on the GPU:
+// the reference's forward_token (crates/sulimo-engine/src/forward_pass.rs:190-417) for a batch
+// of independent sequences that sit at the same position.
+//
+// Per layer (14 launches, all on the context's stream, no host synchronisation):
+//   add_rmsnorm_q8     x (+= previous FFN output), h = rmsnorm(x)*attn_norm -> Q8_0
+//                      (apply_rmsnorm :493-507 + quantize_f32_to_q8_0)
+//   3x GEMV            q, k, v = W . h (dispatch_matvec_q4_0_q8_0, bit-exact AVX2 order)
+//   qkv_rope_store     + biases (add_bias :452-465), RoPE Norm/Neox per head
+//                      (rope_head_scalar, scalar.rs:92-130), K/V quantized into ring slot
+//                      pos % capacity (KvCache::store_key/store_value, kv_cache.rs:93-110)
+//   attention          causal GQA decode over the Q8_0 ring, context pos+1
+//                      (causal_gqa_decode_scalar_ext, scalar.rs:287-359) -- 2 launches
+//   quantize           attention output -> Q8_0
+//   GEMV               o = Wo . a
+//   add_rmsnorm_q8     x += o, h = rmsnorm(x)*ffn_norm -> Q8_0
+//   2x GEMV            gate, up
+//   swiglu_q8          silu(gate)*up -> Q8_0 (swiglu_scalar, scalar.rs:161-170)
+//   GEMV               down
+// then add_rmsnorm_q8 with the output norm and the vocab GEMV (logits, fp32).
+// The glue kernels are fused so every activation vector is read and written once per step;
+// the GEMVs (the weight stream) dominate.  RMSNorm sums squares as a tree (the reference sums
+// eight AVX2 lanes sequentially), and RoPE / SiLU use CUDA's powf / sinf / cosf / expf, so the
+// activations agree with the reference to float rounding, not bit for bit.
+#include "sulimo_common.cuh"
+#include "sulimo_internal.h"
+
+namespace sulimo {
+namespace {
+
+constexpr int GLUE_THREADS = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.0f;
+    if (threadIdx.x < 32) {
+        s = threadIdx.x < (int)(blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (threadIdx.x == 0) red[32] = s;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// One CTA per sequence.  x[seq][E] (+= delta[seq][E] when delta is given, written back), then
+// y = (x * 1/sqrt(mean(x^2) + eps)) * w, quantized to Q8_0 (E/32 blocks) into q8[seq].
+__global__ void __launch_bounds__(GLUE_THREADS)
+    add_rmsnorm_q8_kernel(float* __restrict__ x, const float* __restrict__ delta,
+                          const float* __restrict__ w, int E, float eps,
+                          uint8_t* __restrict__ q8) {
+    extern __shared__ float sx[];  // E floats + 33 reduction slots
+    float* red = sx + E;
+    const int seq = blockIdx.x;
+    float* xs = x + (size_t)seq * E;
+    const float* ds = delta ? delta + (size_t)seq * E : nullptr;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+        float v = xs[i];
+        if (ds) {
+            v = __fadd_rn(v, ds[i]);
+            xs[i] = v;
+        }
+        sx[i] = v;
+        ss = __fmaf_rn(v, v, ss);
+    }
+    const float sum_sq = block_sum(ss, red);
+    const float mean = __fdiv_rn(sum_sq, (float)E);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* qs = q8 + (size_t)seq * (E / 32) * 34;
+    for (int b = warp; b < E / 32; b += blockDim.x >> 5) {
+        const int i = b * 32 + lane;
+        const float y = __fmul_rn(__fmul_rn(sx[i], scale), w[i]);
+        quantize_block_warp(y, qs + b * 34, lane);
+    }
+}
+
+// RoPE of one head in place (rope_head_scalar): pair (2i, 2i+1) in Norm mode (0), (i, i+half)
+// in Neox mode (1); theta = pos / base^(2i/rope_dim).
+__device__ __forceinline__ void rope_pair(float* v, int i, int half, int mode, float c, float s) {
+    const int a = mode == 0 ? 2 * i : i, b = mode == 0 ? 2 * i + 1 : i + half;
+    const float v0 = v[a], v1 = v[b];
+    v[a] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    v[b] = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+}
+
+// One CTA per sequence: biases, RoPE of every q and k head, then K and V quantized into the
+// sequence's rings at slot pos % capacity (kv head h at block h*hd/32 of the slot).
+__global__ void __launch_bounds__(GLUE_THREADS)
+    qkv_rope_store_kernel(float* __restrict__ q, float* __restrict__ k, float* __restrict__ v,
+                          const float* __restrict__ bq, const float* __restrict__ bk,
+                          const float* __restrict__ bv, int H, int Hkv, int hd, int rope_dim,
+                          int mode, float base, size_t pos, uint8_t* __restrict__ k_ring,
+                          uint8_t* __restrict__ v_ring, size_t capacity, size_t seq_stride) {
+    const int seq = blockIdx.x;
+    const int qd = H * hd, kvd = Hkv * hd, half = rope_dim / 2;
+    float* qs = q + (size_t)seq * qd;
+    float* ks = k + (size_t)seq * kvd;
+    float* vs = v + (size_t)seq * kvd;
+    for (int i = threadIdx.x; i < qd; i += blockDim.x)
+        if (bq) qs[i] = __fadd_rn(qs[i], bq[i]);
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
+        if (bk) ks[i] = __fadd_rn(ks[i], bk[i]);
+        if (bv) vs[i] = __fadd_rn(vs[i], bv[i]);
+    }
+    __syncthreads();
+    // one thread per (head, pair)
+    for (int t = threadIdx.x; t < (H + Hkv) * half; t += blockDim.x) {
+        const int head = t / half, i = t - head * half;
+        const float freq = __fdiv_rn(1.0f, powf(base, __fdiv_rn((float)(2 * i), (float)rope_dim)));
+        const float theta = __fmul_rn((float)pos, freq);
+        const float c = cosf(theta), s = sinf(theta);
+        float* hv = head < H ? qs + head * hd : ks + (head - H) * hd;
+        rope_pair(hv, i, half, mode, c, s);
+    }
+    __syncthreads();
+    const size_t slot = pos % capacity;
+    const size_t bpp = (size_t)kvd / 32;
+    uint8_t* kd = k_ring + (size_t)seq * seq_stride + slot * bpp * 34;
+    uint8_t* vd = v_ring + (size_t)seq * seq_stride + slot * bpp * 34;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int b = warp; b < 2 * (int)bpp; b += blockDim.x >> 5) {
+        if (b < (int)bpp)
+            quantize_block_warp(ks[b * 32 + lane], kd + b * 34, lane);
+        else
+            quantize_block_warp(vs[(b - bpp) * 32 + lane], vd + (b - bpp) * 34, lane);
+    }
+}
+
+// silu(gate) * up -> Q8_0: one warp per 32-value block, all sequences' blocks in one grid.
+__global__ void __launch_bounds__(GLUE_THREADS)
+    swiglu_q8_kernel(const float* __restrict__ gate, const float* __restrict__ up, size_t nblocks,
+                     uint8_t* __restrict__ q8) {
+    const int lane = threadIdx.x & 31;
+    size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= nblocks) return;
+    const float g = gate[b * 32 + lane];
+    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    quantize_block_warp(__fmul_rn(silu, up[b * 32 + lane]), q8 + b * 34, lane);
+}
+
+// First index of the maximum of each row (greedy sampling); NaN never wins.
+__global__ void __launch_bounds__(GLUE_THREADS)
+    argmax_rows_kernel(const float* __restrict__ x, int cols, int32_t* __restrict__ out) {
+    __shared__ float bv[GLUE_THREADS / 32];
+    __shared__ int bi[GLUE_THREADS / 32];
+    const float* r = x + (size_t)blockIdx.x * cols;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+        const float v = r[i];
+        if (v > best) {  // strided scan: the first max of this thread's subsequence
+            best = v;
+            idx = i;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+        if (ov > best || (ov == best && oi < idx)) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        bv[warp] = best;
+        bi[warp] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < GLUE_THREADS / 32; w++)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+                best = bv[w];
+                idx = bi[w];
+            }
+        out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+    }
+}
+
+struct Scratch {
+    float *x, *q, *k, *v, *att, *o, *g, *u;
+    uint8_t* q8;
+};
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+// Carves the caller's scratch (the reference's ScratchBuffers, forward_pass.rs:150-186).
+size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scratch* s) {
+    const size_t E = m->embd, F = m->ffn, qd = (size_t)m->head_count * m->head_dim;
+    const size_t kvd = (size_t)m->head_count_kv * m->head_dim;
+    size_t q8n = E > qd ? E : qd;
+    if (F > q8n) q8n = F;
+    const size_t sizes[9] = {E * 4, qd * 4, kvd * 4, kvd * 4, qd * 4, (E > F ? E : F) * 4,
+                             F * 4, F * 4, q8n / 32 * 34};
+    size_t off = 0;
+    uint8_t* p[9];
+    for (int i = 0; i < 9; i++) {
+        p[i] = base ? base + off : nullptr;
+        off += align256(sizes[i] * (size_t)batch);
+    }
+    if (s) {
+        s->x = reinterpret_cast<float*>(p[0]);
+        s->q = reinterpret_cast<float*>(p[1]);
+        s->k = reinterpret_cast<float*>(p[2]);
+        s->v = reinterpret_cast<float*>(p[3]);
+        s->att = reinterpret_cast<float*>(p[4]);
+        s->o = reinterpret_cast<float*>(p[5]);
+        s->g = reinterpret_cast<float*>(p[6]);
+        s->u = reinterpret_cast<float*>(p[7]);
+        s->q8 = p[8];
+    }
+    return off;
+}
+
+}  // namespace
+
+size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch) {
+    return scratch_layout(m, batch, nullptr, nullptr);
+}
+
+int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out) {
+    argmax_rows_kernel<<<rows, GLUE_THREADS, 0, ctx->stream>>>(x, cols, out);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "argmax_rows launch");
+}
+
+int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
+                         int batch, size_t pos, float* logits, void* scratch) {
+    Scratch s;
+    scratch_layout(m, batch, reinterpret_cast<uint8_t*>(scratch), &s);
+    const int E = m->embd, F = m->ffn, H = m->head_count, Hkv = m->head_count_kv,
+              hd = m->head_dim;
+    const int qd = H * hd, kvd = Hkv * hd;
+    const size_t ctx_len = pos + 1;
+    const size_t norm_smem = (size_t)(E + 33) * sizeof(float);
+    int st;
+    static int smem_set_device = -1;
+    if (norm_smem > 48 * 1024 && smem_set_device != ctx->device) {
+        if ((st = check_cuda(cudaFuncSetAttribute(add_rmsnorm_q8_kernel,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)norm_smem),
+                             "rmsnorm smem attribute")))
+            return st;
+        smem_set_device = ctx->device;
+    }
+    // attention workspace for this geometry (grown outside any graph capture by a first call)
+    int splits = 0;
+    const sulimo_layer_desc& L0 = m->layers[0];
+    const size_t pbytes = attn_decode_partial_bytes(ctx_len, m->kv_capacity, H, Hkv, hd, batch,
+                                                    ctx->num_sms, m->kv_seq_stride, L0.k_ring,
+                                                    L0.v_ring, &splits);
+    if ((st = ensure_workspace(ctx, pbytes))) return st;
+
+    // x = token_embd[token] (lookup_token_embedding, forward_pass.rs:419-450: exact f32 dequant)
+    if ((st = launch_dequant_rows(ctx, m->tok_scales, m->tok_quants, E, tokens, batch, s.x,
+                                  SULIMO_OUT_F32)))
+        return st;
+    const float* pending = nullptr;  // the previous layer's FFN output, added to x next
+    for (int l = 0; l < m->n_layers; l++) {
+        const sulimo_layer_desc& L = m->layers[l];
+        add_rmsnorm_q8_kernel<<<batch, GLUE_THREADS, norm_smem, ctx->stream>>>(
+            s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E, m->eps, s.q8);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
+        if ((st = launch_gemv_q4_0_q8_0(ctx, L.wq_scales, L.wq_quants, s.q8, qd, E, batch, s.q)) ||
+            (st = launch_gemv_q4_0_q8_0(ctx, L.wk_scales, L.wk_quants, s.q8, kvd, E, batch, s.k)) ||
+            (st = launch_gemv_q4_0_q8_0(ctx, L.wv_scales, L.wv_quants, s.q8, kvd, E, batch, s.v)))
+            return st;
+        qkv_rope_store_kernel<<<batch, GLUE_THREADS, 0, ctx->stream>>>(
+            s.q, s.k, s.v, reinterpret_cast<const float*>(L.bq),
+            reinterpret_cast<const float*>(L.bk), reinterpret_cast<const float*>(L.bv), H, Hkv, hd,
+            m->rope_dim, m->rope_mode, m->rope_base, pos, reinterpret_cast<uint8_t*>(L.k_ring),
+            reinterpret_cast<uint8_t*>(L.v_ring), m->kv_capacity, m->kv_seq_stride);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
+        if ((st = launch_attn_decode(ctx, s.q, L.k_ring, L.v_ring, m->kv_seq_stride,
+                                     m->kv_capacity, ctx_len, H, Hkv, hd, batch, m->attn_softcap,
+                                     s.att, reinterpret_cast<float*>(ctx->workspace),
+                                     ctx->workspace_bytes)) ||
+            (st = launch_quantize_q8_0(ctx, s.att, s.q8, (size_t)batch * qd)) ||
+            (st = launch_gemv_q4_0_q8_0(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
+            return st;
+        add_rmsnorm_q8_kernel<<<batch, GLUE_THREADS, norm_smem, ctx->stream>>>(
+            s.x, s.o, reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, s.q8);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
+        if ((st = launch_gemv_q4_0_q8_0(ctx, L.wg_scales, L.wg_quants, s.q8, F, E, batch, s.g)) ||
+            (st = launch_gemv_q4_0_q8_0(ctx, L.wu_scales, L.wu_quants, s.q8, F, E, batch, s.u)))
+            return st;
+        const size_t nblk = (size_t)batch * F / 32;
+        swiglu_q8_kernel<<<(unsigned)((nblk + 7) / 8), GLUE_THREADS, 0, ctx->stream>>>(
+            s.g, s.u, nblk, s.q8);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "swiglu_q8 launch"))) return st;
+        if ((st = launch_gemv_q4_0_q8_0(ctx, L.wd_scales, L.wd_quants, s.q8, E, F, batch, s.o)))
+            return st;
+        pending = s.o;
+    }
+    add_rmsnorm_q8_kernel<<<batch, GLUE_THREADS, norm_smem, ctx->stream>>>(
+        s.x, pending, m->out_norm, E, m->eps, s.q8);
+    ctx->launches++;
+    if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
+    return launch_gemv_q4_0_q8_0(ctx, m->out_scales, m->out_quants, s.q8, m->vocab, E, batch,
+                                 logits);
+}
+
+}  // namespace sulimo

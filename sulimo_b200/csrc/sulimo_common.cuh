@@ -132,6 +132,24 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- Q8_0 ----------------------------------------------------------------------------------
+// Quantizes the 32 values of a block held one per lane and writes the 34-byte Q8_0 block
+// exactly as quantize_f32_to_q8_0 (crates/sulimo-core/src/kv_cache.rs:162-192): d = max|x|/127
+// (IEEE f32), stored as f16 RNE; id = 1/d from the f32 d; q = clamp(roundf(x*id), -128, 127).
+__device__ __forceinline__ void quantize_block_warp(float v, uint8_t* dst, int lane) {
+    float a = fabsf(v);  // fmaxf drops NaN like the reference's `a > max_abs` test
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+    float d = __fdiv_rn(a, 127.0f);
+    float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    float q = roundf(__fmul_rn(v, id));
+    if (q != q) q = 0.0f;  // f32 NaN `as i8` == 0
+    q = fminf(fmaxf(q, -128.0f), 127.0f);
+    dst[2 + lane] = (uint8_t)(int8_t)(int)q;
+    // the f16 scale as one 2-byte store (blocks are 34 bytes, so dst is 2-byte aligned)
+    if (lane == 0) *reinterpret_cast<__half*>(dst) = __float2half_rn(d);
+}
+
 // ---- misc ------------------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

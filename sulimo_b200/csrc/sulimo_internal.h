@@ -79,6 +79,12 @@ int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, cons
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
                        float* partials, size_t partial_bytes);
+int launch_unshard_rows(sulimo_ctx* ctx, const void* gathered, void* out, int world,
+                        int m_tokens, size_t fs, size_t f, int elem_size);
+size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch);
+int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
+                         int batch, size_t pos, float* logits, void* scratch);
+int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out);
 // Workspace bytes (and split count) the attention entry point will use for this geometry.
 size_t attn_decode_partial_bytes(size_t context_len, size_t capacity, int head_count,
                                  int head_count_kv, int head_dim, int batch, int num_sms,

@@ -1,0 +1,91 @@
+"""Row-sharded Q4_0 projection over several GPUs (one process per GPU, torch.distributed/NCCL).
+
+The reference runs on one device.  Its Q4_0 projections shard naturally by output rows: with the
+SoA layout (crates/sulimo-core/src/repack.rs:45-81) rows [r0, r1) of a [F][K] tensor are the
+contiguous subranges scales[r0*K/32 : r1*K/32] and quants[r0*K/2 : r1*K/2], whole 32-element
+K blocks untouched.  Rank r holds `fs` rows (the last rank's tail padded with zero-scale rows,
+whose outputs are 0 and dropped), computes Y_r = X W_r^T with the tcgen05 GEMM into its slot of
+a shard-major buffer G[world][M][fs], and one NCCL all-gather (the path's only exchange step)
+fills G on every rank.  `unshard_rows` then writes the row-major Y[M][F] the single-GPU GEMM
+produces (or the caller consumes G shard-major).
+"""
+import sulimo_b200 as sb
+
+ROW_ALIGN = 8  # the GEMM needs a multiple of 8 output rows
+
+
+def shard_rows(f, world, align=ROW_ALIGN):
+    """Rows per shard (`fs`, a multiple of `align`) and the [r0, r1) range of every rank.
+
+    The last range may be shorter than fs; every range is non-empty."""
+    if f <= 0 or world <= 0:
+        raise ValueError("rows and world size must be positive")
+    fs = -(-f // world)
+    fs = -(-fs // align) * align
+    if (world - 1) * fs >= f:
+        raise ValueError(f"{f} rows cannot give {world} non-empty shards of {fs} rows")
+    return fs, [(r * fs, min(f, (r + 1) * fs)) for r in range(world)]
+
+
+def shard_weight(scales, quants, f, k, rank, world):
+    """This rank's rows of a Q4_0 SoA tensor (torch tensors: scales f16 bits, quants bytes),
+    padded to exactly fs rows with zero scales.  Returns (scales_r, quants_r, fs)."""
+    import torch
+    nb = k // 32
+    fs, ranges = shard_rows(f, world)
+    r0, r1 = ranges[rank]
+    sc = scales[r0 * nb:r1 * nb]
+    qu = quants[r0 * nb * 16:r1 * nb * 16]
+    if r1 - r0 < fs:
+        pad = fs - (r1 - r0)
+        sc = torch.cat([sc, torch.zeros(pad * nb, dtype=scales.dtype, device=scales.device)])
+        qu = torch.cat([qu, torch.zeros(pad * nb * 16, dtype=quants.dtype, device=quants.device)])
+    return sc.contiguous(), qu.contiguous(), fs
+
+
+class ShardedQ4Projection:
+    """Y[M][F] = X[M][K] W^T for a W[F][K] Q4_0 tensor split by rows over the process group."""
+
+    def __init__(self, ctx, scales_r, quants_r, f, k, fs, group=None):
+        import torch.distributed as dist
+        self.ctx, self.scales, self.quants = ctx, scales_r, quants_r
+        self.f, self.k, self.fs, self.group = f, k, fs, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+
+    def buffers(self, m, out_dtype=sb.OUT_F16):
+        """(gather buffer [world*m*fs], row-major output [m*F]) for m tokens."""
+        import torch
+        dt = torch.float16 if out_dtype == sb.OUT_F16 else torch.float32
+        g = torch.empty(self.world * m * self.fs, dtype=dt, device="cuda")
+        y = torch.empty(m * self.f, dtype=dt, device="cuda")
+        return g, y
+
+    def local_gemm(self, x, m, gather, out_dtype=sb.OUT_F16):
+        """This rank's rows into its slot of the shard-major buffer (no communication)."""
+        n = m * self.fs
+        slot = gather[self.rank * n:(self.rank + 1) * n]
+        sb.gemm_q4_0_f16(self.ctx, self.scales, self.quants, x, slot, self.fs, self.k, m,
+                         out_dtype)
+        return slot
+
+    def all_gather(self, m, gather):
+        """The exchange step: every rank's [m][fs] slot to every rank (in place, NCCL)."""
+        import torch.distributed as dist
+        if self.world == 1:
+            return
+        n = m * self.fs
+        dist.all_gather_into_tensor(gather, gather[self.rank * n:(self.rank + 1) * n],
+                                    group=self.group)
+
+    def forward(self, x, m, gather, y=None, out_dtype=sb.OUT_F16):
+        """GEMM + all-gather (+ row-major unshard when `y` is given).  Returns y or gather."""
+        self.local_gemm(x, m, gather, out_dtype)
+        self.all_gather(m, gather)
+        if y is None:
+            return gather
+        if self.world == 1 and self.fs == self.f:
+            y.copy_(gather)
+        else:
+            sb.unshard_rows(self.ctx, gather, y, self.world, m, self.fs, self.f)
+        return y
