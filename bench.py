@@ -545,7 +545,7 @@ def run_decode(args, rank, world, local):
     slot = cfg["head_count_kv"] * cfg["head_dim"] // 32 * 34
     scale = torch.tensor([0.02], dtype=torch.float16).view(torch.uint8).cuda()
     lines = []
-    for b in (1, 8, 32):
+    for b in args.decode_batches:
         dm = DecodeModel(ctx, w, batch=b)
         gen = torch.Generator(device="cuda")
         gen.manual_seed(100 + b)
@@ -605,6 +605,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--decode-batches", type=int, nargs="+", default=[1, 8, 32],
+                    help="--mode decode: sequences per GPU to measure")
     ap.add_argument("--mode", default="headline", choices=["headline", "sharded", "decode"],
                     help="headline: the contract line (config 2); sharded: the row-sharded "
                          "lm_head/FFN sweep with an NCCL all-gather; decode: config 4 "

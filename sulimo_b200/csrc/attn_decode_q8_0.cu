@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(ATT_THREADS)
                                float sm_scale, float softcap, float* __restrict__ part,
                                const __grid_constant__ CUtensorMap tmap_k,
                                const __grid_constant__ CUtensorMap tmap_v, int* __restrict__ err) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     using L = AttnLayout<HD>;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     // The dynamic region follows the static `red` array, so its base is only 16-byte aligned;
@@ -362,6 +364,8 @@ __global__ void __launch_bounds__(SLOT_THREADS)
                              const uint8_t* __restrict__ vring, size_t seq_stride,
                              size_t ctx_len, int H, int Hkv, int chunk, float sm_scale,
                              float softcap, float* __restrict__ part, int* __restrict__ err) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     using L = SlotLayout<HD, G>;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
@@ -568,6 +572,8 @@ template <int HD>
 __global__ void __launch_bounds__(COMBINE_THREADS)
     attn_decode_combine_kernel(const float* __restrict__ part, int H, int splits,
                                float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     constexpr int W = COMBINE_THREADS / 32;
     __shared__ float sm_m[W], sm_l[W], sm_o[W][32];
     const int h = blockIdx.x, seq = blockIdx.y, d = blockIdx.z * 32 + (threadIdx.x & 31);
@@ -655,13 +661,14 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
             slot_attr_mask |= sbit;
         }
         dim3 g1(splits, batch);
-        attn_decode_slots_kernel<HD, G><<<g1, SLOT_THREADS, bytes, ctx->stream>>>(
-            q, k, v, seq_stride, ctx_len, H, Hkv, chunk, sm_scale, softcap, part, ctx->d_error);
+        (void)launch_pdl(attn_decode_slots_kernel<HD, G>, g1, dim3(SLOT_THREADS), bytes,
+                         ctx->stream, q, k, v, seq_stride, ctx_len, H, Hkv, chunk, sm_scale,
+                         softcap, part, ctx->d_error);
         int st = check_cuda(cudaGetLastError(), "attn_decode_slots launch");
         if (st) return st;
         dim3 g2(H, batch, (HD + 31) / 32);
-        attn_decode_combine_kernel<HD><<<g2, COMBINE_THREADS, 0, ctx->stream>>>(part, H, splits,
-                                                                                out);
+        (void)launch_pdl(attn_decode_combine_kernel<HD>, g2, dim3(COMBINE_THREADS), 0, ctx->stream,
+                         (const float*)part, H, splits, out);
         ctx->launches += 2;
         return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
     }
@@ -705,19 +712,19 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
     }
     dim3 g1(splits, Hkv, batch);
     if (tma)
-        attn_decode_partial_kernel<HD, G, true>
-            <<<g1, ATT_THREADS, L::tma_bytes(chunk) + ATT_SMEM_SLACK, ctx->stream>>>(
-                q, k, v, seq_stride, capacity, ctx_len, H, Hkv, chunk, sm_scale, softcap, part,
-                tk, tv, ctx->d_error);
+        (void)launch_pdl(attn_decode_partial_kernel<HD, G, true>, g1, dim3(ATT_THREADS),
+                         L::tma_bytes(chunk) + ATT_SMEM_SLACK, ctx->stream, q, k, v, seq_stride,
+                         capacity, ctx_len, H, Hkv, chunk, sm_scale, softcap, part, tk, tv,
+                         ctx->d_error);
     else
-        attn_decode_partial_kernel<HD, G, false><<<g1, ATT_THREADS, L::bytes + ATT_SMEM_SLACK,
-                                                   ctx->stream>>>(
-            q, k, v, seq_stride, capacity, ctx_len, H, Hkv, chunk, sm_scale, softcap, part, tk, tv,
-            ctx->d_error);
+        (void)launch_pdl(attn_decode_partial_kernel<HD, G, false>, g1, dim3(ATT_THREADS),
+                         L::bytes + ATT_SMEM_SLACK, ctx->stream, q, k, v, seq_stride, capacity,
+                         ctx_len, H, Hkv, chunk, sm_scale, softcap, part, tk, tv, ctx->d_error);
     int st = check_cuda(cudaGetLastError(), "attn_decode_partial launch");
     if (st) return st;
     dim3 g2(H, batch, (HD + 31) / 32);
-    attn_decode_combine_kernel<HD><<<g2, COMBINE_THREADS, 0, ctx->stream>>>(part, H, splits, out);
+    (void)launch_pdl(attn_decode_combine_kernel<HD>, g2, dim3(COMBINE_THREADS), 0, ctx->stream,
+                     (const float*)part, H, splits, out);
     ctx->launches += 2;
     return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
 }

@@ -2,10 +2,11 @@
 // the reference's forward_token (crates/sulimo-engine/src/forward_pass.rs:190-417) for a batch
 // of independent sequences that sit at the same position.
 //
-// Per layer (14 launches, all on the context's stream, no host synchronisation):
+// Per layer (11 launches, all on the context's stream, no host synchronisation, each a
+// programmatic dependent of the previous one):
 //   add_rmsnorm_q8     x (+= previous FFN output), h = rmsnorm(x)*attn_norm -> Q8_0
 //                      (apply_rmsnorm :493-507 + quantize_f32_to_q8_0)
-//   3x GEMV            q, k, v = W . h (dispatch_matvec_q4_0_q8_0, bit-exact AVX2 order)
+//   GEMV (one launch)  q, k, v = W . h (dispatch_matvec_q4_0_q8_0, bit-exact AVX2 order)
 //   qkv_rope_store     + biases (add_bias :452-465), RoPE Norm/Neox per head
 //                      (rope_head_scalar, scalar.rs:92-130), K/V quantized into ring slot
 //                      pos % capacity (KvCache::store_key/store_value, kv_cache.rs:93-110)
@@ -14,7 +15,7 @@
 //   quantize           attention output -> Q8_0
 //   GEMV               o = Wo . a
 //   add_rmsnorm_q8     x += o, h = rmsnorm(x)*ffn_norm -> Q8_0
-//   2x GEMV            gate, up
+//   GEMV (one launch)  gate, up
 //   swiglu_q8          silu(gate)*up -> Q8_0 (swiglu_scalar, scalar.rs:161-170)
 //   GEMV               down
 // then add_rmsnorm_q8 with the output norm and the vocab GEMV (logits, fp32).
@@ -29,6 +30,7 @@ namespace sulimo {
 namespace {
 
 constexpr int GLUE_THREADS = 256;
+constexpr int NORM_THREADS = 1024;  // one CTA per sequence: the whole vector in one pass
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
@@ -49,10 +51,12 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // One CTA per sequence.  x[seq][E] (+= delta[seq][E] when delta is given, written back), then
 // y = (x * 1/sqrt(mean(x^2) + eps)) * w, quantized to Q8_0 (E/32 blocks) into q8[seq].
-__global__ void __launch_bounds__(GLUE_THREADS)
+__global__ void __launch_bounds__(NORM_THREADS)
     add_rmsnorm_q8_kernel(float* __restrict__ x, const float* __restrict__ delta,
                           const float* __restrict__ w, int E, float eps,
                           uint8_t* __restrict__ q8) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     extern __shared__ float sx[];  // E floats + 33 reduction slots
     float* red = sx + E;
     const int seq = blockIdx.x;
@@ -97,6 +101,8 @@ __global__ void __launch_bounds__(GLUE_THREADS)
                           const float* __restrict__ bv, int H, int Hkv, int hd, int rope_dim,
                           int mode, float base, size_t pos, uint8_t* __restrict__ k_ring,
                           uint8_t* __restrict__ v_ring, size_t capacity, size_t seq_stride) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     const int seq = blockIdx.x;
     const int qd = H * hd, kvd = Hkv * hd, half = rope_dim / 2;
     float* qs = q + (size_t)seq * qd;
@@ -108,15 +114,20 @@ __global__ void __launch_bounds__(GLUE_THREADS)
         if (bk) ks[i] = __fadd_rn(ks[i], bk[i]);
         if (bv) vs[i] = __fadd_rn(vs[i], bv[i]);
     }
+    // the rotation angle depends on the pair index only: one cos/sin per pair for all heads
+    __shared__ float rc[128], rs[128];
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float freq = __fdiv_rn(1.0f, powf(base, __fdiv_rn((float)(2 * i), (float)rope_dim)));
+        const float theta = __fmul_rn((float)pos, freq);
+        rc[i] = cosf(theta);
+        rs[i] = sinf(theta);
+    }
     __syncthreads();
     // one thread per (head, pair)
     for (int t = threadIdx.x; t < (H + Hkv) * half; t += blockDim.x) {
         const int head = t / half, i = t - head * half;
-        const float freq = __fdiv_rn(1.0f, powf(base, __fdiv_rn((float)(2 * i), (float)rope_dim)));
-        const float theta = __fmul_rn((float)pos, freq);
-        const float c = cosf(theta), s = sinf(theta);
         float* hv = head < H ? qs + head * hd : ks + (head - H) * hd;
-        rope_pair(hv, i, half, mode, c, s);
+        rope_pair(hv, i, half, mode, rc[i], rs[i]);
     }
     __syncthreads();
     const size_t slot = pos % capacity;
@@ -136,6 +147,8 @@ __global__ void __launch_bounds__(GLUE_THREADS)
 __global__ void __launch_bounds__(GLUE_THREADS)
     swiglu_q8_kernel(const float* __restrict__ gate, const float* __restrict__ up, size_t nblocks,
                      uint8_t* __restrict__ q8) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     const int lane = threadIdx.x & 31;
     size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (b >= nblocks) return;
@@ -147,6 +160,8 @@ __global__ void __launch_bounds__(GLUE_THREADS)
 // First index of the maximum of each row (greedy sampling); NaN never wins.
 __global__ void __launch_bounds__(GLUE_THREADS)
     argmax_rows_kernel(const float* __restrict__ x, int cols, int32_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     __shared__ float bv[GLUE_THREADS / 32];
     __shared__ int bi[GLUE_THREADS / 32];
     const float* r = x + (size_t)blockIdx.x * cols;
@@ -226,7 +241,8 @@ size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch) {
 }
 
 int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out) {
-    argmax_rows_kernel<<<rows, GLUE_THREADS, 0, ctx->stream>>>(x, cols, out);
+    (void)launch_pdl(argmax_rows_kernel, dim3(rows), dim3(GLUE_THREADS), 0, ctx->stream, x, cols,
+                     out);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "argmax_rows launch");
 }
@@ -265,19 +281,28 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
     const float* pending = nullptr;  // the previous layer's FFN output, added to x next
     for (int l = 0; l < m->n_layers; l++) {
         const sulimo_layer_desc& L = m->layers[l];
-        add_rmsnorm_q8_kernel<<<batch, GLUE_THREADS, norm_smem, ctx->stream>>>(
-            s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E, m->eps, s.q8);
+        (void)launch_pdl(add_rmsnorm_q8_kernel, dim3(batch), dim3(NORM_THREADS), norm_smem,
+                         ctx->stream, s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E,
+                         m->eps, s.q8);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
-        if ((st = launch_gemv_q4_0_q8_0(ctx, L.wq_scales, L.wq_quants, s.q8, qd, E, batch, s.q)) ||
-            (st = launch_gemv_q4_0_q8_0(ctx, L.wk_scales, L.wk_quants, s.q8, kvd, E, batch, s.k)) ||
-            (st = launch_gemv_q4_0_q8_0(ctx, L.wv_scales, L.wv_quants, s.q8, kvd, E, batch, s.v)))
-            return st;
-        qkv_rope_store_kernel<<<batch, GLUE_THREADS, 0, ctx->stream>>>(
-            s.q, s.k, s.v, reinterpret_cast<const float*>(L.bq),
-            reinterpret_cast<const float*>(L.bk), reinterpret_cast<const float*>(L.bv), H, Hkv, hd,
-            m->rope_dim, m->rope_mode, m->rope_base, pos, reinterpret_cast<uint8_t*>(L.k_ring),
-            reinterpret_cast<uint8_t*>(L.v_ring), m->kv_capacity, m->kv_seq_stride);
+        {  // q, k, v in one launch
+            const GemvMatSrc g[3] = {{L.wq_scales, L.wq_quants, s.q, qd},
+                                     {L.wk_scales, L.wk_quants, s.k, kvd},
+                                     {L.wv_scales, L.wv_quants, s.v, kvd}};
+            bool done = false;
+            if ((st = launch_gemv_group(ctx, g, 3, s.q8, E, batch, &done))) return st;
+            for (int i = 0; i < 3 && !done; i++)
+                if ((st = launch_gemv_q4_0_q8_0(ctx, g[i].scales, g[i].quants, s.q8, g[i].rows, E,
+                                                batch, g[i].out)))
+                    return st;
+        }
+        (void)launch_pdl(qkv_rope_store_kernel, dim3(batch), dim3(GLUE_THREADS), 0, ctx->stream,
+                         s.q, s.k, s.v, reinterpret_cast<const float*>(L.bq),
+                         reinterpret_cast<const float*>(L.bk), reinterpret_cast<const float*>(L.bv),
+                         H, Hkv, hd, m->rope_dim, m->rope_mode, m->rope_base, pos,
+                         reinterpret_cast<uint8_t*>(L.k_ring), reinterpret_cast<uint8_t*>(L.v_ring),
+                         m->kv_capacity, m->kv_seq_stride);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
         if ((st = launch_attn_decode(ctx, s.q, L.k_ring, L.v_ring, m->kv_seq_stride,
@@ -287,24 +312,32 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
             (st = launch_quantize_q8_0(ctx, s.att, s.q8, (size_t)batch * qd)) ||
             (st = launch_gemv_q4_0_q8_0(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
             return st;
-        add_rmsnorm_q8_kernel<<<batch, GLUE_THREADS, norm_smem, ctx->stream>>>(
-            s.x, s.o, reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, s.q8);
+        (void)launch_pdl(add_rmsnorm_q8_kernel, dim3(batch), dim3(NORM_THREADS), norm_smem,
+                         ctx->stream, s.x, (const float*)s.o,
+                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, s.q8);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
-        if ((st = launch_gemv_q4_0_q8_0(ctx, L.wg_scales, L.wg_quants, s.q8, F, E, batch, s.g)) ||
-            (st = launch_gemv_q4_0_q8_0(ctx, L.wu_scales, L.wu_quants, s.q8, F, E, batch, s.u)))
-            return st;
+        {  // gate and up in one launch
+            const GemvMatSrc g[2] = {{L.wg_scales, L.wg_quants, s.g, F},
+                                     {L.wu_scales, L.wu_quants, s.u, F}};
+            bool done = false;
+            if ((st = launch_gemv_group(ctx, g, 2, s.q8, E, batch, &done))) return st;
+            for (int i = 0; i < 2 && !done; i++)
+                if ((st = launch_gemv_q4_0_q8_0(ctx, g[i].scales, g[i].quants, s.q8, g[i].rows, E,
+                                                batch, g[i].out)))
+                    return st;
+        }
         const size_t nblk = (size_t)batch * F / 32;
-        swiglu_q8_kernel<<<(unsigned)((nblk + 7) / 8), GLUE_THREADS, 0, ctx->stream>>>(
-            s.g, s.u, nblk, s.q8);
+        (void)launch_pdl(swiglu_q8_kernel, dim3((unsigned)((nblk + 7) / 8)), dim3(GLUE_THREADS), 0,
+                         ctx->stream, (const float*)s.g, (const float*)s.u, nblk, s.q8);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "swiglu_q8 launch"))) return st;
         if ((st = launch_gemv_q4_0_q8_0(ctx, L.wd_scales, L.wd_quants, s.q8, E, F, batch, s.o)))
             return st;
         pending = s.o;
     }
-    add_rmsnorm_q8_kernel<<<batch, GLUE_THREADS, norm_smem, ctx->stream>>>(
-        s.x, pending, m->out_norm, E, m->eps, s.q8);
+    (void)launch_pdl(add_rmsnorm_q8_kernel, dim3(batch), dim3(NORM_THREADS), norm_smem,
+                     ctx->stream, s.x, pending, m->out_norm, E, m->eps, s.q8);
     ctx->launches++;
     if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
     return launch_gemv_q4_0_q8_0(ctx, m->out_scales, m->out_quants, s.q8, m->vocab, E, batch,

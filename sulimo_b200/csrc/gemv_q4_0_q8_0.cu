@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_q4_0_q8_0_kernel(const uint16_t* __restrict__ wsc, const uint8_t* __restrict__ wq,
                           const uint8_t* __restrict__ xq8, int rows, int nb, int batch,
                           float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     __shared__ GemvSmem sm;
     const int tid = threadIdx.x;
     const int vec = blockIdx.x % batch;
@@ -132,72 +134,102 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 // ---------------------------------------------------------------------------------------------
 // Streaming form for K a multiple of 256 and 16-byte aligned scales (every BASELINE shape).
 //
-// CTA: 64 rows x 4 threads per row (thread p of a row owns AVX2 lanes 2p and 2p+1, i.e. quant
-// word p of every block) + 1 producer warp.  The producer streams the rows' quants and scales
-// through a ring of TS stages of 8 blocks with TMA (quants 128-byte swizzled, so the 4 word reads
-// of 8 rows hit 32 distinct banks); the activations of NV vectors are packed into per-lane words
-// in shared memory once per CTA.  Each thread keeps 2 x NV fp32 lane accumulators and applies
-// exactly the AVX2 FMA sequence; the row's 8 lanes are combined with hsum_256's tree through
-// shuffles inside the 4-thread group.
-constexpr int TS_ROWS = 64;
+// CTA: ROWS rows (64, 32 or 16: chosen so the launch covers the SMs) x 4 threads per row
+// (thread p of a row owns AVX2 lanes 2p and 2p+1, i.e. quant word p of every block) + 1 producer
+// warp.  The producer streams the rows' quants and scales through a ring of TS stages of 8
+// blocks with TMA (quants 128-byte swizzled, so the 4 word reads of 8 rows hit 32 distinct
+// banks); the activations of NV vectors are packed into per-lane words in shared memory once
+// per CTA.  Each thread keeps 2 x NV fp32 lane accumulators and applies exactly the AVX2 FMA
+// sequence; the row's 8 lanes are combined with hsum_256's tree through shuffles inside the
+// 4-thread group.  One launch can cover up to three matrices that share the activations (the
+// decode step's q/k/v and gate/up projections): the CTA index picks the matrix.
 constexpr int TS_BLOCKS = 8;                     // Q4_0 blocks per stage (K = 256)
 constexpr int TS_STAGES = 8;
-constexpr int TS_THREADS = TS_ROWS * 4 + 32;     // + producer warp
-constexpr uint32_t TS_Q_BYTES = TS_ROWS * TS_BLOCKS * 16;  // 8 KB
-constexpr uint32_t TS_S_BYTES = TS_ROWS * TS_BLOCKS * 2;   // 1 KB
-constexpr uint32_t TS_STAGE_BYTES = TS_Q_BYTES + TS_S_BYTES;
+constexpr int TS_MAX_MATS = 3;
+
+// Shared memory: the stages' quant tiles first (each ROWS x 128 bytes, a multiple of the
+// 1024-byte swizzle atom, so every tile starts on an atom), then the stages' scale tiles.
+template <int ROWS>
+struct TsShape {
+    static constexpr int THREADS = ROWS * 4 + 32;  // + producer warp
+    static constexpr uint32_t Q_BYTES = ROWS * TS_BLOCKS * 16;
+    static constexpr uint32_t S_BYTES = ROWS * TS_BLOCKS * 2;
+    static constexpr uint32_t STAGE_BYTES = Q_BYTES + S_BYTES;
+    static_assert(Q_BYTES % 1024 == 0, "swizzled quant tiles must start on 1024-byte atoms");
+};
+
+struct GemvMat {
+    CUtensorMap q, s;  // quants [rows][nb*16] (128-byte swizzle), scales [rows][nb] (u16)
+    float* out;        // [batch][rows]
+    int rows, tile0;   // first CTA (x) index of this matrix
+};
+
+struct GemvGroup {
+    GemvMat m[TS_MAX_MATS];
+    int count;
+};
 
 // exact int -> float for |s| < 2^22: 1.5*2^23 + s has an integer ulp
 __device__ __forceinline__ float small_int_to_float(int s) {
     return __fsub_rn(__int_as_float(0x4B400000 + s), 12582912.0f);
 }
 
-template <int NV>
-__global__ void __launch_bounds__(TS_THREADS, 1)
-    gemv_q4_0_q8_0_tma_kernel(const __grid_constant__ CUtensorMap tmap_q,
-                              const __grid_constant__ CUtensorMap tmap_s,
-                              const uint8_t* __restrict__ xq8, int rows, int nb, int batch,
-                              float* __restrict__ out, int* __restrict__ err) {
+template <int NV, int ROWS>
+__global__ void __launch_bounds__(TsShape<ROWS>::THREADS)
+    gemv_q4_0_q8_0_tma_kernel(const __grid_constant__ GemvGroup grp,
+                              const uint8_t* __restrict__ xq8, int nb, int batch,
+                              int* __restrict__ err) {
+    using T = TsShape<ROWS>;
+    pdl_launch_dependents();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-    uint8_t* stages = sm;                                            // TS_STAGES x stage
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + TS_STAGES * TS_STAGE_BYTES);
+    uint8_t* qtiles = sm;                                   // TS_STAGES x Q_BYTES
+    uint8_t* stiles = sm + TS_STAGES * T::Q_BYTES;          // TS_STAGES x S_BYTES
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + TS_STAGES * T::STAGE_BYTES);
     uint64_t* empty = full + TS_STAGES;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + TS_STAGES);
     int* xw = reinterpret_cast<int*>(empty + TS_STAGES + 1);        // [NV][nb][8]
     int* xc = xw + NV * nb * 8;                                      // [NV][nb][8]
     float* xs = reinterpret_cast<float*>(xc + NV * nb * 8);          // [NV][nb]
 
+    int mi = 0;
+#pragma unroll
+    for (int i = 1; i < TS_MAX_MATS; i++)
+        if (i < grp.count && (int)blockIdx.x >= grp.m[i].tile0) mi = i;
+    const GemvMat& M = grp.m[mi];
+    const int rows = M.rows;
     const int tid = threadIdx.x;
-    const int row0 = blockIdx.x * TS_ROWS;
+    const int row0 = ((int)blockIdx.x - M.tile0) * ROWS;
     const int v0 = blockIdx.y * NV;
     const int nchunks = nb / TS_BLOCKS;
 
     if (tid == 0) {
         for (int s = 0; s < TS_STAGES; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], TS_ROWS * 4);
+            mbar_init(&empty[s], ROWS * 4);
         }
         *abort_flag = 0;
         fence_barrier_init();
+        prefetch_tensormap(&M.q);
+        prefetch_tensormap(&M.s);
     }
+    // weights are not written by the previous kernel of a decode step, but wait anyway before
+    // any global access: the activations are
+    pdl_wait_prerequisites();
     __syncthreads();
 
-    if (tid >= TS_ROWS * 4) {
+    if (tid >= ROWS * 4) {
         // ------------------------------ producer warp ------------------------------
-        if (tid == TS_ROWS * 4) {
-            prefetch_tensormap(&tmap_q);
-            prefetch_tensormap(&tmap_s);
+        if (tid == ROWS * 4) {
             int issued = 0;
             for (int c = 0; c < nchunks; c++) {
                 const int s = c % TS_STAGES;
                 const uint32_t ph = (uint32_t)(c / TS_STAGES) & 1u;
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
-                uint8_t* st = stages + s * TS_STAGE_BYTES;
-                mbar_arrive_expect_tx(&full[s], TS_STAGE_BYTES);
-                tma_load_2d(st, &tmap_q, c * TS_BLOCKS * 16, row0, &full[s]);
-                tma_load_2d(st + TS_Q_BYTES, &tmap_s, c * TS_BLOCKS, row0, &full[s]);
+                mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
+                tma_load_2d(qtiles + s * T::Q_BYTES, &M.q, c * TS_BLOCKS * 16, row0, &full[s]);
+                tma_load_2d(stiles + s * T::S_BYTES, &M.s, c * TS_BLOCKS, row0, &full[s]);
                 issued = c + 1;
             }
             if (*abort_flag)  // the issued copies must land before the CTA releases its smem
@@ -209,7 +241,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     }
 
     // ---- pack the activations: lane j of block b -> {x[2j],x[2j+1],x[16+2j],x[17+2j]} ----
-    for (int it = tid; it < NV * nb * 8; it += TS_ROWS * 4) {
+    for (int it = tid; it < NV * nb * 8; it += ROWS * 4) {
         const int v = it / (nb * 8), rem = it - v * nb * 8;
         const int b = rem >> 3, j = rem & 7;
         uint32_t w = 0;
@@ -226,7 +258,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         xc[it] = -8 * sum;
         if (j == 0) xs[v * nb + b] = d;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(TS_ROWS * 4) : "memory");  // consumers only
+    asm volatile("bar.sync 1, %0;" ::"r"(ROWS * 4) : "memory");  // consumers only
 
     const int rl = tid >> 2, p = tid & 3;
     float acc[NV][2];
@@ -237,9 +269,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const int s = c % TS_STAGES;
         const uint32_t ph = (uint32_t)(c / TS_STAGES) & 1u;
         if (!mbar_wait_bounded(&full[s], ph, err, abort_flag)) break;
-        const uint8_t* qst = stages + s * TS_STAGE_BYTES + rl * 128;
-        const uint16_t* sst =
-            reinterpret_cast<const uint16_t*>(stages + s * TS_STAGE_BYTES + TS_Q_BYTES) + rl * 8;
+        const uint8_t* qst = qtiles + s * T::Q_BYTES + rl * 128;
+        const uint16_t* sst = reinterpret_cast<const uint16_t*>(stiles + s * T::S_BYTES) + rl * 8;
 #pragma unroll
         for (int b = 0; b < TS_BLOCKS; b++) {
             const int kb = c * TS_BLOCKS + b;
@@ -274,76 +305,117 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const float w = __fadd_rn(u0, u1);
         const float r = __fadd_rn(w, __shfl_xor_sync(0xffffffffu, w, 1));
         if (p == 0 && row < rows && v0 + v < batch && !*abort_flag)
-            out[(size_t)(v0 + v) * rows + row] = r;
+            M.out[(size_t)(v0 + v) * rows + row] = r;
     }
 }
 
-template <int NV>
+template <int NV, int ROWS>
 size_t gemv_tma_smem(int nb) {
-    return 1024 + (size_t)TS_STAGES * TS_STAGE_BYTES + 8 * (2 * TS_STAGES + 1) +
+    return 1024 + (size_t)TS_STAGES * TsShape<ROWS>::STAGE_BYTES + 8 * (2 * TS_STAGES + 1) +
            (size_t)NV * nb * (8 * 4 * 2 + 4);
 }
 
-template <int NV>
-int launch_gemv_tma(sulimo_ctx* ctx, const CUtensorMap& tq, const CUtensorMap& ts,
-                    const uint8_t* xq8, int rows, int nb, int batch, float* out) {
-    const size_t smem = gemv_tma_smem<NV>(nb);
+template <int NV, int ROWS>
+int launch_gemv_tma(sulimo_ctx* ctx, const GemvGroup& grp, int tiles, const uint8_t* xq8, int nb,
+                    int batch) {
+    const size_t smem = gemv_tma_smem<NV, ROWS>(nb);
     static uint64_t attr_mask = 0;  // per device
     const uint64_t bit = 1ull << (ctx->device & 63);
     if (!(attr_mask & bit)) {
-        int st = check_cuda(cudaFuncSetAttribute(gemv_q4_0_q8_0_tma_kernel<NV>,
+        int st = check_cuda(cudaFuncSetAttribute(gemv_q4_0_q8_0_tma_kernel<NV, ROWS>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  227 * 1024),
                             "gemv smem attribute");
         if (st) return st;
         attr_mask |= bit;
     }
-    dim3 grid((rows + TS_ROWS - 1) / TS_ROWS, (batch + NV - 1) / NV);
-    gemv_q4_0_q8_0_tma_kernel<NV><<<grid, TS_THREADS, smem, ctx->stream>>>(
-        tq, ts, xq8, rows, nb, batch, out, ctx->d_error);
+    dim3 grid((unsigned)tiles, (batch + NV - 1) / NV);
+    (void)launch_pdl(gemv_q4_0_q8_0_tma_kernel<NV, ROWS>, grid, dim3(TsShape<ROWS>::THREADS), smem,
+                     ctx->stream, grp, xq8, nb, batch, ctx->d_error);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "gemv_q4_0_q8_0_tma launch");
 }
 
+template <int ROWS>
+int launch_gemv_tma_rows(sulimo_ctx* ctx, GemvGroup& grp, const GemvMatSrc* src, int count,
+                         const uint8_t* xq8, int nb, int batch, int nv) {
+    int tiles = 0;
+    for (int i = 0; i < count; i++) {
+        GemvMat& M = grp.m[i];
+        const uint64_t qd[2] = {(uint64_t)nb * 16, (uint64_t)src[i].rows};
+        const uint64_t qs[1] = {(uint64_t)nb * 16};
+        const uint32_t qb[2] = {TS_BLOCKS * 16, (uint32_t)ROWS};
+        int st = encode_tensor_map(&M.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, src[i].quants, 2, qd, qs,
+                                   qb, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+        const uint64_t sd[2] = {(uint64_t)nb, (uint64_t)src[i].rows};
+        const uint64_t ss[1] = {(uint64_t)nb * 2};
+        const uint32_t sbx[2] = {TS_BLOCKS, (uint32_t)ROWS};
+        st = encode_tensor_map(&M.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, src[i].scales, 2, sd, ss, sbx,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+        M.out = src[i].out;
+        M.rows = src[i].rows;
+        M.tile0 = tiles;
+        tiles += (src[i].rows + ROWS - 1) / ROWS;
+    }
+    for (int i = count; i < TS_MAX_MATS; i++) grp.m[i] = grp.m[0];
+    grp.count = count;
+    switch (nv) {
+        case 8: return launch_gemv_tma<8, ROWS>(ctx, grp, tiles, xq8, nb, batch);
+        case 4: return launch_gemv_tma<4, ROWS>(ctx, grp, tiles, xq8, nb, batch);
+        case 2: return launch_gemv_tma<2, ROWS>(ctx, grp, tiles, xq8, nb, batch);
+        default: return launch_gemv_tma<1, ROWS>(ctx, grp, tiles, xq8, nb, batch);
+    }
+}
+
 }  // namespace
+
+// Streams 1..3 matrices of the same K against the same activations in one launch; false when
+// the streaming form does not apply (K not a multiple of 256, scales not 16-byte aligned,
+// activations too large for shared memory).
+int launch_gemv_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const void* x_q8,
+                      int cols, int batch, bool* handled) {
+    *handled = false;
+    const int nb = cols / 32;
+    if (count < 1 || count > TS_MAX_MATS || nb % TS_BLOCKS != 0) return SULIMO_OK;
+    int total_rows = 0;
+    for (int i = 0; i < count; i++) {
+        if (((uintptr_t)src[i].scales % 16) != 0 || src[i].rows <= 0) return SULIMO_OK;
+        total_rows += src[i].rows;
+    }
+    int nv = 8;  // vectors per weight pass: <= batch, packed activations <= 96 KB
+    while (nv > 1 && (nv > batch || (size_t)nv * nb * 68 > 96 * 1024)) nv >>= 1;
+    if ((size_t)nv * nb * 68 > 96 * 1024) return SULIMO_OK;
+    *handled = true;
+    // rows per CTA: 64 unless that leaves more than half of the SMs idle (measured: 32-row
+    // tiles make the one-wave 8960-row config-1 matvec ~1.4x slower, so narrower tiles only
+    // serve the small decode matrices)
+    const int vec_groups = (batch + nv - 1) / nv;
+    const uint8_t* x = reinterpret_cast<const uint8_t*>(x_q8);
+    GemvGroup grp;
+    const size_t half_sms = (size_t)ctx->num_sms / 2;
+    if ((size_t)(total_rows / 64) * vec_groups >= half_sms)
+        return launch_gemv_tma_rows<64>(ctx, grp, src, count, x, nb, batch, nv);
+    if ((size_t)(total_rows / 32) * vec_groups >= half_sms)
+        return launch_gemv_tma_rows<32>(ctx, grp, src, count, x, nb, batch, nv);
+    return launch_gemv_tma_rows<16>(ctx, grp, src, count, x, nb, batch, nv);
+}
 
 int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                           const void* x_q8, int rows, int cols, int batch, float* out) {
     const int nb = cols / 32;
-    // streaming form: K multiple of 256, 16-byte aligned scales, activations of up to 8 vectors
-    // packed in <= 96 KB of shared memory
-    if (nb % TS_BLOCKS == 0 && ((uintptr_t)w_scales % 16) == 0 && rows > 0) {
-        int nv = 8;  // vectors per weight pass: <= batch, packed activations <= 96 KB
-        while (nv > 1 && (nv > batch || (size_t)nv * nb * 68 > 96 * 1024)) nv >>= 1;
-        if ((size_t)nv * nb * 68 <= 96 * 1024) {
-            CUtensorMap tq, ts;
-            const uint64_t qd[2] = {(uint64_t)nb * 16, (uint64_t)rows};
-            const uint64_t qs[1] = {(uint64_t)nb * 16};
-            const uint32_t qb[2] = {TS_BLOCKS * 16, TS_ROWS};
-            int st = encode_tensor_map(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_quants, 2, qd, qs, qb,
-                                       CU_TENSOR_MAP_SWIZZLE_128B);
-            if (st) return st;
-            const uint64_t sd[2] = {(uint64_t)nb, (uint64_t)rows};
-            const uint64_t ss[1] = {(uint64_t)nb * 2};
-            const uint32_t sbx[2] = {TS_BLOCKS, TS_ROWS};
-            st = encode_tensor_map(&ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, w_scales, 2, sd, ss, sbx,
-                                   CU_TENSOR_MAP_SWIZZLE_NONE);
-            if (st) return st;
-            const uint8_t* x = reinterpret_cast<const uint8_t*>(x_q8);
-            switch (nv) {
-                case 8: return launch_gemv_tma<8>(ctx, tq, ts, x, rows, nb, batch, out);
-                case 4: return launch_gemv_tma<4>(ctx, tq, ts, x, rows, nb, batch, out);
-                case 2: return launch_gemv_tma<2>(ctx, tq, ts, x, rows, nb, batch, out);
-                default: return launch_gemv_tma<1>(ctx, tq, ts, x, rows, nb, batch, out);
-            }
-        }
-    }
+    const GemvMatSrc src = {w_scales, w_quants, out, rows};
+    bool handled = false;
+    const int st = launch_gemv_group(ctx, &src, 1, x_q8, cols, batch, &handled);
+    if (handled || st) return st;
     const size_t tiles = ((size_t)rows + GEMV_ROWS - 1) / GEMV_ROWS;
     const size_t grid = tiles * (size_t)batch;
     if (grid > 0x7fffffffu) return set_error(SULIMO_EINVAL, "gemv grid too large");
-    gemv_q4_0_q8_0_kernel<<<(unsigned)grid, GEMV_THREADS, 0, ctx->stream>>>(
-        reinterpret_cast<const uint16_t*>(w_scales), reinterpret_cast<const uint8_t*>(w_quants),
-        reinterpret_cast<const uint8_t*>(x_q8), rows, nb, batch, out);
+    (void)launch_pdl(gemv_q4_0_q8_0_kernel, dim3((unsigned)grid), dim3(GEMV_THREADS), 0,
+                     ctx->stream, reinterpret_cast<const uint16_t*>(w_scales),
+                     reinterpret_cast<const uint8_t*>(w_quants),
+                     reinterpret_cast<const uint8_t*>(x_q8), rows, nb, batch, out);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "gemv_q4_0_q8_0 launch");
 }

@@ -16,6 +16,8 @@ namespace {
 __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float* __restrict__ src,
                                                             uint8_t* __restrict__ dst,
                                                             size_t nblocks) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     const int lane = threadIdx.x & 31;
     size_t w = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const size_t stride = (size_t)gridDim.x * (blockDim.x / 32);
@@ -35,6 +37,8 @@ __global__ void __launch_bounds__(256) kv_store_q8_0_kernel(const T* __restrict_
                                                             uint8_t* __restrict__ kv,
                                                             size_t start_pos, size_t capacity,
                                                             size_t bpp, size_t n) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     const int lane = threadIdx.x & 31;
     size_t w = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const size_t stride = (size_t)gridDim.x * (blockDim.x / 32);
@@ -53,6 +57,8 @@ __global__ void __launch_bounds__(256) dequant_rows_kernel(const uint16_t* __res
                                                            const uint8_t* __restrict__ quants,
                                                            int nb, const int32_t* __restrict__ rows,
                                                            int count, void* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     size_t total = (size_t)count * nb * 16;
     if (idx >= total) return;
@@ -82,6 +88,8 @@ __global__ void __launch_bounds__(256) dequant_rows_kernel(const uint16_t* __res
 __global__ void __launch_bounds__(256) block_sums_kernel(const uint8_t* __restrict__ wq,
                                                          const uint8_t* __restrict__ xq8, int rows,
                                                          int nb, int32_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
     size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (size_t)rows * nb) return;
     int b = (int)(idx % nb);
@@ -105,8 +113,9 @@ int grid_for(size_t warps_needed, int num_sms) {
 
 int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n) {
     size_t nb = n / 32;
-    quantize_q8_0_kernel<<<grid_for(nb, ctx->num_sms), 256, 0, ctx->stream>>>(
-        src, reinterpret_cast<uint8_t*>(dst), nb);
+    cudaError_t le = launch_pdl(quantize_q8_0_kernel, dim3(grid_for(nb, ctx->num_sms)), dim3(256),
+                                0, ctx->stream, src, reinterpret_cast<uint8_t*>(dst), nb);
+    if (le != cudaSuccess) return check_cuda(le, "quantize_q8_0 launch");
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "quantize_q8_0 launch");
 }
@@ -115,13 +124,13 @@ int launch_kv_store_q8_0(sulimo_ctx* ctx, const void* act, int act_dtype, void* 
                          size_t start_pos, size_t capacity, size_t bpp, size_t n) {
     int g = grid_for(n * bpp, ctx->num_sms);
     if (act_dtype == SULIMO_ACT_F16)
-        kv_store_q8_0_kernel<__half><<<g, 256, 0, ctx->stream>>>(
-            reinterpret_cast<const __half*>(act), reinterpret_cast<uint8_t*>(kv), start_pos,
-            capacity, bpp, n);
+        (void)launch_pdl(kv_store_q8_0_kernel<__half>, dim3(g), dim3(256), 0, ctx->stream,
+                         reinterpret_cast<const __half*>(act), reinterpret_cast<uint8_t*>(kv),
+                         start_pos, capacity, bpp, n);
     else
-        kv_store_q8_0_kernel<float><<<g, 256, 0, ctx->stream>>>(
-            reinterpret_cast<const float*>(act), reinterpret_cast<uint8_t*>(kv), start_pos,
-            capacity, bpp, n);
+        (void)launch_pdl(kv_store_q8_0_kernel<float>, dim3(g), dim3(256), 0, ctx->stream,
+                         reinterpret_cast<const float*>(act), reinterpret_cast<uint8_t*>(kv),
+                         start_pos, capacity, bpp, n);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "kv_store_q8_0 launch");
 }
@@ -132,13 +141,13 @@ int launch_dequant_rows(sulimo_ctx* ctx, const void* scales, const void* quants,
     size_t total = (size_t)count * nb * 16;
     int g = (int)((total + 255) / 256);
     if (out_dtype == SULIMO_OUT_F16)
-        dequant_rows_kernel<true><<<g, 256, 0, ctx->stream>>>(
-            reinterpret_cast<const uint16_t*>(scales), reinterpret_cast<const uint8_t*>(quants),
-            nb, row_ids, count, out);
+        (void)launch_pdl(dequant_rows_kernel<true>, dim3(g), dim3(256), 0, ctx->stream,
+                         reinterpret_cast<const uint16_t*>(scales),
+                         reinterpret_cast<const uint8_t*>(quants), nb, row_ids, count, out);
     else
-        dequant_rows_kernel<false><<<g, 256, 0, ctx->stream>>>(
-            reinterpret_cast<const uint16_t*>(scales), reinterpret_cast<const uint8_t*>(quants),
-            nb, row_ids, count, out);
+        (void)launch_pdl(dequant_rows_kernel<false>, dim3(g), dim3(256), 0, ctx->stream,
+                         reinterpret_cast<const uint16_t*>(scales),
+                         reinterpret_cast<const uint8_t*>(quants), nb, row_ids, count, out);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "dequant_rows launch");
 }

@@ -68,6 +68,17 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
                          int x_row_offset);
 int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                           const void* x_q8, int rows, int cols, int batch, float* out);
+// One matrix of a grouped decode GEMV (all of a group share K and the activations).
+struct GemvMatSrc {
+    const void* scales;
+    const void* quants;
+    float* out;
+    int rows;
+};
+// Streams 1..3 matrices in one launch (the exact AVX2-order GEMV); *handled is false when the
+// streaming form does not apply and the caller must launch each matrix on its own.
+int launch_gemv_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const void* x_q8,
+                      int cols, int batch, bool* handled);
 int launch_block_sums(sulimo_ctx* ctx, const void* w_quants, const void* x_q8, int rows, int cols,
                       int32_t* out);
 int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n);
