@@ -166,6 +166,7 @@ int sulimo_cuda_ctx_destroy(sulimo_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     if (ctx->workspace) cudaFree(ctx->workspace);
     if (ctx->d_error) cudaFree(ctx->d_error);
+    if (ctx->argmax_scratch) cudaFree(ctx->argmax_scratch);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return SULIMO_OK;

@@ -93,54 +93,53 @@ __device__ __forceinline__ void rope_pair(float* v, int i, int half, int mode, f
     v[b] = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
 }
 
-// One CTA per sequence: biases, RoPE of every q and k head, then K and V quantized into the
-// sequence's rings at slot pos % capacity (kv head h at block h*hd/32 of the slot).
-__global__ void __launch_bounds__(GLUE_THREADS)
-    qkv_rope_store_kernel(float* __restrict__ q, float* __restrict__ k, float* __restrict__ v,
-                          const float* __restrict__ bq, const float* __restrict__ bk,
-                          const float* __restrict__ bv, int H, int Hkv, int hd, int rope_dim,
-                          int mode, float base, size_t pos, uint8_t* __restrict__ k_ring,
-                          uint8_t* __restrict__ v_ring, size_t capacity, size_t seq_stride) {
+// One CTA per (head, sequence) over the q heads, then the k heads, then the v heads: bias add,
+// RoPE (q and k; angles pos / base^(2i/rope_dim) per pair), then q written back as f32 for the
+// attention and k / v quantized into the sequence's rings at slot pos % capacity (kv head h at
+// block h*hd/32 of the slot).
+__global__ void __launch_bounds__(128)
+    qkv_rope_store_kernel(float* __restrict__ q, const float* __restrict__ k,
+                          const float* __restrict__ v, const float* __restrict__ bq,
+                          const float* __restrict__ bk, const float* __restrict__ bv, int H,
+                          int Hkv, int hd, int rope_dim, int mode, float base, size_t pos,
+                          uint8_t* __restrict__ k_ring, uint8_t* __restrict__ v_ring,
+                          size_t capacity, size_t seq_stride) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
-    const int seq = blockIdx.x;
-    const int qd = H * hd, kvd = Hkv * hd, half = rope_dim / 2;
-    float* qs = q + (size_t)seq * qd;
-    float* ks = k + (size_t)seq * kvd;
-    float* vs = v + (size_t)seq * kvd;
-    for (int i = threadIdx.x; i < qd; i += blockDim.x)
-        if (bq) qs[i] = __fadd_rn(qs[i], bq[i]);
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
-        if (bk) ks[i] = __fadd_rn(ks[i], bk[i]);
-        if (bv) vs[i] = __fadd_rn(vs[i], bv[i]);
-    }
-    // the rotation angle depends on the pair index only: one cos/sin per pair for all heads
-    __shared__ float rc[128], rs[128];
-    for (int i = threadIdx.x; i < half; i += blockDim.x) {
-        const float freq = __fdiv_rn(1.0f, powf(base, __fdiv_rn((float)(2 * i), (float)rope_dim)));
-        const float theta = __fmul_rn((float)pos, freq);
-        rc[i] = cosf(theta);
-        rs[i] = sinf(theta);
+    __shared__ float sv[256];
+    const int head = blockIdx.x, seq = blockIdx.y;
+    const int kind = head < H ? 0 : (head < H + Hkv ? 1 : 2);  // q, k, v
+    const int hh = kind == 0 ? head : (kind == 1 ? head - H : head - H - Hkv);
+    const int dim = kind == 0 ? H * hd : Hkv * hd;
+    const float* src = kind == 0 ? q : (kind == 1 ? k : v);
+    const float* bias = kind == 0 ? bq : (kind == 1 ? bk : bv);
+    const float* vec = src + (size_t)seq * dim + (size_t)hh * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        const float x = vec[i];
+        sv[i] = bias ? __fadd_rn(x, bias[hh * hd + i]) : x;
     }
     __syncthreads();
-    // one thread per (head, pair)
-    for (int t = threadIdx.x; t < (H + Hkv) * half; t += blockDim.x) {
-        const int head = t / half, i = t - head * half;
-        float* hv = head < H ? qs + head * hd : ks + (head - H) * hd;
-        rope_pair(hv, i, half, mode, rc[i], rs[i]);
+    if (kind < 2) {
+        const int half = rope_dim / 2;
+        for (int i = threadIdx.x; i < half; i += blockDim.x) {
+            const float freq =
+                __fdiv_rn(1.0f, powf(base, __fdiv_rn((float)(2 * i), (float)rope_dim)));
+            const float theta = __fmul_rn((float)pos, freq);
+            rope_pair(sv, i, half, mode, cosf(theta), sinf(theta));
+        }
+        __syncthreads();
     }
-    __syncthreads();
-    const size_t slot = pos % capacity;
-    const size_t bpp = (size_t)kvd / 32;
-    uint8_t* kd = k_ring + (size_t)seq * seq_stride + slot * bpp * 34;
-    uint8_t* vd = v_ring + (size_t)seq * seq_stride + slot * bpp * 34;
+    if (kind == 0) {
+        float* dst = q + (size_t)seq * dim + (size_t)hh * hd;
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = sv[i];
+        return;
+    }
+    const size_t bpp = (size_t)Hkv * hd / 32;
+    uint8_t* ring = (kind == 1 ? k_ring : v_ring) + (size_t)seq * seq_stride +
+                    (pos % capacity) * bpp * 34 + (size_t)hh * (hd / 32) * 34;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int b = warp; b < 2 * (int)bpp; b += blockDim.x >> 5) {
-        if (b < (int)bpp)
-            quantize_block_warp(ks[b * 32 + lane], kd + b * 34, lane);
-        else
-            quantize_block_warp(vs[(b - bpp) * 32 + lane], vd + (b - bpp) * 34, lane);
-    }
+    for (int b = warp; b < hd / 32; b += blockDim.x >> 5)
+        quantize_block_warp(sv[b * 32 + lane], ring + b * 34, lane);
 }
 
 // silu(gate) * up -> Q8_0: one warp per 32-value block, all sequences' blocks in one grid.
@@ -157,32 +156,39 @@ __global__ void __launch_bounds__(GLUE_THREADS)
     quantize_block_warp(__fmul_rn(silu, up[b * 32 + lane]), q8 + b * 34, lane);
 }
 
-// First index of the maximum of each row (greedy sampling); NaN never wins.
+// First index of the maximum of each row (greedy sampling); NaN never wins.  ARGMAX_CTAS CTAs
+// per row each scan a column range and publish their (max, first index); the last CTA of a
+// row to finish (a per-row counter) folds the partials in range order, writes the index and
+// resets the counter for the next launch.
+constexpr int ARGMAX_CTAS = 32;
+
+__device__ __forceinline__ void argmax_merge(float& best, int& idx, float v, int i) {
+    if (v > best || (v == best && i < idx)) {
+        best = v;
+        idx = i;
+    }
+}
+
 __global__ void __launch_bounds__(GLUE_THREADS)
-    argmax_rows_kernel(const float* __restrict__ x, int cols, int32_t* __restrict__ out) {
+    argmax_rows_kernel(const float* __restrict__ x, int cols, float* __restrict__ part_v,
+                       int* __restrict__ part_i, unsigned* __restrict__ counters,
+                       int32_t* __restrict__ out) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     __shared__ float bv[GLUE_THREADS / 32];
     __shared__ int bi[GLUE_THREADS / 32];
-    const float* r = x + (size_t)blockIdx.x * cols;
+    __shared__ bool last;
+    const int row = blockIdx.y, c = blockIdx.x;
+    const int per = (cols + ARGMAX_CTAS - 1) / ARGMAX_CTAS;
+    const int c0 = c * per, c1 = min(cols, c0 + per);
+    const float* r = x + (size_t)row * cols;
     float best = -INFINITY;
     int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) {
-        const float v = r[i];
-        if (v > best) {  // strided scan: the first max of this thread's subsequence
-            best = v;
-            idx = i;
-        }
-    }
+    for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) argmax_merge(best, idx, r[i], i);
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
-        if (ov > best || (ov == best && oi < idx)) {
-            best = ov;
-            idx = oi;
-        }
-    }
+    for (int off = 16; off > 0; off >>= 1)
+        argmax_merge(best, idx, __shfl_xor_sync(0xffffffffu, best, off),
+                     __shfl_xor_sync(0xffffffffu, idx, off));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
         bv[warp] = best;
@@ -190,12 +196,22 @@ __global__ void __launch_bounds__(GLUE_THREADS)
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < GLUE_THREADS / 32; w++)
-            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
-                best = bv[w];
-                idx = bi[w];
-            }
-        out[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+        for (int w = 1; w < GLUE_THREADS / 32; w++) argmax_merge(best, idx, bv[w], bi[w]);
+        part_v[row * ARGMAX_CTAS + c] = best;
+        part_i[row * ARGMAX_CTAS + c] = idx;
+        __threadfence();
+        last = atomicAdd(&counters[row], 1u) == ARGMAX_CTAS - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        float b = -INFINITY;
+        int k = 0x7fffffff;
+        for (int w = 0; w < ARGMAX_CTAS; w++)
+            argmax_merge(b, k, __ldcg(part_v + row * ARGMAX_CTAS + w),
+                         __ldcg(part_i + row * ARGMAX_CTAS + w));
+        out[row] = k == 0x7fffffff ? 0 : k;
+        counters[row] = 0u;
     }
 }
 
@@ -241,8 +257,25 @@ size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch) {
 }
 
 int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out) {
-    (void)launch_pdl(argmax_rows_kernel, dim3(rows), dim3(GLUE_THREADS), 0, ctx->stream, x, cols,
-                     out);
+    // per-row partials + counters in a context-owned buffer (grown outside graph capture by a
+    // first call; counters start and end at zero)
+    const size_t need = (size_t)rows * (ARGMAX_CTAS * 8 + 4);
+    if (need > ctx->argmax_bytes) {
+        int st = check_cuda(cudaStreamSynchronize(ctx->stream), "argmax scratch sync");
+        if (st) return st;
+        if (ctx->argmax_scratch) cudaFree(ctx->argmax_scratch);
+        ctx->argmax_scratch = nullptr;
+        ctx->argmax_bytes = 0;
+        if ((st = check_cuda(cudaMalloc(&ctx->argmax_scratch, need), "argmax scratch"))) return st;
+        if ((st = check_cuda(cudaMemset(ctx->argmax_scratch, 0, need), "argmax scratch"))) return st;
+        ctx->argmax_bytes = need;
+    }
+    uint8_t* base = reinterpret_cast<uint8_t*>(ctx->argmax_scratch);
+    float* pv = reinterpret_cast<float*>(base);
+    int* pi = reinterpret_cast<int*>(base + (size_t)rows * ARGMAX_CTAS * 4);
+    unsigned* cnt = reinterpret_cast<unsigned*>(base + (size_t)rows * ARGMAX_CTAS * 8);
+    (void)launch_pdl(argmax_rows_kernel, dim3(ARGMAX_CTAS, rows), dim3(GLUE_THREADS), 0,
+                     ctx->stream, x, cols, pv, pi, cnt, out);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "argmax_rows launch");
 }
@@ -291,18 +324,18 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                                      {L.wk_scales, L.wk_quants, s.k, kvd},
                                      {L.wv_scales, L.wv_quants, s.v, kvd}};
             bool done = false;
-            if ((st = launch_gemv_group(ctx, g, 3, s.q8, E, batch, &done))) return st;
+            if ((st = launch_gemv_group(ctx, g, 3, s.q8, E, batch, &done, true))) return st;
             for (int i = 0; i < 3 && !done; i++)
                 if ((st = launch_gemv_q4_0_q8_0(ctx, g[i].scales, g[i].quants, s.q8, g[i].rows, E,
                                                 batch, g[i].out)))
                     return st;
         }
-        (void)launch_pdl(qkv_rope_store_kernel, dim3(batch), dim3(GLUE_THREADS), 0, ctx->stream,
-                         s.q, s.k, s.v, reinterpret_cast<const float*>(L.bq),
-                         reinterpret_cast<const float*>(L.bk), reinterpret_cast<const float*>(L.bv),
-                         H, Hkv, hd, m->rope_dim, m->rope_mode, m->rope_base, pos,
-                         reinterpret_cast<uint8_t*>(L.k_ring), reinterpret_cast<uint8_t*>(L.v_ring),
-                         m->kv_capacity, m->kv_seq_stride);
+        (void)launch_pdl(qkv_rope_store_kernel, dim3(H + 2 * Hkv, batch), dim3(128), 0,
+                         ctx->stream, s.q, (const float*)s.k, (const float*)s.v,
+                         reinterpret_cast<const float*>(L.bq), reinterpret_cast<const float*>(L.bk),
+                         reinterpret_cast<const float*>(L.bv), H, Hkv, hd, m->rope_dim,
+                         m->rope_mode, m->rope_base, pos, reinterpret_cast<uint8_t*>(L.k_ring),
+                         reinterpret_cast<uint8_t*>(L.v_ring), m->kv_capacity, m->kv_seq_stride);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
         if ((st = launch_attn_decode(ctx, s.q, L.k_ring, L.v_ring, m->kv_seq_stride,
@@ -310,7 +343,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                                      s.att, reinterpret_cast<float*>(ctx->workspace),
                                      ctx->workspace_bytes)) ||
             (st = launch_quantize_q8_0(ctx, s.att, s.q8, (size_t)batch * qd)) ||
-            (st = launch_gemv_q4_0_q8_0(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
+            (st = launch_gemv_static(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
             return st;
         (void)launch_pdl(add_rmsnorm_q8_kernel, dim3(batch), dim3(NORM_THREADS), norm_smem,
                          ctx->stream, s.x, (const float*)s.o,
@@ -321,7 +354,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
             const GemvMatSrc g[2] = {{L.wg_scales, L.wg_quants, s.g, F},
                                      {L.wu_scales, L.wu_quants, s.u, F}};
             bool done = false;
-            if ((st = launch_gemv_group(ctx, g, 2, s.q8, E, batch, &done))) return st;
+            if ((st = launch_gemv_group(ctx, g, 2, s.q8, E, batch, &done, true))) return st;
             for (int i = 0; i < 2 && !done; i++)
                 if ((st = launch_gemv_q4_0_q8_0(ctx, g[i].scales, g[i].quants, s.q8, g[i].rows, E,
                                                 batch, g[i].out)))
@@ -332,7 +365,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                          ctx->stream, (const float*)s.g, (const float*)s.u, nblk, s.q8);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "swiglu_q8 launch"))) return st;
-        if ((st = launch_gemv_q4_0_q8_0(ctx, L.wd_scales, L.wd_quants, s.q8, E, F, batch, s.o)))
+        if ((st = launch_gemv_static(ctx, L.wd_scales, L.wd_quants, s.q8, E, F, batch, s.o)))
             return st;
         pending = s.o;
     }
@@ -340,8 +373,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                      ctx->stream, s.x, pending, m->out_norm, E, m->eps, s.q8);
     ctx->launches++;
     if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
-    return launch_gemv_q4_0_q8_0(ctx, m->out_scales, m->out_quants, s.q8, m->vocab, E, batch,
-                                 logits);
+    return launch_gemv_static(ctx, m->out_scales, m->out_quants, s.q8, m->vocab, E, batch, logits);
 }
 
 }  // namespace sulimo

@@ -144,14 +144,16 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 // 4-thread group.  One launch can cover up to three matrices that share the activations (the
 // decode step's q/k/v and gate/up projections): the CTA index picks the matrix.
 constexpr int TS_BLOCKS = 8;                     // Q4_0 blocks per stage (K = 256)
-constexpr int TS_STAGES = 8;
 constexpr int TS_MAX_MATS = 3;
 
 // Shared memory: the stages' quant tiles first (each ROWS x 128 bytes, a multiple of the
 // 1024-byte swizzle atom, so every tile starts on an atom), then the stages' scale tiles.
+// Ring depth: 8 stages of 64 rows; narrower tiles get proportionally more stages so every CTA
+// keeps the same ~72 KB of weights in flight (the small decode matrices are latency-bound).
 template <int ROWS>
 struct TsShape {
     static constexpr int THREADS = ROWS * 4 + 32;  // + producer warp
+    static constexpr int STAGES = 8 * 64 / ROWS;
     static constexpr uint32_t Q_BYTES = ROWS * TS_BLOCKS * 16;
     static constexpr uint32_t S_BYTES = ROWS * TS_BLOCKS * 2;
     static constexpr uint32_t STAGE_BYTES = Q_BYTES + S_BYTES;
@@ -178,18 +180,18 @@ template <int NV, int ROWS>
 __global__ void __launch_bounds__(TsShape<ROWS>::THREADS)
     gemv_q4_0_q8_0_tma_kernel(const __grid_constant__ GemvGroup grp,
                               const uint8_t* __restrict__ xq8, int nb, int batch,
-                              int* __restrict__ err) {
+                              int static_weights, int* __restrict__ err) {
     using T = TsShape<ROWS>;
     pdl_launch_dependents();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-    uint8_t* qtiles = sm;                                   // TS_STAGES x Q_BYTES
-    uint8_t* stiles = sm + TS_STAGES * T::Q_BYTES;          // TS_STAGES x S_BYTES
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + TS_STAGES * T::STAGE_BYTES);
-    uint64_t* empty = full + TS_STAGES;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + TS_STAGES);
-    int* xw = reinterpret_cast<int*>(empty + TS_STAGES + 1);        // [NV][nb][8]
+    uint8_t* qtiles = sm;                                   // T::STAGES x Q_BYTES
+    uint8_t* stiles = sm + T::STAGES * T::Q_BYTES;          // T::STAGES x S_BYTES
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + T::STAGES * T::STAGE_BYTES);
+    uint64_t* empty = full + T::STAGES;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + T::STAGES);
+    int* xw = reinterpret_cast<int*>(empty + T::STAGES + 1);        // [NV][nb][8]
     int* xc = xw + NV * nb * 8;                                      // [NV][nb][8]
     float* xs = reinterpret_cast<float*>(xc + NV * nb * 8);          // [NV][nb]
 
@@ -204,8 +206,14 @@ __global__ void __launch_bounds__(TsShape<ROWS>::THREADS)
     const int v0 = blockIdx.y * NV;
     const int nchunks = nb / TS_BLOCKS;
 
-    if (tid == 0) {
-        for (int s = 0; s < TS_STAGES; s++) {
+    // The producer thread sets up the ring.  When the caller vouches that the weights are not
+    // written by the previous kernel of the stream (a decode step's static parameters), it also
+    // issues the first ring pass of weight tiles before griddepcontrol.wait, so the weight
+    // stream overlaps the previous kernel's tail; everything else (and always the
+    // activations) is read only after the wait.
+    int prefetched = 0;
+    if (tid == ROWS * 4) {
+        for (int s = 0; s < T::STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], ROWS * 4);
         }
@@ -213,19 +221,25 @@ __global__ void __launch_bounds__(TsShape<ROWS>::THREADS)
         fence_barrier_init();
         prefetch_tensormap(&M.q);
         prefetch_tensormap(&M.s);
+        if (static_weights) {
+            for (int c = 0; c < nchunks && c < T::STAGES; c++) {
+                mbar_arrive_expect_tx(&full[c], T::STAGE_BYTES);
+                tma_load_2d(qtiles + c * T::Q_BYTES, &M.q, c * TS_BLOCKS * 16, row0, &full[c]);
+                tma_load_2d(stiles + c * T::S_BYTES, &M.s, c * TS_BLOCKS, row0, &full[c]);
+            }
+            prefetched = nchunks < T::STAGES ? nchunks : T::STAGES;
+        }
     }
-    // weights are not written by the previous kernel of a decode step, but wait anyway before
-    // any global access: the activations are
     pdl_wait_prerequisites();
     __syncthreads();
 
     if (tid >= ROWS * 4) {
         // ------------------------------ producer warp ------------------------------
         if (tid == ROWS * 4) {
-            int issued = 0;
-            for (int c = 0; c < nchunks; c++) {
-                const int s = c % TS_STAGES;
-                const uint32_t ph = (uint32_t)(c / TS_STAGES) & 1u;
+            int issued = prefetched;
+            for (int c = prefetched; c < nchunks; c++) {
+                const int s = c % T::STAGES;
+                const uint32_t ph = (uint32_t)(c / T::STAGES) & 1u;
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
                 mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
                 tma_load_2d(qtiles + s * T::Q_BYTES, &M.q, c * TS_BLOCKS * 16, row0, &full[s]);
@@ -233,8 +247,8 @@ __global__ void __launch_bounds__(TsShape<ROWS>::THREADS)
                 issued = c + 1;
             }
             if (*abort_flag)  // the issued copies must land before the CTA releases its smem
-                for (int c = (issued > TS_STAGES ? issued - TS_STAGES : 0); c < issued; c++)
-                    mbar_wait_bounded(&full[c % TS_STAGES], (uint32_t)(c / TS_STAGES) & 1u, err,
+                for (int c = (issued > T::STAGES ? issued - T::STAGES : 0); c < issued; c++)
+                    mbar_wait_bounded(&full[c % T::STAGES], (uint32_t)(c / T::STAGES) & 1u, err,
                                       nullptr);
         }
         return;  // the consumers synchronize among themselves (named barrier 1) from here on
@@ -266,8 +280,8 @@ __global__ void __launch_bounds__(TsShape<ROWS>::THREADS)
     for (int v = 0; v < NV; v++) acc[v][0] = acc[v][1] = 0.0f;
 
     for (int c = 0; c < nchunks; c++) {
-        const int s = c % TS_STAGES;
-        const uint32_t ph = (uint32_t)(c / TS_STAGES) & 1u;
+        const int s = c % T::STAGES;
+        const uint32_t ph = (uint32_t)(c / T::STAGES) & 1u;
         if (!mbar_wait_bounded(&full[s], ph, err, abort_flag)) break;
         const uint8_t* qst = qtiles + s * T::Q_BYTES + rl * 128;
         const uint16_t* sst = reinterpret_cast<const uint16_t*>(stiles + s * T::S_BYTES) + rl * 8;
@@ -311,13 +325,14 @@ __global__ void __launch_bounds__(TsShape<ROWS>::THREADS)
 
 template <int NV, int ROWS>
 size_t gemv_tma_smem(int nb) {
-    return 1024 + (size_t)TS_STAGES * TsShape<ROWS>::STAGE_BYTES + 8 * (2 * TS_STAGES + 1) +
+    using T = TsShape<ROWS>;
+    return 1024 + (size_t)T::STAGES * T::STAGE_BYTES + 8 * (2 * T::STAGES + 1) +
            (size_t)NV * nb * (8 * 4 * 2 + 4);
 }
 
 template <int NV, int ROWS>
 int launch_gemv_tma(sulimo_ctx* ctx, const GemvGroup& grp, int tiles, const uint8_t* xq8, int nb,
-                    int batch) {
+                    int batch, int static_weights) {
     const size_t smem = gemv_tma_smem<NV, ROWS>(nb);
     static uint64_t attr_mask = 0;  // per device
     const uint64_t bit = 1ull << (ctx->device & 63);
@@ -331,14 +346,14 @@ int launch_gemv_tma(sulimo_ctx* ctx, const GemvGroup& grp, int tiles, const uint
     }
     dim3 grid((unsigned)tiles, (batch + NV - 1) / NV);
     (void)launch_pdl(gemv_q4_0_q8_0_tma_kernel<NV, ROWS>, grid, dim3(TsShape<ROWS>::THREADS), smem,
-                     ctx->stream, grp, xq8, nb, batch, ctx->d_error);
+                     ctx->stream, grp, xq8, nb, batch, static_weights, ctx->d_error);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "gemv_q4_0_q8_0_tma launch");
 }
 
 template <int ROWS>
 int launch_gemv_tma_rows(sulimo_ctx* ctx, GemvGroup& grp, const GemvMatSrc* src, int count,
-                         const uint8_t* xq8, int nb, int batch, int nv) {
+                         const uint8_t* xq8, int nb, int batch, int nv, int sw) {
     int tiles = 0;
     for (int i = 0; i < count; i++) {
         GemvMat& M = grp.m[i];
@@ -362,10 +377,10 @@ int launch_gemv_tma_rows(sulimo_ctx* ctx, GemvGroup& grp, const GemvMatSrc* src,
     for (int i = count; i < TS_MAX_MATS; i++) grp.m[i] = grp.m[0];
     grp.count = count;
     switch (nv) {
-        case 8: return launch_gemv_tma<8, ROWS>(ctx, grp, tiles, xq8, nb, batch);
-        case 4: return launch_gemv_tma<4, ROWS>(ctx, grp, tiles, xq8, nb, batch);
-        case 2: return launch_gemv_tma<2, ROWS>(ctx, grp, tiles, xq8, nb, batch);
-        default: return launch_gemv_tma<1, ROWS>(ctx, grp, tiles, xq8, nb, batch);
+        case 8: return launch_gemv_tma<8, ROWS>(ctx, grp, tiles, xq8, nb, batch, sw);
+        case 4: return launch_gemv_tma<4, ROWS>(ctx, grp, tiles, xq8, nb, batch, sw);
+        case 2: return launch_gemv_tma<2, ROWS>(ctx, grp, tiles, xq8, nb, batch, sw);
+        default: return launch_gemv_tma<1, ROWS>(ctx, grp, tiles, xq8, nb, batch, sw);
     }
 }
 
@@ -375,7 +390,7 @@ int launch_gemv_tma_rows(sulimo_ctx* ctx, GemvGroup& grp, const GemvMatSrc* src,
 // the streaming form does not apply (K not a multiple of 256, scales not 16-byte aligned,
 // activations too large for shared memory).
 int launch_gemv_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const void* x_q8,
-                      int cols, int batch, bool* handled) {
+                      int cols, int batch, bool* handled, bool static_weights) {
     *handled = false;
     const int nb = cols / 32;
     if (count < 1 || count > TS_MAX_MATS || nb % TS_BLOCKS != 0) return SULIMO_OK;
@@ -388,6 +403,7 @@ int launch_gemv_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const v
     while (nv > 1 && (nv > batch || (size_t)nv * nb * 68 > 96 * 1024)) nv >>= 1;
     if ((size_t)nv * nb * 68 > 96 * 1024) return SULIMO_OK;
     *handled = true;
+    const int sw = static_weights ? 1 : 0;
     // rows per CTA: 64 unless that leaves more than half of the SMs idle (measured: 32-row
     // tiles make the one-wave 8960-row config-1 matvec ~1.4x slower, so narrower tiles only
     // serve the small decode matrices)
@@ -396,10 +412,19 @@ int launch_gemv_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const v
     GemvGroup grp;
     const size_t half_sms = (size_t)ctx->num_sms / 2;
     if ((size_t)(total_rows / 64) * vec_groups >= half_sms)
-        return launch_gemv_tma_rows<64>(ctx, grp, src, count, x, nb, batch, nv);
+        return launch_gemv_tma_rows<64>(ctx, grp, src, count, x, nb, batch, nv, sw);
     if ((size_t)(total_rows / 32) * vec_groups >= half_sms)
-        return launch_gemv_tma_rows<32>(ctx, grp, src, count, x, nb, batch, nv);
-    return launch_gemv_tma_rows<16>(ctx, grp, src, count, x, nb, batch, nv);
+        return launch_gemv_tma_rows<32>(ctx, grp, src, count, x, nb, batch, nv, sw);
+    return launch_gemv_tma_rows<16>(ctx, grp, src, count, x, nb, batch, nv, sw);
+}
+
+int launch_gemv_static(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
+                       const void* x_q8, int rows, int cols, int batch, float* out) {
+    const GemvMatSrc src = {w_scales, w_quants, out, rows};
+    bool handled = false;
+    const int st = launch_gemv_group(ctx, &src, 1, x_q8, cols, batch, &handled, true);
+    if (handled || st) return st;
+    return launch_gemv_q4_0_q8_0(ctx, w_scales, w_quants, x_q8, rows, cols, batch, out);
 }
 
 int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
@@ -407,7 +432,7 @@ int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_q
     const int nb = cols / 32;
     const GemvMatSrc src = {w_scales, w_quants, out, rows};
     bool handled = false;
-    const int st = launch_gemv_group(ctx, &src, 1, x_q8, cols, batch, &handled);
+    const int st = launch_gemv_group(ctx, &src, 1, x_q8, cols, batch, &handled, false);
     if (handled || st) return st;
     const size_t tiles = ((size_t)rows + GEMV_ROWS - 1) / GEMV_ROWS;
     const size_t grid = tiles * (size_t)batch;

@@ -20,6 +20,8 @@ struct sulimo_ctx {
     int* d_error = nullptr;         // device error word (0 = none)
     void* workspace = nullptr;      // attention partials
     size_t workspace_bytes = 0;
+    void* argmax_scratch = nullptr;  // greedy argmax partials + per-row counters (zero at rest)
+    size_t argmax_bytes = 0;
     std::atomic<uint64_t> launches{0};
 };
 
@@ -77,8 +79,13 @@ struct GemvMatSrc {
 };
 // Streams 1..3 matrices in one launch (the exact AVX2-order GEMV); *handled is false when the
 // streaming form does not apply and the caller must launch each matrix on its own.
+// static_weights: the caller guarantees the weights are not written by the previous kernel of
+// the stream, so the first weight tiles may be fetched before the programmatic-launch wait.
 int launch_gemv_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const void* x_q8,
-                      int cols, int batch, bool* handled);
+                      int cols, int batch, bool* handled, bool static_weights);
+// launch_gemv_q4_0_q8_0 for a decode step's static weights (see launch_gemv_group).
+int launch_gemv_static(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
+                       const void* x_q8, int rows, int cols, int batch, float* out);
 int launch_block_sums(sulimo_ctx* ctx, const void* w_quants, const void* x_q8, int rows, int cols,
                       int32_t* out);
 int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n);
