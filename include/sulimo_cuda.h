@@ -213,6 +213,28 @@ int sulimo_cuda_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* model,
                               const int32_t* tokens, int batch, size_t pos, float* logits,
                               void* scratch, size_t scratch_bytes);
 
+/* Bytes of device scratch sulimo_cuda_prefill_ubatch needs for ubatches of up to n tokens.    */
+size_t sulimo_cuda_prefill_scratch_bytes(const sulimo_model_desc* model, int n);
+
+/* One prefill ubatch — replaces execute_prefill_ubatch (crates/sulimo-ocl/src/prefill.rs:     */
+/* 337-566): tokens[n] (device int32) at positions start_pos .. start_pos+n-1 of ONE sequence  */
+/* (kv_seq_stride unused), K/V stored into the rings, logits[vocab] (fp32) of the last token   */
+/* (enqueue_logits_final, prefill.rs:300-330).  Requires start_pos + n <= kv_capacity.        */
+/* Unlike the reference's GPU ubatch this one applies the QKV biases (as forward_token does)  */
+/* and keeps the residual stream in fp32; the GEMM activations are f16 like the reference's.   */
+int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                               const int32_t* tokens, int n, size_t start_pos, float* logits,
+                               void* scratch, size_t scratch_bytes);
+
+/* Causal GQA prefill attention over one layer's Q8_0 ring — replaces                          */
+/* causal_gqa_attention_prefill (kernels/prefill.cl:120-237, enqueue_attention_prefill):       */
+/* q [n][head_count][head_dim] fp32 (after RoPE; the reference passes f16), token t at         */
+/* position start_pos + t attends to positions 0 .. start_pos + t (slot p % capacity);         */
+/* out [n][head_count][head_dim] f16.  head_dim 64 or 128.                                    */
+int sulimo_cuda_attn_prefill_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                                  const void* v_ring, size_t start_pos, size_t capacity, int n,
+                                  int head_count, int head_count_kv, int head_dim, void* out);
+
 /* Greedy pick: out[r] = first index of the maximum of row r of x[rows][cols].                */
 int sulimo_cuda_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out);
 

@@ -12,7 +12,7 @@ from .capi import ACT_F16, ACT_F32, OUT_F16, OUT_F32, SulimoError
 __all__ = [
     "CudaContext", "SulimoError", "gemm_q4_0_f16", "logits_final", "dispatch_matvec_q4_0_q8_0",
     "block_sums_q4_0_q8_0", "quantize_f32_to_q8_0", "kv_store_q8_0", "dequantize_q4_0_rows",
-    "causal_gqa_decode", "live_buffer_count", "unshard_rows", "OUT_F16", "OUT_F32", "ACT_F16",
+    "causal_gqa_decode", "causal_gqa_attention_prefill", "live_buffer_count", "unshard_rows", "OUT_F16", "OUT_F32", "ACT_F16",
     "ACT_F32",
 ]
 
@@ -125,6 +125,13 @@ def unshard_rows(ctx, gathered, out, world, m_tokens, fs, f):
     """Shard-major all-gather result [world][m_tokens][fs] -> row-major [m_tokens][f]."""
     capi.call("sulimo_cuda_unshard_rows", ctx.handle, _ptr(gathered), _ptr(out), world, m_tokens,
               fs, f, gathered.element_size())
+
+
+def causal_gqa_attention_prefill(ctx, q, k_ring, v_ring, start_pos, capacity, n, head_count,
+                                 head_count_kv, head_dim, out):
+    """causal_gqa_attention_prefill (kernels/prefill.cl:120-237): q fp32 [n][H][hd] -> out f16."""
+    capi.call("sulimo_cuda_attn_prefill_q8_0", ctx.handle, _ptr(q), _ptr(k_ring), _ptr(v_ring),
+              start_pos, capacity, n, head_count, head_count_kv, head_dim, _ptr(out))
 
 
 def causal_gqa_decode(ctx, q, k_ring, v_ring, capacity, context_len, head_count, head_count_kv,

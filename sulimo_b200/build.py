@@ -23,6 +23,7 @@ SOURCES = [
     "gemm_q4_0_tc.cu",
     "shard.cu",
     "forward.cu",
+    "attn_prefill_q8_0.cu",
 ]
 
 NVCC_FLAGS = [

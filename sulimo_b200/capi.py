@@ -54,6 +54,9 @@ SIGNATURES = {
     "sulimo_cuda_forward_scratch_bytes": (_sz, [_vp, _i]),
     "sulimo_cuda_forward_token": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _sz]),
     "sulimo_cuda_argmax_rows": (_i, [_vp, _vp, _i, _i, _vp]),
+    "sulimo_cuda_prefill_scratch_bytes": (_sz, [_vp, _i]),
+    "sulimo_cuda_prefill_ubatch": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _sz]),
+    "sulimo_cuda_attn_prefill_q8_0": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _i, _i, _i, _i, _vp]),
     "sulimo_cuda_attn_decode_q8_0": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _i, _i,
                                           _f, _vp]),
     "sulimo_cuda_attn_decode_q8_0_noalloc": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _i,

@@ -533,6 +533,61 @@ int sulimo_cuda_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* model,
     return sulimo::launch_forward_token(ctx, model, tokens, batch, pos, logits, scratch);
 }
 
+size_t sulimo_cuda_prefill_scratch_bytes(const sulimo_model_desc* model, int n) {
+    if (check_model(model) || n <= 0) return 0;
+    return sulimo::prefill_scratch_bytes(model, n);
+}
+
+int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                               const int32_t* tokens, int n, size_t start_pos, float* logits,
+                               void* scratch, size_t scratch_bytes) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if ((st = check_model(model))) return st;
+    if (model->head_dim != 64 && model->head_dim != 128)
+        return set_error(SULIMO_EINVAL, "prefill supports head_dim 64 and 128");
+    if (n <= 0 || n > 65535) return set_error(SULIMO_EINVAL, "n must be in [1, 65535]");
+    if (start_pos + (size_t)n > model->kv_capacity)
+        return set_error(SULIMO_EINVAL, "start_pos + n exceeds the ring capacity");
+    if (!tokens || !logits || !scratch) return set_error(SULIMO_EINVAL, "null pointer");
+    if (scratch_bytes < sulimo::prefill_scratch_bytes(model, n))
+        return set_error(SULIMO_EINVAL, "scratch smaller than sulimo_cuda_prefill_scratch_bytes");
+    if (!aligned(scratch, 256) || !aligned(logits, 16) || !aligned(tokens, 4) ||
+        !aligned(model->tok_quants, 16) || !aligned(model->out_quants, 16))
+        return set_error(SULIMO_EALIGN, "scratch 256-byte, logits / quants 16-byte aligned");
+    for (int l = 0; l < model->n_layers; l++) {
+        const sulimo_layer_desc& L = model->layers[l];
+        const void* q16[] = {L.wq_quants, L.wk_quants, L.wv_quants, L.wo_quants, L.wg_quants,
+                             L.wu_quants, L.wd_quants};
+        for (const void* p : q16)
+            if (!aligned(p, 16)) return set_error(SULIMO_EALIGN, "quants must be 16-byte aligned");
+    }
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_prefill_ubatch(ctx, model, tokens, n, start_pos, logits, scratch);
+}
+
+int sulimo_cuda_attn_prefill_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                                  const void* v_ring, size_t start_pos, size_t capacity, int n,
+                                  int head_count, int head_count_kv, int head_dim, void* out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (head_dim != 64 && head_dim != 128)
+        return set_error(SULIMO_EINVAL, "head_dim must be 64 or 128");
+    if (head_count <= 0 || head_count_kv <= 0 || head_count % head_count_kv)
+        return set_error(SULIMO_EINVAL, "head_count must be a positive multiple of head_count_kv");
+    if (n < 0 || n > 65535 * 64 || capacity == 0 || head_count > 65535)
+        return set_error(SULIMO_EINVAL, "bad n / capacity / head_count");
+    if (start_pos + (size_t)n > capacity)
+        return set_error(SULIMO_EINVAL, "start_pos + n exceeds the ring capacity");
+    if (n == 0) return SULIMO_OK;
+    if (!q || !k_ring || !v_ring || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(q, 8) || !aligned(out, 4) || !aligned(k_ring, 2) || !aligned(v_ring, 2))
+        return set_error(SULIMO_EALIGN, "misaligned");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_attn_prefill(ctx, q, k_ring, v_ring, start_pos, capacity, n, head_count,
+                                       head_count_kv, head_dim, out);
+}
+
 int sulimo_cuda_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out) {
     int st = check_ctx(ctx);
     if (st) return st;

@@ -51,6 +51,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // One CTA per sequence.  x[seq][E] (+= delta[seq][E] when delta is given, written back), then
 // y = (x * 1/sqrt(mean(x^2) + eps)) * w, quantized to Q8_0 (E/32 blocks) into q8[seq].
+// F16_OUT: y as f16 [seq][E] (the prefill GEMMs' activations) instead of Q8_0.
+template <bool F16_OUT>
 __global__ void __launch_bounds__(NORM_THREADS)
     add_rmsnorm_q8_kernel(float* __restrict__ x, const float* __restrict__ delta,
                           const float* __restrict__ w, int E, float eps,
@@ -75,6 +77,12 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const float sum_sq = block_sum(ss, red);
     const float mean = __fdiv_rn(sum_sq, (float)E);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    if (F16_OUT) {
+        __half* ys = reinterpret_cast<__half*>(q8) + (size_t)seq * E;
+        for (int i = threadIdx.x; i < E; i += blockDim.x)
+            ys[i] = __float2half_rn(__fmul_rn(__fmul_rn(sx[i], scale), w[i]));
+        return;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* qs = q8 + (size_t)seq * (E / 32) * 34;
     for (int b = warp; b < E / 32; b += blockDim.x >> 5) {
@@ -101,13 +109,16 @@ __global__ void __launch_bounds__(128)
     qkv_rope_store_kernel(float* __restrict__ q, const float* __restrict__ k,
                           const float* __restrict__ v, const float* __restrict__ bq,
                           const float* __restrict__ bk, const float* __restrict__ bv, int H,
-                          int Hkv, int hd, int rope_dim, int mode, float base, size_t pos,
-                          uint8_t* __restrict__ k_ring, uint8_t* __restrict__ v_ring,
-                          size_t capacity, size_t seq_stride) {
+                          int Hkv, int hd, int rope_dim, int mode, float base, size_t pos0,
+                          size_t pos_step, uint8_t* __restrict__ k_ring,
+                          uint8_t* __restrict__ v_ring, size_t capacity, size_t seq_stride) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     __shared__ float sv[256];
+    // blockIdx.y: a sequence of a decode batch (pos_step 0, own ring) or a token of a prefill
+    // ubatch (pos_step 1, one ring)
     const int head = blockIdx.x, seq = blockIdx.y;
+    const size_t pos = pos0 + (size_t)seq * pos_step;
     const int kind = head < H ? 0 : (head < H + Hkv ? 1 : 2);  // q, k, v
     const int hh = kind == 0 ? head : (kind == 1 ? head - H : head - H - Hkv);
     const int dim = kind == 0 ? H * hd : Hkv * hd;
@@ -140,6 +151,18 @@ __global__ void __launch_bounds__(128)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int b = warp; b < hd / 32; b += blockDim.x >> 5)
         quantize_block_warp(sv[b * 32 + lane], ring + b * 34, lane);
+}
+
+// silu(gate) * up -> f16 (the prefill down-projection GEMM's activations).
+__global__ void __launch_bounds__(GLUE_THREADS)
+    swiglu_f16_kernel(const float* __restrict__ gate, const float* __restrict__ up, size_t n,
+                      __half* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float g = gate[i];
+    out[i] = __float2half_rn(__fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up[i]));
 }
 
 // silu(gate) * up -> Q8_0: one warp per 32-value block, all sequences' blocks in one grid.
@@ -250,7 +273,138 @@ size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scra
     return off;
 }
 
+// The RMSNorm kernels keep the whole vector in shared memory (up to 227 KB per CTA).
+int ensure_norm_attr(sulimo_ctx* ctx) {
+    static uint64_t mask = 0;  // per device
+    const uint64_t bit = 1ull << (ctx->device & 63);
+    if (mask & bit) return SULIMO_OK;
+    int st = check_cuda(cudaFuncSetAttribute(add_rmsnorm_q8_kernel<false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024),
+                        "rmsnorm smem attribute");
+    if (!st)
+        st = check_cuda(cudaFuncSetAttribute(add_rmsnorm_q8_kernel<true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024),
+                        "rmsnorm smem attribute");
+    if (!st) mask |= bit;
+    return st;
+}
+
+// Prefill scratch: x, q, k, v, o, gate, up (f32 [n][dim]) and one f16 activation buffer
+// [n][max(embd, q dim, ffn)] shared by the norm, attention and SwiGLU outputs.
+struct PrefillScratch {
+    float *x, *q, *k, *v, *o, *g, *u;
+    __half* h;
+};
+
+size_t prefill_layout(const sulimo_model_desc* m, int n, uint8_t* base, PrefillScratch* s) {
+    const size_t E = m->embd, F = m->ffn, qd = (size_t)m->head_count * m->head_dim;
+    const size_t kvd = (size_t)m->head_count_kv * m->head_dim;
+    size_t hn = E > qd ? E : qd;
+    if (F > hn) hn = F;
+    const size_t sizes[8] = {E * 4, qd * 4, kvd * 4, kvd * 4, E * 4, F * 4, F * 4, hn * 2};
+    uint8_t* p[8];
+    size_t off = 0;
+    for (int i = 0; i < 8; i++) {
+        p[i] = base ? base + off : nullptr;
+        off += align256(sizes[i] * (size_t)n);
+    }
+    if (s) {
+        s->x = reinterpret_cast<float*>(p[0]);
+        s->q = reinterpret_cast<float*>(p[1]);
+        s->k = reinterpret_cast<float*>(p[2]);
+        s->v = reinterpret_cast<float*>(p[3]);
+        s->o = reinterpret_cast<float*>(p[4]);
+        s->g = reinterpret_cast<float*>(p[5]);
+        s->u = reinterpret_cast<float*>(p[6]);
+        s->h = reinterpret_cast<__half*>(p[7]);
+    }
+    return off;
+}
+
 }  // namespace
+
+size_t prefill_scratch_bytes(const sulimo_model_desc* m, int n) {
+    return prefill_layout(m, n, nullptr, nullptr);
+}
+
+// One prefill ubatch of n tokens at positions start_pos .. start_pos+n-1 of one sequence
+// (execute_prefill_ubatch, crates/sulimo-ocl/src/prefill.rs:337-566): per layer RMSNorm -> f16,
+// q/k/v GEMMs (fp32 out), biases + RoPE + K/V ring store for every token, causal prefill
+// attention (f16 out), o GEMM, residual + RMSNorm, gate/up GEMMs, SwiGLU (f16), down GEMM,
+// residual; then the last token's final norm and the vocab projection (enqueue_logits_final,
+// prefill.rs:300-330) into logits[vocab].  The reference's GPU ubatch skips the QKV biases and
+// keeps activations in f16; this one adds the biases (as forward_token does) and keeps the
+// residual stream in fp32.
+int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
+                          int n, size_t start_pos, float* logits, void* scratch) {
+    PrefillScratch s;
+    prefill_layout(m, n, reinterpret_cast<uint8_t*>(scratch), &s);
+    const int E = m->embd, F = m->ffn, H = m->head_count, Hkv = m->head_count_kv,
+              hd = m->head_dim;
+    const int qd = H * hd, kvd = Hkv * hd;
+    const size_t norm_smem = (size_t)(E + 33) * sizeof(float);
+    uint8_t* h8 = reinterpret_cast<uint8_t*>(s.h);
+    int st;
+    if ((st = ensure_norm_attr(ctx))) return st;
+    if ((st = launch_dequant_rows(ctx, m->tok_scales, m->tok_quants, E, tokens, n, s.x,
+                                  SULIMO_OUT_F32)))
+        return st;
+    auto gemm = [&](const void* sc, const void* qu, const void* x, float* out, int rows, int k) {
+        return launch_gemm_q4_0_f16(ctx, sc, qu, x, out, rows, k, n, SULIMO_OUT_F32, k, 0);
+    };
+    const float* pending = nullptr;
+    for (int l = 0; l < m->n_layers; l++) {
+        const sulimo_layer_desc& L = m->layers[l];
+        (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
+                         ctx->stream, s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E,
+                         m->eps, h8);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
+        if ((st = gemm(L.wq_scales, L.wq_quants, s.h, s.q, qd, E)) ||
+            (st = gemm(L.wk_scales, L.wk_quants, s.h, s.k, kvd, E)) ||
+            (st = gemm(L.wv_scales, L.wv_quants, s.h, s.v, kvd, E)))
+            return st;
+        (void)launch_pdl(qkv_rope_store_kernel, dim3(H + 2 * Hkv, n), dim3(128), 0, ctx->stream,
+                         s.q, (const float*)s.k, (const float*)s.v,
+                         reinterpret_cast<const float*>(L.bq), reinterpret_cast<const float*>(L.bk),
+                         reinterpret_cast<const float*>(L.bv), H, Hkv, hd, m->rope_dim,
+                         m->rope_mode, m->rope_base, start_pos, (size_t)1,
+                         reinterpret_cast<uint8_t*>(L.k_ring), reinterpret_cast<uint8_t*>(L.v_ring),
+                         m->kv_capacity, (size_t)0);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
+        if ((st = launch_attn_prefill(ctx, s.q, L.k_ring, L.v_ring, start_pos, m->kv_capacity, n,
+                                      H, Hkv, hd, s.h)) ||
+            (st = gemm(L.wo_scales, L.wo_quants, s.h, s.o, E, qd)))
+            return st;
+        (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
+                         ctx->stream, s.x, (const float*)s.o,
+                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, h8);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
+        if ((st = gemm(L.wg_scales, L.wg_quants, s.h, s.g, F, E)) ||
+            (st = gemm(L.wu_scales, L.wu_quants, s.h, s.u, F, E)))
+            return st;
+        const size_t nf = (size_t)n * F;
+        (void)launch_pdl(swiglu_f16_kernel, dim3((unsigned)((nf + GLUE_THREADS - 1) / GLUE_THREADS)),
+                         dim3(GLUE_THREADS), 0, ctx->stream, (const float*)s.g, (const float*)s.u,
+                         nf, s.h);
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "swiglu_f16 launch"))) return st;
+        if ((st = gemm(L.wd_scales, L.wd_quants, s.h, s.o, E, F))) return st;
+        pending = s.o;
+    }
+    // the last token only: residual, final norm, vocab projection (fp32 logits)
+    const size_t last = (size_t)(n - 1) * E;
+    (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(1), dim3(NORM_THREADS), norm_smem,
+                     ctx->stream, s.x + last, pending + last, m->out_norm, E, m->eps, h8);
+    ctx->launches++;
+    if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
+    return launch_gemm_q4_0_f16(ctx, m->out_scales, m->out_quants, s.h, logits, m->vocab, E, 1,
+                                SULIMO_OUT_F32, E, 0);
+}
 
 size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch) {
     return scratch_layout(m, batch, nullptr, nullptr);
@@ -290,15 +444,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
     const size_t ctx_len = pos + 1;
     const size_t norm_smem = (size_t)(E + 33) * sizeof(float);
     int st;
-    static int smem_set_device = -1;
-    if (norm_smem > 48 * 1024 && smem_set_device != ctx->device) {
-        if ((st = check_cuda(cudaFuncSetAttribute(add_rmsnorm_q8_kernel,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  (int)norm_smem),
-                             "rmsnorm smem attribute")))
-            return st;
-        smem_set_device = ctx->device;
-    }
+    if ((st = ensure_norm_attr(ctx))) return st;
     // attention workspace for this geometry (grown outside any graph capture by a first call)
     int splits = 0;
     const sulimo_layer_desc& L0 = m->layers[0];
@@ -314,7 +460,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
     const float* pending = nullptr;  // the previous layer's FFN output, added to x next
     for (int l = 0; l < m->n_layers; l++) {
         const sulimo_layer_desc& L = m->layers[l];
-        (void)launch_pdl(add_rmsnorm_q8_kernel, dim3(batch), dim3(NORM_THREADS), norm_smem,
+        (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS), norm_smem,
                          ctx->stream, s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E,
                          m->eps, s.q8);
         ctx->launches++;
@@ -334,7 +480,8 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                          ctx->stream, s.q, (const float*)s.k, (const float*)s.v,
                          reinterpret_cast<const float*>(L.bq), reinterpret_cast<const float*>(L.bk),
                          reinterpret_cast<const float*>(L.bv), H, Hkv, hd, m->rope_dim,
-                         m->rope_mode, m->rope_base, pos, reinterpret_cast<uint8_t*>(L.k_ring),
+                         m->rope_mode, m->rope_base, pos, (size_t)0,
+                         reinterpret_cast<uint8_t*>(L.k_ring),
                          reinterpret_cast<uint8_t*>(L.v_ring), m->kv_capacity, m->kv_seq_stride);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
@@ -345,7 +492,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
             (st = launch_quantize_q8_0(ctx, s.att, s.q8, (size_t)batch * qd)) ||
             (st = launch_gemv_static(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
             return st;
-        (void)launch_pdl(add_rmsnorm_q8_kernel, dim3(batch), dim3(NORM_THREADS), norm_smem,
+        (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS), norm_smem,
                          ctx->stream, s.x, (const float*)s.o,
                          reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, s.q8);
         ctx->launches++;
@@ -369,7 +516,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
             return st;
         pending = s.o;
     }
-    (void)launch_pdl(add_rmsnorm_q8_kernel, dim3(batch), dim3(NORM_THREADS), norm_smem,
+    (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS), norm_smem,
                      ctx->stream, s.x, pending, m->out_norm, E, m->eps, s.q8);
     ctx->launches++;
     if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;

@@ -103,6 +103,12 @@ size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch);
 int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
                          int batch, size_t pos, float* logits, void* scratch);
 int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out);
+size_t prefill_scratch_bytes(const sulimo_model_desc* m, int n);
+int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
+                          int n, size_t start_pos, float* logits, void* scratch);
+int launch_attn_prefill(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
+                        size_t start_pos, size_t capacity, int n_tok, int H, int Hkv, int hd,
+                        void* out);
 // Workspace bytes (and split count) the attention entry point will use for this geometry.
 size_t attn_decode_partial_bytes(size_t context_len, size_t capacity, int head_count,
                                  int head_count_kv, int head_dim, int batch, int num_sms,

@@ -83,6 +83,22 @@ class DecodeModel:
                   self.batch, pos, _p(out), _p(self.scratch), self.scratch.numel())
         return out
 
+    def prefill(self, tokens, start_pos=0, logits=None):
+        """One prefill ubatch of len(tokens) tokens (device int32) of sequence 0 at positions
+        start_pos..; returns the last token's logits [vocab] (execute_prefill_ubatch)."""
+        import torch
+        n = tokens.numel()
+        need = capi.load().sulimo_cuda_prefill_scratch_bytes(self._desc_ptr, n)
+        if need == 0:
+            raise sb.SulimoError(capi.EINVAL, "sulimo_cuda_prefill_scratch_bytes",
+                                 "invalid model description")
+        if getattr(self, "pscratch", None) is None or self.pscratch.numel() < need:
+            self.pscratch = torch.empty(need, dtype=torch.uint8, device="cuda")
+        out = self.logits[:self.cfg["vocab"]] if logits is None else logits
+        capi.call("sulimo_cuda_prefill_ubatch", self.ctx.handle, self._desc_ptr, _p(tokens), n,
+                  start_pos, _p(out), _p(self.pscratch), self.pscratch.numel())
+        return out
+
     def greedy(self, logits=None):
         """Device int32 argmax of each sequence's logits (the greedy sampler's pick)."""
         lg = self.logits if logits is None else logits
