@@ -596,6 +596,69 @@ def run_decode(args, rank, world, local):
     return lines
 
 
+def run_generate(args, rank, world, local):
+    """Config 3: Qwen2.5-1.5B-architecture generation -- prefill of 2048 random token ids as
+    4 ubatches of 512 (execute_prefill_ubatch), then 256 greedy decode tokens into the
+    4096-slot Q8_0 ring (forward_token + on-device argmax; the next token never leaves the
+    GPU).  Prefill and decode are timed separately with CUDA events; decode steps are launched
+    eagerly (the context grows every step).  Replicated per rank."""
+    import torch
+    import sulimo_b200 as sb
+    from sulimo_b200.model import DecodeModel
+    from sulimo_b200.synthetic import QWEN_1_5B, make_model_torch, weight_bytes
+    ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
+    cfg = dict(QWEN_1_5B)
+    w = make_model_torch(cfg, seed=rank, kv_capacity=4096)
+    dm = DecodeModel(ctx, w, batch=1)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7 + rank)
+    n_prompt, ub, n_gen = 2048, 512, args.gen_tokens
+    prompt = torch.randint(0, cfg["vocab"], (n_prompt,), dtype=torch.int32, device="cuda",
+                           generator=gen)
+
+    def prefill():
+        lg = None
+        for s0 in range(0, n_prompt, ub):
+            lg = dm.prefill(prompt[s0:s0 + ub], s0)
+        return lg
+
+    def decode(lg):
+        dm.greedy(lg)
+        for i in range(n_gen):
+            dm.forward_token(dm.next_tokens, n_prompt + i)
+            dm.greedy()
+
+    for _ in range(max(1, args.warmup // 3)):
+        decode(prefill())
+    ctx.finish()
+    barrier(world)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
+    lg = prefill()
+    ev[1].record()
+    decode(lg)
+    ev[2].record()
+    torch.cuda.synchronize()
+    t_pre = max_over_ranks(ev[0].elapsed_time(ev[1]), world)
+    t_dec = max_over_ranks(ev[1].elapsed_time(ev[2]), world)
+    L, E, F = cfg["n_layers"], cfg["embd"], cfg["ffn"]
+    qd, kvd = cfg["head_count"] * cfg["head_dim"], cfg["head_count_kv"] * cfg["head_dim"]
+    layer_params = E * (qd + 2 * kvd) + qd * E + 3 * E * F
+    pre_flop = 2.0 * n_prompt * L * layer_params + 2.0 * cfg["vocab"] * E * (n_prompt // ub)
+    ctx.close()
+    return [{
+        "mode": "generate", "workload": "config 3: Qwen2.5-1.5B-arch, prefill 2048 (4 x 512) + "
+                                        f"{n_gen} greedy decode tokens, 4096-slot Q8_0 ring",
+        "n_gpus": world, "prefill_ms": round(t_pre, 3),
+        "prefill_tok_per_s": round(n_prompt * world / (t_pre * 1e-3), 1),
+        "prefill_tflops_projections": round(pre_flop / (t_pre * 1e-3) / 1e12, 1),
+        "decode_ms": round(t_dec, 3), "decode_ms_per_token": round(t_dec / n_gen, 4),
+        "decode_tok_per_s": round(n_gen * world / (t_dec * 1e-3), 1),
+        "decode_weight_GBps": round(weight_bytes(cfg) * n_gen / (t_dec * 1e-3) / 1e9, 1),
+        "dtype": "q4_0 weights; f16 prefill activations, q8_0 decode activations",
+        "data": "synthetic (seeded Q4_0 weights, random token ids)"}]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -607,10 +670,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--decode-batches", type=int, nargs="+", default=[1, 8, 32],
                     help="--mode decode: sequences per GPU to measure")
-    ap.add_argument("--mode", default="headline", choices=["headline", "sharded", "decode"],
+    ap.add_argument("--gen-tokens", type=int, default=256,
+                    help="--mode generate: greedy decode tokens after the 2048-token prefill")
+    ap.add_argument("--mode", default="headline",
+                    choices=["headline", "sharded", "decode", "generate"],
                     help="headline: the contract line (config 2); sharded: the row-sharded "
                          "lm_head/FFN sweep with an NCCL all-gather; decode: config 4 "
-                         "(Llama-3B decode steps); one JSON line per case")
+                         "(Llama-3B decode steps); generate: config 3 (Qwen-1.5B prefill + "
+                         "greedy decode); one JSON line per case")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -623,8 +690,8 @@ def main():
         return
 
     rank, world, local = dist_setup(args.gpus)
-    if args.mode in ("sharded", "decode"):
-        run = run_sharded if args.mode == "sharded" else run_decode
+    if args.mode in ("sharded", "decode", "generate"):
+        run = {"sharded": run_sharded, "decode": run_decode, "generate": run_generate}[args.mode]
         for line in run(args, rank, world, local):
             if rank == 0:
                 print(json.dumps(line), flush=True)
