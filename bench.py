@@ -527,6 +527,36 @@ def run_sharded(args, rank, world, local):
     return lines
 
 
+def cpu_forward_token_baseline(w, rings, cfg, pos, token, budget_s):
+    """The reference's CPU decode (forward_token, crates/sulimo-engine/src/forward_pass.rs:
+    190-417, restated in the oracle: AVX2 matvecs, 1 thread) on a host copy of the same model
+    and K/V rings, timed at the same position: seconds per token over a bounded sample."""
+    import numpy as np
+    import oracle.ffi as O
+
+    def h(t):
+        if t is None:
+            return None
+        a = t.detach().cpu().numpy()
+        return a.view(np.uint16) if a.dtype == np.int16 else a
+
+    wh = dict(cfg=cfg, tok=(h(w["tok"][0]), h(w["tok"][1])), out_norm=h(w["out_norm"]),
+              layers=[{k: ((h(v[0]), h(v[1])) if isinstance(v, tuple) else h(v))
+                       for k, v in L.items()} for L in w["layers"]])
+    wh["out"] = wh["tok"]
+    om = O.OracleModel(wh)
+    slot = cfg["head_count_kv"] * cfg["head_dim"] // 32 * 34
+    for (kr, vr), (ok, ov) in zip(rings, om.rings):
+        ok[:] = kr.detach().cpu().numpy()[:cfg["kv_capacity"] * slot]
+        ov[:] = vr.detach().cpu().numpy()[:cfg["kv_capacity"] * slot]
+    t0 = time.time()
+    n = 0
+    while n == 0 or time.time() - t0 < budget_s:
+        om.forward_token(token, pos)
+        n += 1
+    return (time.time() - t0) / n, n
+
+
 def run_decode(args, rank, world, local):
     """Config 4: Llama-3.2-3B-architecture decode at context 4096 (each sequence's ring
     pre-filled with 4096 positions of random Q8_0 K/V), batch 1 / 8 / 32 independent sequences.
@@ -590,6 +620,13 @@ def run_decode(args, rank, world, local):
             "frac_of_measured_hbm": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 3),
             "gpu_launches_per_step": launches, "dtype": "q4_0 weights x q8_0 activations",
             "data": "synthetic (seeded Q4_0 weights, random Q8_0 K/V rings)"})
+        if b == 1 and rank == 0 and world == 1 and not args.no_cpu:
+            sec, n = cpu_forward_token_baseline(w, dm.rings, w["cfg"], pos,
+                                                int(tokens[0].item()), args.cpu_seconds)
+            lines[-1]["cpu_baseline"] = {
+                "value": round(1.0 / sec, 3), "unit": "tok/s", "cores": 1, "kind": "port",
+                "sample": f"{n} forward_token call(s) at position {pos} (context {cap}) of the "
+                          "same model and rings, oracle restatement, 1 thread"}
         del graph, dm
         torch.cuda.empty_cache()
     ctx.close()
@@ -645,8 +682,18 @@ def run_generate(args, rank, world, local):
     qd, kvd = cfg["head_count"] * cfg["head_dim"], cfg["head_count_kv"] * cfg["head_dim"]
     layer_params = E * (qd + 2 * kvd) + qd * E + 3 * E * F
     pre_flop = 2.0 * n_prompt * L * layer_params + 2.0 * cfg["vocab"] * E * (n_prompt // ub)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        # the reference's CPU prefill is forward_token per prompt token (engine.rs:287-318)
+        sec, n = cpu_forward_token_baseline(w, dm.rings, w["cfg"], n_prompt - 1,
+                                            int(prompt[-1].item()), args.cpu_seconds)
+        cpu = {"prefill_tok_per_s": round(1.0 / sec, 3), "decode_tok_per_s": round(1.0 / sec, 3),
+               "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": f"{n} forward_token call(s) at position {n_prompt - 1} of the same model "
+                         "and rings (the CPU prefill runs forward_token per prompt token), oracle "
+                         "restatement, 1 thread"}
     ctx.close()
-    return [{
+    out = {
         "mode": "generate", "workload": "config 3: Qwen2.5-1.5B-arch, prefill 2048 (4 x 512) + "
                                         f"{n_gen} greedy decode tokens, 4096-slot Q8_0 ring",
         "n_gpus": world, "prefill_ms": round(t_pre, 3),
@@ -656,7 +703,10 @@ def run_generate(args, rank, world, local):
         "decode_tok_per_s": round(n_gen * world / (t_dec * 1e-3), 1),
         "decode_weight_GBps": round(weight_bytes(cfg) * n_gen / (t_dec * 1e-3) / 1e9, 1),
         "dtype": "q4_0 weights; f16 prefill activations, q8_0 decode activations",
-        "data": "synthetic (seeded Q4_0 weights, random token ids)"}]
+        "data": "synthetic (seeded Q4_0 weights, random token ids)"}
+    if cpu is not None:
+        out["cpu_baseline"] = cpu
+    return [out]
 
 
 def main():
