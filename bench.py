@@ -474,7 +474,7 @@ def run_sharded(args, rank, world, local):
     CUDA events over `steps` iterations after `warmup`, max over ranks.  One JSON line each."""
     import torch
     import sulimo_b200 as sb
-    from sulimo_b200.sharded import ShardedQ4Projection, shard_weight
+    from sulimo_b200.sharded import FusedShardedQ4Projection, ShardedQ4Projection, shard_weight
     ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
     K = 3072
     lines = []
@@ -487,6 +487,7 @@ def run_sharded(args, rank, world, local):
         s_r, q_r, fs = shard_weight(d, qn, F, K, rank, world)
         del d, qn
         proj = ShardedQ4Projection(ctx, s_r, q_r, F, K, fs)
+        fused = FusedShardedQ4Projection(ctx, s_r, q_r, F, K, fs, m_max=8192)
         for M in (1, 16, 128, 1024, 8192):
             x = torch.randn(M * K, device="cuda", dtype=torch.float16, generator=gen)
             g, y = proj.buffers(M, sb.OUT_F16)
@@ -507,6 +508,7 @@ def run_sharded(args, rank, world, local):
             t_gemm = timed(lambda: proj.local_gemm(x, M, g, sb.OUT_F16))
             t_ag = timed(lambda: proj.all_gather(M, g)) if world > 1 else 0.0
             t_e2e = timed(lambda: proj.forward(x, M, g, y, sb.OUT_F16))
+            t_fused = timed(lambda: fused.forward_fused(x, M))
             flop = 2.0 * M * K * F
             ag_bytes = M * F * 2 * (world - 1) / world
             lines.append({
@@ -515,13 +517,18 @@ def run_sharded(args, rank, world, local):
                 "gemm_ms": round(t_gemm, 4), "allgather_ms": round(t_ag, 4),
                 "e2e_ms": round(t_e2e, 4),
                 "e2e_tflops": round(flop / (t_e2e * 1e-3) / 1e12, 2),
+                "fused_ms": round(t_fused, 4),
+                "fused_tflops": round(flop / (t_fused * 1e-3) / 1e12, 2),
                 "gemm_tflops_per_gpu": round(flop / world / (t_gemm * 1e-3) / 1e12, 2),
                 "allgather_GBps_per_gpu": round(ag_bytes / (t_ag * 1e-3) / 1e9, 1)
                 if t_ag > 0 else None,
                 "data": "synthetic (seeded Q4_0 d=f16(|N|*0.02), nibbles U{0..15}; x f16 N(0,1))",
-                "exchange": "NCCL all_gather_into_tensor (shard-major) + unshard_rows kernel"})
+                "exchange": "e2e: NCCL all_gather_into_tensor (shard-major) + unshard_rows "
+                            "kernel; fused: GEMM epilogue TMA-stores every tile into every "
+                            "rank's row-major Y over NVLink + arrival counters"})
             del x, g, y
-        del proj, s_r, q_r
+        fused.close()
+        del proj, fused, s_r, q_r
         torch.cuda.empty_cache()
     ctx.close()
     return lines

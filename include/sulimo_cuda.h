@@ -177,6 +177,30 @@ int sulimo_cuda_dequantize_q4_0_rows(sulimo_ctx* ctx, const void* scales, const 
 int sulimo_cuda_unshard_rows(sulimo_ctx* ctx, const void* gathered, void* out, int world,
                              int m_tokens, size_t fs, size_t f, int elem_size);
 
+/* ---- multi-GPU: the row-sharded projection with the all-gather fused into the GEMM --------- */
+/* CUDA IPC of a library buffer (a cudaMalloc base): 64-byte handle out; another process opens  */
+/* it with sulimo_cuda_ipc_open (peer access enabled) and closes it with sulimo_cuda_ipc_close.  */
+int sulimo_cuda_ipc_handle(sulimo_buf* buf, void* handle_out);
+int sulimo_cuda_ipc_open(sulimo_ctx* ctx, const void* handle, void** dev_ptr_out);
+int sulimo_cuda_ipc_close(sulimo_ctx* ctx, void* dev_ptr);
+
+/* This rank's rows [col0, col0 + m_local) of a Q4_0 [F][k] projection (m_local rows computed,  */
+/* the first m_valid of them stored) for n tokens of x [n][k] f16, written straight into every  */
+/* rank's row-major result Y[n][f_total] (out_bases: host array of `world` device pointers      */
+/* valid in this process, i.e. opened IPC mappings) over NVLink, then one arrival per CTA added */
+/* to every rank's counter (flags: host array of `world` device pointers).  *tiles_out = CTAs   */
+/* of this launch.  A rank's Y is complete once its counter has grown by the sum of all ranks' */
+/* CTAs: sulimo_cuda_wait_counter.  No split-K.                                                 */
+int sulimo_cuda_gemm_q4_0_f16_allgather(sulimo_ctx* ctx, const void* scales, const void* quants,
+                                        const void* x, int m_local, int m_valid, int k, int n,
+                                        int out_dtype, void* const* out_bases, size_t f_total,
+                                        size_t col0, unsigned* const* flags, int world,
+                                        unsigned* tiles_out);
+
+/* Enqueues a bounded wait (one thread; SULIMO_EDEVICE at the next synchronize after ~2 s)     */
+/* until *flag (device) reaches `target` (modulo 2^32 arithmetic).                             */
+int sulimo_cuda_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned target);
+
 /* ---------------------------------------------------------------------------------------- */
 /* Whole decode position — replaces forward_token                                            */
 /* (crates/sulimo-engine/src/forward_pass.rs:190-417; Llama and Qwen2 branches) for a batch   */

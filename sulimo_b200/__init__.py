@@ -60,6 +60,34 @@ class CudaContext:
         """Blocks until the stream drains; raises on a device-side error (OclContext::finish)."""
         capi.call("sulimo_cuda_ctx_synchronize", self.handle)
 
+    # ---- library-owned device buffers (OclBuffer, crates/sulimo-ocl/src/buffer.rs) ----
+    def alloc(self, size):
+        """A device buffer of `size` bytes (a cudaMalloc base); returns its handle."""
+        import ctypes as C
+        h = C.c_void_p()
+        capi.call("sulimo_cuda_buffer_alloc", self.handle, size, C.byref(h))
+        return h.value
+
+    def write(self, buf, data, off=0):
+        """Host bytes / numpy array -> buffer at byte offset `off`."""
+        import numpy as np
+        a = np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray)) else \
+            np.ascontiguousarray(data).view(np.uint8).ravel()
+        capi.call("sulimo_cuda_buffer_write", buf, off, a.ctypes.data, a.nbytes)
+
+    def read(self, buf, out, off=0):
+        """Buffer bytes at `off` -> the numpy array `out` (its nbytes)."""
+        capi.call("sulimo_cuda_buffer_read", buf, off, out.ctypes.data, out.nbytes)
+        return out
+
+    @staticmethod
+    def device_ptr(buf):
+        return capi.load().sulimo_cuda_buffer_device_ptr(buf)
+
+    @staticmethod
+    def free(buf):
+        capi.call("sulimo_cuda_buffer_free", buf)
+
     def close(self):
         if self.handle:
             capi.load().sulimo_cuda_ctx_destroy(self.handle)

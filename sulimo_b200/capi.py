@@ -51,6 +51,12 @@ SIGNATURES = {
     "sulimo_cuda_kv_store_q8_0": (_i, [_vp, _vp, _i, _vp, _sz, _sz, _sz, _sz]),
     "sulimo_cuda_dequantize_q4_0_rows": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i]),
     "sulimo_cuda_unshard_rows": (_i, [_vp, _vp, _vp, _i, _i, _sz, _sz, _i]),
+    "sulimo_cuda_ipc_handle": (_i, [_vp, _vp]),
+    "sulimo_cuda_ipc_open": (_i, [_vp, _vp, C.POINTER(_vp)]),
+    "sulimo_cuda_ipc_close": (_i, [_vp, _vp]),
+    "sulimo_cuda_gemm_q4_0_f16_allgather": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz,
+                                                 _sz, _vp, _i, C.POINTER(C.c_uint)]),
+    "sulimo_cuda_wait_counter": (_i, [_vp, _vp, C.c_uint]),
     "sulimo_cuda_forward_scratch_bytes": (_sz, [_vp, _i]),
     "sulimo_cuda_forward_token": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _sz]),
     "sulimo_cuda_argmax_rows": (_i, [_vp, _vp, _i, _i, _vp]),

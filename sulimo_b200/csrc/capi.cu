@@ -598,6 +598,72 @@ int sulimo_cuda_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols,
     return sulimo::launch_argmax_rows(ctx, x, rows, cols, out);
 }
 
+int sulimo_cuda_ipc_handle(sulimo_buf* buf, void* handle_out) {
+    if (!buf || !buf->dev || !handle_out) return set_error(SULIMO_EINVAL, "null buffer / handle");
+    cudaSetDevice(buf->ctx->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, buf->dev);
+    if (e != cudaSuccess) return sulimo::check_cuda(e, "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    memcpy(handle_out, &h, sizeof(h));
+    return SULIMO_OK;
+}
+
+int sulimo_cuda_ipc_open(sulimo_ctx* ctx, const void* handle, void** dev_ptr_out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (!handle || !dev_ptr_out) return set_error(SULIMO_EINVAL, "null handle / out");
+    if ((st = bind_device(ctx))) return st;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return sulimo::check_cuda(cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess),
+                              "cudaIpcOpenMemHandle");
+}
+
+int sulimo_cuda_ipc_close(sulimo_ctx* ctx, void* dev_ptr) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::check_cuda(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+}
+
+int sulimo_cuda_gemm_q4_0_f16_allgather(sulimo_ctx* ctx, const void* scales, const void* quants,
+                                        const void* x, int m_local, int m_valid, int k, int n,
+                                        int out_dtype, void* const* out_bases, size_t f_total,
+                                        size_t col0, unsigned* const* flags, int world,
+                                        unsigned* tiles_out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (world < 1 || world > 8) return set_error(SULIMO_EINVAL, "world must be in [1, 8]");
+    if (m_local <= 0 || m_local % 8 || m_valid <= 0 || m_valid > m_local || m_valid % 8 ||
+        k <= 0 || k % 32 || n <= 0)
+        return set_error(SULIMO_EINVAL, "m_local, m_valid multiples of 8; k of 32; n > 0");
+    if (out_dtype != SULIMO_OUT_F16 && out_dtype != SULIMO_OUT_F32)
+        return set_error(SULIMO_EINVAL, "bad out_dtype");
+    if (f_total % 8 || col0 % 8 || col0 + (size_t)m_valid > f_total)
+        return set_error(SULIMO_EINVAL, "col0 + m_valid <= f_total, both multiples of 8");
+    if (!scales || !quants || !x || !out_bases || !flags || !tiles_out)
+        return set_error(SULIMO_EINVAL, "null pointer");
+    for (int r = 0; r < world; r++) {
+        if (!out_bases[r] || !flags[r]) return set_error(SULIMO_EINVAL, "null peer pointer");
+        if (!aligned(out_bases[r], 16) || !aligned(flags[r], 4))
+            return set_error(SULIMO_EALIGN, "peer outputs 16-byte, counters 4-byte aligned");
+    }
+    if (!aligned(x, 16) || !aligned(quants, 16) || !aligned(scales, 2))
+        return set_error(SULIMO_EALIGN, "x, quants 16-byte aligned, scales 2-byte");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_gemm_allgather(ctx, scales, quants, x, m_local, m_valid, k, n, out_dtype,
+                                         out_bases, f_total, col0, flags, world, tiles_out);
+}
+
+int sulimo_cuda_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned target) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (!flag || !aligned(flag, 4)) return set_error(SULIMO_EINVAL, "null / misaligned counter");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_wait_counter(ctx, flag, target);
+}
+
 int sulimo_cuda_attn_decode_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
                                  const void* v_ring, size_t seq_stride_bytes, size_t capacity,
                                  size_t context_len, int head_count, int head_count_kv,

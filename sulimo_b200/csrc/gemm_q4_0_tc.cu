@@ -28,6 +28,8 @@
 // Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records a device error,
 // drains its in-flight copies / MMAs (again bounded), frees TMEM and returns.
 // No TMA multicast: each CTA loads its own tiles.
+#include <string.h>
+
 #include "sulimo_common.cuh"
 #include "sulimo_internal.h"
 
@@ -109,6 +111,11 @@ __device__ __forceinline__ void bulk_commit() {
 // writes complete on their own before the grid is complete).
 __device__ __forceinline__ void bulk_wait_read_all() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Waits until the committed bulk stores' global writes are complete and visible to this thread.
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
@@ -258,16 +265,28 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Row-sharded projection with the all-gather fused into the epilogue: every output chunk is
+// stored (TMA tensor store, no multicast) into each rank's row-major result Y[n][F] over
+// NVLink peer mappings, at this rank's column offset; when a CTA's stores are complete it adds
+// 1 to every rank's arrival counter (system-scope atomics).  A rank's result is complete when
+// its counter has received every rank's CTAs (wait_counter_kernel).
+constexpr int MAX_PEERS = 8;
+struct PeerOut {
+    CUtensorMap map[MAX_PEERS];    // [m_local cols][n rows] of rank r's Y, 32-token boxes
+    CUtensorMap map16[MAX_PEERS];  // the same, 16-token boxes (a tile's 16-token remainder)
+    unsigned* flags[MAX_PEERS];    // rank r's arrival counter
+    int world;
+};
+
 // OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace
-// [split][n][m] (all by TMA tensor stores).
+// [split][n][m], 3 / 4 = f16 / f32 to every rank's Y (all by TMA tensor stores).
 template <int OUT_MODE>
-__global__ void __launch_bounds__(THREADS, 1)
-    gemm_q4_0_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                        const __grid_constant__ CUtensorMap tmap_q,
-                        const __grid_constant__ CUtensorMap tmap_out,
-                        const __grid_constant__ CUtensorMap tmap_out16,
-                        const uint16_t* __restrict__ scales, int m, int k, int n, int bn, int nb,
-                        int iters_per_split, int stages, int* __restrict__ err) {
+__device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUtensorMap& tmap_q,
+                                          const CUtensorMap& tmap_out,
+                                          const CUtensorMap& tmap_out16,
+                                          const uint16_t* __restrict__ scales, int m, int k,
+                                          int n, int bn, int nb, int iters_per_split, int stages,
+                                          const PeerOut* peers, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -419,7 +438,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // valid, so a warp that gave up on a wait cannot strand the others.
         const bool have = ok && (num_k == 0 || mbar_wait_bounded(done, 0, err, abort_flag));
         if (have) tc_fence_after();
-        constexpr int ES = (OUT_MODE == 0) ? 2 : 4;
+        constexpr int ES = (OUT_MODE == 0 || OUT_MODE == 3) ? 2 : 4;
         {
             const bool issuer = (warp - 2) % 4 == 0 && lane == 0;
             for (int c0 = group * EPI_TOKENS; c0 < bn; c0 += DEQ_GROUPS * EPI_TOKENS) {
@@ -447,15 +466,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                 named_barrier_sync(1 + group, 128);
                 if (issuer && have && !*abort_flag && n0 + c0 < n) {
                     // a 16-token remainder (bn % 32 == 16) must not spill into the next tile
-                    const CUtensorMap* map = c0 + EPI_TOKENS <= bn ? &tmap_out : &tmap_out16;
-                    if (OUT_MODE == 2)
-                        tma_store_3d(map, m0, n0 + c0, (int)blockIdx.z, tile);
-                    else
-                        tma_store_2d(map, m0, n0 + c0, tile);
+                    const bool whole = c0 + EPI_TOKENS <= bn;
+                    if (OUT_MODE >= 3) {
+                        for (int rk = 0; rk < peers->world; rk++)
+                            tma_store_2d(whole ? &peers->map[rk] : &peers->map16[rk], m0, n0 + c0,
+                                         tile);
+                    } else {
+                        const CUtensorMap* map = whole ? &tmap_out : &tmap_out16;
+                        if (OUT_MODE == 2)
+                            tma_store_3d(map, m0, n0 + c0, (int)blockIdx.z, tile);
+                        else
+                            tma_store_2d(map, m0, n0 + c0, tile);
+                    }
                     bulk_commit();
                 }
             }
-            if (issuer) bulk_wait_read_all();
+            if (issuer) {
+                if (OUT_MODE >= 3)
+                    bulk_wait_all();  // the peers read these rows once the counters say so
+                else
+                    bulk_wait_read_all();
+            }
+        }
+        if (OUT_MODE >= 3) {
+            named_barrier_sync(5, 32 * DEQ_WARPS);
+            if (warp == 2 && lane == 0 && have && !*abort_flag) {
+                __threadfence_system();
+                for (int rk = 0; rk < peers->world; rk++) atomicAdd_system(peers->flags[rk], 1u);
+            }
         }
     }
 
@@ -466,6 +504,48 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(TMEM_COLS)
                      : "memory");
+    }
+}
+
+template <int OUT_MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_q4_0_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                        const __grid_constant__ CUtensorMap tmap_q,
+                        const __grid_constant__ CUtensorMap tmap_out,
+                        const __grid_constant__ CUtensorMap tmap_out16,
+                        const uint16_t* __restrict__ scales, int m, int k, int n, int bn, int nb,
+                        int iters_per_split, int stages, int* __restrict__ err) {
+    gemm_body<OUT_MODE>(tmap_x, tmap_q, tmap_out, tmap_out16, scales, m, k, n, bn, nb,
+                        iters_per_split, stages, nullptr, err);
+}
+
+template <int OUT_MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_q4_0_tc_allgather_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                  const __grid_constant__ CUtensorMap tmap_q,
+                                  const uint16_t* __restrict__ scales, int m, int k, int n, int bn,
+                                  int nb, int stages, const __grid_constant__ PeerOut peers,
+                                  int* __restrict__ err) {
+    gemm_body<OUT_MODE>(tmap_x, tmap_q, tmap_x, tmap_x, scales, m, k, n, bn, nb, (k + BK - 1) / BK,
+                        stages, &peers, err);
+}
+
+// Bounded wait (one thread) until *flag reaches target; records a device error after
+// SULIMO_WAIT_LIMIT_NS instead of hanging.  Waits only on other GPUs' kernels (and this GPU's
+// earlier, already finished, launch).
+__global__ void wait_counter_kernel(const unsigned* __restrict__ flag, unsigned target,
+                                    int* __restrict__ err) {
+    if (threadIdx.x != 0) return;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if ((int)(v - target) >= 0) break;
+        if (globaltimer_ns() - t0 > SULIMO_WAIT_LIMIT_NS) {
+            record_device_error(err, SULIMO_DEVERR_WAIT_TIMEOUT);
+            break;
+        }
+        __nanosleep(256);
     }
 }
 
@@ -490,6 +570,14 @@ int set_smem_attr(int device) {
     static uint64_t mask = 0;  // the attribute is per device
     const uint64_t bit = 1ull << (device & 63);
     if (mask & bit) return SULIMO_OK;
+    if (MODE >= 3) {
+        int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_allgather_kernel<MODE>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)SMEM_LIMIT),
+                            "gemm smem attribute");
+        if (!st) mask |= bit;
+        return st;
+    }
     int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<MODE>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)SMEM_LIMIT),
@@ -593,6 +681,63 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
                          out, nm, splits);
     ctx->launches += 2;
     return check_cuda(e, "splitk_reduce launch");
+}
+
+}  // namespace sulimo
+
+namespace sulimo {
+
+int launch_gemm_allgather(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
+                          int m_local, int m_valid, int k, int n, int out_dtype,
+                          void* const* out_bases, size_t f_total, size_t col0,
+                          unsigned* const* flags, int world, unsigned* tiles_out) {
+    const int nb = k / 32;
+    const int bn = gemm_token_tile(n);
+    const int stages = ring_stages(bn);
+    const uint32_t smem = smem_bytes(bn, stages);
+    const bool f32 = out_dtype == SULIMO_OUT_F32;
+    const int es = f32 ? 4 : 2;
+    CUtensorMap tx, tq;
+    int st = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, (uint64_t)k, (uint64_t)n,
+                       (uint64_t)k * 2, BK, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16, (uint64_t)m_local,
+                   (uint64_t)nb * 16, 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    PeerOut peers;
+    memset(&peers, 0, sizeof(peers));
+    peers.world = world;
+    const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    for (int r = 0; r < world; r++) {
+        const uint8_t* base = reinterpret_cast<const uint8_t*>(out_bases[r]) + col0 * es;
+        // the map spans only this shard's valid columns: zero-scale padding rows are clipped
+        if ((st = encode_2d(&peers.map[r], dt, base, (uint64_t)m_valid, (uint64_t)n,
+                            (uint64_t)f_total * es, BM, (uint32_t)EPI_TOKENS,
+                            CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+            (st = encode_2d(&peers.map16[r], dt, base, (uint64_t)m_valid, (uint64_t)n,
+                            (uint64_t)f_total * es, BM, 16u, CU_TENSOR_MAP_SWIZZLE_NONE)))
+            return st;
+        peers.flags[r] = flags[r];
+    }
+    if ((st = f32 ? set_smem_attr<4>(ctx->device) : set_smem_attr<3>(ctx->device))) return st;
+    const int mt = (m_local + BM - 1) / BM, nt = (n + bn - 1) / bn;
+    if (nt > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
+    *tiles_out = (unsigned)(mt * nt);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(scales);
+    dim3 grid(mt, nt, 1);
+    const cudaError_t e =
+        f32 ? launch_pdl(gemm_q4_0_tc_allgather_kernel<4>, grid, dim3(THREADS), smem, ctx->stream,
+                         tx, tq, sc, m_local, k, n, bn, nb, stages, peers, ctx->d_error)
+            : launch_pdl(gemm_q4_0_tc_allgather_kernel<3>, grid, dim3(THREADS), smem, ctx->stream,
+                         tx, tq, sc, m_local, k, n, bn, nb, stages, peers, ctx->d_error);
+    ctx->launches++;
+    return check_cuda(e, "gemm_q4_0_tc all-gather launch");
+}
+
+int launch_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned target) {
+    wait_counter_kernel<<<1, 32, 0, ctx->stream>>>(flag, target, ctx->d_error);
+    ctx->launches++;
+    return check_cuda(cudaGetLastError(), "wait_counter launch");
 }
 
 }  // namespace sulimo

@@ -68,6 +68,14 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base
 int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                          void* out, int m, int k, int n, int out_dtype, int x_row_stride,
                          int x_row_offset);
+// Row-sharded GEMM with the all-gather in the epilogue (see gemm_q4_0_tc.cu): stores this rank's
+// [n][m_local] result at column col0 of every rank's row-major Y (row pitch f_total elements,
+// out_bases[r] mapped in this process) and adds one per CTA to every rank's counter.
+int launch_gemm_allgather(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
+                          int m_local, int m_valid, int k, int n, int out_dtype,
+                          void* const* out_bases, size_t f_total, size_t col0,
+                          unsigned* const* flags, int world, unsigned* tiles_out);
+int launch_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned target);
 int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                           const void* x_q8, int rows, int cols, int batch, float* out);
 // One matrix of a grouped decode GEMV (all of a group share K and the activations).

@@ -89,3 +89,93 @@ class ShardedQ4Projection:
         else:
             sb.unshard_rows(self.ctx, gather, y, self.world, m, self.fs, self.f)
         return y
+
+
+class FusedShardedQ4Projection(ShardedQ4Projection):
+    """The same projection with the all-gather fused into the GEMM: every rank's epilogue
+    stores its output tiles straight into every rank's row-major Y[M][F] over NVLink (peer
+    mappings of library buffers exchanged as CUDA IPC handles) and bumps every rank's arrival
+    counter; `forward` then waits (bounded, on the device) until this rank's counter has all
+    ranks' CTAs.  No NCCL on the data path, no unshard pass.  Y and the counters are allocated
+    once for up to `m_max` tokens; calls must alternate in lockstep on all ranks (the counter
+    targets advance by one call's arrivals each time), so this path is not captured in graphs.
+    """
+
+    def __init__(self, ctx, scales_r, quants_r, f, k, fs, m_max, out_dtype=sb.OUT_F16,
+                 group=None):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+        from sulimo_b200 import capi
+        super().__init__(ctx, scales_r, quants_r, f, k, fs, group)
+        if f % 8:
+            raise ValueError("F must be a multiple of 8")
+        self.m_max, self.out_dtype = m_max, out_dtype
+        self.es = 2 if out_dtype == sb.OUT_F16 else 4
+        self.y_buf = ctx.alloc(m_max * f * self.es)
+        self.flag_buf = ctx.alloc(256)
+        ctx.write(self.flag_buf, bytes(256))
+        handles = torch.zeros(2, 64, dtype=torch.uint8)
+        hbuf = (C.c_uint8 * 64)()
+        for i, b in enumerate((self.y_buf, self.flag_buf)):
+            capi.call("sulimo_cuda_ipc_handle", b, hbuf)
+            handles[i] = torch.tensor(list(hbuf), dtype=torch.uint8)
+        if self.world > 1:
+            allh = torch.empty(self.world, 2, 64, dtype=torch.uint8, device="cuda")
+            dist.all_gather_into_tensor(allh, handles.cuda(), group=group)
+            allh = allh.cpu()
+        else:
+            allh = handles.unsqueeze(0)
+        self.opened = []
+        bases, flags = [], []
+        for r in range(self.world):
+            if r == self.rank:
+                bases.append(ctx.device_ptr(self.y_buf))
+                flags.append(ctx.device_ptr(self.flag_buf))
+                continue
+            ptrs = []
+            for i in range(2):
+                out = C.c_void_p()
+                h = (C.c_uint8 * 64)(*allh[r, i].tolist())
+                capi.call("sulimo_cuda_ipc_open", ctx.handle, h, C.byref(out))
+                ptrs.append(out.value)
+                self.opened.append(out.value)
+            bases.append(ptrs[0])
+            flags.append(ptrs[1])
+        self.bases = (C.c_void_p * self.world)(*bases)
+        self.flags = (C.c_void_p * self.world)(*flags)
+        self.own_flag = ctx.device_ptr(self.flag_buf)
+        self.epoch_arrivals = 0
+        self.valid = min(f - self.rank * fs, fs)
+
+    def forward_fused(self, x, m):
+        """Y[m][F] on every rank (device pointer of this rank's copy); x [m][k] f16."""
+        import ctypes as C
+        from sulimo_b200 import capi
+        if m > self.m_max:
+            raise ValueError("m exceeds the buffers' m_max")
+        tiles = C.c_uint()
+        capi.call("sulimo_cuda_gemm_q4_0_f16_allgather", self.ctx.handle, self.scales.data_ptr(),
+                  self.quants.data_ptr(), x.data_ptr(), self.fs, self.valid, self.k, m,
+                  self.out_dtype, self.bases, self.f, self.rank * self.fs, self.flags, self.world,
+                  C.byref(tiles))
+        # every rank launches the same tile count (equal fs), so one call adds world * tiles
+        self.epoch_arrivals = (self.epoch_arrivals + self.world * tiles.value) & 0xFFFFFFFF
+        capi.call("sulimo_cuda_wait_counter", self.ctx.handle, self.own_flag, self.epoch_arrivals)
+        return self.ctx.device_ptr(self.y_buf)
+
+    def read(self, m):
+        """Host copy of Y[m][F] (numpy f16 / f32)."""
+        import numpy as np
+        out = np.empty(m * self.f, np.float16 if self.es == 2 else np.float32)
+        self.ctx.read(self.y_buf, out)
+        return out.reshape(m, self.f)
+
+    def close(self):
+        from sulimo_b200 import capi
+        for p in self.opened:
+            capi.call("sulimo_cuda_ipc_close", self.ctx.handle, p)
+        self.opened = []
+        self.ctx.free(self.y_buf)
+        self.ctx.free(self.flag_buf)

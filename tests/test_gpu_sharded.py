@@ -124,3 +124,83 @@ def test_nccl_all_gather_two_gpus():
         assert p.exitcode == 0
     for rank, err in res:
         assert err <= 2e-3, (rank, err)
+
+
+# ---- the all-gather fused into the GEMM epilogue (peer stores over NVLink + counters) ---------
+
+def test_fused_allgather_single_rank(ctx):
+    """world 1: the fused epilogue stores into the rank's own Y and the counter wait passes;
+    two calls in a row (the counter target advances)."""
+    from sulimo_b200.sharded import FusedShardedQ4Projection
+    f, k = 1024, 512
+    ws, wq = make_q4_0(f, k, seed=31)
+    dws, dwq = dev(ws), dev(wq)
+    proj = FusedShardedQ4Projection(ctx, dws, dwq, f, k, f, m_max=48, out_dtype=sb.OUT_F32)
+    try:
+        for m, seed in ((48, 1), (17, 2)):
+            x = np.random.default_rng(seed).standard_normal(m * k).astype(np.float16)
+            proj.forward_fused(dev(x), m)
+            ctx.finish()
+            got = proj.read(m)
+            ref = O.gemm_q4_0_f16_f32out(ws, wq, x.view(np.uint16), f, k, m, threads=8)
+            assert rel_l2(got.ravel(), ref) <= 2e-3
+    finally:
+        proj.close()
+
+
+def _fused_rank(rank, world, port, f, k, m, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from sulimo_b200.sharded import FusedShardedQ4Projection, shard_weight
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        ctx = sb.CudaContext(rank, stream=torch.cuda.current_stream())
+        ws, wq = make_q4_0(f, k, seed=8)
+        dws, dwq = dev(ws), dev(wq)
+        s_r, q_r, fs = shard_weight(dws, dwq, f, k, rank, world)
+        proj = FusedShardedQ4Projection(ctx, s_r, q_r, f, k, fs, m_max=m, out_dtype=sb.OUT_F32)
+        outs = []
+        for seed in (9, 10):  # two calls: the counters' targets advance
+            x = np.random.default_rng(seed).standard_normal(m * k).astype(np.float16)
+            proj.forward_fused(dev(x), m)
+            ctx.finish()
+            outs.append(proj.read(m).copy())
+            dist.barrier()  # a peer's next call stores into this Y: read it first
+        dist.barrier()  # no rank closes its mappings while a peer may still store into them
+        proj.close()
+        q.put((rank, outs))
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_allgather_two_gpus():
+    """Both ranks end with the same full Y, equal to the single-device projection."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    f, k, m = 2000, 1024, 40   # uneven shards: 1000 rows each; ragged token tile
+    c = mp.get_context("spawn")
+    q = c.Queue()
+    procs = [c.Process(target=_fused_rank, args=(r, 2, port, f, k, m, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ws, wq = make_q4_0(f, k, seed=8)
+    for i, seed in enumerate((9, 10)):
+        assert np.array_equal(res[0][i].view(np.uint32), res[1][i].view(np.uint32))
+        x = np.random.default_rng(seed).standard_normal(m * k).astype(np.float16)
+        ref = O.gemm_q4_0_f16_f32out(ws, wq, x.view(np.uint16), f, k, m, threads=8)
+        assert rel_l2(res[0][i].ravel(), ref) <= 2e-3
