@@ -141,6 +141,14 @@ int sulimo_cuda_logits_final(sulimo_ctx* ctx, const void* x_all, const void* sca
 int sulimo_cuda_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                                const void* x_q8, int rows, int cols, int batch, float* out);
 
+/* Same result as sulimo_cuda_gemv_q4_0_q8_0 for weights that the previous kernel on the stream */
+/* does not write (a decode step's model parameters): the first weight tiles are fetched before */
+/* the launch's wait on the previous kernel, so back-to-back matvecs overlap their weight       */
+/* streams.  The activations are always read after the wait.                                    */
+int sulimo_cuda_gemv_q4_0_q8_0_static(sulimo_ctx* ctx, const void* w_scales,
+                                      const void* w_quants, const void* x_q8, int rows, int cols,
+                                      int batch, float* out);
+
 /* Integer per-block sums (debug / parity entry): out[b][r*(cols/32)+j] = sum_i (w_i-8)*x_i, */
 /* the i32 `block_sum` of vec_dot_q4_0_q8_0_scalar (crates/sulimo-cpu/src/scalar.rs:189-199). */
 int sulimo_cuda_block_sums_q4_0_q8_0(sulimo_ctx* ctx, const void* w_quants, const void* x_q8,

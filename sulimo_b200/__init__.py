@@ -116,10 +116,14 @@ def logits_final(ctx, x_all, scales, quants, logits, vocab, embd, token_idx):
               _ptr(logits), vocab, embd, token_idx)
 
 
-def dispatch_matvec_q4_0_q8_0(ctx, w_scales, w_quants, x_q8, rows, cols, out, batch=1):
-    """dispatch_matvec_q4_0_q8_0 (crates/sulimo-cpu/src/avx2.rs:17-37), AVX2-bit-exact."""
-    capi.call("sulimo_cuda_gemv_q4_0_q8_0", ctx.handle, _ptr(w_scales), _ptr(w_quants),
-              _ptr(x_q8), rows, cols, batch, _ptr(out))
+def dispatch_matvec_q4_0_q8_0(ctx, w_scales, w_quants, x_q8, rows, cols, out, batch=1,
+                              static_weights=False):
+    """dispatch_matvec_q4_0_q8_0 (crates/sulimo-cpu/src/avx2.rs:17-37), AVX2-bit-exact.
+    static_weights: the weights are not written by the previous kernel on the stream (model
+    parameters), so the launch may start streaming them before that kernel finishes."""
+    name = "sulimo_cuda_gemv_q4_0_q8_0_static" if static_weights else "sulimo_cuda_gemv_q4_0_q8_0"
+    capi.call(name, ctx.handle, _ptr(w_scales), _ptr(w_quants), _ptr(x_q8), rows, cols, batch,
+              _ptr(out))
 
 
 def block_sums_q4_0_q8_0(ctx, w_quants, x_q8, rows, cols, out):

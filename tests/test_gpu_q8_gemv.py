@@ -195,3 +195,24 @@ def test_gemv_rejects_bad_cols(ctx):
     t = empty(64, torch.uint8)
     with pytest.raises(sb.SulimoError):
         sb.dispatch_matvec_q4_0_q8_0(ctx, t, t, t, 1, 48, empty(1, torch.float32))
+
+
+@pytest.mark.parametrize("rows,cols,batch", [(8960, 1536, 1), (3072, 8192, 1), (300, 2048, 4)])
+def test_gemv_static_weights_bit_exact(ctx, rows, cols, batch):
+    """The static-weights entry (weight tiles fetched before the launch's dependency wait) gives
+    the same bits, also when launched right behind another matvec writing its activations'
+    neighbour buffer."""
+    import torch
+    ws, wq = make_q4_0(rows, cols, seed=rows + 3)
+    x = np.random.default_rng(batch + 5).standard_normal((batch, cols)).astype(np.float32)
+    xq8 = np.concatenate([O.quantize_f32_to_q8_0(x[b]) for b in range(batch)])
+    out = empty(batch * rows, torch.float32)
+    dws, dwq, dx = dev(ws), dev(wq), dev(xq8)
+    for _ in range(2):
+        sb.dispatch_matvec_q4_0_q8_0(ctx, dws, dwq, dx, rows, cols, out, batch, True)
+    ctx.finish()
+    got = host(out).reshape(batch, rows)
+    for b in range(batch):
+        ref = O.matvec_q4_0_q8_0_avx2(ws, wq, xq8[b * cols // 32 * 34:(b + 1) * cols // 32 * 34],
+                                      rows, cols, threads=8)
+        assert np.array_equal(got[b].view(np.uint32), ref.view(np.uint32))
