@@ -149,6 +149,16 @@ int sulimo_cuda_gemv_q4_0_q8_0_static(sulimo_ctx* ctx, const void* w_scales,
                                       const void* w_quants, const void* x_q8, int rows, int cols,
                                       int batch, float* out);
 
+/* Fast mode of the same matvec (SURVEY's exact_mode = 0): the integer block sums are the      */
+/* reference's, exact; each row's blocks are split over 8 fp32 partial sums (block index mod 8) */
+/* combined as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)), so the result differs from the AVX2 add   */
+/* order only by fp32 rounding and is deterministic for a given shape.  This is the form the   */
+/* decode step (sulimo_cuda_forward_token) streams its weights with.  static_weights != 0: the */
+/* weights are not written by the previous kernel on the stream (see the _static entry).       */
+int sulimo_cuda_gemv_q4_0_q8_0_fast(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
+                                    const void* x_q8, int rows, int cols, int batch, float* out,
+                                    int static_weights);
+
 /* Integer per-block sums (debug / parity entry): out[b][r*(cols/32)+j] = sum_i (w_i-8)*x_i, */
 /* the i32 `block_sum` of vec_dot_q4_0_q8_0_scalar (crates/sulimo-cpu/src/scalar.rs:189-199). */
 int sulimo_cuda_block_sums_q4_0_q8_0(sulimo_ctx* ctx, const void* w_quants, const void* x_q8,

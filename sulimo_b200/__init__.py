@@ -126,6 +126,15 @@ def dispatch_matvec_q4_0_q8_0(ctx, w_scales, w_quants, x_q8, rows, cols, out, ba
               _ptr(out))
 
 
+def matvec_q4_0_q8_0_fast(ctx, w_scales, w_quants, x_q8, rows, cols, out, batch=1,
+                          static_weights=False):
+    """Fast mode of dispatch_matvec_q4_0_q8_0: the reference's exact integer block sums, fp32
+    partials over 8 block residues per row combined in a fixed tree (not the AVX2 add order;
+    equal to fp32 rounding, deterministic).  The decode step's matvec."""
+    capi.call("sulimo_cuda_gemv_q4_0_q8_0_fast", ctx.handle, _ptr(w_scales), _ptr(w_quants),
+              _ptr(x_q8), rows, cols, batch, _ptr(out), 1 if static_weights else 0)
+
+
 def block_sums_q4_0_q8_0(ctx, w_quants, x_q8, rows, cols, out):
     capi.call("sulimo_cuda_block_sums_q4_0_q8_0", ctx.handle, _ptr(w_quants), _ptr(x_q8), rows,
               cols, _ptr(out))

@@ -18,6 +18,7 @@ SOURCES = [
     "capi.cu",
     "q8_0.cu",
     "gemv_q4_0_q8_0.cu",
+    "gemv_fast_q4_0_q8_0.cu",
     "attn_decode_q8_0.cu",
     "attn_decode_noalloc.cu",
     "gemm_q4_0_tc.cu",

@@ -47,6 +47,7 @@ SIGNATURES = {
     "sulimo_cuda_logits_final": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
     "sulimo_cuda_gemv_q4_0_q8_0": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "sulimo_cuda_gemv_q4_0_q8_0_static": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "sulimo_cuda_gemv_q4_0_q8_0_fast": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]),
     "sulimo_cuda_block_sums_q4_0_q8_0": (_i, [_vp, _vp, _vp, _i, _i, _vp]),
     "sulimo_cuda_quantize_q8_0": (_i, [_vp, _vp, _vp, _sz]),
     "sulimo_cuda_kv_store_q8_0": (_i, [_vp, _vp, _i, _vp, _sz, _sz, _sz, _sz]),

@@ -564,14 +564,15 @@ int slot_splits(size_t ctx_len, size_t capacity, int H, int Hkv, int HD, int bat
 // the splits; each warp keeps a running (max, sum, output) and folds in COMBINE_BATCH splits per
 // step whose loads are all issued before any is used (the partials are a few MB read once, so
 // the merge is bound by load latency, not bandwidth).  The warps' results are merged in a fixed
-// order through shared memory.
+// order through shared memory.  With q8 set, the merged block is also written as Q8_0
+// (quantize_f32_to_q8_0, the o projection's input in forward_token).
 constexpr int COMBINE_THREADS = 256;
-constexpr int COMBINE_BATCH = 8;
+constexpr int COMBINE_BATCH = 20;  // 148 splits / 8 warps: one batch of loads per warp
 
 template <int HD>
 __global__ void __launch_bounds__(COMBINE_THREADS)
     attn_decode_combine_kernel(const float* __restrict__ part, int H, int splits,
-                               float* __restrict__ out) {
+                               float* __restrict__ out, uint8_t* __restrict__ q8) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     constexpr int W = COMBINE_THREADS / 32;
@@ -623,7 +624,11 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
             L = __fmaf_rn(sm_l[w], f, L);
             O = __fmaf_rn(sm_o[w][lane], f, O);
         }
-        out[((size_t)seq * H + h) * HD + d] = L > 0.0f ? O / L : 0.0f;
+        const float val = L > 0.0f ? O / L : 0.0f;
+        if (out) out[((size_t)seq * H + h) * HD + d] = val;
+        // the CTA's 32 dimensions are exactly one Q8_0 block of the [batch][H*HD] output
+        if (q8) quantize_block_warp(val, q8 + (((size_t)seq * H + h) * (HD / 32) + blockIdx.z) * 34,
+                                    lane);
     }
 }
 
@@ -641,7 +646,7 @@ int pick_splits(size_t ctx_len, int Hkv, int batch, int num_sms) {
 template <int HD, int G>
 int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* v,
               size_t seq_stride, size_t capacity, size_t ctx_len, int H, int Hkv, int batch,
-              float softcap, float* out, float* part, int splits) {
+              float softcap, float* out, float* part, int splits, uint8_t* q8) {
     using L = AttnLayout<HD>;
     const int chunk = (int)((ctx_len + splits - 1) / splits);
     const float sm_scale = 1.0f / sqrtf((float)HD);
@@ -668,7 +673,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
         if (st) return st;
         dim3 g2(H, batch, (HD + 31) / 32);
         (void)launch_pdl(attn_decode_combine_kernel<HD>, g2, dim3(COMBINE_THREADS), 0, ctx->stream,
-                         (const float*)part, H, splits, out);
+                         (const float*)part, H, splits, out, q8);
         ctx->launches += 2;
         return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
     }
@@ -724,7 +729,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
     if (st) return st;
     dim3 g2(H, batch, (HD + 31) / 32);
     (void)launch_pdl(attn_decode_combine_kernel<HD>, g2, dim3(COMBINE_THREADS), 0, ctx->stream,
-                     (const float*)part, H, splits, out);
+                     (const float*)part, H, splits, out, q8);
     ctx->launches += 2;
     return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
 }
@@ -735,10 +740,10 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
 template <int HD>
 int launch_hd(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* v,
               size_t seq_stride, size_t capacity, size_t ctx_len, int H, int Hkv, int batch,
-              float softcap, float* out, float* part, int splits) {
+              float softcap, float* out, float* part, int splits, uint8_t* q8) {
     switch (H / Hkv) {
 #define SULIMO_ATTN_G(g) \
-    case g: return launch_hdg<HD, g>(ctx, q, k, v, seq_stride, capacity, ctx_len, H, Hkv, batch, softcap, out, part, splits);
+    case g: return launch_hdg<HD, g>(ctx, q, k, v, seq_stride, capacity, ctx_len, H, Hkv, batch, softcap, out, part, splits, q8);
         SULIMO_ATTN_G(1) SULIMO_ATTN_G(2) SULIMO_ATTN_G(3) SULIMO_ATTN_G(4)
         SULIMO_ATTN_G(5) SULIMO_ATTN_G(6) SULIMO_ATTN_G(7) SULIMO_ATTN_G(8)
 #undef SULIMO_ATTN_G
@@ -763,11 +768,11 @@ int launch_attn_decode_with_splits(sulimo_ctx* ctx, const float* q, const void* 
     const uint8_t* k = reinterpret_cast<const uint8_t*>(k_ring);
     const uint8_t* v = reinterpret_cast<const uint8_t*>(v_ring);
     switch (head_dim) {
-        case 32: return launch_hd<32>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 64: return launch_hd<64>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 96: return launch_hd<96>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 128: return launch_hd<128>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 256: return launch_hd<256>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
+        case 32: return launch_hd<32>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
+        case 64: return launch_hd<64>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
+        case 96: return launch_hd<96>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
+        case 128: return launch_hd<128>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
+        case 256: return launch_hd<256>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
         default: return set_error(SULIMO_EINVAL, "head_dim must be one of 32, 64, 96, 128, 256");
     }
 }
@@ -793,7 +798,7 @@ size_t attn_decode_partial_bytes(size_t context_len, size_t capacity, int head_c
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
-                       float* partials, size_t partial_bytes) {
+                       float* partials, size_t partial_bytes, uint8_t* out_q8) {
     const int splits = attn_decode_splits(context_len, capacity, head_count, head_count_kv,
                                           head_dim, batch, ctx->num_sms, seq_stride, k_ring,
                                           v_ring);
@@ -802,11 +807,11 @@ int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, cons
     const uint8_t* k = reinterpret_cast<const uint8_t*>(k_ring);
     const uint8_t* v = reinterpret_cast<const uint8_t*>(v_ring);
     switch (head_dim) {
-        case 32: return launch_hd<32>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 64: return launch_hd<64>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 96: return launch_hd<96>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 128: return launch_hd<128>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
-        case 256: return launch_hd<256>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits);
+        case 32: return launch_hd<32>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, out_q8);
+        case 64: return launch_hd<64>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, out_q8);
+        case 96: return launch_hd<96>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, out_q8);
+        case 128: return launch_hd<128>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, out_q8);
+        case 256: return launch_hd<256>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, out_q8);
         default: return set_error(SULIMO_EINVAL, "head_dim must be one of 32, 64, 96, 128, 256");
     }
 }

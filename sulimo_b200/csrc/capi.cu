@@ -419,6 +419,22 @@ int sulimo_cuda_gemv_q4_0_q8_0_static(sulimo_ctx* ctx, const void* w_scales,
     return sulimo::launch_gemv_static(ctx, w_scales, w_quants, x_q8, rows, cols, batch, out);
 }
 
+int sulimo_cuda_gemv_q4_0_q8_0_fast(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
+                                    const void* x_q8, int rows, int cols, int batch, float* out,
+                                    int static_weights) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (rows < 0 || cols <= 0 || batch < 0) return set_error(SULIMO_EINVAL, "bad shape");
+    if (cols % 32 != 0) return set_error(SULIMO_EINVAL, "cols must be a multiple of 32");
+    if (rows == 0 || batch == 0) return SULIMO_OK;
+    if (!w_scales || !w_quants || !x_q8 || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(w_quants, 16) || !aligned(w_scales, 2) || !aligned(x_q8, 2) || !aligned(out, 4))
+        return set_error(SULIMO_EALIGN, "w_quants must be 16-byte aligned, scales/x_q8 2-byte");
+    if ((st = bind_device(ctx))) return st;
+    const sulimo::GemvMatSrc src = {w_scales, w_quants, out, rows};
+    return sulimo::launch_gemv_fast_group(ctx, &src, 1, x_q8, cols, batch, static_weights != 0);
+}
+
 int sulimo_cuda_block_sums_q4_0_q8_0(sulimo_ctx* ctx, const void* w_quants, const void* x_q8,
                                      int rows, int cols, int32_t* out) {
     int st = check_ctx(ctx);

@@ -241,6 +241,7 @@ __global__ void __launch_bounds__(GLUE_THREADS)
 struct Scratch {
     float *x, *q, *k, *v, *att, *o, *g, *u;
     uint8_t* q8;
+    float* x2;  // the residual stream's second buffer (fused norms write x + delta here)
 };
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
@@ -251,11 +252,11 @@ size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scra
     const size_t kvd = (size_t)m->head_count_kv * m->head_dim;
     size_t q8n = E > qd ? E : qd;
     if (F > q8n) q8n = F;
-    const size_t sizes[9] = {E * 4, qd * 4, kvd * 4, kvd * 4, qd * 4, (E > F ? E : F) * 4,
-                             F * 4, F * 4, q8n / 32 * 34};
+    const size_t sizes[10] = {E * 4, qd * 4, kvd * 4, kvd * 4, qd * 4, (E > F ? E : F) * 4,
+                              F * 4, F * 4, q8n / 32 * 34, E * 4};
     size_t off = 0;
-    uint8_t* p[9];
-    for (int i = 0; i < 9; i++) {
+    uint8_t* p[10];
+    for (int i = 0; i < 10; i++) {
         p[i] = base ? base + off : nullptr;
         off += align256(sizes[i] * (size_t)batch);
     }
@@ -269,6 +270,7 @@ size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scra
         s->g = reinterpret_cast<float*>(p[6]);
         s->u = reinterpret_cast<float*>(p[7]);
         s->q8 = p[8];
+        s->x2 = reinterpret_cast<float*>(p[9]);
     }
     return off;
 }
@@ -434,6 +436,53 @@ int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int3
     return check_cuda(cudaGetLastError(), "argmax_rows launch");
 }
 
+// One fast-mode matvec over a decode step's static weights.
+static int gemv_fast_static(sulimo_ctx* ctx, const void* scales, const void* quants,
+                            const void* x_q8, int rows, int cols, int batch, float* out) {
+    const GemvMatSrc src = {scales, quants, out, rows};
+    return launch_gemv_fast_group(ctx, &src, 1, x_q8, cols, batch, true);
+}
+
+// Residual add + RMSNorm + Q8_0 feeding `count` matrices.  For one sequence the norm is
+// folded into the matvec's prologue (each CTA recomputes it from L2 while its weights stream
+// in; v = x + delta goes to the other residual buffer when keep_x, which becomes x).  With more
+// sequences that redundant per-CTA work costs more than the launch it saves (measured on
+// config 4: batch 1 1.48 -> 1.40 ms per step, batch 8 5.19 -> 6.41 ms), so the norm kernel
+// updates x in place and writes q8, then the matvec runs.
+static int norm_and_gemv(sulimo_ctx* ctx, float*& x, float*& x_other, const float* delta,
+                         const float* w, float eps, int E, int batch, uint8_t* q8,
+                         const GemvMatSrc* g, int count, bool keep_x) {
+    const GemvPrologue pro = {GEMV_PRO_NORM, x, delta, w, keep_x ? x_other : nullptr, eps};
+    if (batch == 1 && gemv_fast_fused_ok(g, count, E, batch, pro)) {
+        const int st = launch_gemv_fast_fused(ctx, g, count, pro, E, batch, true);
+        if (!st && keep_x) {
+            float* t = x;
+            x = x_other;
+            x_other = t;
+        }
+        return st;
+    }
+    (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS),
+                     (size_t)(E + 33) * sizeof(float), ctx->stream, x, delta, w, E, eps, q8);
+    ctx->launches++;
+    int st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch");
+    return st ? st : launch_gemv_fast_group(ctx, g, count, q8, E, batch, true);
+}
+
+// SwiGLU + Q8_0 feeding the down projection.  Folding it into the matvec's prologue, as the
+// norm is, was measured slower at every batch size (config 4 batch 1: 1.48 -> 1.61 ms per
+// step): every CTA of the down projection (hundreds) would recompute all F activations with
+// expf, so this one small kernel runs instead.
+static int swiglu_and_gemv(sulimo_ctx* ctx, const float* gate, const float* up, int F, int batch,
+                           uint8_t* q8, const GemvMatSrc& g) {
+    const size_t nblk = (size_t)batch * F / 32;
+    (void)launch_pdl(swiglu_q8_kernel, dim3((unsigned)((nblk + 7) / 8)), dim3(GLUE_THREADS), 0,
+                     ctx->stream, gate, up, nblk, q8);
+    ctx->launches++;
+    int st = check_cuda(cudaGetLastError(), "swiglu_q8 launch");
+    return st ? st : launch_gemv_fast_group(ctx, &g, 1, q8, F, batch, true);
+}
+
 int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
                          int batch, size_t pos, float* logits, void* scratch) {
     Scratch s;
@@ -442,7 +491,6 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
               hd = m->head_dim;
     const int qd = H * hd, kvd = Hkv * hd;
     const size_t ctx_len = pos + 1;
-    const size_t norm_smem = (size_t)(E + 33) * sizeof(float);
     int st;
     if ((st = ensure_norm_attr(ctx))) return st;
     // attention workspace for this geometry (grown outside any graph capture by a first call)
@@ -457,24 +505,19 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
     if ((st = launch_dequant_rows(ctx, m->tok_scales, m->tok_quants, E, tokens, batch, s.x,
                                   SULIMO_OUT_F32)))
         return st;
+    float* x = s.x;        // the residual stream
+    float* x_other = s.x2;
     const float* pending = nullptr;  // the previous layer's FFN output, added to x next
     for (int l = 0; l < m->n_layers; l++) {
         const sulimo_layer_desc& L = m->layers[l];
-        (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS), norm_smem,
-                         ctx->stream, s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E,
-                         m->eps, s.q8);
-        ctx->launches++;
-        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
-        {  // q, k, v in one launch
+        {  // attention norm, then q, k, v in one launch
             const GemvMatSrc g[3] = {{L.wq_scales, L.wq_quants, s.q, qd},
                                      {L.wk_scales, L.wk_quants, s.k, kvd},
                                      {L.wv_scales, L.wv_quants, s.v, kvd}};
-            bool done = false;
-            if ((st = launch_gemv_group(ctx, g, 3, s.q8, E, batch, &done, true))) return st;
-            for (int i = 0; i < 3 && !done; i++)
-                if ((st = launch_gemv_q4_0_q8_0(ctx, g[i].scales, g[i].quants, s.q8, g[i].rows, E,
-                                                batch, g[i].out)))
-                    return st;
+            if ((st = norm_and_gemv(ctx, x, x_other, pending,
+                                    reinterpret_cast<const float*>(L.attn_norm), m->eps, E, batch,
+                                    s.q8, g, 3, true)))
+                return st;
         }
         (void)launch_pdl(qkv_rope_store_kernel, dim3(H + 2 * Hkv, batch), dim3(128), 0,
                          ctx->stream, s.q, (const float*)s.k, (const float*)s.v,
@@ -485,42 +528,29 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                          reinterpret_cast<uint8_t*>(L.v_ring), m->kv_capacity, m->kv_seq_stride);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
+        // attention, its output quantized to Q8_0 in the merge kernel (the o projection's input)
         if ((st = launch_attn_decode(ctx, s.q, L.k_ring, L.v_ring, m->kv_seq_stride,
                                      m->kv_capacity, ctx_len, H, Hkv, hd, batch, m->attn_softcap,
-                                     s.att, reinterpret_cast<float*>(ctx->workspace),
-                                     ctx->workspace_bytes)) ||
-            (st = launch_quantize_q8_0(ctx, s.att, s.q8, (size_t)batch * qd)) ||
-            (st = launch_gemv_static(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
+                                     nullptr, reinterpret_cast<float*>(ctx->workspace),
+                                     ctx->workspace_bytes, s.q8)) ||
+            (st = gemv_fast_static(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
             return st;
-        (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS), norm_smem,
-                         ctx->stream, s.x, (const float*)s.o,
-                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, s.q8);
-        ctx->launches++;
-        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
-        {  // gate and up in one launch
+        {  // FFN norm (x += o), then gate and up in one launch
             const GemvMatSrc g[2] = {{L.wg_scales, L.wg_quants, s.g, F},
                                      {L.wu_scales, L.wu_quants, s.u, F}};
-            bool done = false;
-            if ((st = launch_gemv_group(ctx, g, 2, s.q8, E, batch, &done, true))) return st;
-            for (int i = 0; i < 2 && !done; i++)
-                if ((st = launch_gemv_q4_0_q8_0(ctx, g[i].scales, g[i].quants, s.q8, g[i].rows, E,
-                                                batch, g[i].out)))
-                    return st;
+            if ((st = norm_and_gemv(ctx, x, x_other, s.o,
+                                    reinterpret_cast<const float*>(L.ffn_norm), m->eps, E, batch,
+                                    s.q8, g, 2, true)))
+                return st;
         }
-        const size_t nblk = (size_t)batch * F / 32;
-        (void)launch_pdl(swiglu_q8_kernel, dim3((unsigned)((nblk + 7) / 8)), dim3(GLUE_THREADS), 0,
-                         ctx->stream, (const float*)s.g, (const float*)s.u, nblk, s.q8);
-        ctx->launches++;
-        if ((st = check_cuda(cudaGetLastError(), "swiglu_q8 launch"))) return st;
-        if ((st = launch_gemv_static(ctx, L.wd_scales, L.wd_quants, s.q8, E, F, batch, s.o)))
-            return st;
+        const GemvMatSrc gd = {L.wd_scales, L.wd_quants, s.o, E};
+        if ((st = swiglu_and_gemv(ctx, s.g, s.u, F, batch, s.q8, gd))) return st;
         pending = s.o;
     }
-    (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS), norm_smem,
-                     ctx->stream, s.x, pending, m->out_norm, E, m->eps, s.q8);
-    ctx->launches++;
-    if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch"))) return st;
-    return launch_gemv_static(ctx, m->out_scales, m->out_quants, s.q8, m->vocab, E, batch, logits);
+    // output norm and the vocab projection (the residual is not needed afterwards)
+    const GemvMatSrc go = {m->out_scales, m->out_quants, logits, m->vocab};
+    return norm_and_gemv(ctx, x, x_other, pending, m->out_norm, m->eps, E, batch, s.q8, &go, 1,
+                         false);
 }
 
 }  // namespace sulimo

@@ -94,6 +94,31 @@ int launch_gemv_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const v
 // launch_gemv_q4_0_q8_0 for a decode step's static weights (see launch_gemv_group).
 int launch_gemv_static(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                        const void* x_q8, int rows, int cols, int batch, float* out);
+// Fast-mode matvec (exact integer block sums, fp32 partials over 8 block residues combined in a
+// fixed tree; not the AVX2 add order) for 1..3 matrices sharing x_q8; falls back to the exact
+// kernel when its layout conditions do not hold.
+int launch_gemv_fast_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const void* x_q8,
+                           int cols, int batch, bool static_weights);
+// Activation producer folded into the fast matvec's prologue (every CTA recomputes the vector
+// from L2 after the launch's dependency wait; the quantization is quantize_f32_to_q8_0):
+//   GEMV_PRO_NORM: v = a + b (b may be null), written to a_out by the CTAs of column 0 when
+//                  a_out is set; x = quantize((v * 1/sqrt(mean(v^2) + eps)) * w)
+// a, b, a_out: [batch][cols] f32, 16-byte aligned; a_out never aliases a or b.
+enum { GEMV_PRO_Q8 = 0, GEMV_PRO_NORM = 1 };
+struct GemvPrologue {
+    int mode;
+    const float* a;
+    const float* b;
+    const float* w;
+    float* a_out;
+    float eps;
+};
+// Whether launch_gemv_fast_fused handles this shape (else the caller runs the producer kernel
+// and launch_gemv_fast_group / the exact matvec).
+bool gemv_fast_fused_ok(const GemvMatSrc* src, int count, int cols, int batch,
+                        const GemvPrologue& pro);
+int launch_gemv_fast_fused(sulimo_ctx* ctx, const GemvMatSrc* src, int count,
+                           const GemvPrologue& pro, int cols, int batch, bool static_weights);
 int launch_block_sums(sulimo_ctx* ctx, const void* w_quants, const void* x_q8, int rows, int cols,
                       int32_t* out);
 int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n);
@@ -104,7 +129,7 @@ int launch_dequant_rows(sulimo_ctx* ctx, const void* scales, const void* quants,
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
-                       float* partials, size_t partial_bytes);
+                       float* partials, size_t partial_bytes, uint8_t* out_q8 = nullptr);
 int launch_unshard_rows(sulimo_ctx* ctx, const void* gathered, void* out, int world,
                         int m_tokens, size_t fs, size_t f, int elem_size);
 size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch);

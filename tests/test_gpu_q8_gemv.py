@@ -216,3 +216,33 @@ def test_gemv_static_weights_bit_exact(ctx, rows, cols, batch):
         ref = O.matvec_q4_0_q8_0_avx2(ws, wq, xq8[b * cols // 32 * 34:(b + 1) * cols // 32 * 34],
                                       rows, cols, threads=8)
         assert np.array_equal(got[b].view(np.uint32), ref.view(np.uint32))
+
+
+# ---- fast mode (sulimo_cuda_gemv_q4_0_q8_0_fast): exact block sums, fixed fp32 partial tree ----
+
+@pytest.mark.parametrize("rows,cols,batch", [(8960, 1536, 1), (3072, 8192, 1), (1000, 3072, 3),
+                                             (16, 256, 1), (257, 2048, 8), (300, 96, 2)])
+def test_gemv_fast_matches_avx2_within_rounding(ctx, rows, cols, batch):
+    """Fast mode vs the AVX2 oracle: the same exact integer block sums, fp32 additions grouped
+    differently, so per-row errors stay at fp32 rounding of the row's terms (rel-L2 <= 1e-5,
+    far inside the 2e-3 fast-mode bound); repeated calls, with and without the static-weights
+    prefetch, give the same bits.  Ragged shapes: rows not a multiple of the 8 rows of a CTA,
+    K blocks not a multiple of the 32 lanes (cols 96, 1536, 2048)."""
+    import torch
+    ws, wq = make_q4_0(rows, cols, seed=rows * 7 + cols)
+    x = np.random.default_rng(batch + 11).standard_normal((batch, cols)).astype(np.float32)
+    xq8 = np.concatenate([O.quantize_f32_to_q8_0(x[b]) for b in range(batch)])
+    dws, dwq, dx = dev(ws), dev(wq), dev(xq8)
+    outs = []
+    for static in (False, True):
+        out = empty(batch * rows, torch.float32)
+        sb.matvec_q4_0_q8_0_fast(ctx, dws, dwq, dx, rows, cols, out, batch, static)
+        ctx.finish()
+        outs.append(host(out).reshape(batch, rows))
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    nbx = cols // 32 * 34
+    for b in range(batch):
+        ref = O.matvec_q4_0_q8_0_avx2(ws, wq, xq8[b * nbx:(b + 1) * nbx], rows, cols, threads=8)
+        got = outs[0][b]
+        rel = np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref.astype(np.float64))
+        assert rel <= 1e-5, rel
