@@ -327,7 +327,7 @@ def run_secondary(ctx, hbm):
     out = {}
     rng = np.random.default_rng(7)
 
-    def gemv_case(rows, cols, batch, name, static=False):
+    def gemv_case(rows, cols, batch, name, static=False, fast=False):
         nbytes_w = rows * cols // 32 * 18
         copies = max(2, -(-int(1.5 * L2_BYTES) // nbytes_w))
         ws = [torch.randint(0, 1 << 14, (rows * cols // 32,), dtype=torch.int16, device="cuda")
@@ -338,16 +338,18 @@ def run_secondary(ctx, hbm):
                            device="cuda").view(torch.uint8)
         xq.view(-1, 34)[:, :2] = 0x2C  # sane f16 scales
         y = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
+        fn = sb.matvec_q4_0_q8_0_fast if fast else sb.dispatch_matvec_q4_0_q8_0
         for i in range(5):
-            sb.dispatch_matvec_q4_0_q8_0(ctx, ws[i % copies], wq[i % copies], xq, rows, cols, y,
-                                         batch, static)
+            fn(ctx, ws[i % copies], wq[i % copies], xq, rows, cols, y, batch, static)
         iters = max(20, copies * 4)
-        us = graph_time_us(ctx, lambda i: sb.dispatch_matvec_q4_0_q8_0(
+        us = graph_time_us(ctx, lambda i: fn(
             ctx, ws[i % copies], wq[i % copies], xq, rows, cols, y, batch, static), iters)
         alg = nbytes_w + batch * cols // 32 * 34 + batch * rows * 4
         out[name] = {"us_per_launch": round(us, 2), "GBps": round(alg / us / 1e3, 1),
                      "frac_of_measured_hbm": round(alg / us / 1e3 / hbm, 3),
-                     "alg_bytes": alg, "l2": f"{copies} rotated weight copies"}
+                     "alg_bytes": alg, "l2": f"{copies} rotated weight copies",
+                     "mode": "fast (exact block sums, fp32 lane tree)" if fast
+                             else "bit-exact AVX2 order"}
 
     gemv_case(8960, 1536, 1, "gemv_config1_8960x1536_b1")
     # the decode engine's form: model weights are static, so back-to-back matvecs overlap their
@@ -355,6 +357,10 @@ def run_secondary(ctx, hbm):
     gemv_case(8960, 1536, 1, "gemv_config1_8960x1536_b1_static_weights", static=True)
     gemv_case(151936, 1536, 1, "gemv_lm_head_151936x1536_b1")
     gemv_case(8192, 3072, 8, "gemv_ffn_8192x3072_b8")
+    # fast mode (sulimo_cuda_gemv_q4_0_q8_0_fast): the form the decode step streams weights with
+    gemv_case(8960, 1536, 1, "gemv_config1_8960x1536_b1_fast", static=True, fast=True)
+    gemv_case(151936, 1536, 1, "gemv_lm_head_151936x1536_b1_fast", static=True, fast=True)
+    gemv_case(8192, 3072, 8, "gemv_ffn_8192x3072_b8_fast", static=True, fast=True)
 
     # decode attention, Llama-3.2-3B geometry at ctx 4096, batch 1
     H, Hkv, hd, cap = 24, 8, 128, 4096

@@ -156,7 +156,8 @@ __global__ void __launch_bounds__(ATT_THREADS)
             tma_load_3d(raw_v, &tmap_v, x0, (int)p0, seq, &bar[1]);
         }
     }
-    // query heads of this group
+    // query heads of this group (unrolled: the loads of a batch issue before its stores)
+#pragma unroll 4
     for (int i = tid; i < G * HD; i += ATT_THREADS)
         sq[i] = q[((size_t)seq * H + (size_t)kvh * G) * HD + i];
     if (TMA) {
@@ -320,19 +321,32 @@ __global__ void __launch_bounds__(ATT_THREADS)
 // p0..p0+np-1 of a ring are np contiguous slots, so K and V arrive with one bulk copy each
 // (exactly the algorithmic bytes, no tensor map).  Used when the context does not wrap the
 // ring and the slot size is a multiple of 16 bytes (Qwen2.5-1.5B: 272 B, Llama-3.2-3B: 1088 B).
-//   scores : item (position, kv head), G dot products over the head's Q8_0 blocks read in place
-//            (2-byte loads: 34-byte blocks are 2-byte aligned), block scale applied per block;
+//   scores : item (position, kv head) split over adjacent lanes, one 32-dim Q8_0 block each
+//            (G dot products read in place with 2-byte loads: 34-byte blocks are 2-byte
+//            aligned; times the block scale), summed across the lane group by shuffles;
 //   softmax: one warp per (kv head, query head) row over the split's positions;
 //   V      : weights pre-multiplied by V's block scales, item (kv head, dim) accumulates
 //            sum_pos w[g][pos][b] * v_int[pos][d] for the G query heads.
-constexpr int SLOT_THREADS = 256;
+// Threads per CTA: the phases' serial latency, not bytes, bounds the kernel, so a grid of at
+// most one CTA per SM (one sequence) runs 1024 threads; larger grids (several sequences) run
+// 256 so that two CTAs share an SM (measured on config 4: batch 1 1.39 -> 1.28 ms per step
+// with 1024, batch 8 5.18 -> 5.54 ms with 1024 everywhere).
+constexpr int SLOT_THREADS_WIDE = 1024;
+constexpr int SLOT_THREADS_NARROW = 256;
 constexpr size_t SLOT_SMEM_MAX = 200 * 1024;
+
+// Query row of a kv head in shared memory: [G][NB][34] floats (each 32-dim block padded to 34,
+// so the NB lanes of one score item read different banks) and the row itself padded to
+// 8 (mod 32) words, so 8 kv heads x 4 blocks of float2 reads take the minimum 2 wavefronts.
+__host__ __device__ constexpr int slot_qrow(int G, int NB) {
+    return G * NB * 34 + (8 - (G * NB * 34) % 32 + 32) % 32;
+}
 
 template <int HD, int G>
 struct SlotLayout {
     static constexpr int NB = HD / 32;
     static constexpr int HB = NB * 34;
-    static constexpr int QROW = G * HD + 4;  // padded: kv heads' query rows hit distinct banks
+    static constexpr int QROW = slot_qrow(G, NB);
     __host__ __device__ static size_t raw_bytes(int chunk, int Hkv) {
         return ((size_t)chunk * Hkv * HB + 127) / 128 * 128;
     }
@@ -358,7 +372,7 @@ __device__ __forceinline__ void s8x2_to_f32(uint32_t w, float& lo, float& hi) {
     hi = __fsub_rn(__int_as_float(0x4B400000 + (int)prmt(w, 0u, 0x9991)), 12582912.0f);
 }
 
-template <int HD, int G>
+template <int HD, int G, int SLOT_THREADS>
 __global__ void __launch_bounds__(SLOT_THREADS)
     attn_decode_slots_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kring,
                              const uint8_t* __restrict__ vring, size_t seq_stride,
@@ -397,50 +411,79 @@ __global__ void __launch_bounds__(SLOT_THREADS)
         mbar_arrive_expect_tx(&bar[1], bytes);
         bulk_load(raw_v, vring + (size_t)seq * seq_stride + p0 * bpp, bytes, &bar[1]);
     }
-    // query rows, kv head major, padded
-    for (int i = tid; i < H * HD; i += SLOT_THREADS) {
-        const int h = i / HD, d = i - h * HD;
-        sq[(h / G) * L::QROW + (h % G) * HD + d] = q[(size_t)seq * H * HD + i];
+    // query rows, kv head major, blocks padded.  The loads of a batch are all issued before
+    // the first shared-memory store (one L2 round trip per 4 * SLOT_THREADS float4).
+    {
+        const float4* q4 = reinterpret_cast<const float4*>(q + (size_t)seq * H * HD);
+        const int n4 = H * HD / 4;
+        for (int base = tid; base < n4; base += 4 * SLOT_THREADS) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * SLOT_THREADS;
+                v[u] = i < n4 ? q4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = (base + u * SLOT_THREADS) * 4;
+                if (i < H * HD) {
+                    const int h = i / HD, d = i - h * HD;
+                    float* dst = sq + (h / G) * L::QROW + ((h % G) * L::NB + d / 32) * 34 + d % 32;
+                    *reinterpret_cast<float2*>(dst) = make_float2(v[u].x, v[u].y);
+                    *reinterpret_cast<float2*>(dst + 2) = make_float2(v[u].z, v[u].w);
+                }
+            }
+        }
     }
     bool ok = np > 0 && mbar_wait_bounded(&bar[0], 0, err, nullptr);
     __syncthreads();
 
-    // ---- scores ----
-    if (ok) {
-        for (int item = tid; item < np * Hkv; item += SLOT_THREADS) {
+    // ---- scores: item (position, kv head) split over NBP adjacent lanes, one 32-dim Q8_0
+    // block each (block dot times its scale), summed by xor-shuffles inside the lane group.
+    // Every thread runs the same number of rounds, so the shuffles see full warps. ----
+    {
+        constexpr int NBP = L::NB <= 1 ? 1 : L::NB <= 2 ? 2 : L::NB <= 4 ? 4 : 8;
+        const int units = np * Hkv * NBP;
+        const int rounds = (units + SLOT_THREADS - 1) / SLOT_THREADS;
+        for (int rd = 0; rd < rounds; rd++) {
+            const int u = rd * SLOT_THREADS + tid;
+            const int b = u & (NBP - 1), item = u / NBP;
             const int kvh = item % Hkv, pos = item / Hkv;
-            const uint8_t* row = raw_k + (size_t)pos * bpp + kvh * L::HB;
-            const float* qh = sq + kvh * L::QROW;
-            float dot[G];
+            float acc[G];
 #pragma unroll
-            for (int g = 0; g < G; g++) dot[g] = 0.0f;
-#pragma unroll
-            for (int b = 0; b < L::NB; b++) {
-                const uint16_t* blk = reinterpret_cast<const uint16_t*>(row + b * 34);
-                float acc[G];
-#pragma unroll
-                for (int g = 0; g < G; g++) acc[g] = 0.0f;
+            for (int g = 0; g < G; g++) acc[g] = 0.0f;
+            if (ok && u < units && b < L::NB) {
+                const uint16_t* blk = reinterpret_cast<const uint16_t*>(
+                    raw_k + (size_t)pos * bpp + kvh * L::HB + b * 34);
+                const float* qb = sq + kvh * L::QROW + b * 34;
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
                     float k0, k1;
                     s8x2_to_f32(blk[1 + i], k0, k1);
-                    const int d = b * 32 + 2 * i;
 #pragma unroll
                     for (int g = 0; g < G; g++) {
-                        const float2 qv = *reinterpret_cast<const float2*>(qh + g * HD + d);
+                        const float2 qv =
+                            *reinterpret_cast<const float2*>(qb + g * L::NB * 34 + 2 * i);
                         acc[g] = __fmaf_rn(qv.x, k0, acc[g]);
                         acc[g] = __fmaf_rn(qv.y, k1, acc[g]);
                     }
                 }
-                const float s = f16_bits_to_f32(blk[0]);
+                const float sc = f16_bits_to_f32(blk[0]);
 #pragma unroll
-                for (int g = 0; g < G; g++) dot[g] = __fmaf_rn(acc[g], s, dot[g]);
+                for (int g = 0; g < G; g++) acc[g] = __fmul_rn(acc[g], sc);
             }
 #pragma unroll
-            for (int g = 0; g < G; g++) {
-                float score = __fmul_rn(dot[g], sm_scale);
-                if (softcap > 0.0f) score = tanhf(score / softcap) * softcap;
-                se[(kvh * G + g) * chunk + pos] = score;
+            for (int o = 1; o < NBP; o <<= 1)
+#pragma unroll
+                for (int g = 0; g < G; g++)
+                    acc[g] = __fadd_rn(acc[g], __shfl_xor_sync(0xffffffffu, acc[g], o));
+            if (ok && u < units && b == 0) {
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    float score = __fmul_rn(acc[g], sm_scale);
+                    if (softcap > 0.0f) score = tanhf(score / softcap) * softcap;
+                    se[(kvh * G + g) * chunk + pos] = score;
+                }
             }
         }
     }
@@ -470,15 +513,19 @@ __global__ void __launch_bounds__(SLOT_THREADS)
     if (np > 0) ok = mbar_wait_bounded(&bar[1], 0, err, nullptr) && ok;
     __syncthreads();
 
-    // ---- weights times V's block scales: w[kvh][g][pos][b] ----
+    // ---- weights times V's block scales: w[kvh][g][pos][b]; a warp per row, a lane per
+    // position (no runtime divisions) ----
     if (ok) {
-        for (int it = tid; it < rows * np * L::NB; it += SLOT_THREADS) {
-            const int b = it % L::NB, rp = it / L::NB;
-            const int pos = rp % np, r = rp / np;
+        for (int r = warp; r < rows; r += SLOT_THREADS / 32) {
             const int kvh = r / G;
-            const float s = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
-                raw_v + (size_t)pos * bpp + kvh * L::HB + b * 34));
-            sw[(r * chunk + pos) * L::NB + b] = __fmul_rn(se[r * chunk + pos], s);
+            for (int pos = lane; pos < np; pos += 32) {
+                const float e = se[r * chunk + pos];
+                const uint8_t* vrow = raw_v + (size_t)pos * bpp + kvh * L::HB;
+#pragma unroll
+                for (int b = 0; b < L::NB; b++)
+                    sw[(r * chunk + pos) * L::NB + b] = __fmul_rn(
+                        e, f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(vrow + b * 34)));
+            }
         }
     }
     __syncthreads();
@@ -521,7 +568,7 @@ __global__ void __launch_bounds__(SLOT_THREADS)
 size_t slot_bytes_generic(int chunk, int Hkv, int G, int HD) {
     const int NB = HD / 32, HB = NB * 34;
     const size_t raw = ((size_t)chunk * Hkv * HB + 127) / 128 * 128;
-    size_t off = 2 * raw + (size_t)Hkv * (G * HD + 4) * 4 + (size_t)Hkv * G * chunk * 4 +
+    size_t off = 2 * raw + (size_t)Hkv * slot_qrow(G, NB) * 4 + (size_t)Hkv * G * chunk * 4 +
                  (size_t)Hkv * G * chunk * NB * 4;
     off = (off + (size_t)Hkv * G * 8 + 15) / 16 * 16;
     return off + 16 + 128;
@@ -650,7 +697,8 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
     using L = AttnLayout<HD>;
     const int chunk = (int)((ctx_len + splits - 1) / splits);
     const float sm_scale = 1.0f / sqrtf((float)HD);
-    if (slot_form_ok(ctx_len, capacity, Hkv, G, HD, batch, seq_stride, k, v, chunk)) {
+    if (((uintptr_t)q % 16) == 0 &&
+        slot_form_ok(ctx_len, capacity, Hkv, G, HD, batch, seq_stride, k, v, chunk)) {
         using SL = SlotLayout<HD, G>;
         const size_t bytes = SL::bytes(chunk, Hkv);
         if (bytes != slot_bytes_generic(chunk, Hkv, G, HD))
@@ -658,17 +706,29 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
         static uint64_t slot_attr_mask = 0;  // per device
         const uint64_t sbit = 1ull << (ctx->device & 63);
         if (!(slot_attr_mask & sbit)) {
-            int st = check_cuda(cudaFuncSetAttribute(attn_decode_slots_kernel<HD, G>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     (int)SLOT_SMEM_MAX),
-                                "attn slot smem attribute");
+            int st = check_cuda(
+                cudaFuncSetAttribute(attn_decode_slots_kernel<HD, G, SLOT_THREADS_WIDE>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)SLOT_SMEM_MAX),
+                "attn slot smem attribute");
+            if (!st)
+                st = check_cuda(
+                    cudaFuncSetAttribute(attn_decode_slots_kernel<HD, G, SLOT_THREADS_NARROW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SLOT_SMEM_MAX),
+                    "attn slot smem attribute");
             if (st) return st;
             slot_attr_mask |= sbit;
         }
         dim3 g1(splits, batch);
-        (void)launch_pdl(attn_decode_slots_kernel<HD, G>, g1, dim3(SLOT_THREADS), bytes,
-                         ctx->stream, q, k, v, seq_stride, ctx_len, H, Hkv, chunk, sm_scale,
-                         softcap, part, ctx->d_error);
+        if ((size_t)splits * batch <= (size_t)ctx->num_sms)
+            (void)launch_pdl(attn_decode_slots_kernel<HD, G, SLOT_THREADS_WIDE>, g1,
+                             dim3(SLOT_THREADS_WIDE), bytes, ctx->stream, q, k, v, seq_stride,
+                             ctx_len, H, Hkv, chunk, sm_scale, softcap, part, ctx->d_error);
+        else
+            (void)launch_pdl(attn_decode_slots_kernel<HD, G, SLOT_THREADS_NARROW>, g1,
+                             dim3(SLOT_THREADS_NARROW), bytes, ctx->stream, q, k, v, seq_stride,
+                             ctx_len, H, Hkv, chunk, sm_scale, softcap, part, ctx->d_error);
         int st = check_cuda(cudaGetLastError(), "attn_decode_slots launch");
         if (st) return st;
         dim3 g2(H, batch, (HD + 31) / 32);
