@@ -167,91 +167,71 @@ struct GrPrologue {
     float eps;
 };
 
-// Stages NV vectors' activations in shared memory from the residual stream (PRO =
-// GEMV_PRO_NORM): float4 f of vector v covers elements 4f..4f+3, so 8 adjacent lanes hold one
-// Q8_0 block.  The loops run a whole number of CTA passes so every warp takes every shuffle.
-template <int NV, int PRO>
-__device__ __forceinline__ void stage_from_f32(const GrPrologue& pro, int v0, int nv, int nb,
-                                               uint32_t* xw32, int2* aux, float* red) {
+// Stages one vector's activations in shared memory from the residual stream (PRO =
+// GEMV_PRO_NORM, batch 1, cols <= 32 * GR_NORM_F4 * GR_THREADS / 8): thread t holds float4
+// f = t + k * GR_THREADS (k < GR_NORM_F4) of x + delta and of the norm weight in registers, so
+// x, delta and w come in one L2 round trip; 8 adjacent lanes hold one Q8_0 block.  Every
+// thread runs all GR_NORM_F4 rounds, so every warp takes every shuffle.
+constexpr int GR_NORM_F4 = 4;
+
+__device__ __forceinline__ void stage_norm(const GrPrologue& pro, int v0, int nb,
+                                           uint32_t* xw32, int2* aux, float* red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n4 = nb * 8;                                         // float4 per vector
-    const int passes = (n4 + GR_THREADS - 1) / GR_THREADS;
-    float scale[NV];
-    if (PRO == GEMV_PRO_NORM) {
-        // pass A: v = a + b, sum of squares (the CTAs of column 0 also store v)
-        float ss[NV];
+    const int n4 = nb * 8;  // float4 per vector
+    const float4* a4 = reinterpret_cast<const float4*>(pro.a) + (size_t)v0 * n4;
+    const float4* b4 = pro.b ? reinterpret_cast<const float4*>(pro.b) + (size_t)v0 * n4 : nullptr;
+    const float4* w4 = reinterpret_cast<const float4*>(pro.w);
+    float4* o4 = (pro.a_out && blockIdx.x == 0)
+                     ? reinterpret_cast<float4*>(pro.a_out) + (size_t)v0 * n4
+                     : nullptr;
+    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float4 xv[GR_NORM_F4], dv[GR_NORM_F4], wv[GR_NORM_F4];
 #pragma unroll
-        for (int v = 0; v < NV; v++) {
-            ss[v] = 0.0f;
-            if (v < nv) {
-                const float4* a4 = reinterpret_cast<const float4*>(pro.a) + (size_t)(v0 + v) * n4;
-                const float4* b4 =
-                    pro.b ? reinterpret_cast<const float4*>(pro.b) + (size_t)(v0 + v) * n4 : nullptr;
-                float4* o4 = (pro.a_out && blockIdx.x == 0)
-                                 ? reinterpret_cast<float4*>(pro.a_out) + (size_t)(v0 + v) * n4
-                                 : nullptr;
-                for (int f = tid; f < n4; f += GR_THREADS) {
-                    float4 x = a4[f];
-                    if (b4) {
-                        const float4 d = b4[f];
-                        x = make_float4(__fadd_rn(x.x, d.x), __fadd_rn(x.y, d.y),
-                                        __fadd_rn(x.z, d.z), __fadd_rn(x.w, d.w));
-                    }
-                    if (o4) o4[f] = x;
-                    ss[v] = __fmaf_rn(x.x, x.x, ss[v]);
-                    ss[v] = __fmaf_rn(x.y, x.y, ss[v]);
-                    ss[v] = __fmaf_rn(x.z, x.z, ss[v]);
-                    ss[v] = __fmaf_rn(x.w, x.w, ss[v]);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss[v] += __shfl_xor_sync(0xffffffffu, ss[v], o);
-            if (lane == 0) red[v * GR_WARPS + warp] = ss[v];
-        }
-        __syncthreads();
-#pragma unroll
-        for (int v = 0; v < NV; v++) {
-            float t = 0.0f;
-#pragma unroll
-            for (int w = 0; w < GR_WARPS; w++) t += red[v * GR_WARPS + w];
-            const float mean = __fdiv_rn(t, (float)(n4 * 4));
-            scale[v] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, pro.eps)));
-        }
+    for (int k = 0; k < GR_NORM_F4; k++) {
+        const int f = tid + k * GR_THREADS;
+        xv[k] = f < n4 ? a4[f] : zero;
+        dv[k] = (b4 && f < n4) ? b4[f] : zero;
+        wv[k] = f < n4 ? w4[f] : zero;
     }
-    // pass B: y, quantized per block by 8-lane groups
+    float ss = 0.0f;
 #pragma unroll
-    for (int v = 0; v < NV; v++) {
-        const float4* a4 = reinterpret_cast<const float4*>(pro.a) + (size_t)(v0 + v) * n4;
-        const float4* b4 =
-            pro.b ? reinterpret_cast<const float4*>(pro.b) + (size_t)(v0 + v) * n4 : nullptr;
-        const float4* w4 = reinterpret_cast<const float4*>(pro.w);
-        for (int p = 0; p < passes; p++) {
-            const int f = p * GR_THREADS + tid;
-            float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (v < nv && f < n4) {
-                const float4 x = a4[f];
-                if (PRO == GEMV_PRO_NORM) {
-                    float4 t = x;
-                    if (b4) {
-                        const float4 d = b4[f];
-                        t = make_float4(__fadd_rn(x.x, d.x), __fadd_rn(x.y, d.y),
-                                        __fadd_rn(x.z, d.z), __fadd_rn(x.w, d.w));
-                    }
-                    const float4 g = w4[f];
-                    y = make_float4(__fmul_rn(__fmul_rn(t.x, scale[v]), g.x),
-                                    __fmul_rn(__fmul_rn(t.y, scale[v]), g.y),
-                                    __fmul_rn(__fmul_rn(t.z, scale[v]), g.z),
-                                    __fmul_rn(__fmul_rn(t.w, scale[v]), g.w));
-                }
-            }
-            float dx;
-            int qsum;
-            const uint32_t word = quantize_block_8lanes(y, &dx, &qsum);
-            if (f < n4) {
-                const int vb = v * nb + (f >> 3);
-                xw32[vb * 8 + (f & 7)] = word;
-                if ((f & 7) == 0) aux[vb] = make_int2(__float_as_int(dx), GR_BIAS - 8 * qsum);
-            }
+    for (int k = 0; k < GR_NORM_F4; k++) {
+        const int f = tid + k * GR_THREADS;
+        float4 x = xv[k];
+        if (b4)
+            x = make_float4(__fadd_rn(x.x, dv[k].x), __fadd_rn(x.y, dv[k].y),
+                            __fadd_rn(x.z, dv[k].z), __fadd_rn(x.w, dv[k].w));
+        xv[k] = x;
+        if (o4 && f < n4) o4[f] = x;
+        ss = __fmaf_rn(x.x, x.x, ss);
+        ss = __fmaf_rn(x.y, x.y, ss);
+        ss = __fmaf_rn(x.z, x.z, ss);
+        ss = __fmaf_rn(x.w, x.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < GR_WARPS; w++) t += red[w];
+    const float mean = __fdiv_rn(t, (float)(n4 * 4));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, pro.eps)));
+#pragma unroll
+    for (int k = 0; k < GR_NORM_F4; k++) {
+        const int f = tid + k * GR_THREADS;
+        const float4 x = xv[k], g = wv[k];
+        const float4 y = make_float4(__fmul_rn(__fmul_rn(x.x, scale), g.x),
+                                     __fmul_rn(__fmul_rn(x.y, scale), g.y),
+                                     __fmul_rn(__fmul_rn(x.z, scale), g.z),
+                                     __fmul_rn(__fmul_rn(x.w, scale), g.w));
+        float dx;
+        int qsum;
+        const uint32_t word = quantize_block_8lanes(y, &dx, &qsum);
+        if (f < n4) {
+            const int b = f >> 3;
+            xw32[b * 8 + (f & 7)] = word;
+            if ((f & 7) == 0) aux[b] = make_int2(__float_as_int(dx), GR_BIAS - 8 * qsum);
         }
     }
 }
@@ -284,8 +264,8 @@ __global__ void __launch_bounds__(GR_THREADS)
             if (r + k < grp.total_rows) load_row<BPL>(grp, r + k, nb, lane, cur[k]);
 
     // ---- activations: per block 8 aligned words, d_x, -8 * sum(x) + bias ----
-    if (PRO != GEMV_PRO_Q8)
-        stage_from_f32<NV, PRO>(pro, v0, nv, nb, reinterpret_cast<uint32_t*>(xw), aux, red);
+    if (PRO == GEMV_PRO_NORM)
+        stage_norm(pro, v0, nb, reinterpret_cast<uint32_t*>(xw), aux, red);
     else
     for (int vb = tid; vb < NV * nb; vb += GR_THREADS) {
         uint32_t w[8];
@@ -389,11 +369,15 @@ int launch_fast_nv(sulimo_ctx* ctx, const FastArgs& a) {
                 return launch_fast<BPL, 1, 2, PRO>(ctx, a);
         }
     }
-    switch (a.nv) {
-        case 8: return launch_fast<BPL, 8, 1, PRO>(ctx, a);
-        case 4: return launch_fast<BPL, 4, 1, PRO>(ctx, a);
-        case 2: return launch_fast<BPL, 2, 1, PRO>(ctx, a);
-        default: return launch_fast<BPL, 1, 1, PRO>(ctx, a);
+    if constexpr (PRO == GEMV_PRO_NORM) {
+        return launch_fast<BPL, 1, 1, PRO>(ctx, a);  // batch 1 only (gemv_fast_fused_ok)
+    } else {
+        switch (a.nv) {
+            case 8: return launch_fast<BPL, 8, 1, PRO>(ctx, a);
+            case 4: return launch_fast<BPL, 4, 1, PRO>(ctx, a);
+            case 2: return launch_fast<BPL, 2, 1, PRO>(ctx, a);
+            default: return launch_fast<BPL, 1, 1, PRO>(ctx, a);
+        }
     }
 }
 
@@ -474,8 +458,8 @@ bool gemv_fast_fused_ok(const GemvMatSrc* src, int count, int cols, int batch,
     int nv = 1;
     if (!fast_applies(src, count, cols, batch, &nv)) return false;
     auto al = [](const void* p) { return ((uintptr_t)p % 16) == 0; };
-    return pro.mode == GEMV_PRO_NORM && pro.a && pro.w && al(pro.a) && al(pro.b) && al(pro.w) &&
-           al(pro.a_out);
+    return pro.mode == GEMV_PRO_NORM && batch == 1 && cols / 4 <= GR_NORM_F4 * GR_THREADS &&
+           pro.a && pro.w && al(pro.a) && al(pro.b) && al(pro.w) && al(pro.a_out);
 }
 
 int launch_gemv_fast_fused(sulimo_ctx* ctx, const GemvMatSrc* src, int count,

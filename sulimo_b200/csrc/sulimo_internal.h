@@ -103,7 +103,8 @@ int launch_gemv_fast_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, co
 // from L2 after the launch's dependency wait; the quantization is quantize_f32_to_q8_0):
 //   GEMV_PRO_NORM: v = a + b (b may be null), written to a_out by the CTAs of column 0 when
 //                  a_out is set; x = quantize((v * 1/sqrt(mean(v^2) + eps)) * w)
-// a, b, a_out: [batch][cols] f32, 16-byte aligned; a_out never aliases a or b.
+// a, b, a_out: [batch][cols] f32, 16-byte aligned; a_out never aliases a or b.  Batch 1 and
+// cols <= 4096 (the vector is held in registers, one L2 round trip).
 enum { GEMV_PRO_Q8 = 0, GEMV_PRO_NORM = 1 };
 struct GemvPrologue {
     int mode;
