@@ -74,56 +74,75 @@ __device__ __forceinline__ void load_row(const GrGroup& grp, int r, int nb, int 
     }
 }
 
-// One row against the staged activations: lane partials, butterfly sum, store.
-template <int BPL, int NV>
-__device__ __forceinline__ void row_dot(const GrGroup& grp, const RowRegs<BPL>& w, int r, int nb,
-                                        int lane, int v0, int nv, const uint4* xw,
-                                        const int2* aux) {
-    float acc[NV];
+// R rows (r0 .. r0 + R - 1, those below total) against the staged activations: lane partials,
+// butterfly sums, stores.  The rows share every activation load (shared memory traffic per row
+// falls by R when several vectors are staged); each row accumulates its blocks in the same
+// order for any R.
+template <int BPL, int NV, int R>
+__device__ __forceinline__ void rows_dot(const GrGroup& grp, const RowRegs<BPL> (&w)[R], int r0,
+                                         int nb, int lane, int v0, int nv, const uint4* xw,
+                                         const int2* aux) {
+    float acc[R][NV];
 #pragma unroll
-    for (int v = 0; v < NV; v++) acc[v] = 0.0f;
+    for (int k = 0; k < R; k++)
+#pragma unroll
+        for (int v = 0; v < NV; v++) acc[k][v] = 0.0f;
 #pragma unroll
     for (int j = 0; j < BPL; j++) {
         const int b = lane + 32 * j;
         if (b < nb) {
-            const uint32_t qw[4] = {w.q[j].x, w.q[j].y, w.q[j].z, w.q[j].w};
-            uint32_t lo[4], hi[4];
+            uint32_t lo[R][4], hi[R][4];
+            float dw[R];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                lo[i] = qw[i] & 0x0F0F0F0Fu;         // weights 4i..4i+3 -> x bytes 4i..
-                hi[i] = (qw[i] >> 4) & 0x0F0F0F0Fu;  // weights 16+4i.. -> x bytes 16+4i..
+            for (int k = 0; k < R; k++) {
+                const uint32_t qw[4] = {w[k].q[j].x, w[k].q[j].y, w[k].q[j].z, w[k].q[j].w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    lo[k][i] = qw[i] & 0x0F0F0F0Fu;         // weights 4i..4i+3 -> x bytes 4i..
+                    hi[k][i] = (qw[i] >> 4) & 0x0F0F0F0Fu;  // weights 16+4i.. -> x 16+4i..
+                }
+                dw[k] = f16_bits_to_f32(w[k].s[j]);
             }
-            const float dw = f16_bits_to_f32(w.s[j]);
 #pragma unroll
             for (int v = 0; v < NV; v++) {
                 const int vb = v * nb + b;
                 const uint4 x0 = xw[2 * vb], x1 = xw[2 * vb + 1];
                 const int2 ax = aux[vb];
-                int sacc = ax.y;
-                sacc = dp4a_us(lo[0], x0.x, sacc);
-                sacc = dp4a_us(lo[1], x0.y, sacc);
-                sacc = dp4a_us(lo[2], x0.z, sacc);
-                sacc = dp4a_us(lo[3], x0.w, sacc);
-                sacc = dp4a_us(hi[0], x1.x, sacc);
-                sacc = dp4a_us(hi[1], x1.y, sacc);
-                sacc = dp4a_us(hi[2], x1.z, sacc);
-                sacc = dp4a_us(hi[3], x1.w, sacc);
-                const float sf = __fsub_rn(__int_as_float(sacc), 12582912.0f);  // |s| < 2^15
-                acc[v] = __fmaf_rn(sf, __fmul_rn(dw, __int_as_float(ax.x)), acc[v]);
+                const float dx = __int_as_float(ax.x);
+#pragma unroll
+                for (int k = 0; k < R; k++) {
+                    int sacc = ax.y;
+                    sacc = dp4a_us(lo[k][0], x0.x, sacc);
+                    sacc = dp4a_us(lo[k][1], x0.y, sacc);
+                    sacc = dp4a_us(lo[k][2], x0.z, sacc);
+                    sacc = dp4a_us(lo[k][3], x0.w, sacc);
+                    sacc = dp4a_us(hi[k][0], x1.x, sacc);
+                    sacc = dp4a_us(hi[k][1], x1.y, sacc);
+                    sacc = dp4a_us(hi[k][2], x1.z, sacc);
+                    sacc = dp4a_us(hi[k][3], x1.w, sacc);
+                    const float sf = __fsub_rn(__int_as_float(sacc), 12582912.0f);  // |s| < 2^15
+                    acc[k][v] = __fmaf_rn(sf, __fmul_rn(dw[k], dx), acc[k][v]);
+                }
             }
         }
     }
-    int m = 0;
 #pragma unroll
-    for (int i = 1; i < GR_MAX_MATS; i++)
-        if (i < grp.count && r >= grp.first_row[i]) m = i;
-    const int lr = r - grp.first_row[m];
+    for (int k = 0; k < R; k++) {
+        const int r = r0 + k;
+        if (r >= grp.total_rows) break;  // warp-uniform
+        int m = 0;
 #pragma unroll
-    for (int v = 0; v < NV; v++) {
-        float t = acc[v];
+        for (int i = 1; i < GR_MAX_MATS; i++)
+            if (i < grp.count && r >= grp.first_row[i]) m = i;
+        const int lr = r - grp.first_row[m];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
-        if (lane == 0 && v < nv) grp.out[m][(size_t)(v0 + v) * grp.rows[m] + lr] = t;
+        for (int v = 0; v < NV; v++) {
+            float t = acc[k][v];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+            if (lane == 0 && v < nv) grp.out[m][(size_t)(v0 + v) * grp.rows[m] + lr] = t;
+        }
     }
 }
 
@@ -252,7 +271,7 @@ __global__ void __launch_bounds__(GR_THREADS)
     const int stride = gridDim.x * GR_WARPS * R;
     int r = (blockIdx.x * GR_WARPS + (tid >> 5)) * R;
 
-    RowRegs<BPL> cur[R];
+    RowRegs<BPL> cur[R] = {};
     if (static_weights)
 #pragma unroll
         for (int k = 0; k < R; k++)
@@ -291,15 +310,12 @@ __global__ void __launch_bounds__(GR_THREADS)
     __syncthreads();
 
     for (; r < grp.total_rows; r += stride) {
-        RowRegs<BPL> nxt[R];
+        RowRegs<BPL> nxt[R] = {};
 #pragma unroll
         for (int k = 0; k < R; k++)
             if (r + stride + k < grp.total_rows)
                 load_row<BPL>(grp, r + stride + k, nb, lane, nxt[k]);
-#pragma unroll
-        for (int k = 0; k < R; k++)
-            if (r + k < grp.total_rows)
-                row_dot<BPL, NV>(grp, cur[k], r + k, nb, lane, v0, nv, xw, aux);
+        rows_dot<BPL, NV, R>(grp, cur, r, nb, lane, v0, nv, xw, aux);
 #pragma unroll
         for (int k = 0; k < R; k++) cur[k] = nxt[k];
     }
@@ -371,6 +387,15 @@ int launch_fast_nv(sulimo_ctx* ctx, const FastArgs& a) {
     }
     if constexpr (PRO == GEMV_PRO_NORM) {
         return launch_fast<BPL, 1, 1, PRO>(ctx, a);  // batch 1 only (gemv_fast_fused_ok)
+    } else if constexpr (BPL <= 4) {
+        // several vectors: two rows per warp share each staged activation load (the rows'
+        // re-reads of the vectors, not the weights, bound the batched matvec)
+        switch (a.nv) {
+            case 8: return launch_fast<BPL, 8, 2, PRO>(ctx, a);
+            case 4: return launch_fast<BPL, 4, 2, PRO>(ctx, a);
+            case 2: return launch_fast<BPL, 2, 2, PRO>(ctx, a);
+            default: return launch_fast<BPL, 1, 1, PRO>(ctx, a);
+        }
     } else {
         switch (a.nv) {
             case 8: return launch_fast<BPL, 8, 1, PRO>(ctx, a);
