@@ -47,6 +47,12 @@ def lib():
             "oracle_softmax_scalar": (None, [vp, sz]),
             "oracle_swiglu_scalar": (None, [vp, vp, vp, sz]),
             "oracle_causal_gqa_decode": (None, [vp, vp, vp, sz, sz, sz, sz, sz, vp, vp, f32]),
+            "oracle_rmsnorm_f16": (None, [vp, vp, vp, sz, f32, sz]),
+            "oracle_rope_f16": (None, [vp, sz, sz, sz, f32, i32, sz, sz]),
+            "oracle_attention_prefill_f16": (None, [vp, vp, vp, vp, sz, sz, sz, sz, sz, sz]),
+            "oracle_silu_mul_f16": (None, [vp, vp, vp, sz]),
+            "oracle_add_f16": (None, [vp, vp, sz]),
+            "oracle_prefill_ubatch": (i32, [vp, vp, sz, sz, vp, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -283,3 +289,65 @@ class OracleModel:
         lib().oracle_forward_token(C.byref(self.m), C.c_uint32(token), C.c_size_t(pos),
                                    out.ctypes.data_as(C.POINTER(C.c_float)))
         return out
+
+    def embed_f16(self, tokens):
+        """lookup_token_embedding_f16 per token (crates/sulimo-engine/src/scheduler.rs:329-374):
+        the f16 rows the engine writes into the prefill ubatch's x."""
+        E = self.cfg["embd"]
+        return np.concatenate([lookup_token_embedding_f16(self.w["tok"][0], self.w["tok"][1], E,
+                                                          int(t)) for t in tokens])
+
+    def prefill_ubatch(self, tokens, start_pos, threads=1, x_f16=None):
+        """oracle_prefill_ubatch (execute_prefill_ubatch, crates/sulimo-ocl/src/prefill.rs:337-566)
+        for `tokens` at positions start_pos..: returns (last-token fp32 logits, the f16 residual
+        stream [n][embd]).  The K/V rings of this model advance."""
+        x = self.embed_f16(tokens) if x_f16 is None else np.array(x_f16, np.uint16, copy=True)
+        logits = np.empty(self.cfg["vocab"], np.float32)
+        st = lib().oracle_prefill_ubatch(C.byref(self.m), _p(x), start_pos, len(tokens),
+                                         _p(logits), threads)
+        assert st == 0, "oracle_prefill_ubatch rejected its arguments"
+        return logits, x.reshape(len(tokens), -1)
+
+
+def _f16_buf(a):
+    return np.array(a, dtype=np.uint16, copy=True)
+
+
+def rmsnorm_f16(x_f16, w, eps, D):
+    x = np.ascontiguousarray(x_f16, np.uint16)
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm_f16(_p(x), _p(np.ascontiguousarray(w, np.float32)), _p(out), D, eps,
+                             x.size // D)
+    return out
+
+
+def rope_f16(vec_f16, head_count, head_dim, rope_dim, base, mode, start_pos):
+    v = _f16_buf(vec_f16)
+    lib().oracle_rope_f16(_p(v), head_count, head_dim, rope_dim, base, mode, start_pos,
+                          v.size // (head_count * head_dim))
+    return v
+
+
+def attention_prefill_f16(q_f16, k_ring, v_ring, start_pos, capacity, head_count, head_count_kv,
+                          head_dim):
+    q = np.ascontiguousarray(q_f16, np.uint16)
+    out = np.empty_like(q)
+    lib().oracle_attention_prefill_f16(_p(q), _p(np.ascontiguousarray(k_ring, np.uint8)),
+                                       _p(np.ascontiguousarray(v_ring, np.uint8)), _p(out),
+                                       start_pos, capacity, head_count, head_count_kv, head_dim,
+                                       q.size // (head_count * head_dim))
+    return out
+
+
+def silu_mul_f16(gate_f16, up_f16):
+    g = np.ascontiguousarray(gate_f16, np.uint16)
+    u = np.ascontiguousarray(up_f16, np.uint16)
+    out = np.empty_like(g)
+    lib().oracle_silu_mul_f16(_p(g), _p(u), _p(out), g.size)
+    return out
+
+
+def add_f16(a_f16, b_f16):
+    a = _f16_buf(a_f16)
+    lib().oracle_add_f16(_p(a), _p(np.ascontiguousarray(b_f16, np.uint16)), a.size)
+    return a

@@ -627,3 +627,170 @@ void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, flo
     free(x); free(h); free(q); free(k); free(v); free(att); free(g); free(u); free(sw);
     free(dn); free(scores); free(q8);
 }
+
+/* ------------------------------------------------------------------ */
+/* GPU prefill ubatch on f16 storage                                   */
+/* ------------------------------------------------------------------ */
+/* The reference's GPU prefill (execute_prefill_ubatch, crates/sulimo-ocl/src/prefill.rs:337-566)
+ * keeps every activation in f16 between kernels; each helper below restates one kernel of
+ * kernels/prefill.cl on those f16 buffers, with its float operations in source order. */
+
+static inline uint16_t f16r(float x) { return oracle_f32_to_f16(x); }
+static inline float f16w(uint16_t h) { return oracle_f16_to_f32(h); }
+
+/* rmsnorm_f16_f32w — kernels/prefill.cl:4-29 */
+void oracle_rmsnorm_f16(const uint16_t* x, const float* w, uint16_t* out, size_t D, float eps,
+                        size_t N) {
+    for (size_t n = 0; n < N; n++) {
+        const uint16_t* xr = x + n * D;
+        float sum_sq = 0.0f;
+        for (size_t i = 0; i < D; i++) {
+            float v = f16w(xr[i]);
+            sum_sq += v * v;
+        }
+        float mean = sum_sq / (float)D;
+        float scale = 1.0f / sqrtf(mean + eps);
+        for (size_t i = 0; i < D; i++) out[n * D + i] = f16r(f16w(xr[i]) * scale * w[i]);
+    }
+}
+
+/* rope_f16 — kernels/prefill.cl:32-68: the rotation of rope_head_scalar on f16 storage */
+void oracle_rope_f16(uint16_t* vec, size_t head_count, size_t head_dim, size_t rope_dim,
+                     float freq_base, int mode, size_t start_pos, size_t N) {
+    float* tmp = (float*)__builtin_alloca(head_dim * sizeof(float));
+    for (size_t n = 0; n < N; n++)
+        for (size_t h = 0; h < head_count; h++) {
+            uint16_t* hp = vec + (n * head_count + h) * head_dim;
+            for (size_t i = 0; i < head_dim; i++) tmp[i] = f16w(hp[i]);
+            oracle_rope_head_scalar(tmp, start_pos + n, rope_dim, freq_base, mode);
+            for (size_t i = 0; i < rope_dim; i++) hp[i] = f16r(tmp[i]);
+        }
+}
+
+/* causal_gqa_attention_prefill — kernels/prefill.cl:120-237: scores in fp32 from f16 q and the
+ * Q8_0 ring (each K element dequantised as q*d before the product), softmax over positions
+ * 0..start_pos+n, then the output accumulated IN F16: out += f16(w * v) per key, per element.
+ * The kernel recomputes the identical scores in each of its three passes; they are computed
+ * once here. */
+void oracle_attention_prefill_f16(const uint16_t* q, const uint8_t* k_ring, const uint8_t* v_ring,
+                                  uint16_t* out, size_t start_pos, size_t capacity,
+                                  size_t head_count, size_t head_count_kv, size_t head_dim,
+                                  size_t N) {
+    const size_t hpk = head_count / head_count_kv;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    const size_t bph = head_dim / 32, head_bytes = bph * 34;
+    const size_t bytes_per_pos = head_count_kv * head_bytes;
+    float* scores = (float*)malloc((start_pos + N) * sizeof(float));
+    for (size_t n = 0; n < N; n++)
+        for (size_t h = 0; h < head_count; h++) {
+            const size_t kvh = h / hpk, num_keys = start_pos + n + 1;
+            const uint16_t* qh = q + (n * head_count + h) * head_dim;
+            float max_score = -1e30f;
+            for (size_t p = 0; p < num_keys; p++) {
+                const uint8_t* kp = k_ring + (p % capacity) * bytes_per_pos + kvh * head_bytes;
+                float dot = 0.0f;
+                for (size_t b = 0; b < bph; b++) {
+                    const uint8_t* blk = kp + b * 34;
+                    float d = le_f16(blk);
+                    for (int i = 0; i < 32; i++)
+                        dot += f16w(qh[b * 32 + i]) * ((float)(int8_t)blk[2 + i] * d);
+                }
+                float s = dot * scale;
+                scores[p] = s;
+                if (s > max_score) max_score = s;
+            }
+            float sum_exp = 0.0f;
+            for (size_t p = 0; p < num_keys; p++) sum_exp += expf(scores[p] - max_score);
+            const float inv = (sum_exp > 0.0f) ? (1.0f / sum_exp) : 0.0f;
+            uint16_t* oh = out + (n * head_count + h) * head_dim;
+            for (size_t i = 0; i < head_dim; i++) oh[i] = 0;
+            for (size_t p = 0; p < num_keys; p++) {
+                const float wgt = expf(scores[p] - max_score) * inv;
+                const uint8_t* vp = v_ring + (p % capacity) * bytes_per_pos + kvh * head_bytes;
+                for (size_t b = 0; b < bph; b++) {
+                    const uint8_t* blk = vp + b * 34;
+                    float d = le_f16(blk);
+                    for (int i = 0; i < 32; i++) {
+                        float vv = (float)(int8_t)blk[2 + i] * d;
+                        uint16_t* o = &oh[b * 32 + i];
+                        *o = f16r(f16w(*o) + f16w(f16r(wgt * vv)));
+                    }
+                }
+            }
+        }
+    free(scores);
+}
+
+/* silu_mul_f16 — kernels/prefill.cl:240-253 */
+void oracle_silu_mul_f16(const uint16_t* gate, const uint16_t* up, uint16_t* out, size_t n) {
+    for (size_t i = 0; i < n; i++) {
+        float g = f16w(gate[i]), u = f16w(up[i]);
+        float silu = g / (1.0f + expf(-g));
+        out[i] = f16r(silu * u);
+    }
+}
+
+/* add_f16 — kernels/prefill.cl:256-266 */
+void oracle_add_f16(uint16_t* a, const uint16_t* b, size_t n) {
+    for (size_t i = 0; i < n; i++) a[i] = f16r(f16w(a[i]) + f16w(b[i]));
+}
+
+/* One GEMM of the ubatch with f16 results: gemm_q4_0_f16_portable (kernels/gemm_q4_0.cl:13-58),
+ * whose arithmetic is gemm_dot's, rounded once to f16. */
+static void pf_gemm_f16(const uint8_t* scales, const uint8_t* quants, const uint16_t* x,
+                        size_t m, size_t k, size_t n, uint16_t* out, float* tmp, int threads) {
+    oracle_gemm_q4_0_f16_scalar_f32out((const uint16_t*)scales, quants, x, m, k, n, tmp, threads);
+    oracle_f32_to_f16_array(tmp, out, m * n);
+}
+
+/* execute_prefill_ubatch — crates/sulimo-ocl/src/prefill.rs:337-566, step for step (steps 1-14
+ * of its body).  x: [n][embd] f16, the ubatch's embeddings on entry (lookup_token_embedding_f16
+ * per token, crates/sulimo-engine/src/engine.rs:249-256) and the residual stream on return;
+ * K/V go to ring slots (start_pos + t) % kv_capacity; logits[vocab] = the last token's fp32
+ * logits.  As in the reference, the o projection is embd x embd (head_count*head_dim == embd)
+ * and no QKV bias or softcap is applied.  Returns 0, or -1 for invalid arguments. */
+int oracle_prefill_ubatch(const oracle_model* m, uint16_t* x, size_t start_pos, size_t n,
+                          float* logits, int threads) {
+    if (!m || !x || !logits || n == 0) return -1;
+    const size_t E = (size_t)m->embd, F = (size_t)m->ffn, hd = (size_t)m->head_dim;
+    const size_t H = (size_t)m->head_count, Hkv = (size_t)m->head_count_kv;
+    const size_t qd = H * hd, kvd = Hkv * hd;
+    if (qd != E) return -1;
+    size_t big = E > F ? E : F;
+    uint16_t* h = (uint16_t*)malloc(n * E * 2);
+    uint16_t* q = (uint16_t*)malloc(n * qd * 2);
+    uint16_t* k = (uint16_t*)malloc(n * kvd * 2);
+    uint16_t* v = (uint16_t*)malloc(n * kvd * 2);
+    uint16_t* att = (uint16_t*)malloc(n * qd * 2);
+    uint16_t* g = (uint16_t*)malloc(n * F * 2);
+    uint16_t* u = (uint16_t*)malloc(n * F * 2);
+    uint16_t* sw = (uint16_t*)malloc(n * F * 2);
+    uint16_t* dn = (uint16_t*)malloc(n * E * 2);
+    float* tmp = (float*)malloc(n * big * 4);
+    for (int l = 0; l < m->n_layers; l++) {
+        const oracle_layer* L = &m->layers[l];
+        oracle_rmsnorm_f16(x, L->attn_norm, h, E, m->eps, n);
+        pf_gemm_f16(L->wq_s, L->wq_q, h, qd, E, n, q, tmp, threads);
+        pf_gemm_f16(L->wk_s, L->wk_q, h, kvd, E, n, k, tmp, threads);
+        pf_gemm_f16(L->wv_s, L->wv_q, h, kvd, E, n, v, tmp, threads);
+        oracle_rope_f16(q, H, hd, (size_t)m->rope_dim, m->rope_base, m->rope_mode, start_pos, n);
+        oracle_rope_f16(k, Hkv, hd, (size_t)m->rope_dim, m->rope_base, m->rope_mode, start_pos, n);
+        oracle_kv_store_q8_0(k, L->k_ring, start_pos, m->kv_capacity, kvd / 32, n);
+        oracle_kv_store_q8_0(v, L->v_ring, start_pos, m->kv_capacity, kvd / 32, n);
+        oracle_attention_prefill_f16(q, L->k_ring, L->v_ring, att, start_pos, m->kv_capacity, H,
+                                     Hkv, hd, n);
+        pf_gemm_f16(L->wo_s, L->wo_q, att, E, E, n, h, tmp, threads);
+        oracle_add_f16(x, h, n * E);
+        oracle_rmsnorm_f16(x, L->ffn_norm, h, E, m->eps, n);
+        pf_gemm_f16(L->wg_s, L->wg_q, h, F, E, n, g, tmp, threads);
+        pf_gemm_f16(L->wu_s, L->wu_q, h, F, E, n, u, tmp, threads);
+        oracle_silu_mul_f16(g, u, sw, n * F);
+        pf_gemm_f16(L->wd_s, L->wd_q, sw, E, F, n, dn, tmp, threads);
+        oracle_add_f16(x, dn, n * E);
+    }
+    oracle_rmsnorm_f16(x, m->out_norm, h, E, m->eps, n);
+    oracle_gemm_q4_0_f16_scalar_f32out((const uint16_t*)m->out_s, m->out_q, h + (n - 1) * E,
+                                       (size_t)m->vocab, E, 1, logits, threads);
+    free(h); free(q); free(k); free(v); free(att); free(g); free(u); free(sw); free(dn); free(tmp);
+    return 0;
+}

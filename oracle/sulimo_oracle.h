@@ -6,12 +6,17 @@
  * bench.py times beside them.  Nothing in the product path (the C-ABI
  * library libsulimo_cuda.so and the sulimo_b200 package) links or calls it.
  *
- * Every function restates one function of the reference (a Rust workspace;
- * paths below are relative to the reference repository root) and cites the
- * lines it follows.  The reference cannot be built in this environment (no
- * Rust toolchain), so the restatement is pinned by re-running the
- * reference's own unit tests against it (tests/test_oracle.py) rather than
- * by reference-produced values.
+ * Every function restates one function of the reference (a Rust workspace
+ * with OpenCL C kernels; paths below are relative to the reference repository
+ * root) and cites the lines it follows.  Pinning: the reference's Rust crates
+ * cannot be built without a Rust toolchain, but its OpenCL C kernels
+ * (kernels/gemm_q4_0.cl, kernels/prefill.cl) compile unchanged for the host
+ * (oracle/_ref via oracle/ref_build.py); the GEMM, KV store, logits, the
+ * prefill kernels and the whole prefill ubatch here are bit-identical to them
+ * (tests/test_ref_pinning.py, fixture tests/golden/ref_ocl.npz).  The CPU
+ * decode path (AVX2 matvec, Q8_0, attention, forward_token) is pinned by the
+ * reference's own unit tests re-expressed here (tests/test_oracle.py) and by
+ * an exact-arithmetic second restatement (tests/golden/exact_ref.py).
  *
  * Numeric conventions carried over from Rust:
  *   - no FMA contraction (the library is built with -ffp-contract=off);
@@ -131,6 +136,25 @@ typedef struct oracle_model {
 
 /* logits [vocab] for `token` at position `pos` (context pos+1); stores K/V at pos. */
 void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, float* logits);
+
+
+/* ---- GPU prefill ubatch on f16 storage (crates/sulimo-ocl/src/prefill.rs:337-566 over the
+ * kernels of kernels/prefill.cl): every activation is f16 between kernels, as in the
+ * reference.  x: [n][embd] f16 embeddings in, residual stream out; writes ring slots
+ * (start_pos+t) % kv_capacity; logits[vocab] of the last token.  No QKV bias (the reference's
+ * GPU ubatch applies none).  Requires head_count*head_dim == embd.  0 or -1. */
+void oracle_rmsnorm_f16(const uint16_t* x, const float* w, uint16_t* out, size_t D, float eps,
+                        size_t N);
+void oracle_rope_f16(uint16_t* vec, size_t head_count, size_t head_dim, size_t rope_dim,
+                     float freq_base, int mode, size_t start_pos, size_t N);
+void oracle_attention_prefill_f16(const uint16_t* q, const uint8_t* k_ring, const uint8_t* v_ring,
+                                  uint16_t* out, size_t start_pos, size_t capacity,
+                                  size_t head_count, size_t head_count_kv, size_t head_dim,
+                                  size_t N);
+void oracle_silu_mul_f16(const uint16_t* gate, const uint16_t* up, uint16_t* out, size_t n);
+void oracle_add_f16(uint16_t* a, const uint16_t* b, size_t n);
+int oracle_prefill_ubatch(const oracle_model* m, uint16_t* x, size_t start_pos, size_t n,
+                          float* logits, int threads);
 
 #ifdef __cplusplus
 }

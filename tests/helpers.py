@@ -66,3 +66,55 @@ def cosine(a, b):
     if na == 0 or nb == 0:
         return 0.0
     return float(a @ b / (na * nb))
+
+
+def make_norm_pattern_prefill(dim, seed):
+    """crates/sulimo-ocl/tests/test_prefill.rs:248-272 (helper_alloc_norm): 1 + 0.02*((i+seed)%5)."""
+    i = np.arange(dim)
+    return (np.float32(1.0) + np.float32(0.02) * ((i + seed) % 5).astype(np.float32)).astype(np.float32)
+
+
+# The model of crates/sulimo-ocl/tests/test_prefill.rs:296-331: Llama, 2 layers, embd 64,
+# ffn 128, 4 query / 2 KV heads of 16, vocab 64, ring capacity 64, RoPE base 1e4, eps 1e-5.
+PREFILL_TEST_CFG = dict(n_layers=2, embd=64, ffn=128, head_count=4, head_count_kv=2, head_dim=16,
+                        vocab=64, rope_dim=16, rope_mode=0, eps=1e-5, rope_base=10000.0,
+                        attn_softcap=0.0, bias=False, kv_capacity=64)
+
+
+def make_model_pattern_prefill():
+    """The reference test's weights (test_prefill.rs:398-463): layer l's q/k/v/o/gate/up/down use
+    helper_alloc_q4 seeds l*10+2 .. l*10+9, norms seeds l*10+1 and l*10+6, the output norm
+    seed 99 and the output projection seed 100.  Returns the numpy model dict that
+    oracle.ffi.OracleModel and sulimo_b200.synthetic.to_device take (the token embedding is
+    the output matrix; the test feeds x directly, make_x_pattern_prefill)."""
+    cfg = dict(PREFILL_TEST_CFG)
+    E, F = cfg["embd"], cfg["ffn"]
+    qd = cfg["head_count"] * cfg["head_dim"]
+    kvd = cfg["head_count_kv"] * cfg["head_dim"]
+    shapes = dict(wq=(qd, E), wk=(kvd, E), wv=(kvd, E), wo=(E, qd), wg=(F, E), wu=(F, E),
+                  wd=(E, F))
+    seeds = dict(wq=2, wk=3, wv=4, wo=5, wg=7, wu=8, wd=9)
+    layers = []
+    for l in range(cfg["n_layers"]):
+        L = {name: make_q4_0_pattern_prefill(*shapes[name], l * 10 + seeds[name])
+             for name in shapes}
+        L["attn_norm"] = make_norm_pattern_prefill(E, l * 10 + 1)
+        L["ffn_norm"] = make_norm_pattern_prefill(E, l * 10 + 6)
+        L["bq"] = L["bk"] = L["bv"] = None
+        layers.append(L)
+    out = make_q4_0_pattern_prefill(cfg["vocab"], E, 100)
+    return dict(cfg=cfg, tok=out, out=out, out_norm=make_norm_pattern_prefill(E, 99),
+                layers=layers)
+
+
+def make_x_pattern_prefill(n, embd):
+    """test_prefill.rs:516-522: x = f16(((i % 17) - 8) * 0.15) as f16 bits [n*embd]."""
+    i = np.arange(n * embd)
+    return (((i % 17) - 8.0).astype(np.float32) * np.float32(0.15)).astype(np.float16).view(np.uint16)
+
+
+def make_act_pattern_kv_store(n_tokens, blocks_per_pos):
+    """test_prefill.rs:84-89: f16(sin(0.17 i) * 5 + (i % 7 - 3)), with numpy's float32 sin."""
+    i = np.arange(n_tokens * blocks_per_pos * 32)
+    v = np.sin(i.astype(np.float32) * np.float32(0.17)) * np.float32(5.0) + ((i % 7) - 3).astype(np.float32)
+    return v.astype(np.float32).astype(np.float16).view(np.uint16)
