@@ -81,6 +81,10 @@ void* sulimo_cuda_ctx_get_stream(sulimo_ctx* ctx);
 int sulimo_cuda_ctx_device(sulimo_ctx* ctx);
 /* Launches issued by this library since the context was created (a kernel-count probe). */
 uint64_t sulimo_cuda_ctx_launch_count(sulimo_ctx* ctx);
+/* Bytes of device memory the context has allocated for itself on demand (the attention      */
+/* workspace and the argmax partials; caller-owned buffers excluded) — a memory diagnostic    */
+/* in the spirit of active_cl_mem_count (crates/sulimo-ocl/src/buffer.rs:21).                 */
+size_t sulimo_cuda_ctx_workspace_bytes(sulimo_ctx* ctx);
 
 /* ---------------------------------------------------------------------------------------- */
 /* Buffers — replace OclBuffer::from_host_ptr / map_read / Drop / active_cl_mem_count        */
@@ -208,12 +212,21 @@ int sulimo_cuda_ipc_close(sulimo_ctx* ctx, void* dev_ptr);
 /* valid in this process, i.e. opened IPC mappings) over NVLink, then one arrival per CTA added */
 /* to every rank's counter (flags: host array of `world` device pointers).  *tiles_out = CTAs   */
 /* of this launch.  A rank's Y is complete once its counter has grown by the sum of all ranks' */
-/* CTAs: sulimo_cuda_wait_counter.  No split-K.                                                 */
+/* CTAs: sulimo_cuda_wait_counter.  No split-K.  (The reference runs on one device; this is     */
+/* the row-sharded form of enqueue_gemm_q4_0_f16, crates/sulimo-ocl/src/prefill.rs:69-105.)    */
+/* Release handshake: `epoch` numbers the calls (1, 2, ... on every rank, modulo 2^32, never   */
+/* 0) and release[r] is rank r's release word (a 4-byte device word, zero before the first     */
+/* call).  The kernel sets this rank's word to `epoch` once the work enqueued on this          */
+/* context's stream before the call has completed, and stores into rank r's Y only after       */
+/* rank r's word has reached `epoch` (bounded wait, then SULIMO_EDEVICE).  So a rank's readers */
+/* of the previous Y, enqueued on its stream before its next call, finish before any peer      */
+/* overwrites it.                                                                              */
 int sulimo_cuda_gemm_q4_0_f16_allgather(sulimo_ctx* ctx, const void* scales, const void* quants,
                                         const void* x, int m_local, int m_valid, int k, int n,
                                         int out_dtype, void* const* out_bases, size_t f_total,
-                                        size_t col0, unsigned* const* flags, int world,
-                                        unsigned* tiles_out);
+                                        size_t col0, unsigned* const* flags,
+                                        unsigned* const* release, int world, int rank,
+                                        unsigned epoch, unsigned* tiles_out);
 
 /* Enqueues a bounded wait (one thread; SULIMO_EDEVICE at the next synchronize after ~2 s)     */
 /* until *flag (device) reaches `target` (modulo 2^32 arithmetic).                             */
@@ -262,11 +275,20 @@ size_t sulimo_cuda_prefill_scratch_bytes(const sulimo_model_desc* model, int n);
 /* 337-566): tokens[n] (device int32) at positions start_pos .. start_pos+n-1 of ONE sequence  */
 /* (kv_seq_stride unused), K/V stored into the rings, logits[vocab] (fp32) of the last token   */
 /* (enqueue_logits_final, prefill.rs:300-330).  Requires start_pos + n <= kv_capacity.        */
-/* Unlike the reference's GPU ubatch this one applies the QKV biases (as forward_token does)  */
-/* and keeps the residual stream in fp32; the GEMM activations are f16 like the reference's.   */
+/* The embeddings are the f16 rows of lookup_token_embedding_f16 (scheduler.rs:329-374), as   */
+/* the reference's engine writes them (engine.rs:249-256).  Unlike the reference's GPU ubatch  */
+/* this one applies the QKV biases (as forward_token does) and keeps the residual stream in    */
+/* fp32; the GEMM activations are f16 like the reference's.                                   */
 int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
                                const int32_t* tokens, int n, size_t start_pos, float* logits,
                                void* scratch, size_t scratch_bytes);
+
+/* The same ubatch for a caller that has written the embeddings itself — the reference's      */
+/* contract exactly (execute_prefill_ubatch reads them from scratch.x, prefill.rs:337-566):     */
+/* x_f16 [n][embd] f16 on the device (8-byte aligned), not modified.                          */
+int sulimo_cuda_prefill_ubatch_x(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                                 const void* x_f16, int n, size_t start_pos, float* logits,
+                                 void* scratch, size_t scratch_bytes);
 
 /* Causal GQA prefill attention over one layer's Q8_0 ring — replaces                          */
 /* causal_gqa_attention_prefill (kernels/prefill.cl:120-237, enqueue_attention_prefill):       */

@@ -53,6 +53,7 @@ def lib():
             "oracle_silu_mul_f16": (None, [vp, vp, vp, sz]),
             "oracle_add_f16": (None, [vp, vp, sz]),
             "oracle_prefill_ubatch": (i32, [vp, vp, sz, sz, vp, i32]),
+            "oracle_prefill_ubatch_f32": (i32, [vp, vp, sz, sz, vp, i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -307,6 +308,18 @@ class OracleModel:
                                          _p(logits), threads)
         assert st == 0, "oracle_prefill_ubatch rejected its arguments"
         return logits, x.reshape(len(tokens), -1)
+
+    def prefill_ubatch_f32(self, tokens, start_pos, threads=1, x_f16=None):
+        """oracle_prefill_ubatch_f32: the reference prefill test's CPU oracle
+        (crates/sulimo-ocl/tests/test_prefill.rs:583-800), fp32 residual; returns the last
+        token's logits.  The K/V rings of this model advance."""
+        x = self.embed_f16(tokens) if x_f16 is None else np.ascontiguousarray(x_f16, np.uint16)
+        n = x.size // self.cfg["embd"]
+        logits = np.empty(self.cfg["vocab"], np.float32)
+        st = lib().oracle_prefill_ubatch_f32(C.byref(self.m), _p(x), start_pos, n, _p(logits),
+                                             threads)
+        assert st == 0, "oracle_prefill_ubatch_f32 rejected its arguments"
+        return logits
 
 
 def _f16_buf(a):

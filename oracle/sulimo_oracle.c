@@ -540,6 +540,9 @@ void oracle_causal_gqa_decode(const float* q, const uint8_t* k_ring, const uint8
     size_t head_bytes = (head_dim / 32) * 34;
     size_t bytes_per_pos = head_count_kv * head_bytes;
     float* deq = (float*)__builtin_alloca(head_dim * sizeof(float));
+    /* the reference's dequant buffer starts zeroed (test_prefill.rs:690, ScratchBuffers); with
+     * head_dim < 32 no block is dequantised into it and the zeros are what is read */
+    memset(deq, 0, head_dim * sizeof(float));
     for (size_t h = 0; h < head_count; h++) {
         size_t kvh = h / heads_per_kv;
         const float* qh = q + h * head_dim;
@@ -792,5 +795,90 @@ int oracle_prefill_ubatch(const oracle_model* m, uint16_t* x, size_t start_pos, 
     oracle_gemm_q4_0_f16_scalar_f32out((const uint16_t*)m->out_s, m->out_q, h + (n - 1) * E,
                                        (size_t)m->vocab, E, 1, logits, threads);
     free(h); free(q); free(k); free(v); free(att); free(g); free(u); free(sw); free(dn); free(tmp);
+    return 0;
+}
+
+/* The CPU oracle of the reference's prefill test (crates/sulimo-ocl/tests/test_prefill.rs:
+ * 583-800), the reference's own definition of a correct GPU prefill, which its GPU ubatch must
+ * match within one Q8_0 step of K/V, cosine 0.99 and the same greedy token (:826-890): an fp32
+ * residual stream, rmsnorm_scalar (scalar.rs:23-40) rounded to f16 for each GEMM, f16 GEMM
+ * outputs widened to f32, rope_head_scalar in fp32, quantize_f32_to_q8_0 into the ring,
+ * causal_gqa_decode_scalar per token, SwiGLU in fp32, and the last token's final norm kept in
+ * fp32 for the logits (:781-800).  Positions start at start_pos (the test uses 0) and ring slots
+ * are (start_pos + t) % kv_capacity.  QKV biases, when the model has them, are added to the
+ * widened projections as forward_token adds them (forward_pass.rs:452-465); the test's Llama
+ * model has none.  x_f16: [n][embd] embeddings in; logits[vocab] of the last token.  0 / -1. */
+int oracle_prefill_ubatch_f32(const oracle_model* m, const uint16_t* x_f16, size_t start_pos,
+                              size_t n, float* logits, int threads) {
+    if (!m || !x_f16 || !logits || n == 0) return -1;
+    const size_t E = (size_t)m->embd, F = (size_t)m->ffn, hd = (size_t)m->head_dim;
+    const size_t H = (size_t)m->head_count, Hkv = (size_t)m->head_count_kv;
+    const size_t qd = H * hd, kvd = Hkv * hd;
+    const size_t ctx_max = start_pos + n;
+    size_t big = qd > F ? qd : F;
+    if (E > big) big = E;
+    float* x = (float*)malloc(n * E * 4);
+    float* hf = (float*)malloc(n * E * 4);
+    uint16_t* h16 = (uint16_t*)malloc(n * big * 2);
+    float* q = (float*)malloc(n * qd * 4);
+    float* k = (float*)malloc(n * kvd * 4);
+    float* v = (float*)malloc(n * kvd * 4);
+    float* att = (float*)malloc(n * qd * 4);
+    float* g = (float*)malloc(n * F * 4);
+    float* u = (float*)malloc(n * F * 4);
+    float* tmp = (float*)malloc(n * big * 4);
+    float* scores = (float*)malloc(ctx_max * 4);
+    oracle_f16_to_f32_array(x_f16, x, n * E);
+    /* a GEMM with f16 inputs and f16 outputs widened back to f32 (gemm_q4_0_f16_scalar_reference
+     * then f16::to_f32) */
+#define PF32_GEMM(W_S, W_Q, IN16, ROWS, COLS, OUT)                                              \
+    do {                                                                                       \
+        oracle_gemm_q4_0_f16_scalar_f32out((const uint16_t*)(W_S), (W_Q), (IN16), (ROWS), (COLS), \
+                                           n, tmp, threads);                                   \
+        for (size_t i_ = 0; i_ < (size_t)(ROWS) * n; i_++) (OUT)[i_] = f16w(f16r(tmp[i_]));    \
+    } while (0)
+    for (int l = 0; l < m->n_layers; l++) {
+        const oracle_layer* L = &m->layers[l];
+        for (size_t t = 0; t < n; t++) oracle_rmsnorm_scalar(x + t * E, L->attn_norm, E, m->eps, hf + t * E);
+        oracle_f32_to_f16_array(hf, h16, n * E);
+        PF32_GEMM(L->wq_s, L->wq_q, h16, qd, E, q);
+        PF32_GEMM(L->wk_s, L->wk_q, h16, kvd, E, k);
+        PF32_GEMM(L->wv_s, L->wv_q, h16, kvd, E, v);
+        for (size_t t = 0; t < n; t++) {
+            if (L->bq) for (size_t i = 0; i < qd; i++) q[t * qd + i] += L->bq[i];
+            if (L->bk) for (size_t i = 0; i < kvd; i++) k[t * kvd + i] += L->bk[i];
+            if (L->bv) for (size_t i = 0; i < kvd; i++) v[t * kvd + i] += L->bv[i];
+            for (size_t hh = 0; hh < H; hh++)
+                oracle_rope_head_scalar(q + t * qd + hh * hd, start_pos + t, (size_t)m->rope_dim,
+                                        m->rope_base, m->rope_mode);
+            for (size_t hh = 0; hh < Hkv; hh++)
+                oracle_rope_head_scalar(k + t * kvd + hh * hd, start_pos + t, (size_t)m->rope_dim,
+                                        m->rope_base, m->rope_mode);
+            oracle_kv_store_f32(k + t * kvd, L->k_ring, start_pos + t, m->kv_capacity, kvd / 32);
+            oracle_kv_store_f32(v + t * kvd, L->v_ring, start_pos + t, m->kv_capacity, kvd / 32);
+        }
+        for (size_t t = 0; t < n; t++)
+            oracle_causal_gqa_decode(q + t * qd, L->k_ring, L->v_ring, m->kv_capacity,
+                                     start_pos + t + 1, H, Hkv, hd, scores, att + t * qd, 0.0f);
+        oracle_f32_to_f16_array(att, h16, n * qd);
+        PF32_GEMM(L->wo_s, L->wo_q, h16, E, qd, hf);
+        for (size_t i = 0; i < n * E; i++) x[i] += hf[i];
+        for (size_t t = 0; t < n; t++) oracle_rmsnorm_scalar(x + t * E, L->ffn_norm, E, m->eps, hf + t * E);
+        oracle_f32_to_f16_array(hf, h16, n * E);
+        PF32_GEMM(L->wg_s, L->wg_q, h16, F, E, g);
+        PF32_GEMM(L->wu_s, L->wu_q, h16, F, E, u);
+        oracle_swiglu_scalar(g, u, g, n * F);
+        oracle_f32_to_f16_array(g, h16, n * F);
+        PF32_GEMM(L->wd_s, L->wd_q, h16, E, F, hf);
+        for (size_t i = 0; i < n * E; i++) x[i] += hf[i];
+    }
+#undef PF32_GEMM
+    oracle_rmsnorm_scalar(x + (n - 1) * E, m->out_norm, E, m->eps, hf);
+    /* logits from the fp32 final norm (test_prefill.rs:781-800): gemm_dot on f32 inputs */
+    const size_t nbr = E / 32;
+    for (size_t r = 0; r < (size_t)m->vocab; r++)
+        logits[r] = gemm_dot((const uint16_t*)m->out_s, m->out_q, hf, r, nbr);
+    free(x); free(hf); free(h16); free(q); free(k); free(v); free(att); free(g); free(u);
+    free(tmp); free(scores);
     return 0;
 }

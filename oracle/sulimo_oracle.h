@@ -155,6 +155,12 @@ void oracle_silu_mul_f16(const uint16_t* gate, const uint16_t* up, uint16_t* out
 void oracle_add_f16(uint16_t* a, const uint16_t* b, size_t n);
 int oracle_prefill_ubatch(const oracle_model* m, uint16_t* x, size_t start_pos, size_t n,
                           float* logits, int threads);
+/* The CPU oracle of the reference's prefill test (crates/sulimo-ocl/tests/test_prefill.rs:
+ * 583-800): fp32 residual, f16 GEMM inputs and outputs, scalar RMSNorm / RoPE / Q8_0 store /
+ * causal decode attention per token, fp32 final norm; QKV biases added when present.  x_f16
+ * [n][embd] is not modified.  0 or -1. */
+int oracle_prefill_ubatch_f32(const oracle_model* m, const uint16_t* x_f16, size_t start_pos,
+                              size_t n, float* logits, int threads);
 
 #ifdef __cplusplus
 }

@@ -58,14 +58,20 @@ def build(force=False, verbose=False, extra_flags=()):
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
     nvcc = nvcc_path()
+    headers = [d for d in deps if not d.endswith(".cu")]
     jobs = []
     for s in SOURCES:
         src = os.path.join(CSRC, s)
         obj = os.path.join(objdir, s.replace(".cu", ".o"))
-        jobs.append(([nvcc, *NVCC_FLAGS, *extra_flags, "-c", src, "-o", obj], obj))
+        # an object is reused when it is newer than its source and every header (and the flags
+        # did not change: extra flags force a rebuild)
+        fresh = not force and not extra_flags and _newer(obj, [src] + headers)
+        jobs.append(([nvcc, *NVCC_FLAGS, *extra_flags, "-c", src, "-o", obj], obj, fresh))
     from concurrent.futures import ThreadPoolExecutor
 
     def run(job):
+        if job[2]:
+            return job[1]
         if verbose:
             print(" ".join(job[0]), flush=True)
         subprocess.run(job[0], check=True)

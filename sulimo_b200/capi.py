@@ -32,6 +32,7 @@ SIGNATURES = {
     "sulimo_cuda_ctx_get_stream": (_vp, [_vp]),
     "sulimo_cuda_ctx_device": (_i, [_vp]),
     "sulimo_cuda_ctx_launch_count": (_u64, [_vp]),
+    "sulimo_cuda_ctx_workspace_bytes": (_sz, [_vp]),
     "sulimo_cuda_buffer_from_host": (_i, [_vp, _vp, _sz, _i, _i, C.POINTER(_vp)]),
     "sulimo_cuda_buffer_alloc": (_i, [_vp, _sz, C.POINTER(_vp)]),
     "sulimo_cuda_buffer_write": (_i, [_vp, _sz, _vp, _sz]),
@@ -57,13 +58,15 @@ SIGNATURES = {
     "sulimo_cuda_ipc_open": (_i, [_vp, _vp, C.POINTER(_vp)]),
     "sulimo_cuda_ipc_close": (_i, [_vp, _vp]),
     "sulimo_cuda_gemm_q4_0_f16_allgather": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz,
-                                                 _sz, _vp, _i, C.POINTER(C.c_uint)]),
+                                                 _sz, _vp, _vp, _i, _i, C.c_uint,
+                                                 C.POINTER(C.c_uint)]),
     "sulimo_cuda_wait_counter": (_i, [_vp, _vp, C.c_uint]),
     "sulimo_cuda_forward_scratch_bytes": (_sz, [_vp, _i]),
     "sulimo_cuda_forward_token": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _sz]),
     "sulimo_cuda_argmax_rows": (_i, [_vp, _vp, _i, _i, _vp]),
     "sulimo_cuda_prefill_scratch_bytes": (_sz, [_vp, _i]),
     "sulimo_cuda_prefill_ubatch": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _sz]),
+    "sulimo_cuda_prefill_ubatch_x": (_i, [_vp, _vp, _vp, _i, _sz, _vp, _vp, _sz]),
     "sulimo_cuda_attn_prefill_q8_0": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _i, _i, _i, _i, _vp]),
     "sulimo_cuda_attn_decode_q8_0": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _i, _i,
                                           _f, _vp]),

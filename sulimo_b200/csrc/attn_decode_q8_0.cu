@@ -703,9 +703,8 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
         const size_t bytes = SL::bytes(chunk, Hkv);
         if (bytes != slot_bytes_generic(chunk, Hkv, G, HD))
             return set_error(SULIMO_ELAUNCH, "slot layout size mismatch");
-        static uint64_t slot_attr_mask = 0;  // per device
-        const uint64_t sbit = 1ull << (ctx->device & 63);
-        if (!(slot_attr_mask & sbit)) {
+        static DeviceBits slot_done;  // per device
+        if (!slot_done.test(ctx->device)) {
             int st = check_cuda(
                 cudaFuncSetAttribute(attn_decode_slots_kernel<HD, G, SLOT_THREADS_WIDE>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -718,7 +717,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
                                          (int)SLOT_SMEM_MAX),
                     "attn slot smem attribute");
             if (st) return st;
-            slot_attr_mask |= sbit;
+            slot_done.set(ctx->device);
         }
         dim3 g1(splits, batch);
         if ((size_t)splits * batch <= (size_t)ctx->num_sms)
@@ -737,9 +736,8 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
         ctx->launches += 2;
         return check_cuda(cudaGetLastError(), "attn_decode_combine launch");
     }
-    static uint64_t attr_set_mask = 0;  // one bit per device: the attribute is per device
-    const uint64_t bit = 1ull << (ctx->device & 63);
-    if (!(attr_set_mask & bit)) {
+    static DeviceBits attr_done;  // the attribute is per device
+    if (!attr_done.test(ctx->device)) {
         const int max_bytes =
             (int)(L::BOXW <= 256 ? L::tma_bytes(ATT_PMAX) : L::bytes) + ATT_SMEM_SLACK;
         int st = check_cuda(cudaFuncSetAttribute(attn_decode_partial_kernel<HD, G, false>,
@@ -752,7 +750,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
                                                  max_bytes),
                             "attn smem attribute");
         if (st) return st;
-        attr_set_mask |= bit;
+        attr_done.set(ctx->device);
     }
     // TMA staging when the ring geometry allows 16-byte aligned tensor-map copies and the
     // context does not wrap the ring (positions 0..ctx-1 are slots 0..ctx-1)

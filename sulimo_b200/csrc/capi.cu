@@ -203,6 +203,10 @@ int sulimo_cuda_ctx_device(sulimo_ctx* ctx) { return ctx ? ctx->device : -1; }
 
 uint64_t sulimo_cuda_ctx_launch_count(sulimo_ctx* ctx) { return ctx ? ctx->launches.load() : 0; }
 
+size_t sulimo_cuda_ctx_workspace_bytes(sulimo_ctx* ctx) {
+    return ctx ? ctx->workspace_bytes + ctx->argmax_bytes : 0;
+}
+
 // ---- buffers ------------------------------------------------------------------------------
 
 int sulimo_cuda_buffer_alloc(sulimo_ctx* ctx, size_t size, sulimo_buf** out) {
@@ -569,9 +573,9 @@ size_t sulimo_cuda_prefill_scratch_bytes(const sulimo_model_desc* model, int n) 
     return sulimo::prefill_scratch_bytes(model, n);
 }
 
-int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
-                               const int32_t* tokens, int n, size_t start_pos, float* logits,
-                               void* scratch, size_t scratch_bytes) {
+static int prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model, const int32_t* tokens,
+                          const void* x_f16, int n, size_t start_pos, float* logits,
+                          void* scratch, size_t scratch_bytes) {
     int st = check_ctx(ctx);
     if (st) return st;
     if ((st = check_model(model))) return st;
@@ -580,10 +584,11 @@ int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
     if (n <= 0 || n > 65535) return set_error(SULIMO_EINVAL, "n must be in [1, 65535]");
     if (start_pos + (size_t)n > model->kv_capacity)
         return set_error(SULIMO_EINVAL, "start_pos + n exceeds the ring capacity");
-    if (!tokens || !logits || !scratch) return set_error(SULIMO_EINVAL, "null pointer");
+    if ((!tokens && !x_f16) || !logits || !scratch) return set_error(SULIMO_EINVAL, "null pointer");
     if (scratch_bytes < sulimo::prefill_scratch_bytes(model, n))
         return set_error(SULIMO_EINVAL, "scratch smaller than sulimo_cuda_prefill_scratch_bytes");
     if (!aligned(scratch, 256) || !aligned(logits, 16) || !aligned(tokens, 4) ||
+        !aligned(x_f16, 8) ||
         !aligned(model->tok_quants, 16) || !aligned(model->out_quants, 16))
         return set_error(SULIMO_EALIGN, "scratch 256-byte, logits / quants 16-byte aligned");
     for (int l = 0; l < model->n_layers; l++) {
@@ -594,7 +599,23 @@ int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
             if (!aligned(p, 16)) return set_error(SULIMO_EALIGN, "quants must be 16-byte aligned");
     }
     if ((st = bind_device(ctx))) return st;
-    return sulimo::launch_prefill_ubatch(ctx, model, tokens, n, start_pos, logits, scratch);
+    return sulimo::launch_prefill_ubatch(ctx, model, tokens, x_f16, n, start_pos, logits, scratch);
+}
+
+int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                               const int32_t* tokens, int n, size_t start_pos, float* logits,
+                               void* scratch, size_t scratch_bytes) {
+    if (!tokens) return set_error(SULIMO_EINVAL, "null pointer");
+    return prefill_ubatch(ctx, model, tokens, nullptr, n, start_pos, logits, scratch,
+                          scratch_bytes);
+}
+
+int sulimo_cuda_prefill_ubatch_x(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                                 const void* x_f16, int n, size_t start_pos, float* logits,
+                                 void* scratch, size_t scratch_bytes) {
+    if (!x_f16) return set_error(SULIMO_EINVAL, "null pointer");
+    return prefill_ubatch(ctx, model, nullptr, x_f16, n, start_pos, logits, scratch,
+                          scratch_bytes);
 }
 
 int sulimo_cuda_attn_prefill_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
@@ -661,11 +682,14 @@ int sulimo_cuda_ipc_close(sulimo_ctx* ctx, void* dev_ptr) {
 int sulimo_cuda_gemm_q4_0_f16_allgather(sulimo_ctx* ctx, const void* scales, const void* quants,
                                         const void* x, int m_local, int m_valid, int k, int n,
                                         int out_dtype, void* const* out_bases, size_t f_total,
-                                        size_t col0, unsigned* const* flags, int world,
-                                        unsigned* tiles_out) {
+                                        size_t col0, unsigned* const* flags,
+                                        unsigned* const* release, int world, int rank,
+                                        unsigned epoch, unsigned* tiles_out) {
     int st = check_ctx(ctx);
     if (st) return st;
     if (world < 1 || world > 8) return set_error(SULIMO_EINVAL, "world must be in [1, 8]");
+    if (rank < 0 || rank >= world) return set_error(SULIMO_EINVAL, "rank must be in [0, world)");
+    if (epoch == 0) return set_error(SULIMO_EINVAL, "epoch must be nonzero");
     if (m_local <= 0 || m_local % 8 || m_valid <= 0 || m_valid > m_local || m_valid % 8 ||
         k <= 0 || k % 32 || n <= 0)
         return set_error(SULIMO_EINVAL, "m_local, m_valid multiples of 8; k of 32; n > 0");
@@ -673,18 +697,20 @@ int sulimo_cuda_gemm_q4_0_f16_allgather(sulimo_ctx* ctx, const void* scales, con
         return set_error(SULIMO_EINVAL, "bad out_dtype");
     if (f_total % 8 || col0 % 8 || col0 + (size_t)m_valid > f_total)
         return set_error(SULIMO_EINVAL, "col0 + m_valid <= f_total, both multiples of 8");
-    if (!scales || !quants || !x || !out_bases || !flags || !tiles_out)
+    if (!scales || !quants || !x || !out_bases || !flags || !release || !tiles_out)
         return set_error(SULIMO_EINVAL, "null pointer");
     for (int r = 0; r < world; r++) {
-        if (!out_bases[r] || !flags[r]) return set_error(SULIMO_EINVAL, "null peer pointer");
-        if (!aligned(out_bases[r], 16) || !aligned(flags[r], 4))
+        if (!out_bases[r] || !flags[r] || !release[r])
+            return set_error(SULIMO_EINVAL, "null peer pointer");
+        if (!aligned(out_bases[r], 16) || !aligned(flags[r], 4) || !aligned(release[r], 4))
             return set_error(SULIMO_EALIGN, "peer outputs 16-byte, counters 4-byte aligned");
     }
     if (!aligned(x, 16) || !aligned(quants, 16) || !aligned(scales, 2))
         return set_error(SULIMO_EALIGN, "x, quants 16-byte aligned, scales 2-byte");
     if ((st = bind_device(ctx))) return st;
     return sulimo::launch_gemm_allgather(ctx, scales, quants, x, m_local, m_valid, k, n, out_dtype,
-                                         out_bases, f_total, col0, flags, world, tiles_out);
+                                         out_bases, f_total, col0, flags, release, world, rank,
+                                         epoch, tiles_out);
 }
 
 int sulimo_cuda_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned target) {

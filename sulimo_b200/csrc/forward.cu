@@ -173,6 +173,19 @@ __global__ void __launch_bounds__(GLUE_THREADS)
                         *reinterpret_cast<const uint32_t*>(&hi));
 }
 
+// f16 [n4 * 4] -> f32: a prefill ubatch's caller-written f16 embeddings into the fp32 residual.
+__global__ void __launch_bounds__(GLUE_THREADS)
+    widen_f16_kernel(const uint2* __restrict__ in, size_t n4, float4* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    const uint2 v = in[i];
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    out[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
 // silu(gate) * up -> Q8_0: one warp per 32-value block, all sequences' blocks in one grid.
 __global__ void __launch_bounds__(GLUE_THREADS)
     swiglu_q8_kernel(const float* __restrict__ gate, const float* __restrict__ up, size_t nblocks,
@@ -285,9 +298,8 @@ size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scra
 
 // The RMSNorm kernels keep the whole vector in shared memory (up to 227 KB per CTA).
 int ensure_norm_attr(sulimo_ctx* ctx) {
-    static uint64_t mask = 0;  // per device
-    const uint64_t bit = 1ull << (ctx->device & 63);
-    if (mask & bit) return SULIMO_OK;
+    static DeviceBits done;
+    if (done.test(ctx->device)) return SULIMO_OK;
     int st = check_cuda(cudaFuncSetAttribute(add_rmsnorm_q8_kernel<false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              227 * 1024),
@@ -297,7 +309,7 @@ int ensure_norm_attr(sulimo_ctx* ctx) {
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              227 * 1024),
                         "rmsnorm smem attribute");
-    if (!st) mask |= bit;
+    if (!st) done.set(ctx->device);
     return st;
 }
 
@@ -348,7 +360,8 @@ size_t prefill_scratch_bytes(const sulimo_model_desc* m, int n) {
 // keeps activations in f16; this one adds the biases (as forward_token does) and keeps the
 // residual stream in fp32.
 int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
-                          int n, size_t start_pos, float* logits, void* scratch) {
+                          const void* x_f16, int n, size_t start_pos, float* logits,
+                          void* scratch) {
     PrefillScratch s;
     prefill_layout(m, n, reinterpret_cast<uint8_t*>(scratch), &s);
     const int E = m->embd, F = m->ffn, H = m->head_count, Hkv = m->head_count_kv,
@@ -358,9 +371,19 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
     uint8_t* h8 = reinterpret_cast<uint8_t*>(s.h);
     int st;
     if ((st = ensure_norm_attr(ctx))) return st;
-    if ((st = launch_dequant_rows(ctx, m->tok_scales, m->tok_quants, E, tokens, n, s.x,
-                                  SULIMO_OUT_F32)))
-        return st;
+    if (tokens) {
+        if ((st = launch_dequant_rows(ctx, m->tok_scales, m->tok_quants, E, tokens, n, s.x,
+                                      DEQUANT_F16_WIDE)))
+            return st;
+    } else {
+        const size_t nh4 = (size_t)n * E / 4;  // E is a multiple of 32
+        (void)launch_pdl(widen_f16_kernel,
+                         dim3((unsigned)((nh4 + GLUE_THREADS - 1) / GLUE_THREADS)),
+                         dim3(GLUE_THREADS), 0, ctx->stream, reinterpret_cast<const uint2*>(x_f16),
+                         nh4, reinterpret_cast<float4*>(s.x));
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "widen_f16 launch"))) return st;
+    }
     auto gemm = [&](const void* sc, const void* qu, const void* x, float* out, int rows, int k) {
         return launch_gemm_q4_0_f16(ctx, sc, qu, x, out, rows, k, n, SULIMO_OUT_F32, k, 0);
     };

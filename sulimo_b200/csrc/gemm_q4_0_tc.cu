@@ -270,13 +270,36 @@ __global__ void __launch_bounds__(256)
 // NVLink peer mappings, at this rank's column offset; when a CTA's stores are complete it adds
 // 1 to every rank's arrival counter (system-scope atomics).  A rank's result is complete when
 // its counter has received every rank's CTAs (wait_counter_kernel).
+// Release handshake (no write-after-read on Y across calls): call `epoch` of rank r first
+// publishes epoch in r's release word, from every CTA right after griddepcontrol.wait, i.e.
+// once everything r enqueued on its stream before this call (its readers of the previous Y)
+// has completed; a CTA stores into peer r's Y only after it has seen r's release word reach
+// this call's epoch (bounded wait).
 constexpr int MAX_PEERS = 8;
 struct PeerOut {
     CUtensorMap map[MAX_PEERS];    // [m_local cols][n rows] of rank r's Y, 32-token boxes
     CUtensorMap map16[MAX_PEERS];  // the same, 16-token boxes (a tile's 16-token remainder)
     unsigned* flags[MAX_PEERS];    // rank r's arrival counter
-    int world;
+    unsigned* release[MAX_PEERS];  // rank r's release word
+    unsigned epoch;                // this call's number (modulo 2^32, never 0)
+    int world, rank;
 };
+
+// Bounded wait until a release word reaches `epoch` (modulo 2^32); false after
+// SULIMO_WAIT_LIMIT_NS, with the device error recorded.
+__device__ __forceinline__ bool wait_release(const unsigned* word, unsigned epoch, int* err) {
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(word) : "memory");
+        if ((int)(v - epoch) >= 0) return true;
+        if (globaltimer_ns() - t0 > SULIMO_WAIT_LIMIT_NS) {
+            record_device_error(err, SULIMO_DEVERR_WAIT_TIMEOUT);
+            return false;
+        }
+        __nanosleep(128);
+    }
+}
 
 // OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace
 // [split][n][m], 3 / 4 = f16 / f32 to every rank's Y (all by TMA tensor stores).
@@ -325,6 +348,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
         // before the first global read (the __syncthreads below orders the other threads).
         pdl_launch_dependents();
         pdl_wait_prerequisites();
+        if (OUT_MODE >= 3)  // this rank's earlier stream work is done: its Y may be rewritten
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers->release[peers->rank]),
+                         "r"(peers->epoch)
+                         : "memory");
         // The first ring pass needs no empty-slot waits: issue it before the TMEM allocation.
         for (int j = 0; j < num_k && j < stages; j++) {
             mbar_arrive_expect_tx(&full[j], x_stage + Q_STAGE);
@@ -441,6 +468,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
         constexpr int ES = (OUT_MODE == 0 || OUT_MODE == 3) ? 2 : 4;
         {
             const bool issuer = (warp - 2) % 4 == 0 && lane == 0;
+            bool released = false;  // every peer's release word seen at this epoch
             for (int c0 = group * EPI_TOKENS; c0 < bn; c0 += DEQ_GROUPS * EPI_TOKENS) {
                 uint8_t* tile = sx + (size_t)c0 * BM * ES;
                 if (have) {
@@ -468,9 +496,20 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
                     // a 16-token remainder (bn % 32 == 16) must not spill into the next tile
                     const bool whole = c0 + EPI_TOKENS <= bn;
                     if (OUT_MODE >= 3) {
-                        for (int rk = 0; rk < peers->world; rk++)
-                            tma_store_2d(whole ? &peers->map[rk] : &peers->map16[rk], m0, n0 + c0,
-                                         tile);
+                        if (!released) {
+                            for (int rk = 0; rk < peers->world; rk++)
+                                if (rk != peers->rank &&
+                                    !wait_release(peers->release[rk], peers->epoch, err)) {
+                                    *abort_flag = 1;
+                                    break;
+                                }
+                            asm volatile("fence.proxy.async.global;" ::: "memory");
+                            released = true;
+                        }
+                        if (!*abort_flag)
+                            for (int rk = 0; rk < peers->world; rk++)
+                                tma_store_2d(whole ? &peers->map[rk] : &peers->map16[rk], m0,
+                                             n0 + c0, tile);
                     } else {
                         const CUtensorMap* map = whole ? &tmap_out : &tmap_out16;
                         if (OUT_MODE == 2)
@@ -567,22 +606,21 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
 
 template <int MODE>
 int set_smem_attr(int device) {
-    static uint64_t mask = 0;  // the attribute is per device
-    const uint64_t bit = 1ull << (device & 63);
-    if (mask & bit) return SULIMO_OK;
+    static DeviceBits done;  // the attribute is per device
+    if (done.test(device)) return SULIMO_OK;
     if (MODE >= 3) {
         int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_allgather_kernel<MODE>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)SMEM_LIMIT),
                             "gemm smem attribute");
-        if (!st) mask |= bit;
+        if (!st) done.set(device);
         return st;
     }
     int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<MODE>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)SMEM_LIMIT),
                         "gemm smem attribute");
-    if (!st) mask |= bit;
+    if (!st) done.set(device);
     return st;
 }
 
@@ -690,7 +728,8 @@ namespace sulimo {
 int launch_gemm_allgather(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                           int m_local, int m_valid, int k, int n, int out_dtype,
                           void* const* out_bases, size_t f_total, size_t col0,
-                          unsigned* const* flags, int world, unsigned* tiles_out) {
+                          unsigned* const* flags, unsigned* const* release, int world, int rank,
+                          unsigned epoch, unsigned* tiles_out) {
     const int nb = k / 32;
     const int bn = gemm_token_tile(n);
     const int stages = ring_stages(bn);
@@ -707,6 +746,8 @@ int launch_gemm_allgather(sulimo_ctx* ctx, const void* scales, const void* quant
     PeerOut peers;
     memset(&peers, 0, sizeof(peers));
     peers.world = world;
+    peers.rank = rank;
+    peers.epoch = epoch;
     const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     for (int r = 0; r < world; r++) {
         const uint8_t* base = reinterpret_cast<const uint8_t*>(out_bases[r]) + col0 * es;
@@ -718,6 +759,7 @@ int launch_gemm_allgather(sulimo_ctx* ctx, const void* scales, const void* quant
                             (uint64_t)f_total * es, BM, 16u, CU_TENSOR_MAP_SWIZZLE_NONE)))
             return st;
         peers.flags[r] = flags[r];
+        peers.release[r] = release[r];
     }
     if ((st = f32 ? set_smem_attr<4>(ctx->device) : set_smem_attr<3>(ctx->device))) return st;
     const int mt = (m_local + BM - 1) / BM, nt = (n + bn - 1) / bn;

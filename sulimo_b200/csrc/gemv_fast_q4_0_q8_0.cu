@@ -324,11 +324,10 @@ __global__ void __launch_bounds__(GR_THREADS)
 // Resident CTAs per SM of one instantiation (cached per device).
 template <int BPL, int NV, int R, int PRO>
 int fast_occupancy(sulimo_ctx* ctx, int* blocks) {
-    static uint64_t attr_mask = 0;
-    static int occ[64] = {0};
+    static DeviceBits done;
+    static std::atomic<int> occ[64];
     const int dev = ctx->device & 63;
-    const uint64_t bit = 1ull << dev;
-    if (!(attr_mask & bit)) {
+    if (!done.test(dev)) {
         int st = check_cuda(cudaFuncSetAttribute(gemv_fast_kernel<BPL, NV, R, PRO>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)GR_ACT_LIMIT),
@@ -339,10 +338,10 @@ int fast_occupancy(sulimo_ctx* ctx, int* blocks) {
                             &b, gemv_fast_kernel<BPL, NV, R, PRO>, GR_THREADS, GR_ACT_LIMIT),
                         "gemv_fast occupancy");
         if (st) return st;
-        occ[dev] = b < 1 ? 1 : b;
-        attr_mask |= bit;
+        occ[dev].store(b < 1 ? 1 : b, std::memory_order_relaxed);
+        done.set(dev);
     }
-    *blocks = occ[dev];
+    *blocks = occ[dev].load(std::memory_order_relaxed);
     return SULIMO_OK;
 }
 

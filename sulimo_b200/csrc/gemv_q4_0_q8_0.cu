@@ -334,15 +334,14 @@ template <int NV, int ROWS>
 int launch_gemv_tma(sulimo_ctx* ctx, const GemvGroup& grp, int tiles, const uint8_t* xq8, int nb,
                     int batch, int static_weights) {
     const size_t smem = gemv_tma_smem<NV, ROWS>(nb);
-    static uint64_t attr_mask = 0;  // per device
-    const uint64_t bit = 1ull << (ctx->device & 63);
-    if (!(attr_mask & bit)) {
+    static DeviceBits done;  // per device
+    if (!done.test(ctx->device)) {
         int st = check_cuda(cudaFuncSetAttribute(gemv_q4_0_q8_0_tma_kernel<NV, ROWS>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  227 * 1024),
                             "gemv smem attribute");
         if (st) return st;
-        attr_mask |= bit;
+        done.set(ctx->device);
     }
     dim3 grid((unsigned)tiles, (batch + NV - 1) / NV);
     (void)launch_pdl(gemv_q4_0_q8_0_tma_kernel<NV, ROWS>, grid, dim3(TsShape<ROWS>::THREADS), smem,

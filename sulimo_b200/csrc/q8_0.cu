@@ -51,8 +51,11 @@ __global__ void __launch_bounds__(256) kv_store_q8_0_kernel(const T* __restrict_
     }
 }
 
-// One thread per (row, block, byte i): writes weights i and i+16 of the block.
-template <bool F16OUT>
+// One thread per (row, block, byte i): writes weights i and i+16 of the block.  MODE:
+// DEQUANT_F32 exact f32 (dequantize_q4_0_soa, repack.rs:107-131), DEQUANT_F16 f16
+// (lookup_token_embedding_f16, scheduler.rs:345-357), DEQUANT_F16_WIDE that f16 value stored
+// as f32 (the f16 embedding row widened into an fp32 residual stream).
+template <int MODE>
 __global__ void __launch_bounds__(256) dequant_rows_kernel(const uint16_t* __restrict__ scales,
                                                            const uint8_t* __restrict__ quants,
                                                            int nb, const int32_t* __restrict__ rows,
@@ -73,10 +76,14 @@ __global__ void __launch_bounds__(256) dequant_rows_kernel(const uint16_t* __res
     float w0 = __fmul_rn((float)((int)(byte & 0x0F) - 8), d);
     float w1 = __fmul_rn((float)((int)(byte >> 4) - 8), d);
     size_t o = (size_t)c * nb * 32 + (size_t)b * 32 + i;
-    if (F16OUT) {
+    if (MODE == DEQUANT_F16) {
         __half* oh = reinterpret_cast<__half*>(out);
         oh[o] = __float2half_rn(w0);
         oh[o + 16] = __float2half_rn(w1);
+    } else if (MODE == DEQUANT_F16_WIDE) {
+        float* of = reinterpret_cast<float*>(out);
+        of[o] = __half2float(__float2half_rn(w0));
+        of[o + 16] = __half2float(__float2half_rn(w1));
     } else {
         float* of = reinterpret_cast<float*>(out);
         of[o] = w0;
@@ -140,14 +147,17 @@ int launch_dequant_rows(sulimo_ctx* ctx, const void* scales, const void* quants,
     int nb = cols / 32;
     size_t total = (size_t)count * nb * 16;
     int g = (int)((total + 255) / 256);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(scales);
+    const uint8_t* qu = reinterpret_cast<const uint8_t*>(quants);
     if (out_dtype == SULIMO_OUT_F16)
-        (void)launch_pdl(dequant_rows_kernel<true>, dim3(g), dim3(256), 0, ctx->stream,
-                         reinterpret_cast<const uint16_t*>(scales),
-                         reinterpret_cast<const uint8_t*>(quants), nb, row_ids, count, out);
+        (void)launch_pdl(dequant_rows_kernel<DEQUANT_F16>, dim3(g), dim3(256), 0, ctx->stream, sc,
+                         qu, nb, row_ids, count, out);
+    else if (out_dtype == DEQUANT_F16_WIDE)
+        (void)launch_pdl(dequant_rows_kernel<DEQUANT_F16_WIDE>, dim3(g), dim3(256), 0, ctx->stream,
+                         sc, qu, nb, row_ids, count, out);
     else
-        (void)launch_pdl(dequant_rows_kernel<false>, dim3(g), dim3(256), 0, ctx->stream,
-                         reinterpret_cast<const uint16_t*>(scales),
-                         reinterpret_cast<const uint8_t*>(quants), nb, row_ids, count, out);
+        (void)launch_pdl(dequant_rows_kernel<DEQUANT_F32>, dim3(g), dim3(256), 0, ctx->stream, sc,
+                         qu, nb, row_ids, count, out);
     ctx->launches++;
     return check_cuda(cudaGetLastError(), "dequant_rows launch");
 }

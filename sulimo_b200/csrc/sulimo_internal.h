@@ -27,6 +27,17 @@ struct sulimo_ctx {
 
 namespace sulimo {
 
+// One "done" bit per device (device index mod 64) for per-device, idempotent set-up such as
+// cudaFuncSetAttribute.  Atomic, so host threads driving different devices may test and set
+// it concurrently; two threads that both see the bit clear both do the (idempotent) set-up.
+struct DeviceBits {
+    std::atomic<uint64_t> bits{0};
+    bool test(int device) const {
+        return (bits.load(std::memory_order_acquire) >> (device & 63)) & 1;
+    }
+    void set(int device) { bits.fetch_or(1ull << (device & 63), std::memory_order_release); }
+};
+
 // Launches a kernel with programmatic stream serialization: it may begin (prologue, TMEM
 // allocation, barrier setup) while the previous kernel of the stream drains, and orders its
 // global accesses after that kernel with griddepcontrol.wait.
@@ -74,7 +85,8 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
 int launch_gemm_allgather(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                           int m_local, int m_valid, int k, int n, int out_dtype,
                           void* const* out_bases, size_t f_total, size_t col0,
-                          unsigned* const* flags, int world, unsigned* tiles_out);
+                          unsigned* const* flags, unsigned* const* release, int world, int rank,
+                          unsigned epoch, unsigned* tiles_out);
 int launch_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned target);
 int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                           const void* x_q8, int rows, int cols, int batch, float* out);
@@ -125,6 +137,9 @@ int launch_block_sums(sulimo_ctx* ctx, const void* w_quants, const void* x_q8, i
 int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n);
 int launch_kv_store_q8_0(sulimo_ctx* ctx, const void* act, int act_dtype, void* kv,
                          size_t start_pos, size_t capacity, size_t blocks_per_pos, size_t n);
+// Dequantisation output modes: SULIMO_OUT_F16 / SULIMO_OUT_F32 (DEQUANT_F32) as in the C ABI,
+// and DEQUANT_F16_WIDE (the f16-rounded weight stored as f32; internal).
+enum { DEQUANT_F16 = SULIMO_OUT_F16, DEQUANT_F32 = SULIMO_OUT_F32, DEQUANT_F16_WIDE = 2 };
 int launch_dequant_rows(sulimo_ctx* ctx, const void* scales, const void* quants, int cols,
                         const int32_t* row_ids, int count, void* out, int out_dtype);
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
@@ -138,8 +153,11 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                          int batch, size_t pos, float* logits, void* scratch);
 int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int32_t* out);
 size_t prefill_scratch_bytes(const sulimo_model_desc* m, int n);
+// tokens != nullptr: embeddings looked up on the device (f16-rounded, as the reference's
+// lookup_token_embedding_f16); else x_f16 [n][embd] holds them (the reference's scratch.x).
 int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
-                          int n, size_t start_pos, float* logits, void* scratch);
+                          const void* x_f16, int n, size_t start_pos, float* logits,
+                          void* scratch);
 int launch_attn_prefill(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                         size_t start_pos, size_t capacity, int n_tok, int H, int Hkv, int hd,
                         void* out);

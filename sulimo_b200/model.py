@@ -83,11 +83,15 @@ class DecodeModel:
                   self.batch, pos, _p(out), _p(self.scratch), self.scratch.numel())
         return out
 
-    def prefill(self, tokens, start_pos=0, logits=None):
+    def prefill(self, tokens, start_pos=0, logits=None, x_f16=None):
         """One prefill ubatch of len(tokens) tokens (device int32) of sequence 0 at positions
-        start_pos..; returns the last token's logits [vocab] (execute_prefill_ubatch)."""
+        start_pos..; returns the last token's logits [vocab] (execute_prefill_ubatch).  With
+        x_f16 (device f16 [n][embd]) the caller supplies the embeddings instead of tokens."""
         import torch
-        n = tokens.numel()
+        if x_f16 is not None:
+            n = x_f16.numel() // self.cfg["embd"]
+        else:
+            n = tokens.numel()
         need = capi.load().sulimo_cuda_prefill_scratch_bytes(self._desc_ptr, n)
         if need == 0:
             raise sb.SulimoError(capi.EINVAL, "sulimo_cuda_prefill_scratch_bytes",
@@ -95,8 +99,12 @@ class DecodeModel:
         if getattr(self, "pscratch", None) is None or self.pscratch.numel() < need:
             self.pscratch = torch.empty(need, dtype=torch.uint8, device="cuda")
         out = self.logits[:self.cfg["vocab"]] if logits is None else logits
-        capi.call("sulimo_cuda_prefill_ubatch", self.ctx.handle, self._desc_ptr, _p(tokens), n,
-                  start_pos, _p(out), _p(self.pscratch), self.pscratch.numel())
+        if x_f16 is not None:
+            capi.call("sulimo_cuda_prefill_ubatch_x", self.ctx.handle, self._desc_ptr, _p(x_f16),
+                      n, start_pos, _p(out), _p(self.pscratch), self.pscratch.numel())
+        else:
+            capi.call("sulimo_cuda_prefill_ubatch", self.ctx.handle, self._desc_ptr, _p(tokens),
+                      n, start_pos, _p(out), _p(self.pscratch), self.pscratch.numel())
         return out
 
     def greedy(self, logits=None):

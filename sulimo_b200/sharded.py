@@ -97,9 +97,15 @@ class FusedShardedQ4Projection(ShardedQ4Projection):
     mappings of library buffers exchanged as CUDA IPC handles) and bumps every rank's arrival
     counter; `forward` then waits (bounded, on the device) until this rank's counter has all
     ranks' CTAs.  No NCCL on the data path, no unshard pass.  Y and the counters are allocated
-    once for up to `m_max` tokens; calls must alternate in lockstep on all ranks (the counter
-    targets advance by one call's arrivals each time), so this path is not captured in graphs.
+    once for up to `m_max` tokens.  Every rank makes the same sequence of calls (the counter
+    targets and the release epochs advance by one call each time), so this path is not captured
+    in graphs.  Y may be read until the next call: a call stores into a peer's Y only after that
+    peer's own next call has started on its stream (the kernel's release handshake), so readers
+    of the returned Y that the caller enqueues on this context's stream before its next call
+    always see this call's result.
     """
+
+    RELEASE_OFFSET = 128  # bytes from a rank's arrival counter to its release word
 
     def __init__(self, ctx, scales_r, quants_r, f, k, fs, m_max, out_dtype=sb.OUT_F16,
                  group=None):
@@ -146,7 +152,10 @@ class FusedShardedQ4Projection(ShardedQ4Projection):
         self.bases = (C.c_void_p * self.world)(*bases)
         self.flags = (C.c_void_p * self.world)(*flags)
         self.own_flag = ctx.device_ptr(self.flag_buf)
+        # the release word sits 128 bytes into each rank's flag buffer (its own cache line)
+        self.releases = (C.c_void_p * self.world)(*[p + self.RELEASE_OFFSET for p in flags])
         self.epoch_arrivals = 0
+        self.calls = 0
         self.valid = min(f - self.rank * fs, fs)
 
     def forward_fused(self, x, m):
@@ -156,10 +165,11 @@ class FusedShardedQ4Projection(ShardedQ4Projection):
         if m > self.m_max:
             raise ValueError("m exceeds the buffers' m_max")
         tiles = C.c_uint()
+        self.calls = (self.calls + 1) & 0xFFFFFFFF or 1
         capi.call("sulimo_cuda_gemm_q4_0_f16_allgather", self.ctx.handle, self.scales.data_ptr(),
                   self.quants.data_ptr(), x.data_ptr(), self.fs, self.valid, self.k, m,
-                  self.out_dtype, self.bases, self.f, self.rank * self.fs, self.flags, self.world,
-                  C.byref(tiles))
+                  self.out_dtype, self.bases, self.f, self.rank * self.fs, self.flags,
+                  self.releases, self.world, self.rank, self.calls, C.byref(tiles))
         # every rank launches the same tile count (equal fs), so one call adds world * tiles
         self.epoch_arrivals = (self.epoch_arrivals + self.world * tiles.value) & 0xFFFFFFFF
         capi.call("sulimo_cuda_wait_counter", self.ctx.handle, self.own_flag, self.epoch_arrivals)

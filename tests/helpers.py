@@ -81,13 +81,14 @@ PREFILL_TEST_CFG = dict(n_layers=2, embd=64, ffn=128, head_count=4, head_count_k
                         attn_softcap=0.0, bias=False, kv_capacity=64)
 
 
-def make_model_pattern_prefill():
+def make_model_pattern_prefill(overrides=None):
     """The reference test's weights (test_prefill.rs:398-463): layer l's q/k/v/o/gate/up/down use
     helper_alloc_q4 seeds l*10+2 .. l*10+9, norms seeds l*10+1 and l*10+6, the output norm
     seed 99 and the output projection seed 100.  Returns the numpy model dict that
     oracle.ffi.OracleModel and sulimo_b200.synthetic.to_device take (the token embedding is
-    the output matrix; the test feeds x directly, make_x_pattern_prefill)."""
-    cfg = dict(PREFILL_TEST_CFG)
+    the output matrix; the test feeds x directly, make_x_pattern_prefill).  `overrides`
+    changes dimensions (same generators)."""
+    cfg = dict(PREFILL_TEST_CFG, **(overrides or {}))
     E, F = cfg["embd"], cfg["ffn"]
     qd = cfg["head_count"] * cfg["head_dim"]
     kvd = cfg["head_count_kv"] * cfg["head_dim"]

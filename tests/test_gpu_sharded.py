@@ -152,6 +152,7 @@ def _fused_rank(rank, world, port, f, k, m, q):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
+    from sulimo_b200 import capi
     from sulimo_b200.sharded import FusedShardedQ4Projection, shard_weight
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -163,13 +164,17 @@ def _fused_rank(rank, world, port, f, k, m, q):
         dws, dwq = dev(ws), dev(wq)
         s_r, q_r, fs = shard_weight(dws, dwq, f, k, rank, world)
         proj = FusedShardedQ4Projection(ctx, s_r, q_r, f, k, fs, m_max=m, out_dtype=sb.OUT_F32)
-        outs = []
-        for seed in (9, 10):  # two calls: the counters' targets advance
-            x = np.random.default_rng(seed).standard_normal(m * k).astype(np.float16)
-            proj.forward_fused(dev(x), m)
-            ctx.finish()
-            outs.append(proj.read(m).copy())
-            dist.barrier()  # a peer's next call stores into this Y: read it first
+        # calls back to back with no host synchronisation: each result is read by a copy kernel
+        # enqueued on this rank's stream before its next call, while the peer's next call may
+        # already be running; the release handshake keeps the peer from overwriting Y early
+        xs = [dev(np.random.default_rng(seed).standard_normal(m * k).astype(np.float16))
+              for seed in SEEDS]
+        snaps = [torch.empty(m * f, dtype=torch.float32, device="cuda") for _ in SEEDS]
+        for x, snap in zip(xs, snaps):
+            y = proj.forward_fused(x, m)
+            capi.call("sulimo_cuda_unshard_rows", ctx.handle, y, snap.data_ptr(), 1, m, f, f, 4)
+        ctx.finish()
+        outs = [host(t).reshape(m, f) for t in snaps]
         dist.barrier()  # no rank closes its mappings while a peer may still store into them
         proj.close()
         q.put((rank, outs))
@@ -178,8 +183,12 @@ def _fused_rank(rank, world, port, f, k, m, q):
         dist.destroy_process_group()
 
 
+SEEDS = (9, 10, 11, 12, 13, 14)
+
+
 def test_fused_allgather_two_gpus():
-    """Both ranks end with the same full Y, equal to the single-device projection."""
+    """Both ranks end with the same full Y for each of six back-to-back calls, equal to the
+    single-device projection of that call's input."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -199,7 +208,7 @@ def test_fused_allgather_two_gpus():
         p.join(timeout=120)
         assert p.exitcode == 0
     ws, wq = make_q4_0(f, k, seed=8)
-    for i, seed in enumerate((9, 10)):
+    for i, seed in enumerate(SEEDS):
         assert np.array_equal(res[0][i].view(np.uint32), res[1][i].view(np.uint32))
         x = np.random.default_rng(seed).standard_normal(m * k).astype(np.float16)
         ref = O.gemm_q4_0_f16_f32out(ws, wq, x.view(np.uint16), f, k, m, threads=8)

@@ -192,3 +192,27 @@ def test_execute_prefill_ubatch_seeded_models(rope_mode, H, Hkv):
         pos += n
     for (ka, va), (kb, vb) in zip(a.rings, b.rings):
         assert same(ka, kb) and same(va, vb)
+
+
+@live
+def test_reference_prefill_test_replayed_on_the_host():
+    """crates/sulimo-ocl/tests/test_prefill.rs:296-890 end to end on the host: the reference's
+    own GPU kernels (execute_prefill_ubatch over kernels/prefill.cl and gemm_q4_0.cl) against the
+    restated CPU oracle of that test, with the test's model, prompt and bars: every K/V element
+    within 1.05 * d + 1e-4 of the oracle's, logits cosine >= 0.99, the same greedy token."""
+    w = make_model_pattern_prefill()
+    gpu, cpu = O.OracleModel(w), O.OracleModel(w)
+    x0 = make_x_pattern_prefill(16, w["cfg"]["embd"])
+    lg, _ = R.execute_prefill_ubatch(gpu, np.zeros(16, np.int32), 0, x_f16=x0)
+    lc = cpu.prefill_ubatch_f32(None, 0, x_f16=x0)
+    slot = w["cfg"]["head_count_kv"] * w["cfg"]["head_dim"] // 32 * 34
+    nbytes = 16 * slot
+    for (kg, vg), (kc, vc) in zip(gpu.rings, cpu.rings):
+        for a, b in ((kg, kc), (vg, vc)):
+            g = O.dequantize_q8_0_to_f32(a[:nbytes], nbytes // 34)
+            c = O.dequantize_q8_0_to_f32(b[:nbytes], nbytes // 34)
+            d = O.f16_to_f32(b[:nbytes].reshape(-1, 34)[:, :2].copy().view(np.uint16).ravel())
+            assert np.all(np.abs(g - c) <= np.repeat(d, 32) * 1.05 + 1e-4)
+    cos = float(lg.astype(np.float64) @ lc / (np.linalg.norm(lg) * np.linalg.norm(lc)))
+    assert cos >= 0.99
+    assert int(np.argmax(lg)) == int(np.argmax(lc))
