@@ -1,17 +1,26 @@
-"""bench.py — Q4_0 prefill GEMM throughput on B200, driver contract.
+"""bench.py — Q4_0 prefill GEMM throughput on B200 (benchmark config 2), driver contract.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one pass of the hot path over one ubatch: the two prefill projections of BASELINE
-config 2 — 512 tokens x K 1536 -> 8960 features (up/gate shape) and 512 tokens x K 8960 -> 1536
-(down shape), f16 activations, Q4_0 weights (d = f16(|N(0,1)|*0.02), nibbles U{0..15}), fp32
-accumulation, f16 outputs.  2 * 14,092,861,440 FLOP per step.
+Benchmark configs (seeded synthetic data: Q4_0 weights d = f16(|N(0,1)|*0.02), nibbles U{0..15};
+activations N(0,1)):
+  1  decode matvec, 8960 x 1536 Q4_0 x Q8_0, batch 1;
+  2  prefill GEMM, 512 tokens x K 1536 -> 8960 features and 512 x K 8960 -> 1536, f16 in/out;
+  3  Qwen2.5-1.5B-architecture prefill of 2048 tokens + 256 greedy decode tokens;
+  4  Llama-3.2-3B-architecture decode at context 4096, batch 1 / 8 / 32;
+  5  row-sharded lm_head 128256 x 3072 and FFN 8192 x 3072 over the GPUs, M in 1..8192.
 
-value: whole-job TFLOP/s with inputs resident in HBM, CUDA events on the launch stream, max over
-ranks; a pool of input sets larger than L2 is rotated between steps.  e2e: the same metric through
-the C ABI with host buffers (pinned host -> device copies of the step's activations, device ->
-host copies of its outputs, inside the timed region).  --gpus N > 1: one process per GPU, each rank
-prefilling its own ubatches (independent prompts, no collective: weak scaling).
+The headline is config 2: a step is both projections, f16 activations, fp32 accumulation, f16
+outputs, 2 * 14,092,861,440 FLOP per step.  value: whole-job TFLOP/s with inputs resident in HBM,
+the median of several timed replays of a K-step CUDA graph (CUDA events on the launch stream, max
+over ranks, spread in `timing_spread`); a pool of input sets larger than L2 is rotated between
+steps.  e2e: the same metric through the C ABI with host buffers (pinned host -> device copies of
+the step's activations, device -> host copies of its outputs, inside the timed region).
+--gpus N > 1: one process per GPU, each rank prefilling its own ubatches (independent prompts,
+no collective: weak scaling).  The same line carries `secondary` (config 1 and the decode
+attention kernel, GB/s), `sharded` (config 5 at this run's GPU count, with the exchange step,
+a g = 1 reference and a bit-identity parity flag) and, at N = 1, `decode` (config 4) and
+`generate` (config 3), each with its CPU baseline (--no-extras: headline only).
 --impl reference: the reference's own CPU implementation of the path (the C restatement of
 sulimo-cpu's AVX2 prefill: per token quantize_f32_to_q8_0 + matvec_q4_0_q8_0_avx2), all host threads.
 """
@@ -33,6 +42,7 @@ FLOP_PER_GEMM = 2 * T * K_UP * F_UP       # == 2 * T * K_DN * F_DN
 FLOP_PER_STEP = 2 * FLOP_PER_GEMM
 METRIC = "Q4_0 prefill GEMM TFLOP/s"
 L2_BYTES = 126 * 1024 * 1024
+REPEATS = 9                               # timed replays of the headline's K-step graph
 
 
 def peaks():
@@ -203,26 +213,48 @@ def run_ours(args, rank, world, local):
     sampler = ClockSampler(local)
     sampler.start()
     t_w = time.time()
+    n_w = 0
     while time.time() - t_w < 1.0:   # keep the GPU under the same load until the timed region
         graph.replay()
         torch.cuda.synchronize()
+        n_w += 1
+    # timed replays of the K-step graph (about half a second of them, at least REPEATS), each
+    # bracketed by events on the launch stream; the value is the median replay (max over ranks),
+    # the spread is reported beside it
+    per_replay_s = (time.time() - t_w) / max(n_w, 1)
+    reps_n = int(min(2000, max(REPEATS, 0.5 / max(per_replay_s, 1e-6))))
+    reps_n = int(max_over_ranks(float(reps_n), world))  # every rank replays the same count
     barrier(world)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps_n)]
     t0 = time.time()
-    e0.record()
-    graph.replay()
-    e1.record()
+    for e0, e1 in evs:
+        e0.record()
+        graph.replay()
+        e1.record()
     torch.cuda.synchronize()
     t1 = time.time()
     barrier(world)
-    ms = e0.elapsed_time(e1)
-    clocks = sampler.stop(t0, t1)
-    clocks["window"] = "1 s of identical graph replays before the timed replay + the timed replay"
+    reps = [e0.elapsed_time(e1) for e0, e1 in evs]
+    if world > 1:  # one collective for all replays: the max over ranks of each
+        import torch.distributed as dist
+        t = torch.tensor(reps, dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        reps = t.tolist()
+    clocks = sampler.stop(t_w, t1)
+    clocks["window"] = (f"1 s of identical graph replays before the timed replays + the "
+                        f"{reps_n} timed replays ({t1 - t0:.2f} s)")
     ctx.finish()
     del graph
-    ms_max = max_over_ranks(ms, world)
+    ms_max = statistics.median(reps)
+    ms = ms_max
     value = FLOP_PER_STEP * args.steps * world / (ms_max / 1e3) / 1e12
+    spread = {"replays": reps_n, "steps_per_replay": args.steps,
+              "median_ms": round(ms_max, 5), "min_ms": round(min(reps), 5),
+              "max_ms": round(max(reps), 5),
+              "tflops_min_max": [round(FLOP_PER_STEP * args.steps * world / (t / 1e3) / 1e12, 1)
+                                 for t in (max(reps), min(reps))]}
 
     # ---- e2e through the C ABI with host buffers ----
     e2e = run_e2e(args, ctx, sets[0], world)
@@ -246,7 +278,7 @@ def run_ours(args, rank, world, local):
         cpu = cpu_baseline(time_budget_s=args.cpu_seconds)
 
     return dict(value=value, ms=ms_max, launches=launches, clocks=clocks, e2e=e2e, roof=roof,
-                secondary=secondary, cpu=cpu, n_sets=n_sets, set_bytes=per_set)
+                secondary=secondary, cpu=cpu, n_sets=n_sets, set_bytes=per_set, spread=spread)
 
 
 def run_e2e(args, ctx, s, world):
@@ -476,13 +508,18 @@ def run_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
-def run_sharded(args, rank, world, local):
-    """Row-sharded Q4_0 projections with one NCCL all-gather (the sharded sweep of the path's
-    measurement plan): W_lm 128256x3072 and W_ffn 8192x3072 split by rows over the ranks, X
-    [M, 3072] f16 replicated, M in {1, 16, 128, 1024, 8192}.  Per (weight, M): the local GEMM, the
-    all-gather and the whole forward (GEMM + all-gather + row-major unshard), each timed with
-    CUDA events over `steps` iterations after `warmup`, max over ranks.  One JSON line each."""
+def run_sharded(args, rank, world, local, parity_m=128):
+    """Row-sharded Q4_0 projections (config 5): W_lm 128256x3072 and W_ffn 8192x3072 split by
+    rows over the ranks, X [M, 3072] f16 replicated, M in {1, 16, 128, 1024, 8192}.  Per
+    (weight, M), each timed with CUDA events over `steps` iterations after `warmup`, max over
+    ranks: the unsharded single-GPU GEMM of the whole weight on every rank at once (the g = 1
+    reference), this rank's shard GEMM, the NCCL all-gather, the NCCL end-to-end forward (GEMM +
+    all-gather + row-major unshard) and the fused forward (all-gather in the GEMM epilogue).
+    Parity at M = parity_m for the lm_head: every rank's fused and NCCL results bit-identical to
+    the unsharded GEMM's (same per-output arithmetic: neither splits K at that size; the FFN's
+    unsharded GEMM does, so its results differ in summation order).  One dict per (weight, M)."""
     import torch
+    import torch.distributed as dist
     import sulimo_b200 as sb
     from sulimo_b200.sharded import FusedShardedQ4Projection, ShardedQ4Projection, shard_weight
     ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
@@ -495,12 +532,12 @@ def run_sharded(args, rank, world, local):
         d = (torch.randn(nb, device="cuda", generator=gen).abs() * 0.02).half().view(torch.int16)
         qn = torch.randint(0, 256, (nb * 16,), device="cuda", dtype=torch.uint8, generator=gen)
         s_r, q_r, fs = shard_weight(d, qn, F, K, rank, world)
-        del d, qn
         proj = ShardedQ4Projection(ctx, s_r, q_r, F, K, fs)
         fused = FusedShardedQ4Projection(ctx, s_r, q_r, F, K, fs, m_max=8192)
         for M in (1, 16, 128, 1024, 8192):
             x = torch.randn(M * K, device="cuda", dtype=torch.float16, generator=gen)
             g, y = proj.buffers(M, sb.OUT_F16)
+            y1 = torch.empty(M * F, dtype=torch.float16, device="cuda")
 
             def timed(fn):
                 for _ in range(args.warmup):
@@ -515,30 +552,49 @@ def run_sharded(args, rank, world, local):
                 torch.cuda.synchronize()
                 return max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
 
+            t_single = timed(lambda: sb.gemm_q4_0_f16(ctx, d, qn, x, y1, F, K, M, sb.OUT_F16))
             t_gemm = timed(lambda: proj.local_gemm(x, M, g, sb.OUT_F16))
             t_ag = timed(lambda: proj.all_gather(M, g)) if world > 1 else 0.0
             t_e2e = timed(lambda: proj.forward(x, M, g, y, sb.OUT_F16))
             t_fused = timed(lambda: fused.forward_fused(x, M))
             flop = 2.0 * M * K * F
             ag_bytes = M * F * 2 * (world - 1) / world
-            lines.append({
-                "mode": "sharded", "weight": wname, "m_tokens": M, "n_gpus": world,
-                "rows_per_gpu": fs, "dtype": "f16", "steps": args.steps, "warmup": args.warmup,
-                "gemm_ms": round(t_gemm, 4), "allgather_ms": round(t_ag, 4),
-                "e2e_ms": round(t_e2e, 4),
-                "e2e_tflops": round(flop / (t_e2e * 1e-3) / 1e12, 2),
+            wbytes = nb * 18
+            ent = {
+                "weight": wname, "m_tokens": M, "rows_per_gpu": fs,
+                "single_gpu_ms": round(t_single, 4), "gemm_ms": round(t_gemm, 4),
+                "allgather_ms": round(t_ag, 4), "nccl_e2e_ms": round(t_e2e, 4),
                 "fused_ms": round(t_fused, 4),
                 "fused_tflops": round(flop / (t_fused * 1e-3) / 1e12, 2),
+                "nccl_e2e_tflops": round(flop / (t_e2e * 1e-3) / 1e12, 2),
                 "gemm_tflops_per_gpu": round(flop / world / (t_gemm * 1e-3) / 1e12, 2),
+                "gemm_weight_GBps_per_gpu": round(wbytes / world / (t_gemm * 1e-3) / 1e9, 1),
                 "allgather_GBps_per_gpu": round(ag_bytes / (t_ag * 1e-3) / 1e9, 1)
                 if t_ag > 0 else None,
-                "data": "synthetic (seeded Q4_0 d=f16(|N|*0.02), nibbles U{0..15}; x f16 N(0,1))",
-                "exchange": "e2e: NCCL all_gather_into_tensor (shard-major) + unshard_rows "
-                            "kernel; fused: GEMM epilogue TMA-stores every tile into every "
-                            "rank's row-major Y over NVLink + arrival counters"})
-            del x, g, y
+                "efficiency_fused_vs_g1": round(t_single / (world * t_fused), 3),
+                "efficiency_nccl_vs_g1": round(t_single / (world * t_e2e), 3)}
+            if M == parity_m and F > 100000:
+                fused.forward_fused(x, M)
+                yf = torch.empty(M * F, dtype=torch.float16, device="cuda")
+                from sulimo_b200 import capi
+                # a stream-ordered copy of this rank's fused Y (a library buffer) into yf
+                capi.call("sulimo_cuda_unshard_rows", ctx.handle,
+                          ctx.device_ptr(fused.y_buf), yf.data_ptr(), 1, M, F, F, 2)
+                proj.forward(x, M, g, y, sb.OUT_F16)
+                sb.gemm_q4_0_f16(ctx, d, qn, x, y1, F, K, M, sb.OUT_F16)
+                ctx.finish()
+                ok = torch.tensor([int(torch.equal(yf.view(torch.int16), y1.view(torch.int16)) and
+                                       torch.equal(y.view(torch.int16), y1.view(torch.int16)))],
+                                  device="cuda")
+                if world > 1:
+                    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+                ent["parity_bit_identical_to_single_gpu"] = bool(ok.item())
+                del yf
+            lines.append(ent)
+            del x, g, y, y1
+        barrier(world)  # no rank unmaps its peers' buffers while a store may be in flight
         fused.close()
-        del proj, fused, s_r, q_r
+        del proj, fused, s_r, q_r, d, qn
         torch.cuda.empty_cache()
     ctx.close()
     return lines
@@ -726,6 +782,90 @@ def run_generate(args, rank, world, local):
     return [out]
 
 
+def run_probe(args, local):
+    """One kernel on a fixed case, for profiler captures (`ncu ... python bench.py --mode probe
+    --kernel K`): `warmup` + `steps` eager launches on rotated inputs, then one JSON line with
+    the mean time per launch from CUDA events.  Kernels:
+      gemm_up / gemm_down   benchmark config 2's two projections (512 tokens), f16 out;
+      gemv_fast / gemv_exact  config 1 (8960 x 1536 Q4_0 x Q8_0, batch 1), fast / AVX2-order;
+      attn                  decode attention, Llama-3.2-3B geometry (24 / 8 heads, hd 128),
+                            context 4096, batch 1, random Q8_0 rings;
+      decode_step           one config-4 forward_token at context 4096, batch 1."""
+    import numpy as np
+    import torch
+    import sulimo_b200 as sb
+    ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+
+    def q4(rows, cols):
+        nb = rows * cols // 32
+        d = (torch.randn(nb, device="cuda", generator=g).abs() * 0.02).half().view(torch.int16)
+        return d, torch.randint(0, 256, (nb * 16,), device="cuda", dtype=torch.uint8, generator=g)
+
+    kern = args.kernel
+    sets = []
+    if kern in ("gemm_up", "gemm_down"):
+        f, k = (F_UP, K_UP) if kern == "gemm_up" else (F_DN, K_DN)
+        for _ in range(4):
+            sets.append((q4(f, k), torch.randn(T * k, device="cuda", generator=g).half(),
+                         torch.empty(T * f, device="cuda", dtype=torch.float16)))
+
+        def launch(s):
+            sb.gemm_q4_0_f16(ctx, s[0][0], s[0][1], s[1], s[2], f, k, T)
+    elif kern in ("gemv_fast", "gemv_exact"):
+        rows, cols = 8960, 1536
+        for _ in range(20):
+            xq = torch.empty(cols // 32 * 34, device="cuda", dtype=torch.uint8)
+            sb.quantize_f32_to_q8_0(ctx, torch.randn(cols, device="cuda", generator=g), xq)
+            sets.append((q4(rows, cols), xq, torch.empty(rows, device="cuda")))
+
+        def launch(s):
+            if kern == "gemv_fast":
+                sb.matvec_q4_0_q8_0_fast(ctx, s[0][0], s[0][1], s[1], rows, cols, s[2],
+                                         static_weights=True)
+            else:
+                sb.dispatch_matvec_q4_0_q8_0(ctx, s[0][0], s[0][1], s[1], rows, cols, s[2])
+    elif kern == "attn":
+        H, Hkv, hd, cap = 24, 8, 128, 4096
+        for _ in range(20):
+            ring = lambda: torch.randint(0, 256, (cap * Hkv * hd // 32 * 34,), device="cuda",  # noqa: E731
+                                         dtype=torch.uint8, generator=g)
+            kr, vr = ring(), ring()
+            for r in (kr, vr):
+                r.view(-1, 34)[:, 0:2] = torch.tensor([0.02], dtype=torch.float16).view(
+                    torch.uint8).cuda()
+            sets.append((torch.randn(H * hd, device="cuda", generator=g), kr, vr,
+                         torch.empty(H * hd, device="cuda")))
+
+        def launch(s):
+            sb.causal_gqa_decode(ctx, s[0], s[1], s[2], cap, cap, H, Hkv, hd, s[3])
+    elif kern == "decode_step":
+        from sulimo_b200.model import DecodeModel
+        from sulimo_b200.synthetic import LLAMA_3B, make_model_torch
+        w = make_model_torch(dict(LLAMA_3B), seed=0, kv_capacity=4096)
+        dm = DecodeModel(ctx, w, batch=1)
+        tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+        sets.append(None)
+
+        def launch(s):
+            dm.forward_token(tok, 4095)
+    else:
+        raise SystemExit(f"unknown --kernel {kern}")
+    for i in range(args.warmup):
+        launch(sets[i % len(sets)])
+    ctx.finish()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        launch(sets[i % len(sets)])
+    e1.record()
+    torch.cuda.synchronize()
+    ctx.close()
+    return {"mode": "probe", "kernel": kern, "launches": args.steps,
+            "us_per_launch_eager": round(e0.elapsed_time(e1) * 1e3 / args.steps, 3)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -734,13 +874,20 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="headline only: skip the config 3/4 (N = 1) and config 5 keys")
+    ap.add_argument("--extra-steps", type=int, default=30,
+                    help="timed steps of each extra key's cases (capped by --steps)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--decode-batches", type=int, nargs="+", default=[1, 8, 32],
                     help="--mode decode: sequences per GPU to measure")
     ap.add_argument("--gen-tokens", type=int, default=256,
                     help="--mode generate: greedy decode tokens after the 2048-token prefill")
+    ap.add_argument("--kernel", default="attn",
+                    help="--mode probe: gemm_up, gemm_down, gemv_fast, gemv_exact, attn, "
+                         "decode_step")
     ap.add_argument("--mode", default="headline",
-                    choices=["headline", "sharded", "decode", "generate"],
+                    choices=["headline", "sharded", "decode", "generate", "probe"],
                     help="headline: the contract line (config 2); sharded: the row-sharded "
                          "lm_head/FFN sweep with an NCCL all-gather; decode: config 4 "
                          "(Llama-3B decode steps); generate: config 3 (Qwen-1.5B prefill + "
@@ -757,6 +904,9 @@ def main():
         return
 
     rank, world, local = dist_setup(args.gpus)
+    if args.mode == "probe":
+        print(json.dumps(run_probe(args, local)), flush=True)
+        return
     if args.mode in ("sharded", "decode", "generate"):
         run = {"sharded": run_sharded, "decode": run_decode, "generate": run_generate}[args.mode]
         for line in run(args, rank, world, local):
@@ -768,6 +918,26 @@ def main():
             dist.destroy_process_group()
         return
     r = run_ours(args, rank, world, local)
+    extras = {}
+    if not args.no_extras:
+        import torch
+        torch.cuda.empty_cache()
+        xa = argparse.Namespace(**vars(args))
+        xa.steps = max(3, min(args.steps, args.extra_steps))
+        xa.warmup = max(3, min(args.warmup, 10))
+        # config 5 on every rank (the row-sharded lm_head / FFN with its exchange step)
+        extras["sharded"] = {
+            "workload": "config 5: row-sharded Q4_0 lm_head 128256x3072 and FFN 8192x3072, "
+                        f"x [M][3072] f16, over the {world} GPU(s) of this run",
+            "steps": xa.steps, "warmup": xa.warmup,
+            "cases": run_sharded(xa, rank, world, local)}
+        torch.cuda.empty_cache()
+        if world == 1:
+            # configs 4 and 3 (decode is replicated, not sharded: measured on one GPU)
+            extras["decode"] = run_decode(xa, rank, world, local)
+            torch.cuda.empty_cache()
+            extras["generate"] = run_generate(xa, rank, world, local)[0]
+            torch.cuda.empty_cache()
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(r["value"], 3), "unit": "TFLOP/s",
@@ -775,7 +945,7 @@ def main():
             "ms_per_step": round(r["ms"] / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded Q4_0 weights d=f16(|N|*0.02), nibbles U{0..15}; x f16 N(0,1))",
-            "config": {"workload": "BASELINE config 2: Q4_0 prefill GEMM, 512 tokens x K1536 -> "
+            "config": {"workload": "benchmark config 2: Q4_0 prefill GEMM, 512 tokens x K1536 -> "
                                    "N8960 and 512 x K8960 -> N1536 per step",
                        "global_batch": T * world, "seq_len": T,
                        "parallelism": f"dp{world} (independent ubatches per rank)",
@@ -788,6 +958,8 @@ def main():
             line["cpu_baseline"] = r["cpu"]
         if r["secondary"] is not None:
             line["secondary"] = r["secondary"]
+        line["timing_spread"] = r["spread"]
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

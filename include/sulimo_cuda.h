@@ -52,6 +52,8 @@ enum {
 
 /* Output element types for the prefill GEMM. */
 enum { SULIMO_OUT_F16 = 0, SULIMO_OUT_F32 = 1 };
+/* Tensor types of the reference's loader (GgmlType, crates/sulimo-core/src/gguf.rs:118-122).  */
+enum { SULIMO_GGML_F32 = 0, SULIMO_GGML_F16 = 1, SULIMO_GGML_Q4_0 = 2 };
 /* Activation element types. */
 enum { SULIMO_ACT_F16 = 0, SULIMO_ACT_F32 = 1 };
 
@@ -153,7 +155,7 @@ int sulimo_cuda_gemv_q4_0_q8_0_static(sulimo_ctx* ctx, const void* w_scales,
                                       const void* w_quants, const void* x_q8, int rows, int cols,
                                       int batch, float* out);
 
-/* Fast mode of the same matvec (SURVEY's exact_mode = 0): the integer block sums are the      */
+/* Fast mode of the same matvec (exact_mode = 0 of the entry above): the integer block sums are the      */
 /* reference's, exact; each row's blocks are split over 8 fp32 partial sums (block index mod 8) */
 /* combined as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)), so the result differs from the AVX2 add   */
 /* order only by fp32 rounding and is deterministic for a given shape.  This is the form the   */
@@ -162,6 +164,24 @@ int sulimo_cuda_gemv_q4_0_q8_0_static(sulimo_ctx* ctx, const void* w_scales,
 int sulimo_cuda_gemv_q4_0_q8_0_fast(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                                     const void* x_q8, int rows, int cols, int batch, float* out,
                                     int static_weights);
+
+/* Raw F32 / F16 weight matvecs — replace dispatch_matvec_f32 / dispatch_matvec_f16           */
+/* (crates/sulimo-cpu/src/avx2.rs:72-104; AVX2 kernels :259-331): w [rows][cols] (f32, or f16  */
+/* little-endian bytes), x [batch][cols] fp32, out [batch][rows] fp32; bit-identical to the     */
+/* AVX2 kernels (eight FMA lanes per row in column order, the hsum_256 tree, then the tail     */
+/* columns multiply-then-add).  Any cols >= 1.                                                 */
+int sulimo_cuda_matvec_f32(sulimo_ctx* ctx, const float* w, const float* x, int rows, int cols,
+                           int batch, float* out);
+int sulimo_cuda_matvec_f16(sulimo_ctx* ctx, const void* w_f16, const float* x, int rows,
+                           int cols, int batch, float* out);
+
+/* apply_matvec (crates/sulimo-engine/src/forward_pass.rs:509-527): routes by tensor type.     */
+/* SULIMO_GGML_Q4_0: w0 = scales, w1 = quants, x_q8 the Q8_0 activations (the AVX2-order       */
+/* matvec, sulimo_cuda_gemv_q4_0_q8_0); SULIMO_GGML_F32 / F16: w0 = the raw weights, w1 unused, */
+/* x_f32 the fp32 activations (sulimo_cuda_matvec_f32 / _f16).  Any other type: SULIMO_EINVAL. */
+int sulimo_cuda_apply_matvec(sulimo_ctx* ctx, int ggml_type, const void* w0, const void* w1,
+                             const void* x_q8, const float* x_f32, int rows, int cols, int batch,
+                             float* out);
 
 /* Integer per-block sums (debug / parity entry): out[b][r*(cols/32)+j] = sum_i (w_i-8)*x_i, */
 /* the i32 `block_sum` of vec_dot_q4_0_q8_0_scalar (crates/sulimo-cpu/src/scalar.rs:189-199). */
@@ -289,6 +309,32 @@ int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
 int sulimo_cuda_prefill_ubatch_x(sulimo_ctx* ctx, const sulimo_model_desc* model,
                                  const void* x_f16, int n, size_t start_pos, float* logits,
                                  void* scratch, size_t scratch_bytes);
+
+/* Context repack on capacity overflow — replaces repack_context (crates/sulimo-engine/src/     */
+/* scheduler.rs:316-326) and the re-prefill that follows it (engine.rs:226-239), on the device: */
+/* the plan keeps the first sys_len = min(clamp(capacity/8, 4, 64), n_past) tokens and the last */
+/* recent_len = min(capacity/2, n_past - sys_len); the entry point gathers those tokens of      */
+/* past_tokens[n_past] (device int32) into new_tokens (device, not overlapping), re-prefills    */
+/* them from position 0 in ubatches of at most `ubatch` tokens (sulimo_cuda_prefill_ubatch;     */
+/* scratch >= sulimo_cuda_prefill_scratch_bytes(model, ubatch)), leaves the last token's logits */
+/* in logits[vocab] and the new position (sys_len + recent_len) in *new_pos_out.  No host round */
+/* trip: the counts are functions of n_past and kv_capacity.                                   */
+void sulimo_cuda_repack_context_plan(size_t n_past, size_t capacity, size_t* sys_len,
+                                     size_t* recent_len);
+int sulimo_cuda_repack_context(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                               const int32_t* past_tokens, size_t n_past, int32_t* new_tokens,
+                               int ubatch, float* logits, void* scratch, size_t scratch_bytes,
+                               size_t* new_pos_out);
+
+/* GGUF Q4_0 blocks to the SoA layout on the device — replaces repack_q4_0_aos_to_soa           */
+/* (crates/sulimo-core/src/repack.rs:45-81): src_aos = src_len bytes of 18-byte blocks          */
+/* [d: f16][qs: 16 B] (device, 2-byte aligned), dst_scales[nb] f16 (2-byte aligned),             */
+/* dst_quants[nb][16] (16-byte aligned); *num_blocks_out = nb.  The reference's errors:         */
+/* src_len % 18 != 0 (InvalidAosLength), scales_len < 2 nb (ScalesBufferTooSmall), quants_len  */
+/* < 16 nb (QuantsBufferTooSmall) -> SULIMO_EINVAL.                                             */
+int sulimo_cuda_repack_q4_0_aos_to_soa(sulimo_ctx* ctx, const void* src_aos, size_t src_len,
+                                       void* dst_scales, size_t scales_len, void* dst_quants,
+                                       size_t quants_len, size_t* num_blocks_out);
 
 /* Causal GQA prefill attention over one layer's Q8_0 ring — replaces                          */
 /* causal_gqa_attention_prefill (kernels/prefill.cl:120-237, enqueue_attention_prefill):       */

@@ -54,6 +54,10 @@ def lib():
             "oracle_add_f16": (None, [vp, vp, sz]),
             "oracle_prefill_ubatch": (i32, [vp, vp, sz, sz, vp, i32]),
             "oracle_prefill_ubatch_f32": (i32, [vp, vp, sz, sz, vp, i32]),
+            "oracle_matvec_f32_avx2": (None, [vp, vp, sz, sz, vp]),
+            "oracle_matvec_f16_avx2": (None, [vp, vp, sz, sz, vp]),
+            "oracle_matvec_f32_scalar": (None, [vp, vp, sz, sz, vp]),
+            "oracle_matvec_f16_scalar": (None, [vp, vp, sz, sz, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -320,6 +324,17 @@ class OracleModel:
                                              threads)
         assert st == 0, "oracle_prefill_ubatch_f32 rejected its arguments"
         return logits
+
+
+def matvec_dense(w, x, rows, cols, kind="f32", avx2=True):
+    """matvec_f32/f16 (avx2.rs:259-331 when avx2, else scalar.rs:228-251): w [rows][cols] f32 or
+    f16 bits, x [cols] f32 -> [rows] f32."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32 if kind == "f32" else np.uint16)
+    out = np.empty(rows, np.float32)
+    fn = f"oracle_matvec_{kind}_{'avx2' if avx2 else 'scalar'}"
+    getattr(lib(), fn)(_p(w), _p(x), rows, cols, _p(out))
+    return out
 
 
 def _f16_buf(a):

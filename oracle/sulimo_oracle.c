@@ -882,3 +882,58 @@ int oracle_prefill_ubatch_f32(const oracle_model* m, const uint16_t* x_f16, size
     free(tmp); free(scores);
     return 0;
 }
+
+/* ------------------------------------------------------------------ */
+/* Raw F32 / F16 matvecs (apply_matvec's other branches)               */
+/* ------------------------------------------------------------------ */
+
+/* matvec_f32_avx2 — crates/sulimo-cpu/src/avx2.rs:259-280; same intrinsics in the same order */
+void oracle_matvec_f32_avx2(const float* w, const float* x, size_t rows, size_t cols,
+                            float* out) {
+    size_t chunks = cols / 8;
+    for (size_t r = 0; r < rows; r++) {
+        const float* wr = w + r * cols;
+        __m256 acc = _mm256_setzero_ps();
+        for (size_t c = 0; c < chunks; c++)
+            acc = _mm256_fmadd_ps(_mm256_loadu_ps(wr + c * 8), _mm256_loadu_ps(x + c * 8), acc);
+        float sum = hsum_256(acc);
+        for (size_t c = chunks * 8; c < cols; c++) sum += wr[c] * x[c];
+        out[r] = sum;
+    }
+}
+
+/* matvec_f16_avx2 — avx2.rs:287-331: F16C widening, same lanes and tree */
+void oracle_matvec_f16_avx2(const uint16_t* w, const float* x, size_t rows, size_t cols,
+                            float* out) {
+    size_t chunks = cols / 8;
+    for (size_t r = 0; r < rows; r++) {
+        const uint16_t* wr = w + r * cols;
+        __m256 acc = _mm256_setzero_ps();
+        for (size_t c = 0; c < chunks; c++) {
+            __m256 wv = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i*)(wr + c * 8)));
+            acc = _mm256_fmadd_ps(wv, _mm256_loadu_ps(x + c * 8), acc);
+        }
+        float sum = hsum_256(acc);
+        for (size_t c = chunks * 8; c < cols; c++) sum += oracle_f16_to_f32(wr[c]) * x[c];
+        out[r] = sum;
+    }
+}
+
+/* matvec_f32_scalar / matvec_f16_scalar — crates/sulimo-cpu/src/scalar.rs:228-251 */
+void oracle_matvec_f32_scalar(const float* w, const float* x, size_t rows, size_t cols,
+                              float* out) {
+    for (size_t r = 0; r < rows; r++) {
+        float sum = 0.0f;
+        for (size_t c = 0; c < cols; c++) sum += w[r * cols + c] * x[c];
+        out[r] = sum;
+    }
+}
+
+void oracle_matvec_f16_scalar(const uint16_t* w, const float* x, size_t rows, size_t cols,
+                              float* out) {
+    for (size_t r = 0; r < rows; r++) {
+        float sum = 0.0f;
+        for (size_t c = 0; c < cols; c++) sum += oracle_f16_to_f32(w[r * cols + c]) * x[c];
+        out[r] = sum;
+    }
+}

@@ -78,6 +78,15 @@ void oracle_matvec_q4_0_q8_0_avx2(const uint8_t* w_scales, const uint8_t* w_quan
 void oracle_matvec_q4_0_q8_0_avx2_mt(const uint8_t* w_scales, const uint8_t* w_quants,
                                      const uint8_t* x_q8, size_t rows, size_t cols, float* out,
                                      int threads);
+/* Raw F32 / F16 weight matvecs (apply_matvec's other branches, forward_pass.rs:509-527):
+ * AVX2 kernels avx2.rs:259-331 (same intrinsics, same order) and scalar.rs:228-251. */
+void oracle_matvec_f32_avx2(const float* w, const float* x, size_t rows, size_t cols, float* out);
+void oracle_matvec_f16_avx2(const uint16_t* w, const float* x, size_t rows, size_t cols,
+                            float* out);
+void oracle_matvec_f32_scalar(const float* w, const float* x, size_t rows, size_t cols,
+                              float* out);
+void oracle_matvec_f16_scalar(const uint16_t* w, const float* x, size_t rows, size_t cols,
+                              float* out);
 /* Integer per-block sums: out[r*nb+b] = sum_i (w_i-8)*x_i (exact i32). */
 void oracle_block_sums_q4_0_q8_0(const uint8_t* w_scales, const uint8_t* w_quants,
                                  const uint8_t* x_q8, size_t rows, size_t cols, int32_t* out);

@@ -7,13 +7,15 @@ over that C ABI, used by the tests and bench.py.  Tensor arguments are CUDA torc
 raw device pointers as ints); torch only supplies device memory and streams.
 """
 from . import capi
-from .capi import ACT_F16, ACT_F32, OUT_F16, OUT_F32, SulimoError
+from .capi import (ACT_F16, ACT_F32, GGML_F16, GGML_F32, GGML_Q4_0, OUT_F16, OUT_F32,
+                   SulimoError)
 
 __all__ = [
     "CudaContext", "SulimoError", "gemm_q4_0_f16", "logits_final", "dispatch_matvec_q4_0_q8_0",
     "block_sums_q4_0_q8_0", "quantize_f32_to_q8_0", "kv_store_q8_0", "dequantize_q4_0_rows",
     "causal_gqa_decode", "causal_gqa_attention_prefill", "live_buffer_count", "unshard_rows", "OUT_F16", "OUT_F32", "ACT_F16",
-    "ACT_F32",
+    "ACT_F32", "GGML_F32", "GGML_F16", "GGML_Q4_0", "dispatch_matvec_f32", "dispatch_matvec_f16",
+    "apply_matvec",
 ]
 
 
@@ -124,6 +126,24 @@ def dispatch_matvec_q4_0_q8_0(ctx, w_scales, w_quants, x_q8, rows, cols, out, ba
     name = "sulimo_cuda_gemv_q4_0_q8_0_static" if static_weights else "sulimo_cuda_gemv_q4_0_q8_0"
     capi.call(name, ctx.handle, _ptr(w_scales), _ptr(w_quants), _ptr(x_q8), rows, cols, batch,
               _ptr(out))
+
+
+def dispatch_matvec_f32(ctx, w, x, rows, cols, out, batch=1):
+    """dispatch_matvec_f32 (crates/sulimo-cpu/src/avx2.rs:72-85), AVX2-bit-exact."""
+    capi.call("sulimo_cuda_matvec_f32", ctx.handle, _ptr(w), _ptr(x), rows, cols, batch, _ptr(out))
+
+
+def dispatch_matvec_f16(ctx, w_f16, x, rows, cols, out, batch=1):
+    """dispatch_matvec_f16 (crates/sulimo-cpu/src/avx2.rs:88-104), AVX2-bit-exact."""
+    capi.call("sulimo_cuda_matvec_f16", ctx.handle, _ptr(w_f16), _ptr(x), rows, cols, batch,
+              _ptr(out))
+
+
+def apply_matvec(ctx, ggml_type, w0, w1, x_q8, x_f32, rows, cols, out, batch=1):
+    """apply_matvec (crates/sulimo-engine/src/forward_pass.rs:509-527): Q4_0 tensors (w0 scales,
+    w1 quants) against x_q8, F32 / F16 tensors (w0) against x_f32."""
+    capi.call("sulimo_cuda_apply_matvec", ctx.handle, ggml_type, _ptr(w0), _ptr(w1), _ptr(x_q8),
+              _ptr(x_f32), rows, cols, batch, _ptr(out))
 
 
 def matvec_q4_0_q8_0_fast(ctx, w_scales, w_quants, x_q8, rows, cols, out, batch=1,

@@ -21,6 +21,9 @@ SOURCES = [
     "gemv_fast_q4_0_q8_0.cu",
     "attn_decode_q8_0.cu",
     "attn_decode_noalloc.cu",
+    "attn_decode_mma.cu",
+    "matvec_dense.cu",
+    "repack_q4_0.cu",
     "gemm_q4_0_tc.cu",
     "shard.cu",
     "forward.cu",

@@ -12,6 +12,7 @@ LIB_PATH = os.path.join(HERE, "libsulimo_cuda.so")
 
 OK, EINVAL, ENODEV, EOOM, ELAUNCH, ETIMEOUT, ENCCL, EALIGN, EDEVICE = range(9)
 OUT_F16, OUT_F32 = 0, 1
+GGML_F32, GGML_F16, GGML_Q4_0 = 0, 1, 2
 ACT_F16, ACT_F32 = 0, 1
 
 STATUS_NAMES = {
@@ -33,6 +34,14 @@ SIGNATURES = {
     "sulimo_cuda_ctx_device": (_i, [_vp]),
     "sulimo_cuda_ctx_launch_count": (_u64, [_vp]),
     "sulimo_cuda_ctx_workspace_bytes": (_sz, [_vp]),
+    "sulimo_cuda_matvec_f32": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "sulimo_cuda_matvec_f16": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "sulimo_cuda_apply_matvec": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "sulimo_cuda_repack_context_plan": (None, [_sz, _sz, C.POINTER(_sz), C.POINTER(_sz)]),
+    "sulimo_cuda_repack_context": (_i, [_vp, _vp, _vp, _sz, _vp, _i, _vp, _vp, _sz,
+                                        C.POINTER(_sz)]),
+    "sulimo_cuda_repack_q4_0_aos_to_soa": (_i, [_vp, _vp, _sz, _vp, _sz, _vp, _sz,
+                                                C.POINTER(_sz)]),
     "sulimo_cuda_buffer_from_host": (_i, [_vp, _vp, _sz, _i, _i, C.POINTER(_vp)]),
     "sulimo_cuda_buffer_alloc": (_i, [_vp, _sz, C.POINTER(_vp)]),
     "sulimo_cuda_buffer_write": (_i, [_vp, _sz, _vp, _sz]),

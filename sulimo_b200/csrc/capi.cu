@@ -145,13 +145,20 @@ int sulimo_cuda_ctx_create(int device, sulimo_ctx** out) {
     ctx->stream = ctx->own_stream;
     e = cudaMalloc(&ctx->d_error, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ctx->d_error, 0, sizeof(int));
+    if (e == cudaSuccess)
+        e = cudaMalloc(&ctx->attn_counters, sulimo::ATTN_COUNTERS * sizeof(unsigned));
+    if (e == cudaSuccess)
+        e = cudaMemset(ctx->attn_counters, 0, sulimo::ATTN_COUNTERS * sizeof(unsigned));
     if (e != cudaSuccess) {
+        if (ctx->d_error) cudaFree(ctx->d_error);
+        if (ctx->attn_counters) cudaFree(ctx->attn_counters);
         cudaStreamDestroy(ctx->own_stream);
         delete ctx;
-        return sulimo::check_cuda(e, "error word");
+        return sulimo::check_cuda(e, "error word / attention counters");
     }
     if (!sulimo::get_encode_tiled()) {
         cudaFree(ctx->d_error);
+        cudaFree(ctx->attn_counters);
         cudaStreamDestroy(ctx->own_stream);
         delete ctx;
         return set_error(SULIMO_ENODEV, "cuTensorMapEncodeTiled unavailable");
@@ -167,6 +174,7 @@ int sulimo_cuda_ctx_destroy(sulimo_ctx* ctx) {
     if (ctx->workspace) cudaFree(ctx->workspace);
     if (ctx->d_error) cudaFree(ctx->d_error);
     if (ctx->argmax_scratch) cudaFree(ctx->argmax_scratch);
+    if (ctx->attn_counters) cudaFree(ctx->attn_counters);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return SULIMO_OK;
@@ -408,6 +416,44 @@ int sulimo_cuda_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void
     return sulimo::launch_gemv_q4_0_q8_0(ctx, w_scales, w_quants, x_q8, rows, cols, batch, out);
 }
 
+static int matvec_dense(sulimo_ctx* ctx, int wtype, const void* w, const float* x, int rows,
+                        int cols, int batch, float* out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (rows < 0 || cols <= 0 || batch < 0) return set_error(SULIMO_EINVAL, "bad shape");
+    if ((size_t)rows * 8 > 0x7fffffffu) return set_error(SULIMO_EINVAL, "too many rows");
+    if (rows == 0 || batch == 0) return SULIMO_OK;
+    if (!w || !x || !out) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(w, wtype == SULIMO_GGML_F32 ? 4 : 2) || !aligned(x, 4) || !aligned(out, 4))
+        return set_error(SULIMO_EALIGN, "w, x, out must be aligned to their element size");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_matvec_dense(ctx, wtype, w, x, rows, cols, batch, out);
+}
+
+int sulimo_cuda_matvec_f32(sulimo_ctx* ctx, const float* w, const float* x, int rows, int cols,
+                           int batch, float* out) {
+    return matvec_dense(ctx, SULIMO_GGML_F32, w, x, rows, cols, batch, out);
+}
+
+int sulimo_cuda_matvec_f16(sulimo_ctx* ctx, const void* w_f16, const float* x, int rows,
+                           int cols, int batch, float* out) {
+    return matvec_dense(ctx, SULIMO_GGML_F16, w_f16, x, rows, cols, batch, out);
+}
+
+int sulimo_cuda_apply_matvec(sulimo_ctx* ctx, int ggml_type, const void* w0, const void* w1,
+                             const void* x_q8, const float* x_f32, int rows, int cols, int batch,
+                             float* out) {
+    switch (ggml_type) {
+        case SULIMO_GGML_Q4_0:
+            return sulimo_cuda_gemv_q4_0_q8_0(ctx, w0, w1, x_q8, rows, cols, batch, out);
+        case SULIMO_GGML_F32:
+        case SULIMO_GGML_F16:
+            return matvec_dense(ctx, ggml_type, w0, x_f32, rows, cols, batch, out);
+        default:
+            return set_error(SULIMO_EINVAL, "tensor type must be F32, F16 or Q4_0");
+    }
+}
+
 int sulimo_cuda_gemv_q4_0_q8_0_static(sulimo_ctx* ctx, const void* w_scales,
                                       const void* w_quants, const void* x_q8, int rows, int cols,
                                       int batch, float* out) {
@@ -616,6 +662,65 @@ int sulimo_cuda_prefill_ubatch_x(sulimo_ctx* ctx, const sulimo_model_desc* model
     if (!x_f16) return set_error(SULIMO_EINVAL, "null pointer");
     return prefill_ubatch(ctx, model, nullptr, x_f16, n, start_pos, logits, scratch,
                           scratch_bytes);
+}
+
+void sulimo_cuda_repack_context_plan(size_t n_past, size_t capacity, size_t* sys_len,
+                                     size_t* recent_len) {
+    size_t s = 0, r = 0;
+    sulimo::repack_context_plan(n_past, capacity, &s, &r);
+    if (sys_len) *sys_len = s;
+    if (recent_len) *recent_len = r;
+}
+
+int sulimo_cuda_repack_context(sulimo_ctx* ctx, const sulimo_model_desc* model,
+                               const int32_t* past_tokens, size_t n_past, int32_t* new_tokens,
+                               int ubatch, float* logits, void* scratch, size_t scratch_bytes,
+                               size_t* new_pos_out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if ((st = check_model(model))) return st;
+    if (!new_pos_out) return set_error(SULIMO_EINVAL, "null pointer");
+    *new_pos_out = 0;
+    if (ubatch <= 0 || ubatch > 65535) return set_error(SULIMO_EINVAL, "ubatch must be in [1, 65535]");
+    size_t s, r;
+    sulimo::repack_context_plan(n_past, model->kv_capacity, &s, &r);
+    if (s + r == 0) return SULIMO_OK;
+    if (!past_tokens || !new_tokens || !logits || !scratch)
+        return set_error(SULIMO_EINVAL, "null pointer");
+    const uint8_t* p0 = reinterpret_cast<const uint8_t*>(past_tokens);
+    const uint8_t* q0 = reinterpret_cast<const uint8_t*>(new_tokens);
+    if (q0 < p0 + n_past * 4 && p0 < q0 + (s + r) * 4)
+        return set_error(SULIMO_EINVAL, "past_tokens and new_tokens overlap");
+    if (scratch_bytes < sulimo::prefill_scratch_bytes(model, ubatch))
+        return set_error(SULIMO_EINVAL, "scratch smaller than sulimo_cuda_prefill_scratch_bytes(ubatch)");
+    if (!aligned(past_tokens, 4) || !aligned(new_tokens, 4) || !aligned(logits, 16) ||
+        !aligned(scratch, 256))
+        return set_error(SULIMO_EALIGN, "tokens 4-byte, logits 16-byte, scratch 256-byte aligned");
+    if (model->head_dim != 64 && model->head_dim != 128)
+        return set_error(SULIMO_EINVAL, "prefill supports head_dim 64 and 128");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_repack_context(ctx, model, past_tokens, n_past, new_tokens, ubatch, logits,
+                                         scratch, new_pos_out);
+}
+
+int sulimo_cuda_repack_q4_0_aos_to_soa(sulimo_ctx* ctx, const void* src_aos, size_t src_len,
+                                       void* dst_scales, size_t scales_len, void* dst_quants,
+                                       size_t quants_len, size_t* num_blocks_out) {
+    int st = check_ctx(ctx);
+    if (st) return st;
+    if (!num_blocks_out) return set_error(SULIMO_EINVAL, "null pointer");
+    *num_blocks_out = 0;
+    if (src_len % 18) return set_error(SULIMO_EINVAL, "InvalidAosLength: src_len % 18 != 0");
+    const size_t nb = src_len / 18;
+    if (scales_len < nb * 2) return set_error(SULIMO_EINVAL, "ScalesBufferTooSmall");
+    if (quants_len < nb * 16) return set_error(SULIMO_EINVAL, "QuantsBufferTooSmall");
+    *num_blocks_out = nb;
+    if (nb == 0) return SULIMO_OK;
+    if (!src_aos || !dst_scales || !dst_quants) return set_error(SULIMO_EINVAL, "null pointer");
+    if (!aligned(src_aos, 2) || !aligned(dst_scales, 2) || !aligned(dst_quants, 16))
+        return set_error(SULIMO_EALIGN, "src / scales 2-byte, quants 16-byte aligned");
+    if ((st = bind_device(ctx))) return st;
+    return sulimo::launch_repack_q4_0(ctx, src_aos, nb, dst_scales, dst_quants);
 }
 
 int sulimo_cuda_attn_prefill_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,

@@ -2,27 +2,30 @@
 // the reference's forward_token (crates/sulimo-engine/src/forward_pass.rs:190-417) for a batch
 // of independent sequences that sit at the same position.
 //
-// Per layer (11 launches, all on the context's stream, no host synchronisation, each a
+// Per layer, at one sequence (8 launches on the context's stream, no host synchronisation, each a
 // programmatic dependent of the previous one):
-//   add_rmsnorm_q8     x (+= previous FFN output), h = rmsnorm(x)*attn_norm -> Q8_0
-//                      (apply_rmsnorm :493-507 + quantize_f32_to_q8_0)
-//   GEMV (one launch)  q, k, v = W . h (dispatch_matvec_q4_0_q8_0, bit-exact AVX2 order)
+//   GEMV q,k,v         one fast-mode launch for the three matrices; its prologue adds the
+//                      previous FFN output to the residual, RMSNorms it (apply_rmsnorm
+//                      :493-507) and quantizes it to Q8_0 (quantize_f32_to_q8_0), recomputed by
+//                      every CTA from L2 while its first weight tiles stream in
 //   qkv_rope_store     + biases (add_bias :452-465), RoPE Norm/Neox per head
 //                      (rope_head_scalar, scalar.rs:92-130), K/V quantized into ring slot
 //                      pos % capacity (KvCache::store_key/store_value, kv_cache.rs:93-110)
 //   attention          causal GQA decode over the Q8_0 ring, context pos+1
-//                      (causal_gqa_decode_scalar_ext, scalar.rs:287-359) -- 2 launches
-//   quantize           attention output -> Q8_0
-//   GEMV               o = Wo . a
-//   add_rmsnorm_q8     x += o, h = rmsnorm(x)*ffn_norm -> Q8_0
-//   GEMV (one launch)  gate, up
+//                      (causal_gqa_decode_scalar_ext, scalar.rs:287-359): split-K slots kernel
+//                      + merge, the merge writing the o projection's Q8_0 input -- 2 launches
+//   GEMV o             o = Wo . a
+//   GEMV gate,up       one launch; prologue: x += o, RMSNorm (ffn_norm), Q8_0
 //   swiglu_q8          silu(gate)*up -> Q8_0 (swiglu_scalar, scalar.rs:161-170)
-//   GEMV               down
-// then add_rmsnorm_q8 with the output norm and the vocab GEMV (logits, fp32).
-// The glue kernels are fused so every activation vector is read and written once per step;
-// the GEMVs (the weight stream) dominate.  RMSNorm sums squares as a tree (the reference sums
-// eight AVX2 lanes sequentially), and RoPE / SiLU use CUDA's powf / sinf / cosf / expf, so the
-// activations agree with the reference to float rounding, not bit for bit.
+//   GEMV down
+// then the vocab GEMV with the output norm in its prologue (logits, fp32).  With several
+// sequences the norm + quantize is a separate add_rmsnorm_q8 launch before each fused GEMV
+// (recomputing it per CTA for every sequence costs more than the launch).  The GEMVs run the
+// fast mode (gemv_fast_q4_0_q8_0.cu): exact integer block sums, one fp32 FMA per block and a
+// fixed lane tree, equal to the AVX2 kernel to fp32 rounding; they dominate the step (the weight
+// stream).  RMSNorm sums squares as a tree (the reference sums eight AVX2 lanes sequentially),
+// and RoPE / SiLU use CUDA's powf / sinf / cosf / expf, so the activations agree with the
+// reference to float rounding, not bit for bit.
 #include "sulimo_common.cuh"
 #include "sulimo_internal.h"
 
@@ -171,6 +174,18 @@ __global__ void __launch_bounds__(GLUE_THREADS)
     const __half2 hi = __floats2half2_rn(silu_mul(g.z, u.z), silu_mul(g.w, u.w));
     out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo),
                         *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+// The token list of repack_context (crates/sulimo-engine/src/scheduler.rs:316-326): the first
+// sys_len tokens, then the last recent_len.
+__global__ void __launch_bounds__(GLUE_THREADS)
+    gather_context_kernel(const int32_t* __restrict__ past, size_t n_past, size_t sys_len,
+                          size_t recent_len, int32_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= sys_len + recent_len) return;
+    out[i] = i < sys_len ? past[i] : past[n_past - recent_len + (i - sys_len)];
 }
 
 // f16 [n4 * 4] -> f32: a prefill ubatch's caller-written f16 embeddings into the fp32 residual.
@@ -439,6 +454,39 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
     if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
     return launch_gemm_q4_0_f16(ctx, m->out_scales, m->out_quants, s.h, logits, m->vocab, E, 1,
                                 SULIMO_OUT_F32, E, 0);
+}
+
+void repack_context_plan(size_t n_past, size_t capacity, size_t* sys_len, size_t* recent_len) {
+    size_t s = capacity / 8;
+    s = s < 4 ? 4 : (s > 64 ? 64 : s);
+    if (s > n_past) s = n_past;
+    size_t r = capacity / 2;
+    if (r > n_past - s) r = n_past - s;
+    *sys_len = s;
+    *recent_len = r;
+}
+
+// repack_context + the re-prefill from position 0 that follows it (engine.rs:226-239), with the
+// token list gathered on the device: ubatches of at most `ubatch` tokens of new_tokens (no host
+// round trip), the last one's logits in `logits`.
+int launch_repack_context(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* past,
+                          size_t n_past, int32_t* new_tokens, int ubatch, float* logits,
+                          void* scratch, size_t* new_pos) {
+    size_t sys_len, recent_len;
+    repack_context_plan(n_past, m->kv_capacity, &sys_len, &recent_len);
+    const size_t n = sys_len + recent_len;
+    *new_pos = n;
+    if (n == 0) return SULIMO_OK;
+    (void)launch_pdl(gather_context_kernel,
+                     dim3((unsigned)((n + GLUE_THREADS - 1) / GLUE_THREADS)), dim3(GLUE_THREADS),
+                     0, ctx->stream, past, n_past, sys_len, recent_len, new_tokens);
+    ctx->launches++;
+    int st = check_cuda(cudaGetLastError(), "gather_context launch");
+    for (size_t p0 = 0; !st && p0 < n; p0 += (size_t)ubatch) {
+        const int cnt = (int)(n - p0 < (size_t)ubatch ? n - p0 : (size_t)ubatch);
+        st = launch_prefill_ubatch(ctx, m, new_tokens + p0, nullptr, cnt, p0, logits, scratch);
+    }
+    return st;
 }
 
 size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch) {

@@ -335,7 +335,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
         for (int s = 0; s < stages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 4 * 32);
+            mbar_init(&afull[s], 4);  // one arrival per dequant warp of the stage's group
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -444,7 +444,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
             const uint32_t ph = (uint32_t)(j / stages) & 1u;
             const uint32_t sa = sa_next, sb = sb_next;
             load_scales(j + DEQ_GROUPS, sa_next, sb_next);
-            if (!mbar_wait_bounded(&full[s], ph, err, abort_flag)) {
+            // warp-uniform, so the warp reaches its __syncwarp below together
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], ph, err, abort_flag))) {
                 ok = false;
                 break;
             }
@@ -456,7 +457,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
             tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * 32u, cols);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&afull[s]);
+            __syncwarp();  // every lane's stores are complete before the warp's single arrival
+            if (lane == 0) mbar_arrive(&afull[s]);
         }
         // Epilogue: each group takes 32-token chunks of the accumulators (chunk c = group,
         // group + DEQ_GROUPS, ...), stages chunk c as a [32 tokens][128 features] tile in the

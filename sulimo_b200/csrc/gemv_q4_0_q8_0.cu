@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 }
 
 // ---------------------------------------------------------------------------------------------
-// Streaming form for K a multiple of 256 and 16-byte aligned scales (every BASELINE shape).
+// Streaming form for K a multiple of 256 and 16-byte aligned scales (every projection of the supported models).
 //
 // CTA: ROWS rows (64, 32 or 16: chosen so the launch covers the SMs) x 4 threads per row
 // (thread p of a row owns AVX2 lanes 2p and 2p+1, i.e. quant word p of every block) + 1 producer

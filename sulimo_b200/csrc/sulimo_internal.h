@@ -22,6 +22,7 @@ struct sulimo_ctx {
     size_t workspace_bytes = 0;
     void* argmax_scratch = nullptr;  // greedy argmax partials + per-row counters (zero at rest)
     size_t argmax_bytes = 0;
+    unsigned* attn_counters = nullptr;  // decode attention merge counters (zero at rest)
     std::atomic<uint64_t> launches{0};
 };
 
@@ -132,6 +133,8 @@ bool gemv_fast_fused_ok(const GemvMatSrc* src, int count, int cols, int batch,
                         const GemvPrologue& pro);
 int launch_gemv_fast_fused(sulimo_ctx* ctx, const GemvMatSrc* src, int count,
                            const GemvPrologue& pro, int cols, int batch, bool static_weights);
+int launch_matvec_dense(sulimo_ctx* ctx, int wtype, const void* w, const float* x, int rows,
+                        int cols, int batch, float* out);
 int launch_block_sums(sulimo_ctx* ctx, const void* w_quants, const void* x_q8, int rows, int cols,
                       int32_t* out);
 int launch_quantize_q8_0(sulimo_ctx* ctx, const float* src, void* dst, size_t n);
@@ -142,6 +145,19 @@ int launch_kv_store_q8_0(sulimo_ctx* ctx, const void* act, int act_dtype, void* 
 enum { DEQUANT_F16 = SULIMO_OUT_F16, DEQUANT_F32 = SULIMO_OUT_F32, DEQUANT_F16_WIDE = 2 };
 int launch_dequant_rows(sulimo_ctx* ctx, const void* scales, const void* quants, int cols,
                         const int32_t* row_ids, int count, void* out, int out_dtype);
+// Decode attention merge counters per context: [sequence][cluster rank], up to the batch limit.
+constexpr size_t ATTN_COUNTERS = (size_t)65536 * 8;
+// The tensor-core decode attention (attn_decode_mma.cu).  *used = false (and nothing launched)
+// when the geometry or the workspace does not fit it; the caller then runs the scalar kernels.
+int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                           const void* v_ring, size_t seq_stride, size_t capacity,
+                           size_t context_len, int head_count, int head_count_kv, int head_dim,
+                           int batch, float softcap, float* out, float* partials,
+                           size_t partial_bytes, unsigned* counters, uint8_t* out_q8,
+                           bool* used);
+size_t attn_decode_mma_partial_bytes(size_t ctx_len, size_t capacity, int H, int Hkv, int HD,
+                                     int batch, int num_sms, size_t seq_stride, const void* k,
+                                     const void* v);
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
@@ -158,6 +174,13 @@ size_t prefill_scratch_bytes(const sulimo_model_desc* m, int n);
 int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
                           const void* x_f16, int n, size_t start_pos, float* logits,
                           void* scratch);
+// repack_context's arithmetic (scheduler.rs:316-326) and the device-side repack + re-prefill.
+void repack_context_plan(size_t n_past, size_t capacity, size_t* sys_len, size_t* recent_len);
+int launch_repack_context(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* past,
+                          size_t n_past, int32_t* new_tokens, int ubatch, float* logits,
+                          void* scratch, size_t* new_pos);
+int launch_repack_q4_0(sulimo_ctx* ctx, const void* src_aos, size_t nblocks, void* dst_scales,
+                       void* dst_quants);
 int launch_attn_prefill(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                         size_t start_pos, size_t capacity, int n_tok, int H, int Hkv, int hd,
                         void* out);

@@ -4,7 +4,7 @@
 
 Inputs are the deterministic patterns of the reference's own unit tests (computed here in
 float32 and stored explicitly, so the fixtures do not depend on a libm) plus a small seeded
-sample of BASELINE config 1.  Outputs are what the reference's arithmetic produces on them,
+sample of benchmark config 1.  Outputs are what the reference's arithmetic produces on them,
 evaluated exactly and rounded once per IEEE operation.  tests/test_oracle.py checks the C
 oracle against these bit for bit; the GPU tests check the kernels against the C oracle.
 """
@@ -99,7 +99,7 @@ def case_gemm_small():
 
 
 def case_config1_sample():
-    """8 rows of BASELINE config 1 (seed 0): d=f16(|N(0,1)|*0.02), nibbles U{0..15}, K=1536."""
+    """8 rows of benchmark config 1 (seed 0): d=f16(|N(0,1)|*0.02), nibbles U{0..15}, K=1536."""
     rng = np.random.default_rng(0)
     rows, cols = 8, 1536
     nb = cols // 32

@@ -1,6 +1,6 @@
 """Shared generators and metrics for the parity tests.
 
-Generators follow BASELINE.json's synthetic distributions (seeded numpy):
+Generators follow the benchmark's synthetic distributions (seeded numpy):
   Q4_0 weights: d = f16(|N(0,1)| * 0.02), nibbles uniform 0..15 (w = d*(q-8)), SoA layout
   activations:  fp32 / fp16 N(0,1)
 and the deterministic patterns of the reference's own tests.

@@ -1,4 +1,4 @@
-"""GPU parity at the full sizes of BASELINE configs 3 and 4 (28 layers, real vocabularies,
+"""GPU parity at the full sizes of benchmark configs 3 and 4 (28 layers, real vocabularies,
 4096-slot rings), against the oracle on a host copy of the same model and rings.
 
 - Config 4 (Llama-3.2-3B architecture): rings pre-filled with N(0,1) K/V quantised to Q8_0 at

@@ -65,7 +65,7 @@ def torch_reference(ws, wq, x16, m, k, n):
 
 @pytest.mark.parametrize("n,k,m", [(512, 1536, 8960), (512, 8960, 1536)])
 def test_gemm_config2_full_size(ctx, n, k, m):
-    """BASELINE config 2 (up/gate and down shapes), seed 0, d=f16(|N|*0.02), x f16 N(0,1)."""
+    """benchmark config 2 (up/gate and down shapes), seed 0, d=f16(|N|*0.02), x f16 N(0,1)."""
     ws, wq = make_q4_0(m, k, seed=0)
     x = np.random.default_rng(1).standard_normal(n * k).astype(np.float16)
     got32 = run_gemm(ctx, ws, wq, x, m, k, n, sb.OUT_F32).reshape(n, m)

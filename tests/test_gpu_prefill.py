@@ -130,7 +130,7 @@ LLAMA_NOBIAS = dict(n_layers=3, embd=384, ffn=1024, head_count=6, head_count_kv=
 @pytest.mark.parametrize("cfg,splits", [(QWEN_NOBIAS, [200, 57]), (LLAMA_NOBIAS, [64, 1, 31])],
                          ids=["qwen2-shape", "llama-shape"])
 def test_prefill_ubatch_matches_prefill_oracle(ctx, cfg, splits):
-    """Seeded models (BASELINE distributions), several ubatches continuing the same rings, then
+    """Seeded models (benchmark distributions), several ubatches continuing the same rings, then
     one decode position from each side's own rings (forward_token on both)."""
     import torch
     from sulimo_b200.model import DecodeModel

@@ -136,7 +136,7 @@ def run_gemv(ctx, ws, wq, xq8, rows, cols, batch):
 
 
 def test_gemv_config1_bit_exact(ctx):
-    """8960 x 1536 Q4_0 x Q8_0, batch 1, seed 0 — bit-identical to the
+    """benchmark config 1: 8960 x 1536 Q4_0 x Q8_0, batch 1, seed 0 — bit-identical to the
     AVX2 kernel (and the integer block sums equal, test above)."""
     rows, cols = 8960, 1536
     ws, wq = make_q4_0(rows, cols, seed=0)

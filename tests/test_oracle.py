@@ -196,3 +196,25 @@ def test_kv_store_ring_wraps():
         s = (3 + t) % cap
         exp[s * bpp * 34:(s + 1) * bpp * 34] = blk
     assert np.array_equal(kv, exp)
+
+
+# ---- crates/sulimo-cpu/src/{avx2,scalar}.rs: the raw F32 / F16 matvecs ------------------------
+
+@pytest.mark.parametrize("kind", ["f32", "f16"])
+def test_dense_matvec_avx2_vs_scalar(kind):
+    """matvec_f32/f16_avx2 (avx2.rs:259-331) against the scalar kernels (scalar.rs:228-251) and
+    a float64 product: only the summation order differs."""
+    rng = np.random.default_rng(11)
+    rows, cols = 48, 1001
+    w = rng.standard_normal((rows, cols)).astype(np.float32)
+    if kind == "f16":
+        w = w.astype(np.float16).view(np.uint16)
+        wd = w.view(np.float16).astype(np.float64)
+    else:
+        wd = w.astype(np.float64)
+    x = rng.standard_normal(cols).astype(np.float32)
+    a = O.matvec_dense(w, x, rows, cols, kind, avx2=True)
+    s = O.matvec_dense(w, x, rows, cols, kind, avx2=False)
+    exact = wd @ x.astype(np.float64)
+    assert np.max(np.abs(a - exact)) < 1e-3 and np.max(np.abs(s - exact)) < 1e-3
+    assert not np.array_equal(a, s)  # different orders: the AVX2 lanes are what the GPU mirrors

@@ -86,7 +86,7 @@ def test_gemm_reference_test_shapes(n, k, m):
 
 @live
 def test_gemm_config2_sample():
-    """BASELINE config 2's generators (seeded Q4_0 8960 x 1536, f16 N(0,1) activations) on a
+    """benchmark config 2's generators (seeded Q4_0 8960 x 1536, f16 N(0,1) activations) on a
     48-token sample, f16 outputs and (logits_f16_output) fp32 outputs."""
     m, k, n = 8960, 1536, 48
     s, q = make_q4_0(m, k, seed=0)
@@ -175,7 +175,7 @@ def test_execute_prefill_ubatch_reference_test_model():
 @live
 @pytest.mark.parametrize("rope_mode,H,Hkv", [(1, 4, 2), (0, 8, 2), (1, 4, 4)])
 def test_execute_prefill_ubatch_seeded_models(rope_mode, H, Hkv):
-    """Seeded models (BASELINE distributions), three ubatches of 16/9/7 tokens continuing the
+    """Seeded models (benchmark distributions), three ubatches of 16/9/7 tokens continuing the
     same rings, embeddings from lookup_token_embedding_f16."""
     hd = 256 // H
     cfg = dict(n_layers=2, embd=256, ffn=512, head_count=H, head_count_kv=Hkv, head_dim=hd,
