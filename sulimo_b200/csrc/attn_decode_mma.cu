@@ -6,61 +6,63 @@
 //   out_h = sum_p softmax_p(score[h]) * dequant(V[p % cap][kv(h)])
 // in one kernel, split over the context ("flash-decoding") and merged on the device.
 //
-// Grid: (splits, sequences) in thread-block clusters of `cl` CTAs along the splits.  A CTA
-// covers `chunk` consecutive positions of one sequence for ALL kv heads: every position is one
-// ring slot (Hkv * hd/32 Q8_0 blocks), so each slot arrives with one bulk copy per tensor.
-//   producer (warp 8): bulk copies of K and V slots into padded shared-memory rows (the row
-//     stride is chosen so that eight rows start in eight different bank quads), `stages`-deep
-//     ring of stages of `sp` positions, full / empty mbarriers;
-//   consumers (warps 0-7): warp w works on kv head w % Hkv and on every (8/Hkv)-th 16-position
-//     tile of a stage.  Per tile, with mma.sync.m16n8k16 (f16 in, fp32 accumulate):
-//       S^T[head][pos] = Q . K^T: the A operand holds the query rows split in two f16 parts,
-//         hi = f16(q) in rows 0-7 and lo = f16(q - hi) in rows 8-15 (so q enters at ~22 bits);
-//         B = K's int8 codes, exact in f16; each 32-dimension Q8_0 block is two k-steps into a
-//         fresh accumulator, then (hi + lo) * d_K[pos] is added in fp32;
+// Grid: (context splits, kv heads, sequences).  A CTA covers `chunk` consecutive positions of
+// one kv head of one sequence:
+//   producer (warp 8): per stage of `sp` positions, one TMA tensor copy each of K and V: the box
+//     starts at the 16-byte boundary at or below the head's first byte in the slot and is BOXW
+//     bytes wide (the head's hd/32 Q8_0 blocks plus that lead-in; BOXW / 4 is 4 (mod 8) words,
+//     so eight consecutive rows start in eight different bank quads), `stages`-deep ring,
+//     full / empty mbarriers;
+//   consumers (warps 0-7): warp w takes 16-position tiles w, w + 8, ... of each stage.  Per
+//     tile, with mma.sync.m16n8k16 (f16 in, fp32 accumulate):
+//       S^T[head][pos] = Q . K^T: the A operand holds the group's query rows split in two f16
+//         parts, hi = f16(q) in rows 0-7 and lo = f16(q - hi) in rows 8-15 (q enters at ~22
+//         bits); B = K's int8 codes, exact in f16; each 32-dimension Q8_0 block is two k-steps
+//         into a fresh accumulator, then (hi + lo) * d_K[pos] is added in fp32;
 //       online softmax per head in fp32 (running max / sum, exp2);
 //       O[head][dim] += P' . V: per 32-dimension block b the A operand is P * d_V[pos][b], again
 //         hi / lo f16 in rows 0-7 / 8-15, B = V's int8 codes; O accumulates in fp32.
-//   merge: the warps of a kv head through shared memory, the CTAs of a cluster through
-//     distributed shared memory (CTA rank r merges heads r, r + cl, ...), then, when a sequence
-//     has several clusters, each cluster writes its partial (m, l, o) and the last CTA of each
-//     rank (per-sequence counters, zero at rest) merges the clusters' partials and writes the
-//     output (and, for the decode step, its Q8_0 quantization).
+//   merge: the eight warps' (m, l, o) through shared memory into the CTA's partial, written to
+//     the workspace; the last CTA of a (sequence, kv head) (arrival counter, zero at rest)
+//     computes each head's softmax weights over the splits once, then every output dimension
+//     as one weighted sum over the splits, and writes the output (and, for the decode step, its
+//     Q8_0 quantization).  With one split the CTA writes the output directly.
 // Numerics: products are exact, sums are fp32 in a different order than the reference's
 // sequential loop, and q / P' carry ~22 significant bits: the result matches the reference
 // within fp32-level rounding (the parity tests bound the relative L2 error at 2e-3).
+#include <string.h>
+
+#include <algorithm>
+
 #include "sulimo_common.cuh"
 #include "sulimo_internal.h"
 
 namespace sulimo {
 namespace {
 
-constexpr int AM_CONSUMERS = 8;                    // consumer warps
+constexpr int AM_CONSUMERS = 8;                      // consumer warps
 constexpr int AM_THREADS = (AM_CONSUMERS + 1) * 32;  // + one producer warp
-constexpr size_t AM_SMEM_MAX = 220 * 1024;
-constexpr size_t AM_STAGE_TARGET = 72 * 1024;      // K + V bytes per stage
+constexpr int AM_SP = 16 * AM_CONSUMERS;             // positions per stage: one tile per warp
+constexpr int AM_MAX_STAGES = 4;
+constexpr int AM_MAX_SPLITS = 32;   // splits per (sequence, kv head): the final merge reads
+                                    // each output dimension's partials in one batch
+constexpr size_t AM_SMEM_MAX = 200 * 1024;
 constexpr float AM_LOG2E = 1.4426950408889634f;
 
 struct AttnMmaArgs {
     const float* q;         // [batch][H][HD] fp32
-    const uint8_t* kring;   // ring of sequence s at kring + s * seq_stride
-    const uint8_t* vring;
-    size_t seq_stride;
-    size_t capacity;        // ring slots
-    size_t ctx_len;         // positions 0 .. ctx_len-1, slot p % capacity
-    int H, Hkv, G, wph;     // query heads, kv heads, H / Hkv, consumer warps per kv head
+    size_t ctx_len;         // positions 0 .. ctx_len-1 (<= capacity: slot = position)
+    size_t static_before;   // positions < this are not written by the previous kernel
+    int H, Hkv, G;          // query heads, kv heads, H / Hkv
     int chunk;              // positions per CTA
-    int sp;                 // positions per stage
     int stages;
-    int cl;                 // CTAs per cluster
-    uint32_t bpp;           // ring bytes per slot (all kv heads)
-    uint32_t rs;            // shared-memory bytes per staged slot
+    int boxw;               // bytes per staged row
     float sm_scale;         // 1 / sqrt(hd)
     float softcap;          // <= 0: none
     float* out;             // [batch][H][HD] or null
     uint8_t* q8;            // [batch][H * HD / 32] Q8_0 blocks or null
-    float* part;            // [batch][clusters][H][HD + 2]
-    unsigned* counters;     // [batch][cl]
+    float* part;            // [batch][Hkv][splits][G][HD + 2]
+    unsigned* counters;     // [batch][Hkv]
     int* err;
 };
 
@@ -96,30 +98,6 @@ __device__ __forceinline__ void mma_16816(float* c, const uint32_t* a, uint32_t 
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// shared-memory address of `p` in CTA `rank` of this cluster
-__device__ __forceinline__ uint32_t map_rank(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-    return r;
-}
-
-__device__ __forceinline__ float ld_cluster(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
 }
 
 // Merge of n partials (m_i, l_i, o_i[d]) held as [HD + 2] float rows:
@@ -162,21 +140,27 @@ __device__ __forceinline__ void merge_rows(int n, int d, Read rd, float* o_out, 
 
 template <int HD>
 __global__ void __launch_bounds__(AM_THREADS, 1)
-    attn_decode_mma_kernel(const __grid_constant__ AttnMmaArgs a) {
+    attn_decode_mma_kernel(const __grid_constant__ AttnMmaArgs a,
+                           const __grid_constant__ CUtensorMap tmap_k,
+                           const __grid_constant__ CUtensorMap tmap_v) {
     constexpr int NB = HD / 32, HB = NB * 34, KS = HD / 16, NT = HD / 8;
+    constexpr int HD2 = HD + 2;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
-    const uint32_t stage_bytes = 2u * (uint32_t)a.sp * a.rs;
+    const uint32_t rs = (uint32_t)a.boxw;
+    const uint32_t stage_bytes = 2u * AM_SP * rs;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.stages * stage_bytes);
     uint64_t* empty = full + a.stages;
     int* last_flag = reinterpret_cast<int*>(empty + a.stages);
 
-    const int split = blockIdx.x, seq = blockIdx.y;
+    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z, splits = gridDim.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, tig = lane & 3;
     const size_t p0 = (size_t)split * a.chunk;
     const int np = p0 < a.ctx_len ? (int)min((size_t)a.chunk, a.ctx_len - p0) : 0;
-    const int nstage = (np + a.sp - 1) / a.sp;
+    const int nstage = (np + AM_SP - 1) / AM_SP;
+    const int x0 = (kvh * HB) & ~15;           // TMA x coordinate: 16-byte aligned
+    const int off = kvh * HB - x0;             // the head's first byte inside a staged row
 
     if (tid == 0) {
         for (int s = 0; s < a.stages; s++) {
@@ -184,48 +168,43 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
             mbar_init(&empty[s], AM_CONSUMERS);
         }
         fence_barrier_init();
+        prefetch_tensormap(&tmap_k);
+        prefetch_tensormap(&tmap_v);
     }
     __syncthreads();
-    // q and the ring's newest slot are written by the previous kernel of the step
     pdl_launch_dependents();
+    // Stages whose positions all lie below static_before (in a decode step: every slot but the
+    // newest) are not written by the previous kernel: their copies start before the wait, so
+    // the context streams in while the previous kernels of the step still run.
+    int early = 0;
+    if (warp == AM_CONSUMERS && lane == 0) {
+        while (early < nstage && early < a.stages &&
+               p0 + (size_t)min(np, (early + 1) * AM_SP) <= a.static_before) {
+            uint8_t* dk = smem + (size_t)early * stage_bytes;
+            mbar_arrive_expect_tx(&full[early], stage_bytes);
+            const int y = (int)(p0 + (size_t)early * AM_SP);
+            tma_load_3d(dk, &tmap_k, x0, y, seq, &full[early]);
+            tma_load_3d(dk + (size_t)AM_SP * rs, &tmap_v, x0, y, seq, &full[early]);
+            early++;
+        }
+    }
+    // q and the ring's newest slot are written by the previous kernel of the step
     pdl_wait_prerequisites();
 
     if (warp == AM_CONSUMERS) {
         // ------------------------------ producer ------------------------------
-        const uint8_t* kseq = a.kring + (size_t)seq * a.seq_stride;
-        const uint8_t* vseq = a.vring + (size_t)seq * a.seq_stride;
-        for (int st = 0; st < nstage; st++) {
-            const int s = st % a.stages;
-            if (st >= a.stages &&
-                !mbar_wait_bounded(&empty[s], (uint32_t)((st / a.stages) - 1) & 1u, a.err,
-                                   nullptr))
-                break;
-            const int q0 = st * a.sp;
-            const int n = min(a.sp, np - q0);
-            uint8_t* dk = smem + (size_t)s * stage_bytes;
-            uint8_t* dv = dk + (size_t)a.sp * a.rs;
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)n * a.bpp);
-            __syncwarp();
-            if (a.rs == a.bpp) {
-                // contiguous rows: at most two runs per tensor (the ring may wrap inside)
-                if (lane == 0) {
-                    const size_t s0 = (p0 + q0) % a.capacity;
-                    const int n1 = (int)min((size_t)n, a.capacity - s0);
-                    bulk_load(dk, kseq + s0 * a.bpp, (uint32_t)n1 * a.bpp, &full[s]);
-                    bulk_load(dv, vseq + s0 * a.bpp, (uint32_t)n1 * a.bpp, &full[s]);
-                    if (n1 < n) {
-                        bulk_load(dk + (size_t)n1 * a.rs, kseq, (uint32_t)(n - n1) * a.bpp,
-                                  &full[s]);
-                        bulk_load(dv + (size_t)n1 * a.rs, vseq, (uint32_t)(n - n1) * a.bpp,
-                                  &full[s]);
-                    }
-                }
-            } else {
-                for (int i = lane; i < n; i += 32) {
-                    const size_t slot = (p0 + q0 + i) % a.capacity;
-                    bulk_load(dk + (size_t)i * a.rs, kseq + slot * a.bpp, a.bpp, &full[s]);
-                    bulk_load(dv + (size_t)i * a.rs, vseq + slot * a.bpp, a.bpp, &full[s]);
-                }
+        if (lane == 0) {
+            for (int st = early; st < nstage; st++) {
+                const int s = st % a.stages;
+                if (st >= a.stages &&
+                    !mbar_wait_bounded(&empty[s], (uint32_t)((st / a.stages) - 1) & 1u, a.err,
+                                       nullptr))
+                    break;
+                uint8_t* dk = smem + (size_t)s * stage_bytes;
+                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                const int y = (int)(p0 + (size_t)st * AM_SP);
+                tma_load_3d(dk, &tmap_k, x0, y, seq, &full[s]);
+                tma_load_3d(dk + (size_t)AM_SP * rs, &tmap_v, x0, y, seq, &full[s]);
             }
         }
     }
@@ -235,7 +214,6 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
     float m_run = -INFINITY, l_run = 0.0f;
 #pragma unroll
     for (int n = 0; n < NT; n++) oc[n][0] = oc[n][1] = oc[n][2] = oc[n][3] = 0.0f;
-    const int kvh = warp % a.Hkv, wj = warp / a.Hkv;
     if (warp < AM_CONSUMERS) {
         // query fragments: row g = f16(q) of head g of this kv head's group, row g + 8 = the
         // f16 remainder; columns 2*tig, 2*tig + 1 (+8) of each 16-dimension k-step
@@ -248,15 +226,14 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
 #pragma unroll
                 for (int hf = 0; hf < 2; hf++) {
                     const int d = ks * 16 + hf * 8 + 2 * tig;
-                    const float x0 = hv ? qh[d] : 0.0f, x1 = hv ? qh[d + 1] : 0.0f;
-                    const __half2 hi = __floats2half2_rn(x0, x1);
+                    const float x0f = hv ? qh[d] : 0.0f, x1f = hv ? qh[d + 1] : 0.0f;
+                    const __half2 hi = __floats2half2_rn(x0f, x1f);
                     const float2 hf2 = __half22float2(hi);
-                    const __half2 lo = __floats2half2_rn(x0 - hf2.x, x1 - hf2.y);
+                    const __half2 lo = __floats2half2_rn(x0f - hf2.x, x1f - hf2.y);
                     qa[ks][2 * hf] = h2_bits(hi);
                     qa[ks][2 * hf + 1] = h2_bits(lo);
                 }
         }
-        const float score_scale = a.sm_scale;
         const bool capped = a.softcap > 0.0f;
         for (int st = 0; st < nstage; st++) {
             const int s = st % a.stages;
@@ -264,19 +241,19 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
             const bool landed = __all_sync(
                 0xffffffffu,
                 mbar_wait_bounded(&full[s], (uint32_t)(st / a.stages) & 1u, a.err, nullptr));
-            const int q0 = st * a.sp;
-            const uint8_t* kst = smem + (size_t)s * stage_bytes + kvh * HB;
-            const uint8_t* vst = kst + (size_t)a.sp * a.rs;
-            for (int t = wj * 16; landed && t < a.sp && q0 + t < np; t += a.wph * 16) {
+            const int q0 = st * AM_SP;
+            const uint8_t* kst = smem + (size_t)s * stage_bytes + off;
+            const uint8_t* vst = kst + (size_t)AM_SP * rs;
+            for (int t = warp * 16; landed && t < AM_SP && q0 + t < np; t += AM_CONSUMERS * 16) {
                 const int valid = np - (q0 + t);  // rows of this tile that hold positions
-                const uint8_t* kt = kst + (size_t)t * a.rs;
-                const uint8_t* vt = vst + (size_t)t * a.rs;
+                const uint8_t* kt = kst + (size_t)t * rs;
+                const uint8_t* vt = vst + (size_t)t * rs;
                 // ---- scores: two 8-position n-tiles ----
                 float x[4];
 #pragma unroll
                 for (int nt = 0; nt < 2; nt++) {
-                    const uint8_t* krow = kt + (size_t)(nt * 8 + g) * a.rs;
-                    const uint8_t* srow = kt + (size_t)(nt * 8 + 2 * tig) * a.rs;
+                    const uint8_t* krow = kt + (size_t)(nt * 8 + g) * rs;
+                    const uint8_t* srow = kt + (size_t)(nt * 8 + 2 * tig) * rs;
                     float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
                     for (int b = 0; b < NB; b++) {
@@ -288,11 +265,11 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
                                       s8pair_to_h2(lds_u16(p + 8)));
                         }
                         s0 = __fmaf_rn(c[0] + c[2], lds_f16(srow + b * 34), s0);
-                        s1 = __fmaf_rn(c[1] + c[3], lds_f16(srow + a.rs + b * 34), s1);
+                        s1 = __fmaf_rn(c[1] + c[3], lds_f16(srow + rs + b * 34), s1);
                     }
 #pragma unroll
                     for (int j = 0; j < 2; j++) {
-                        float v = (j ? s1 : s0) * score_scale;
+                        float v = (j ? s1 : s0) * a.sm_scale;
                         if (capped) v = tanhf(v / a.softcap) * a.softcap;
                         x[nt * 2 + j] = (nt * 8 + 2 * tig + j < valid) ? v : -INFINITY;
                     }
@@ -324,14 +301,14 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
                     }
                 }
                 // ---- O += P' . V, per 32-dimension block ----
-                const uint8_t* v0 = vt + (size_t)(2 * tig) * a.rs;  // rows 2tig, +1, +8, +9
+                const uint8_t* v0 = vt + (size_t)(2 * tig) * rs;  // rows 2tig, +1, +8, +9
 #pragma unroll
                 for (int b = 0; b < NB; b++) {
                     float pp[4];
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         const int row = (i >> 1) * 8 + (i & 1);
-                        pp[i] = p[i] != 0.0f ? p[i] * lds_f16(v0 + (size_t)row * a.rs + b * 34)
+                        pp[i] = p[i] != 0.0f ? p[i] * lds_f16(v0 + (size_t)row * rs + b * 34)
                                              : 0.0f;
                     }
                     uint32_t A[4];
@@ -348,8 +325,8 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
 #pragma unroll
                     for (int n4 = 0; n4 < 4; n4++) {
                         const uint8_t* col = v0 + b * 34 + 2 + n4 * 8 + g;
-                        const uint32_t b0 = s8two_to_h2(col[0], col[a.rs]);
-                        const uint32_t b1 = s8two_to_h2(col[(size_t)8 * a.rs], col[(size_t)9 * a.rs]);
+                        const uint32_t b0 = s8two_to_h2(col[0], col[rs]);
+                        const uint32_t b1 = s8two_to_h2(col[(size_t)8 * rs], col[(size_t)9 * rs]);
                         mma_16816(oc[b * 4 + n4], A, b0, b1);
                     }
                 }
@@ -360,10 +337,8 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
     }
     __syncthreads();  // every stage consumed: the stage memory becomes the merge area
 
-    // ---- this warp's (m, l, o) per head -> wpart[warp][g][HD + 2] ----
-    const int HD2 = HD + 2;
+    // ---- the warps' (m, l, o) per head -> wpart[warp][g][HD + 2] -> the CTA partial ----
     float* wpart = reinterpret_cast<float*>(smem);
-    float* cpart = wpart + (size_t)AM_CONSUMERS * a.G * HD2;  // [H][HD + 2]
     if (warp < AM_CONSUMERS) {
         float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
         l_tot += __shfl_xor_sync(0xffffffffu, l_tot, 2);
@@ -381,37 +356,19 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
         }
     }
     __syncthreads();
-    // ---- the warps of each kv head -> the CTA's partial per query head ----
-    for (int it = tid; it < a.H * HD2; it += AM_THREADS) {
-        const int h = it / HD2, d = it - h * HD2;
-        const int kv = h / a.G, gg = h - kv * a.G;
-        auto rd = [&](int i, int dd) {
-            return wpart[((size_t)(kv + i * a.Hkv) * a.G + gg) * HD2 + dd];
-        };
-        float o, l, m;
-        merge_rows<HD>(a.wph, d < HD ? d : HD, rd, &o, &l, &m);
-        cpart[(size_t)h * HD2 + d] = d < HD ? o : (d == HD ? m : l);
-    }
-    cluster_sync_all();  // every CTA of the cluster has its partials in shared memory
-
-    // ---- the cluster's CTAs -> heads r, r + cl, ... merged by CTA rank r ----
-    const uint32_t rank = cluster_rank();
-    const int nclusters = (int)gridDim.x / a.cl, cid = (int)blockIdx.x / a.cl;
-    const bool direct = nclusters == 1;  // the cluster holds the whole sequence
-    // items (owned head, d), d in [0, HDP): the output dimensions, then m and l; HDP is a
-    // multiple of 32 so that every warp's 32 dimensions are one Q8_0 block of one head
+    const bool direct = splits == 1;
+    float* dst_part = a.part + (((size_t)seq * a.Hkv + kvh) * splits + split) * a.G * HD2;
+    // items (g, d), d in [0, HD + 32): dimensions, then m and l; warps align to Q8_0 blocks
     constexpr int HDP = HD + 32;
-    const int owned = ((int)a.H - (int)rank + a.cl - 1) / a.cl;
-    for (int it = tid; it < owned * HDP; it += AM_THREADS) {
-        const int h = (int)rank + (it / HDP) * a.cl, d = it % HDP;
-        if (d >= HD2) continue;  // whole warps: HDP - HD2 >= 30 idle lanes sit past HD2
-        auto rd = [&](int i, int dd) {
-            return ld_cluster(map_rank(cpart + (size_t)h * HD2 + dd, (uint32_t)i));
-        };
+    for (int it = tid; it < a.G * HDP; it += AM_THREADS) {
+        const int gg = it / HDP, d = it % HDP;
+        if (d >= HD2) continue;
+        auto rd = [&](int i, int dd) { return wpart[((size_t)i * a.G + gg) * HD2 + dd]; };
         float o, l, m;
-        merge_rows<HD>(a.cl, d < HD ? d : HD, rd, &o, &l, &m);
+        merge_rows<HD>(AM_CONSUMERS, d < HD ? d : HD, rd, &o, &l, &m);
         if (direct) {
             if (d < HD) {
+                const size_t h = (size_t)kvh * a.G + gg;
                 const float val = l > 0.0f ? o / l : 0.0f;
                 if (a.out) a.out[((size_t)seq * a.H + h) * HD + d] = val;
                 if (a.q8)
@@ -419,101 +376,130 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
                                         lane);
             }
         } else {
-            float* dst = a.part + (((size_t)seq * nclusters + cid) * a.H + h) * HD2;
-            dst[d] = d < HD ? o : (d == HD ? m : l);
+            dst_part[(size_t)gg * HD2 + d] = d < HD ? o : (d == HD ? m : l);
         }
     }
-    cluster_sync_all();  // no CTA leaves while a peer still reads its shared memory
     if (direct) return;
 
-    // ---- the last CTA of each rank merges the clusters' partials of its heads ----
+    // ---- the last CTA of this (sequence, kv head) merges the splits ----
+    __threadfence();  // this thread's partial before the arrival count
     __syncthreads();
     if (tid == 0) {
+        const unsigned old = atomicAdd(a.counters + (size_t)seq * a.Hkv + kvh, 1u);
+        *last_flag = old == (unsigned)(splits - 1);
         __threadfence();
-        unsigned* ctr = a.counters + (size_t)seq * a.cl + rank;
-        const unsigned old = atomicAdd(ctr, 1u);
-        *last_flag = old == (unsigned)(nclusters - 1);
-        if (*last_flag) __threadfence();
     }
     __syncthreads();
     if (!*last_flag) return;
-    for (int it = tid; it < owned * HDP; it += AM_THREADS) {
-        const int h = (int)rank + (it / HDP) * a.cl, d = it % HDP;
-        if (d >= HD) continue;
-        const float* base = a.part + ((size_t)seq * nclusters * a.H + h) * HD2;
-        auto rd = [&](int i, int dd) { return __ldcg(base + (size_t)i * a.H * HD2 + dd); };
-        float o, l, m;
-        merge_rows<HD>(nclusters, d, rd, &o, &l, &m);
-        const float val = l > 0.0f ? o / l : 0.0f;
-        if (a.out) a.out[((size_t)seq * a.H + h) * HD + d] = val;
-        if (a.q8)
-            quantize_block_warp(val, a.q8 + (((size_t)seq * a.H + h) * NB + d / 32) * 34, lane);
+    const float* base = a.part + ((size_t)seq * a.Hkv + kvh) * splits * a.G * HD2;
+    // softmax weights of every split per head, w[g][s] = e^(m_s - M) / L: (m, l) of all splits
+    // loaded in one pass, then one warp per head
+    float* wts = reinterpret_cast<float*>(smem);          // [G][splits]
+    float* lsum = wts + (size_t)a.G * AM_MAX_SPLITS;      // [G][splits]
+    for (int i = tid; i < a.G * splits; i += AM_THREADS) {
+        const int gg = i / splits, sp = i % splits;
+        const float* r = base + ((size_t)sp * a.G + gg) * HD2 + HD;
+        wts[i] = __ldcg(r);
+        lsum[i] = __ldcg(r + 1);
     }
-    if (tid == 0) a.counters[(size_t)seq * a.cl + rank] = 0u;  // zero at rest for the next call
+    __syncthreads();
+    if (warp < a.G) {
+        float* wg = wts + (size_t)warp * splits;
+        const float* lg = lsum + (size_t)warp * splits;
+        float M = -INFINITY;
+        for (int sp = lane; sp < splits; sp += 32) M = fmaxf(M, wg[sp]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f;
+        for (int sp = lane; sp < splits; sp += 32) {
+            const float mi = wg[sp];
+            const float e = (mi == -INFINITY) ? 0.0f : exp2f((mi - M) * AM_LOG2E);
+            L = __fmaf_rn(lg[sp], e, L);
+            wg[sp] = e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        __syncwarp();
+        for (int sp = lane; sp < splits; sp += 32) wg[sp] *= inv;
+    }
+    __syncthreads();
+    // every output dimension: one weighted sum over the splits, all loads issued first
+    for (int it = tid; it < a.G * HD; it += AM_THREADS) {
+        const int gg = it / HD, d = it % HD;
+        const float* wg = wts + (size_t)gg * splits;
+        const float* col = base + (size_t)gg * HD2 + d;
+        const size_t sstride = (size_t)a.G * HD2;
+        float acc = 0.0f;
+        for (int s0 = 0; s0 < splits; s0 += 32) {
+            float o[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                o[j] = s0 + j < splits ? __ldcg(col + (size_t)(s0 + j) * sstride) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (s0 + j < splits) acc = __fmaf_rn(o[j], wg[s0 + j], acc);
+        }
+        const size_t h = (size_t)kvh * a.G + gg;
+        if (a.out) a.out[((size_t)seq * a.H + h) * HD + d] = acc;
+        if (a.q8) quantize_block_warp(acc, a.q8 + (((size_t)seq * a.H + h) * NB + d / 32) * 34, lane);
+    }
+    if (tid == 0) a.counters[(size_t)seq * a.Hkv + kvh] = 0u;  // zero at rest for the next call
 }
 
 struct MmaPlan {
-    int wph, sp, stages, cl, chunk, splits, nclusters;
-    uint32_t rs;
+    int splits, chunk, stages, boxw;
     size_t smem;
 };
 
 // Geometry of the tensor-core form, or false when it does not apply (the caller falls back to
-// the scalar kernels).
+// the scalar kernels): hd 64 / 128, at most 8 query heads per kv head, 16-byte slots and ring
+// bases, a context inside the ring (positions are slots), and at least 8 (kv head, sequence)
+// pairs.  With fewer pairs (Qwen2.5-1.5B's 2 kv heads at batch 1) the context splits 16+ ways
+// per head and the merge's latency outweighs the tensor cores: the slot form of the scalar
+// kernel, one CTA per split over all kv heads, is faster there (config 3 decode: 1.03 against
+// 1.28 ms per token).
 bool mma_plan(size_t ctx_len, size_t capacity, int H, int Hkv, int HD, int batch, int num_sms,
               size_t seq_stride, const void* k, const void* v, MmaPlan* pl) {
     if (HD != 64 && HD != 128) return false;
-    if (Hkv < 1 || Hkv > AM_CONSUMERS || AM_CONSUMERS % Hkv != 0 || H % Hkv != 0) return false;
-    const int G = H / Hkv;
-    if (G < 1 || G > 8) return false;
-    const size_t bpp = (size_t)Hkv * (HD / 32) * 34;
+    if (Hkv < 1 || H % Hkv != 0 || H / Hkv > 8 || Hkv > 65535) return false;
+    if ((size_t)Hkv * batch < 8) return false;
+    const size_t HB = (size_t)(HD / 32) * 34, bpp = (size_t)Hkv * HB;
     if (bpp % 16 || ((uintptr_t)k % 16) || ((uintptr_t)v % 16)) return false;
     if (batch > 1 && seq_stride % 16) return false;
-    if (ctx_len < 1 || capacity < 1 || batch < 1 || batch > 65535) return false;
-    uint32_t rs = (uint32_t)bpp;
-    while (((rs / 4) % 32) % 8 != 4) rs += 16;  // eight rows in eight different bank quads
-    pl->rs = rs;
-    pl->wph = AM_CONSUMERS / Hkv;
-    int tpw = (int)(AM_STAGE_TARGET / (2u * 16u * pl->wph * rs));
-    if (tpw < 1) tpw = 1;
-    pl->sp = 16 * pl->wph * tpw;
-    const size_t stage = 2u * (size_t)pl->sp * rs;
-    pl->stages = (int)((AM_SMEM_MAX - 1024) / stage);
-    if (pl->stages > 3) pl->stages = 3;
+    if (ctx_len < 1 || ctx_len > capacity || capacity > 0x7fffffff || batch < 1 ||
+        batch > 65535)
+        return false;
+    int lead = 0;
+    for (int h = 0; h < Hkv && h < 16; h++) lead = std::max(lead, (int)((h * HB) % 16));
+    int boxw = (int)((lead + HB + 15) / 16 * 16);
+    while ((boxw / 4) % 8 != 4) boxw += 16;  // eight rows in eight different bank quads
+    if (boxw > 256) return false;
+    pl->boxw = boxw;
+    const size_t stage = 2u * AM_SP * boxw;
+    pl->stages = (int)((AM_SMEM_MAX - 512) / stage);
+    if (pl->stages > AM_MAX_STAGES) pl->stages = AM_MAX_STAGES;
     if (pl->stages < 1) return false;
-    // merge area (inside the stage memory): per-warp and per-CTA partials
-    const size_t merge = ((size_t)AM_CONSUMERS * G + H) * (HD + 2) * 4;
-    if (merge > (size_t)pl->stages * stage) return false;
-    pl->smem = (size_t)pl->stages * stage + 2 * 8 * pl->stages + 16 + 128;
-    // one CTA per SM over all sequences; chunks of whole 16-position tiles per warp
-    const int unit = 16 * pl->wph;
-    size_t target = (size_t)num_sms / batch;
+    const size_t G = (size_t)(H / Hkv);
+    if ((size_t)AM_CONSUMERS * G * (HD + 2) * 4 > (size_t)pl->stages * stage) return false;
+    pl->smem = (size_t)pl->stages * stage + 16 * pl->stages + 16 + 128;
+    // about one CTA per SM over all (kv head, sequence) pairs; chunks of whole tiles
+    size_t target = (size_t)num_sms / ((size_t)Hkv * batch);
     if (target < 1) target = 1;
+    if (target > AM_MAX_SPLITS) target = AM_MAX_SPLITS;
     size_t chunk = (ctx_len + target - 1) / target;
-    chunk = (chunk + unit - 1) / unit * unit;
-    if (chunk < (size_t)unit) chunk = unit;
-    if (chunk > 0x3fffffff) return false;
+    chunk = (chunk + 15) / 16 * 16;
     const size_t splits = (ctx_len + chunk - 1) / chunk;
-    int best = 1;
-    size_t best_waste = (size_t)-1;
-    for (int c = 8; c >= 1; c >>= 1) {  // the cluster size wasting the fewest idle CTAs
-        const size_t padded = (splits + c - 1) / c * c;
-        if (padded - splits < best_waste) {
-            best_waste = padded - splits;
-            best = c;
-        }
-    }
-    pl->cl = best;
+    if (splits > AM_MAX_SPLITS || G * AM_MAX_SPLITS * 8 > (size_t)pl->stages * stage)
+        return false;
     pl->chunk = (int)chunk;
-    const size_t padded = (splits + best - 1) / best * best;
-    if (padded > 0x7fffffff) return false;
-    pl->splits = (int)padded;
-    pl->nclusters = pl->splits / pl->cl;
+    pl->splits = (int)splits;
     return true;
 }
 
 template <int HD>
-int launch_mma_hd(sulimo_ctx* ctx, const AttnMmaArgs& args, const MmaPlan& pl, int batch) {
+int launch_mma_hd(sulimo_ctx* ctx, const AttnMmaArgs& args, const MmaPlan& pl, int batch,
+                  const CUtensorMap& tk, const CUtensorMap& tv) {
     static DeviceBits attr_done;
     if (!attr_done.test(ctx->device)) {
         int st = check_cuda(cudaFuncSetAttribute(attn_decode_mma_kernel<HD>,
@@ -523,21 +509,10 @@ int launch_mma_hd(sulimo_ctx* ctx, const AttnMmaArgs& args, const MmaPlan& pl, i
         if (st) return st;
         attr_done.set(ctx->device);
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)pl.splits, (unsigned)batch, 1);
-    cfg.blockDim = dim3(AM_THREADS);
-    cfg.dynamicSmemBytes = pl.smem;
-    cfg.stream = ctx->stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = (unsigned)pl.cl;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_mma_kernel<HD>, args);
+    const cudaError_t e =
+        launch_pdl(attn_decode_mma_kernel<HD>, dim3((unsigned)pl.splits, (unsigned)args.Hkv,
+                                                    (unsigned)batch),
+                   dim3(AM_THREADS), pl.smem, ctx->stream, args, tk, tv);
     ctx->launches++;
     return check_cuda(e, "attn_decode_mma launch");
 }
@@ -549,7 +524,7 @@ size_t attn_decode_mma_partial_bytes(size_t ctx_len, size_t capacity, int H, int
                                      const void* v) {
     MmaPlan pl;
     if (!mma_plan(ctx_len, capacity, H, Hkv, HD, batch, num_sms, seq_stride, k, v, &pl)) return 0;
-    return (size_t)batch * pl.nclusters * H * (HD + 2) * sizeof(float);
+    return (size_t)batch * H * pl.splits * (HD + 2) * sizeof(float);
 }
 
 int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
@@ -557,32 +532,41 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
                            size_t context_len, int head_count, int head_count_kv, int head_dim,
                            int batch, float softcap, float* out, float* partials,
                            size_t partial_bytes, unsigned* counters, uint8_t* out_q8,
-                           bool* used) {
+                           bool* used, size_t static_before) {
     *used = false;
     MmaPlan pl;
-    if (!counters ||
+    if (!counters || (size_t)batch * head_count_kv > ATTN_COUNTERS ||
         !mma_plan(context_len, capacity, head_count, head_count_kv, head_dim, batch, ctx->num_sms,
                   seq_stride, k_ring, v_ring, &pl))
         return SULIMO_OK;
-    const size_t need = (size_t)batch * pl.nclusters * head_count * (head_dim + 2) * sizeof(float);
-    if (need > partial_bytes) return SULIMO_OK;
+    const size_t need = (size_t)batch * head_count * pl.splits * (head_dim + 2) * sizeof(float);
+    if (pl.splits > 1 && need > partial_bytes) return SULIMO_OK;
+    const size_t bpp = (size_t)head_count_kv * (head_dim / 32) * 34;
+    const size_t stride = batch > 1 ? seq_stride : bpp * capacity;
+    CUtensorMap tk, tv;
+    memset(&tk, 0, sizeof(tk));
+    memset(&tv, 0, sizeof(tv));
+    {
+        const uint64_t dims[3] = {(uint64_t)bpp, (uint64_t)capacity, (uint64_t)batch};
+        const uint64_t strides[2] = {(uint64_t)bpp, (uint64_t)stride};
+        const uint32_t box[3] = {(uint32_t)pl.boxw, (uint32_t)AM_SP, 1};
+        int st = encode_tensor_map(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_ring, 3, dims, strides,
+                                   box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!st)
+            st = encode_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, v_ring, 3, dims, strides,
+                                   box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
     AttnMmaArgs args;
     args.q = q;
-    args.kring = reinterpret_cast<const uint8_t*>(k_ring);
-    args.vring = reinterpret_cast<const uint8_t*>(v_ring);
-    args.seq_stride = batch > 1 ? seq_stride : 0;
-    args.capacity = capacity;
     args.ctx_len = context_len;
+    args.static_before = static_before;
     args.H = head_count;
     args.Hkv = head_count_kv;
     args.G = head_count / head_count_kv;
-    args.wph = pl.wph;
     args.chunk = pl.chunk;
-    args.sp = pl.sp;
     args.stages = pl.stages;
-    args.cl = pl.cl;
-    args.bpp = (uint32_t)((size_t)head_count_kv * (head_dim / 32) * 34);
-    args.rs = pl.rs;
+    args.boxw = pl.boxw;
     args.sm_scale = 1.0f / sqrtf((float)head_dim);
     args.softcap = softcap;
     args.out = out;
@@ -591,8 +575,8 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
     args.counters = counters;
     args.err = ctx->d_error;
     *used = true;
-    return head_dim == 64 ? launch_mma_hd<64>(ctx, args, pl, batch)
-                          : launch_mma_hd<128>(ctx, args, pl, batch);
+    return head_dim == 64 ? launch_mma_hd<64>(ctx, args, pl, batch, tk, tv)
+                          : launch_mma_hd<128>(ctx, args, pl, batch, tk, tv);
 }
 
 }  // namespace sulimo

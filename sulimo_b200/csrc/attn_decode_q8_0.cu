@@ -860,16 +860,15 @@ size_t attn_decode_partial_bytes(size_t context_len, size_t capacity, int head_c
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
-                       float* partials, size_t partial_bytes, uint8_t* out_q8) {
+                       float* partials, size_t partial_bytes, uint8_t* out_q8,
+                       size_t static_before) {
     // the tensor-core kernel where its geometry applies; the scalar kernels otherwise
-    if ((size_t)batch * 8 <= ATTN_COUNTERS) {
-        bool used = false;
-        const int st = launch_attn_decode_mma(ctx, q, k_ring, v_ring, seq_stride, capacity,
-                                              context_len, head_count, head_count_kv, head_dim,
-                                              batch, softcap, out, partials, partial_bytes,
-                                              ctx->attn_counters, out_q8, &used);
-        if (st || used) return st;
-    }
+    bool used = false;
+    const int st = launch_attn_decode_mma(ctx, q, k_ring, v_ring, seq_stride, capacity,
+                                          context_len, head_count, head_count_kv, head_dim,
+                                          batch, softcap, out, partials, partial_bytes,
+                                          ctx->attn_counters, out_q8, &used, static_before);
+    if (st || used) return st;
     const int splits = attn_decode_splits(context_len, capacity, head_count, head_count_kv,
                                           head_dim, batch, ctx->num_sms, seq_stride, k_ring,
                                           v_ring);

@@ -610,10 +610,11 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
         // attention, its output quantized to Q8_0 in the merge kernel (the o projection's input)
+        // every ring slot but the newest (written by qkv_rope_store) is static during the step
         if ((st = launch_attn_decode(ctx, s.q, L.k_ring, L.v_ring, m->kv_seq_stride,
                                      m->kv_capacity, ctx_len, H, Hkv, hd, batch, m->attn_softcap,
                                      nullptr, reinterpret_cast<float*>(ctx->workspace),
-                                     ctx->workspace_bytes, s.q8)) ||
+                                     ctx->workspace_bytes, s.q8, pos)) ||
             (st = gemv_fast_static(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
             return st;
         {  // FFN norm (x += o), then gate and up in one launch

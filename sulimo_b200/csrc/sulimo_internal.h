@@ -154,14 +154,15 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
                            size_t context_len, int head_count, int head_count_kv, int head_dim,
                            int batch, float softcap, float* out, float* partials,
                            size_t partial_bytes, unsigned* counters, uint8_t* out_q8,
-                           bool* used);
+                           bool* used, size_t static_before = 0);
 size_t attn_decode_mma_partial_bytes(size_t ctx_len, size_t capacity, int H, int Hkv, int HD,
                                      int batch, int num_sms, size_t seq_stride, const void* k,
                                      const void* v);
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
-                       float* partials, size_t partial_bytes, uint8_t* out_q8 = nullptr);
+                       float* partials, size_t partial_bytes, uint8_t* out_q8 = nullptr,
+                       size_t static_before = 0);
 int launch_unshard_rows(sulimo_ctx* ctx, const void* gathered, void* out, int world,
                         int m_tokens, size_t fs, size_t f, int elem_size);
 size_t forward_scratch_bytes(const sulimo_model_desc* m, int batch);
