@@ -380,7 +380,9 @@ def run_secondary(ctx, hbm):
         out[name] = {"us_per_launch": round(us, 2), "GBps": round(alg / us / 1e3, 1),
                      "frac_of_measured_hbm": round(alg / us / 1e3 / hbm, 3),
                      "alg_bytes": alg, "l2": f"{copies} rotated weight copies",
-                     "mode": "fast (exact block sums, fp32 lane tree)" if fast
+                     "mode": ("fast, tensor-core form (exact block sums, fp32 block-order "
+                              "accumulation)" if batch > 1 else
+                              "fast (exact block sums, fp32 lane tree)") if fast
                              else "bit-exact AVX2 order"}
 
     gemv_case(8960, 1536, 1, "gemv_config1_8960x1536_b1")
@@ -393,6 +395,7 @@ def run_secondary(ctx, hbm):
     gemv_case(8960, 1536, 1, "gemv_config1_8960x1536_b1_fast", static=True, fast=True)
     gemv_case(151936, 1536, 1, "gemv_lm_head_151936x1536_b1_fast", static=True, fast=True)
     gemv_case(8192, 3072, 8, "gemv_ffn_8192x3072_b8_fast", static=True, fast=True)
+    gemv_case(8192, 3072, 32, "gemv_ffn_8192x3072_b32_fast", static=True, fast=True)
 
     # decode attention, Llama-3.2-3B geometry at ctx 4096, batch 1
     H, Hkv, hd, cap = 24, 8, 128, 4096
@@ -788,9 +791,12 @@ def run_probe(args, local):
     the mean time per launch from CUDA events.  Kernels:
       gemm_up / gemm_down   benchmark config 2's two projections (512 tokens), f16 out;
       gemv_fast / gemv_exact  config 1 (8960 x 1536 Q4_0 x Q8_0, batch 1), fast / AVX2-order;
+      gemv_batched          config 4's gate projection (8192 x 3072) in fast mode for
+                            --probe-batch sequences (the tensor-core form from 2);
       attn                  decode attention, Llama-3.2-3B geometry (24 / 8 heads, hd 128),
                             context 4096, batch 1, random Q8_0 rings;
-      decode_step           one config-4 forward_token at context 4096, batch 1."""
+      decode_step           one config-4 forward_token at context 4096 for --probe-batch
+                            sequences."""
     import numpy as np
     import torch
     import sulimo_b200 as sb
@@ -826,6 +832,16 @@ def run_probe(args, local):
                                          static_weights=True)
             else:
                 sb.dispatch_matvec_q4_0_q8_0(ctx, s[0][0], s[0][1], s[1], rows, cols, s[2])
+    elif kern == "gemv_batched":
+        rows, cols, nb = 8192, 3072, args.probe_batch if args.probe_batch > 1 else 8
+        for _ in range(8):
+            xq = torch.empty(nb * cols // 32 * 34, device="cuda", dtype=torch.uint8)
+            sb.quantize_f32_to_q8_0(ctx, torch.randn(nb * cols, device="cuda", generator=g), xq)
+            sets.append((q4(rows, cols), xq, torch.empty(nb * rows, device="cuda")))
+
+        def launch(s):
+            sb.matvec_q4_0_q8_0_fast(ctx, s[0][0], s[0][1], s[1], rows, cols, s[2], nb,
+                                     static_weights=True)
     elif kern == "attn":
         H, Hkv, hd, cap = 24, 8, 128, 4096
         for _ in range(20):
@@ -844,8 +860,8 @@ def run_probe(args, local):
         from sulimo_b200.model import DecodeModel
         from sulimo_b200.synthetic import LLAMA_3B, make_model_torch
         w = make_model_torch(dict(LLAMA_3B), seed=0, kv_capacity=4096)
-        dm = DecodeModel(ctx, w, batch=1)
-        tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+        dm = DecodeModel(ctx, w, batch=args.probe_batch)
+        tok = torch.zeros(args.probe_batch, dtype=torch.int32, device="cuda")
         sets.append(None)
 
         def launch(s):
@@ -883,15 +899,18 @@ def main():
                     help="--mode decode: sequences per GPU to measure")
     ap.add_argument("--gen-tokens", type=int, default=256,
                     help="--mode generate: greedy decode tokens after the 2048-token prefill")
+    ap.add_argument("--probe-batch", type=int, default=1,
+                    help="sequences per launch for --mode probe (gemv_batched: 8 if 1)")
     ap.add_argument("--kernel", default="attn",
-                    help="--mode probe: gemm_up, gemm_down, gemv_fast, gemv_exact, attn, "
-                         "decode_step")
+                    help="--mode probe: gemm_up, gemm_down, gemv_fast, gemv_exact, "
+                         "gemv_batched, attn, decode_step")
     ap.add_argument("--mode", default="headline",
-                    choices=["headline", "sharded", "decode", "generate", "probe"],
+                    choices=["headline", "sharded", "decode", "generate", "probe", "secondary"],
                     help="headline: the contract line (config 2); sharded: the row-sharded "
                          "lm_head/FFN sweep with an NCCL all-gather; decode: config 4 "
                          "(Llama-3B decode steps); generate: config 3 (Qwen-1.5B prefill + "
-                         "greedy decode); one JSON line per case")
+                         "greedy decode); one JSON line per case; secondary: the decode-side "
+                         "kernel table of the headline line alone")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -906,6 +925,14 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     if args.mode == "probe":
         print(json.dumps(run_probe(args, local)), flush=True)
+        return
+    if args.mode == "secondary":
+        import torch
+        import sulimo_b200 as sb
+        ctx = sb.CudaContext(local, stream=torch.cuda.current_stream())
+        print(json.dumps({"mode": "secondary", "cases": run_secondary(ctx, peaks()[0])}),
+              flush=True)
+        ctx.close()
         return
     if args.mode in ("sharded", "decode", "generate"):
         run = {"sharded": run_sharded, "decode": run_decode, "generate": run_generate}[args.mode]

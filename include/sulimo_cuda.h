@@ -130,6 +130,16 @@ int sulimo_cuda_event_free(sulimo_event* ev);
 int sulimo_cuda_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants,
                               const void* x, void* out, int m, int k, int n, int out_dtype);
 
+/* Exact-weight prefill GEMM — the same operation and arguments as sulimo_cuda_gemm_q4_0_f16  */
+/* (the reference's gemm_q4_0_f16, gemm.rs:28-102, and its scalar oracle gemm.rs:106-147),    */
+/* with every weight d*(q-8) carried exactly into the tensor cores as two f16 parts            */
+/* hi = f16(d*(q-8)) and lo = f16(d*(q-8) - hi), so each product equals the reference's and    */
+/* only the fp32 summation order differs (the bar of crates/sulimo-ocl/tests/test_gemm.rs:    */
+/* 207-214).  Twice the tensor work of sulimo_cuda_gemm_q4_0_f16.                             */
+int sulimo_cuda_gemm_q4_0_f16_exact(sulimo_ctx* ctx, const void* scales, const void* quants,
+                                    const void* x, void* out, int m, int k, int n,
+                                    int out_dtype);
+
 /* Last-token logits — replaces enqueue_logits_final (prefill.rs:300-330): fp32 logits of    */
 /* token row `token_idx` of x_all [*, embd] against a [vocab][embd] Q4_0 matrix.             */
 int sulimo_cuda_logits_final(sulimo_ctx* ctx, const void* x_all, const void* scales,

@@ -112,6 +112,13 @@ def gemm_q4_0_f16(ctx, scales, quants, x, out, m, k, n, out_dtype=OUT_F16):
               _ptr(out), m, k, n, out_dtype)
 
 
+def gemm_q4_0_f16_exact(ctx, scales, quants, x, out, m, k, n, out_dtype=OUT_F16):
+    """gemm_q4_0_f16 with every weight d*(q-8) carried exactly (two f16 parts, twice the MMAs):
+    the products are the reference's, only the fp32 summation order differs."""
+    capi.call("sulimo_cuda_gemm_q4_0_f16_exact", ctx.handle, _ptr(scales), _ptr(quants), _ptr(x),
+              _ptr(out), m, k, n, out_dtype)
+
+
 def logits_final(ctx, x_all, scales, quants, logits, vocab, embd, token_idx):
     """enqueue_logits_final (prefill.rs:300-330)."""
     capi.call("sulimo_cuda_logits_final", ctx.handle, _ptr(x_all), _ptr(scales), _ptr(quants),

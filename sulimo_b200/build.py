@@ -19,12 +19,14 @@ SOURCES = [
     "q8_0.cu",
     "gemv_q4_0_q8_0.cu",
     "gemv_fast_q4_0_q8_0.cu",
+    "gemv_mma_q4_0_q8_0.cu",
     "attn_decode_q8_0.cu",
     "attn_decode_noalloc.cu",
     "attn_decode_mma.cu",
     "matvec_dense.cu",
     "repack_q4_0.cu",
     "gemm_q4_0_tc.cu",
+    "gemm_q4_0_pair.cu",
     "shard.cu",
     "forward.cu",
     "attn_prefill_q8_0.cu",

@@ -54,6 +54,7 @@ SIGNATURES = {
     "sulimo_cuda_event_wait": (_i, [_vp, _u64]),
     "sulimo_cuda_event_free": (_i, [_vp]),
     "sulimo_cuda_gemm_q4_0_f16": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),
+    "sulimo_cuda_gemm_q4_0_f16_exact": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     "sulimo_cuda_logits_final": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
     "sulimo_cuda_gemv_q4_0_q8_0": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "sulimo_cuda_gemv_q4_0_q8_0_static": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),

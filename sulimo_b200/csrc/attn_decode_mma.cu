@@ -60,7 +60,7 @@ struct AttnMmaArgs {
     float sm_scale;         // 1 / sqrt(hd)
     float softcap;          // <= 0: none
     float* out;             // [batch][H][HD] or null
-    uint8_t* q8;            // [batch][H * HD / 32] Q8_0 blocks or null
+    Q8Out q8;               // the output as Q8_0 rows [batch][H * HD] (forms it names)
     float* part;            // [batch][Hkv][splits][G][HD + 2]
     unsigned* counters;     // [batch][Hkv]
     int* err;
@@ -371,9 +371,8 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
                 const size_t h = (size_t)kvh * a.G + gg;
                 const float val = l > 0.0f ? o / l : 0.0f;
                 if (a.out) a.out[((size_t)seq * a.H + h) * HD + d] = val;
-                if (a.q8)
-                    quantize_block_warp(val, a.q8 + (((size_t)seq * a.H + h) * NB + d / 32) * 34,
-                                        lane);
+                if (a.q8.aos || a.q8.codes)
+                    q8_store_block(a.q8, val, (size_t)seq, (int)(h * NB + d / 32), lane);
             }
         } else {
             dst_part[(size_t)gg * HD2 + d] = d < HD ? o : (d == HD ? m : l);
@@ -442,7 +441,7 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
         }
         const size_t h = (size_t)kvh * a.G + gg;
         if (a.out) a.out[((size_t)seq * a.H + h) * HD + d] = acc;
-        if (a.q8) quantize_block_warp(acc, a.q8 + (((size_t)seq * a.H + h) * NB + d / 32) * 34, lane);
+        if (a.q8.aos || a.q8.codes) q8_store_block(a.q8, acc, (size_t)seq, (int)(h * NB + d / 32), lane);
     }
     if (tid == 0) a.counters[(size_t)seq * a.Hkv + kvh] = 0u;  // zero at rest for the next call
 }
@@ -531,7 +530,7 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
                            const void* v_ring, size_t seq_stride, size_t capacity,
                            size_t context_len, int head_count, int head_count_kv, int head_dim,
                            int batch, float softcap, float* out, float* partials,
-                           size_t partial_bytes, unsigned* counters, uint8_t* out_q8,
+                           size_t partial_bytes, unsigned* counters, const Q8Out& out_q8,
                            bool* used, size_t static_before) {
     *used = false;
     MmaPlan pl;

@@ -612,14 +612,14 @@ int slot_splits(size_t ctx_len, size_t capacity, int H, int Hkv, int HD, int bat
 // step whose loads are all issued before any is used (the partials are a few MB read once, so
 // the merge is bound by load latency, not bandwidth).  The warps' results are merged in a fixed
 // order through shared memory.  With q8 set, the merged block is also written as Q8_0
-// (quantize_f32_to_q8_0, the o projection's input in forward_token).
+// (quantize_f32_to_q8_0, the o projection's input in forward_token), in the form(s) q8 names.
 constexpr int COMBINE_THREADS = 256;
 constexpr int COMBINE_BATCH = 20;  // 148 splits / 8 warps: one batch of loads per warp
 
 template <int HD>
 __global__ void __launch_bounds__(COMBINE_THREADS)
     attn_decode_combine_kernel(const float* __restrict__ part, int H, int splits,
-                               float* __restrict__ out, uint8_t* __restrict__ q8) {
+                               float* __restrict__ out, const Q8Out q8) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     constexpr int W = COMBINE_THREADS / 32;
@@ -674,8 +674,8 @@ __global__ void __launch_bounds__(COMBINE_THREADS)
         const float val = L > 0.0f ? O / L : 0.0f;
         if (out) out[((size_t)seq * H + h) * HD + d] = val;
         // the CTA's 32 dimensions are exactly one Q8_0 block of the [batch][H*HD] output
-        if (q8) quantize_block_warp(val, q8 + (((size_t)seq * H + h) * (HD / 32) + blockIdx.z) * 34,
-                                    lane);
+        if (q8.aos || q8.codes)
+            q8_store_block(q8, val, (size_t)seq, h * (HD / 32) + (int)blockIdx.z, lane);
     }
 }
 
@@ -693,7 +693,7 @@ int pick_splits(size_t ctx_len, int Hkv, int batch, int num_sms) {
 template <int HD, int G>
 int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* v,
               size_t seq_stride, size_t capacity, size_t ctx_len, int H, int Hkv, int batch,
-              float softcap, float* out, float* part, int splits, uint8_t* q8) {
+              float softcap, float* out, float* part, int splits, const Q8Out& q8) {
     using L = AttnLayout<HD>;
     const int chunk = (int)((ctx_len + splits - 1) / splits);
     const float sm_scale = 1.0f / sqrtf((float)HD);
@@ -798,7 +798,7 @@ int launch_hdg(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t*
 template <int HD>
 int launch_hd(sulimo_ctx* ctx, const float* q, const uint8_t* k, const uint8_t* v,
               size_t seq_stride, size_t capacity, size_t ctx_len, int H, int Hkv, int batch,
-              float softcap, float* out, float* part, int splits, uint8_t* q8) {
+              float softcap, float* out, float* part, int splits, const Q8Out& q8) {
     switch (H / Hkv) {
 #define SULIMO_ATTN_G(g) \
     case g: return launch_hdg<HD, g>(ctx, q, k, v, seq_stride, capacity, ctx_len, H, Hkv, batch, softcap, out, part, splits, q8);
@@ -823,14 +823,15 @@ int launch_attn_decode_with_splits(sulimo_ctx* ctx, const float* q, const void* 
                                    size_t context_len, int head_count, int head_count_kv,
                                    int head_dim, int batch, float softcap, float* out,
                                    float* partials, int splits) {
+    const Q8Out none = {nullptr, nullptr, nullptr, 0};
     const uint8_t* k = reinterpret_cast<const uint8_t*>(k_ring);
     const uint8_t* v = reinterpret_cast<const uint8_t*>(v_ring);
     switch (head_dim) {
-        case 32: return launch_hd<32>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
-        case 64: return launch_hd<64>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
-        case 96: return launch_hd<96>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
-        case 128: return launch_hd<128>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
-        case 256: return launch_hd<256>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, nullptr);
+        case 32: return launch_hd<32>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, none);
+        case 64: return launch_hd<64>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, none);
+        case 96: return launch_hd<96>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, none);
+        case 128: return launch_hd<128>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, none);
+        case 256: return launch_hd<256>(ctx, q, k, v, seq_stride, capacity, context_len, head_count, head_count_kv, batch, softcap, out, partials, splits, none);
         default: return set_error(SULIMO_EINVAL, "head_dim must be one of 32, 64, 96, 128, 256");
     }
 }
@@ -860,8 +861,10 @@ size_t attn_decode_partial_bytes(size_t context_len, size_t capacity, int head_c
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
-                       float* partials, size_t partial_bytes, uint8_t* out_q8,
+                       float* partials, size_t partial_bytes, const Q8Out* out_q8_form,
                        size_t static_before) {
+    const Q8Out none = {nullptr, nullptr, nullptr, 0};
+    const Q8Out& out_q8 = out_q8_form ? *out_q8_form : none;
     // the tensor-core kernel where its geometry applies; the scalar kernels otherwise
     bool used = false;
     const int st = launch_attn_decode_mma(ctx, q, k_ring, v_ring, seq_stride, capacity,

@@ -175,6 +175,7 @@ int sulimo_cuda_ctx_destroy(sulimo_ctx* ctx) {
     if (ctx->d_error) cudaFree(ctx->d_error);
     if (ctx->argmax_scratch) cudaFree(ctx->argmax_scratch);
     if (ctx->attn_counters) cudaFree(ctx->attn_counters);
+    if (ctx->q8_stage) cudaFree(ctx->q8_stage);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return SULIMO_OK;
@@ -368,8 +369,10 @@ int sulimo_cuda_event_free(sulimo_event* ev) {
 
 // ---- kernels ------------------------------------------------------------------------------
 
-int sulimo_cuda_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants,
-                              const void* x, void* out, int m, int k, int n, int out_dtype) {
+namespace {
+
+int gemm_entry(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x, void* out,
+               int m, int k, int n, int out_dtype, bool exact) {
     int st = check_ctx(ctx);
     if (st) return st;
     if (m <= 0 || k <= 0 || n < 0) return set_error(SULIMO_EINVAL, "m, k must be > 0, n >= 0");
@@ -382,7 +385,21 @@ int sulimo_cuda_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* q
     if (!aligned(x, 16) || !aligned(quants, 16) || !aligned(out, 16) || !aligned(scales, 2))
         return set_error(SULIMO_EALIGN, "x, quants, out must be 16-byte aligned, scales 2-byte");
     if ((st = bind_device(ctx))) return st;
-    return sulimo::launch_gemm_q4_0_f16(ctx, scales, quants, x, out, m, k, n, out_dtype, k, 0);
+    return sulimo::launch_gemm_q4_0_f16(ctx, scales, quants, x, out, m, k, n, out_dtype, k, 0,
+                                        exact);
+}
+
+}  // namespace
+
+int sulimo_cuda_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants,
+                              const void* x, void* out, int m, int k, int n, int out_dtype) {
+    return gemm_entry(ctx, scales, quants, x, out, m, k, n, out_dtype, false);
+}
+
+int sulimo_cuda_gemm_q4_0_f16_exact(sulimo_ctx* ctx, const void* scales, const void* quants,
+                                    const void* x, void* out, int m, int k, int n,
+                                    int out_dtype) {
+    return gemm_entry(ctx, scales, quants, x, out, m, k, n, out_dtype, true);
 }
 
 int sulimo_cuda_logits_final(sulimo_ctx* ctx, const void* x_all, const void* scales,

@@ -53,13 +53,13 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // One CTA per sequence.  x[seq][E] (+= delta[seq][E] when delta is given, written back), then
-// y = (x * 1/sqrt(mean(x^2) + eps)) * w, quantized to Q8_0 (E/32 blocks) into q8[seq].
-// F16_OUT: y as f16 [seq][E] (the prefill GEMMs' activations) instead of Q8_0.
+// y = (x * 1/sqrt(mean(x^2) + eps)) * w, quantized to Q8_0 (E/32 blocks) as q8 names (row seq).
+// F16_OUT: y as f16 [seq][E] into y16 (the prefill GEMMs' activations) instead.
 template <bool F16_OUT>
 __global__ void __launch_bounds__(NORM_THREADS)
     add_rmsnorm_q8_kernel(float* __restrict__ x, const float* __restrict__ delta,
-                          const float* __restrict__ w, int E, float eps,
-                          uint8_t* __restrict__ q8) {
+                          const float* __restrict__ w, int E, float eps, const Q8Out q8,
+                          __half* __restrict__ y16) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     extern __shared__ float sx[];  // E floats + 33 reduction slots
@@ -81,17 +81,16 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const float mean = __fdiv_rn(sum_sq, (float)E);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
     if (F16_OUT) {
-        __half* ys = reinterpret_cast<__half*>(q8) + (size_t)seq * E;
+        __half* ys = y16 + (size_t)seq * E;
         for (int i = threadIdx.x; i < E; i += blockDim.x)
             ys[i] = __float2half_rn(__fmul_rn(__fmul_rn(sx[i], scale), w[i]));
         return;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t* qs = q8 + (size_t)seq * (E / 32) * 34;
     for (int b = warp; b < E / 32; b += blockDim.x >> 5) {
         const int i = b * 32 + lane;
         const float y = __fmul_rn(__fmul_rn(sx[i], scale), w[i]);
-        quantize_block_warp(y, qs + b * 34, lane);
+        q8_store_block(q8, y, (size_t)seq, b, lane);
     }
 }
 
@@ -201,10 +200,11 @@ __global__ void __launch_bounds__(GLUE_THREADS)
     out[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
-// silu(gate) * up -> Q8_0: one warp per 32-value block, all sequences' blocks in one grid.
+// silu(gate) * up -> Q8_0 (rows of F = q8.K values): one warp per 32-value block, all
+// sequences' blocks in one grid.
 __global__ void __launch_bounds__(GLUE_THREADS)
     swiglu_q8_kernel(const float* __restrict__ gate, const float* __restrict__ up, size_t nblocks,
-                     uint8_t* __restrict__ q8) {
+                     const Q8Out q8) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     const int lane = threadIdx.x & 31;
@@ -212,7 +212,8 @@ __global__ void __launch_bounds__(GLUE_THREADS)
     if (b >= nblocks) return;
     const float g = gate[b * 32 + lane];
     const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-    quantize_block_warp(__fmul_rn(silu, up[b * 32 + lane]), q8 + b * 34, lane);
+    const size_t nb = (size_t)(q8.K / 32);
+    q8_store_block(q8, __fmul_rn(silu, up[b * 32 + lane]), b / nb, (int)(b % nb), lane);
 }
 
 // First index of the maximum of each row (greedy sampling); NaN never wins.  ARGMAX_CTAS CTAs
@@ -277,12 +278,14 @@ __global__ void __launch_bounds__(GLUE_THREADS)
 struct Scratch {
     float *x, *q, *k, *v, *att, *o, *g, *u;
     uint8_t* q8;
-    float* x2;  // the residual stream's second buffer (fused norms write x + delta here)
+    float* x2;   // the residual stream's second buffer (fused norms write x + delta here)
+    void* q8s;   // staged Q8_0 activations for the batched tensor-core matvec
 };
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
-// Carves the caller's scratch (the reference's ScratchBuffers, forward_pass.rs:150-186).
+// Carves the caller's scratch (the reference's ScratchBuffers, forward_pass.rs:150-186, plus the
+// staged activation form of the batched matvec).
 size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scratch* s) {
     const size_t E = m->embd, F = m->ffn, qd = (size_t)m->head_count * m->head_dim;
     const size_t kvd = (size_t)m->head_count_kv * m->head_dim;
@@ -291,11 +294,13 @@ size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scra
     const size_t sizes[10] = {E * 4, qd * 4, kvd * 4, kvd * 4, qd * 4, (E > F ? E : F) * 4,
                               F * 4, F * 4, q8n / 32 * 34, E * 4};
     size_t off = 0;
-    uint8_t* p[10];
+    uint8_t* p[11];
     for (int i = 0; i < 10; i++) {
         p[i] = base ? base + off : nullptr;
         off += align256(sizes[i] * (size_t)batch);
     }
+    p[10] = base ? base + off : nullptr;
+    off += align256(q8_staged_bytes(batch, (int)q8n));
     if (s) {
         s->x = reinterpret_cast<float*>(p[0]);
         s->q = reinterpret_cast<float*>(p[1]);
@@ -307,6 +312,7 @@ size_t scratch_layout(const sulimo_model_desc* m, int batch, uint8_t* base, Scra
         s->u = reinterpret_cast<float*>(p[7]);
         s->q8 = p[8];
         s->x2 = reinterpret_cast<float*>(p[9]);
+        s->q8s = p[10];
     }
     return off;
 }
@@ -383,7 +389,8 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
               hd = m->head_dim;
     const int qd = H * hd, kvd = Hkv * hd;
     const size_t norm_smem = (size_t)(E + 33) * sizeof(float);
-    uint8_t* h8 = reinterpret_cast<uint8_t*>(s.h);
+    __half* h16 = reinterpret_cast<__half*>(s.h);
+    const Q8Out no_q8 = {nullptr, nullptr, nullptr, 0};
     int st;
     if ((st = ensure_norm_attr(ctx))) return st;
     if (tokens) {
@@ -407,7 +414,7 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
         const sulimo_layer_desc& L = m->layers[l];
         (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
                          ctx->stream, s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E,
-                         m->eps, h8);
+                         m->eps, no_q8, h16);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
         if ((st = gemm(L.wq_scales, L.wq_quants, s.h, s.q, qd, E)) ||
@@ -429,7 +436,7 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
             return st;
         (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
                          ctx->stream, s.x, (const float*)s.o,
-                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, h8);
+                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, no_q8, h16);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
         if ((st = gemm(L.wg_scales, L.wg_quants, s.h, s.g, F, E)) ||
@@ -449,7 +456,8 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
     // the last token only: residual, final norm, vocab projection (fp32 logits)
     const size_t last = (size_t)(n - 1) * E;
     (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(1), dim3(NORM_THREADS), norm_smem,
-                     ctx->stream, s.x + last, pending + last, m->out_norm, E, m->eps, h8);
+                     ctx->stream, s.x + last, pending + last, m->out_norm, E, m->eps, no_q8,
+                     h16);
     ctx->launches++;
     if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
     return launch_gemm_q4_0_f16(ctx, m->out_scales, m->out_quants, s.h, logits, m->vocab, E, 1,
@@ -517,11 +525,22 @@ int launch_argmax_rows(sulimo_ctx* ctx, const float* x, int rows, int cols, int3
     return check_cuda(cudaGetLastError(), "argmax_rows launch");
 }
 
-// One fast-mode matvec over a decode step's static weights.
-static int gemv_fast_static(sulimo_ctx* ctx, const void* scales, const void* quants,
-                            const void* x_q8, int rows, int cols, int batch, float* out) {
-    const GemvMatSrc src = {scales, quants, out, rows};
-    return launch_gemv_fast_group(ctx, &src, 1, x_q8, cols, batch, true);
+// The Q8_0 form a decode step's producer writes for the matvec over g: the staged form when the
+// batched tensor-core matvec takes it, else the block array.
+static Q8Out step_q8_form(sulimo_ctx* ctx, const Scratch& s, const GemvMatSrc* g, int count,
+                          int K, int batch) {
+    if (batch >= GEMV_MMA_MIN_BATCH && ((uintptr_t)s.q8s % 16) == 0 &&
+        gemv_mma_applies(g, count, K, batch, ctx->num_sms))
+        return q8_staged_view(s.q8s, batch, K);
+    const Q8Out o = {s.q8, nullptr, nullptr, K};
+    return o;
+}
+
+// The fast-mode matvec over a decode step's static weights, from the form the producer wrote.
+static int step_gemv(sulimo_ctx* ctx, const GemvMatSrc* g, int count, const Q8Out& x, int K,
+                     int batch) {
+    if (x.codes) return launch_gemv_mma_group(ctx, g, count, x, K, batch, true);
+    return launch_gemv_fast_group(ctx, g, count, x.aos, K, batch, true);
 }
 
 // Residual add + RMSNorm + Q8_0 feeding `count` matrices.  For one sequence the norm is
@@ -529,9 +548,9 @@ static int gemv_fast_static(sulimo_ctx* ctx, const void* scales, const void* qua
 // in; v = x + delta goes to the other residual buffer when keep_x, which becomes x).  With more
 // sequences that redundant per-CTA work costs more than the launch it saves (measured on
 // config 4: batch 1 1.48 -> 1.40 ms per step, batch 8 5.19 -> 6.41 ms), so the norm kernel
-// updates x in place and writes q8, then the matvec runs.
-static int norm_and_gemv(sulimo_ctx* ctx, float*& x, float*& x_other, const float* delta,
-                         const float* w, float eps, int E, int batch, uint8_t* q8,
+// updates x in place and writes the activations, then the matvec runs.
+static int norm_and_gemv(sulimo_ctx* ctx, const Scratch& s, float*& x, float*& x_other,
+                         const float* delta, const float* w, float eps, int E, int batch,
                          const GemvMatSrc* g, int count, bool keep_x) {
     const GemvPrologue pro = {GEMV_PRO_NORM, x, delta, w, keep_x ? x_other : nullptr, eps};
     if (batch == 1 && gemv_fast_fused_ok(g, count, E, batch, pro)) {
@@ -543,25 +562,28 @@ static int norm_and_gemv(sulimo_ctx* ctx, float*& x, float*& x_other, const floa
         }
         return st;
     }
+    const Q8Out form = step_q8_form(ctx, s, g, count, E, batch);
     (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS),
-                     (size_t)(E + 33) * sizeof(float), ctx->stream, x, delta, w, E, eps, q8);
+                     (size_t)(E + 33) * sizeof(float), ctx->stream, x, delta, w, E, eps, form,
+                     (__half*)nullptr);
     ctx->launches++;
     int st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch");
-    return st ? st : launch_gemv_fast_group(ctx, g, count, q8, E, batch, true);
+    return st ? st : step_gemv(ctx, g, count, form, E, batch);
 }
 
 // SwiGLU + Q8_0 feeding the down projection.  Folding it into the matvec's prologue, as the
 // norm is, was measured slower at every batch size (config 4 batch 1: 1.48 -> 1.61 ms per
 // step): every CTA of the down projection (hundreds) would recompute all F activations with
 // expf, so this one small kernel runs instead.
-static int swiglu_and_gemv(sulimo_ctx* ctx, const float* gate, const float* up, int F, int batch,
-                           uint8_t* q8, const GemvMatSrc& g) {
+static int swiglu_and_gemv(sulimo_ctx* ctx, const Scratch& s, const float* gate, const float* up,
+                           int F, int batch, const GemvMatSrc& g) {
     const size_t nblk = (size_t)batch * F / 32;
+    const Q8Out form = step_q8_form(ctx, s, &g, 1, F, batch);
     (void)launch_pdl(swiglu_q8_kernel, dim3((unsigned)((nblk + 7) / 8)), dim3(GLUE_THREADS), 0,
-                     ctx->stream, gate, up, nblk, q8);
+                     ctx->stream, gate, up, nblk, form);
     ctx->launches++;
     int st = check_cuda(cudaGetLastError(), "swiglu_q8 launch");
-    return st ? st : launch_gemv_fast_group(ctx, &g, 1, q8, F, batch, true);
+    return st ? st : step_gemv(ctx, &g, 1, form, F, batch);
 }
 
 int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
@@ -595,9 +617,9 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
             const GemvMatSrc g[3] = {{L.wq_scales, L.wq_quants, s.q, qd},
                                      {L.wk_scales, L.wk_quants, s.k, kvd},
                                      {L.wv_scales, L.wv_quants, s.v, kvd}};
-            if ((st = norm_and_gemv(ctx, x, x_other, pending,
+            if ((st = norm_and_gemv(ctx, s, x, x_other, pending,
                                     reinterpret_cast<const float*>(L.attn_norm), m->eps, E, batch,
-                                    s.q8, g, 3, true)))
+                                    g, 3, true)))
                 return st;
         }
         (void)launch_pdl(qkv_rope_store_kernel, dim3(H + 2 * Hkv, batch), dim3(128), 0,
@@ -611,27 +633,29 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
         // attention, its output quantized to Q8_0 in the merge kernel (the o projection's input)
         // every ring slot but the newest (written by qkv_rope_store) is static during the step
+        const GemvMatSrc go = {L.wo_scales, L.wo_quants, s.o, E};
+        const Q8Out att_form = step_q8_form(ctx, s, &go, 1, qd, batch);
         if ((st = launch_attn_decode(ctx, s.q, L.k_ring, L.v_ring, m->kv_seq_stride,
                                      m->kv_capacity, ctx_len, H, Hkv, hd, batch, m->attn_softcap,
                                      nullptr, reinterpret_cast<float*>(ctx->workspace),
-                                     ctx->workspace_bytes, s.q8, pos)) ||
-            (st = gemv_fast_static(ctx, L.wo_scales, L.wo_quants, s.q8, E, qd, batch, s.o)))
+                                     ctx->workspace_bytes, &att_form, pos)) ||
+            (st = step_gemv(ctx, &go, 1, att_form, qd, batch)))
             return st;
         {  // FFN norm (x += o), then gate and up in one launch
             const GemvMatSrc g[2] = {{L.wg_scales, L.wg_quants, s.g, F},
                                      {L.wu_scales, L.wu_quants, s.u, F}};
-            if ((st = norm_and_gemv(ctx, x, x_other, s.o,
+            if ((st = norm_and_gemv(ctx, s, x, x_other, s.o,
                                     reinterpret_cast<const float*>(L.ffn_norm), m->eps, E, batch,
-                                    s.q8, g, 2, true)))
+                                    g, 2, true)))
                 return st;
         }
         const GemvMatSrc gd = {L.wd_scales, L.wd_quants, s.o, E};
-        if ((st = swiglu_and_gemv(ctx, s.g, s.u, F, batch, s.q8, gd))) return st;
+        if ((st = swiglu_and_gemv(ctx, s, s.g, s.u, F, batch, gd))) return st;
         pending = s.o;
     }
     // output norm and the vocab projection (the residual is not needed afterwards)
-    const GemvMatSrc go = {m->out_scales, m->out_quants, logits, m->vocab};
-    return norm_and_gemv(ctx, x, x_other, pending, m->out_norm, m->eps, E, batch, s.q8, &go, 1,
+    const GemvMatSrc gl = {m->out_scales, m->out_quants, logits, m->vocab};
+    return norm_and_gemv(ctx, s, x, x_other, pending, m->out_norm, m->eps, E, batch, &gl, 1,
                          false);
 }
 

@@ -1,0 +1,531 @@
+// gemm_q4_0_pair.cu — the Q4_0-weight prefill GEMM on CTA pairs (tcgen05 cta_group::2).
+//
+// Same contraction and numerics as gemm_q4_0_tc.cu (the reference's gemm_q4_0_f16,
+// kernels/gemm_q4_0.cl:13-130, host crates/sulimo-ocl/src/gemm.rs:28-102):
+//     out[t][r] = sum_b d[r][b] * sum_i x[t][32b+i] * (q[r][b][i] - 8)
+// with the weights dequantized once to f16(d*(q-8)), f16 activations, fp32 accumulation.
+//
+// A thread-block cluster of two CTAs (one per SM) computes a 256-feature x bn-token tile with
+// one tcgen05.mma.cta_group::2 stream issued by a single thread of CTA 0:
+//   - A (weights, 256 x K) comes from TMEM: CTA r dequantizes its own 128 feature rows
+//     m0 = 256 * pair + 128 * r into the same TMEM columns of its own SM;
+//   - B (activations, bn tokens x K) comes from shared memory: CTA r holds tokens
+//     n0 + r * bn/2 .. n0 + (r + 1) * bn/2 - 1 at the same offsets in its own SM;
+//   - D (fp32, 128 rows x bn tokens per CTA) lands in each CTA's TMEM.
+// Against the one-CTA kernel this halves the instructions the issuing thread spends per unit
+// of tensor work (each MMA covers two SMs) and halves each SM's activation traffic (it loads
+// bn/2 tokens, not bn).  K advances 128 values (four Q4_0 blocks, eight K=16 MMAs) per ring
+// stage, so the per-stage barrier test, fence and commit are paid once per 128 k.
+//
+// Roles per CTA (576 threads):
+//   warp 0    one thread: TMA loads of this CTA's activation half (two 64-k boxes, 128-byte
+//             swizzle, K-major) and its 128 rows' raw nibbles (64 bytes per row) into the
+//             stage; no multicast.  Waits on its own `empty` barrier before refilling a stage.
+//   warps 2-17 dequant in four groups of four warps (one warp per TMEM lane quarter; group g
+//             takes Q4_0 block g of every stage): 16 f16x2 TMEM columns per stage per row; then
+//             each warp arrives on CTA 0's `afull` barrier of the stage (32 arrivals: both CTAs).
+//   warp 1    CTA 0, one thread: waits `afull`, issues the eight MMAs of the stage and commits
+//             to the `empty` barriers of both CTAs (multicast commit); a final commit to both
+//             CTAs' `done` barriers releases the epilogues.
+//   warps 2-17 epilogue (each CTA, its own 128 rows): tcgen05.ld -> f16 / f32 -> smem -> one
+//             TMA tensor store per 32-token chunk; fp32 split-K partials as in the one-CTA form.
+// TMEM is allocated with cta_group::2 (512 columns on each SM: the stages' weights, then the
+// accumulators).  Every wait is bounded by %globaltimer; a CTA that gives up records a device
+// error, drains what it issued and still reaches the closing cluster barrier, so neither CTA
+// leaves while the other may still signal its shared memory.
+#include <string.h>
+
+#include "sulimo_common.cuh"
+#include "sulimo_internal.h"
+#include "tc_sm100.cuh"
+
+namespace sulimo {
+namespace {
+
+constexpr int PM = 128;            // feature rows per CTA = TMEM lanes (a pair covers 256)
+constexpr int PK = 128;            // k per stage: four Q4_0 blocks
+constexpr int P_BN_MAX = 256;      // tokens per pair tile = MMA N (each CTA holds half)
+constexpr int P_MAX_STAGES = 8;
+constexpr uint32_t P_SMEM_LIMIT = 232448;
+constexpr int P_DEQ_GROUPS = 4;
+constexpr int P_DEQ_WARPS = 4 * P_DEQ_GROUPS;
+constexpr int P_THREADS = 64 + 32 * P_DEQ_WARPS;
+constexpr int P_EPI_TOKENS = 32;
+constexpr uint32_t P_TMEM_COLS = 512;
+constexpr uint32_t P_STAGE_COLS = PK / 2;   // f16x2 TMEM columns of a stage's weights
+constexpr uint32_t P_Q_STAGE = PM * 64;     // raw nibbles per stage: 128 rows x 4 blocks x 16 B
+constexpr uint32_t P_BAR_BYTES = 512;
+static_assert((3 * P_MAX_STAGES + 1) * 8 + 8 <= P_BAR_BYTES, "barrier block");
+
+// Shared memory per CTA: stages x (activation half: bn/2 rows x 256 bytes, nibbles), barriers,
+// 1024 bytes of alignment slack.
+__host__ __device__ constexpr uint32_t p_x_stage(int bn) { return (uint32_t)bn * 128u; }
+__host__ __device__ constexpr uint32_t p_smem_bytes(int bn, int stages) {
+    return (uint32_t)stages * (p_x_stage(bn) + P_Q_STAGE) + P_BAR_BYTES + 1024;
+}
+__host__ __device__ constexpr int p_ring_stages(int bn) {
+    int s = P_MAX_STAGES;
+    const int by_tmem = (int)((P_TMEM_COLS - (uint32_t)bn) / P_STAGE_COLS);
+    if (by_tmem < s) s = by_tmem;
+    while (s > 2 && p_smem_bytes(bn, s) > P_SMEM_LIMIT) s--;
+    return s;
+}
+static_assert(p_ring_stages(P_BN_MAX) == 4, "256-token pair ring");
+// the epilogue stages a CTA's whole fp32 tile (128 rows x bn) in the ring
+static_assert(4u * (p_x_stage(256) + P_Q_STAGE) >= 256u * PM * 4u, "epilogue tile fits (256)");
+static_assert(6u * (p_x_stage(128) + P_Q_STAGE) >= 128u * PM * 4u, "epilogue tile fits (128)");
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Cluster barrier with a relaxed arrival: it orders no memory by itself (the mbarrier
+// initializations are published by fence.mbarrier_init, the TMEM address by __syncthreads), so
+// it does not wait for the arriving thread's memory operations in flight.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile(
+        "barrier.cluster.arrive.relaxed.aligned;\n\t"
+        "barrier.cluster.wait.aligned;" ::: "memory");
+}
+
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+    return out;
+}
+
+// Arrival on an mbarrier in either CTA of the cluster (shared::cluster address).  The TMEM
+// stores it publishes are ordered by tcgen05.wait::st + tcgen05.fence::before_thread_sync on
+// this side and tcgen05.fence::after_thread_sync after the leader's wait, so the arrival keeps
+// the default CTA-scope release: a cluster-scope release would also wait for this thread's
+// unrelated loads in flight (the next stage's block scales).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// The eight K=16 MMAs of one 128-k stage (two 64-k activation halves of the stage, four MMAs
+// each), A from TMEM, B from shared memory, into the pair's accumulators.  The first MMA
+// overwrites the accumulators when `accumulate` is 0.
+__device__ __forceinline__ void mma_pair_stage(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0,
+                                               uint64_t b1, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred pa, pt;\n\t"
+        "setp.ne.b32 pa, %4, 0;\n\t"
+        "setp.eq.u32 pt, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, pa;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%9], %10, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%11], %12, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%13], %14, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%15], %16, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%17], %18, %3, pt;\n\t}"
+        :
+        : "r"(d_tmem), "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate), "r"(a_tmem + 8u),
+          "l"(b0 + 2), "r"(a_tmem + 16u), "l"(b0 + 4), "r"(a_tmem + 24u), "l"(b0 + 6),
+          "r"(a_tmem + 32u), "l"(b1), "r"(a_tmem + 40u), "l"(b1 + 2), "r"(a_tmem + 48u),
+          "l"(b1 + 4), "r"(a_tmem + 56u), "l"(b1 + 6)
+        : "memory");
+}
+
+// Arrives on the barrier at this shared-memory offset in both CTAs of the pair once every MMA
+// issued before it has completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+        "[%0], %1;" ::"r"(smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+// OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace [split][n][m].
+template <int OUT_MODE>
+__global__ void __launch_bounds__(P_THREADS, 1)
+    gemm_q4_0_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                          const __grid_constant__ CUtensorMap tmap_q,
+                          const __grid_constant__ CUtensorMap tmap_out,
+                          const __grid_constant__ CUtensorMap tmap_out16,
+                          const uint16_t* __restrict__ scales, int m, int k, int n, int bn, int nb,
+                          int iters_per_split, int stages, int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    // the same offset in both CTAs: the leader's B descriptors address both SMs' stages
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const uint32_t x_stage = p_x_stage(bn);       // two 64-k halves of bn/2 rows x 128 bytes
+    const uint32_t x_half = x_stage / 2;
+    const uint32_t acc_col = (uint32_t)stages * P_STAGE_COLS;  // accumulators: bn columns
+    uint8_t* sx = smem;
+    uint8_t* sq = smem + stages * x_stage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sq + stages * P_Q_STAGE);
+    uint64_t* empty = full + P_MAX_STAGES;
+    uint64_t* afull = empty + P_MAX_STAGES;
+    uint64_t* done = afull + P_MAX_STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t crank = cluster_ctarank();
+    const int m0 = (blockIdx.x >> 1) * (2 * PM) + (int)crank * PM;
+    const int n0 = blockIdx.y * bn;
+    const int nx0 = n0 + (int)crank * (bn / 2);  // this CTA's activation rows
+    const int num_k_total = (k + PK - 1) / PK;
+    const int i_begin = blockIdx.z * iters_per_split;
+    const int i_end = min(num_k_total, i_begin + iters_per_split);
+    const int num_k = max(0, i_end - i_begin);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&afull[s], 2 * P_DEQ_WARPS);  // every dequant warp of both CTAs
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmap_x);
+        prefetch_tensormap(&tmap_q);
+        prefetch_tensormap(&tmap_out);
+        pdl_launch_dependents();
+        pdl_wait_prerequisites();
+        // the first ring pass needs no empty-slot waits
+        for (int j = 0; j < num_k && j < stages; j++) {
+            const int kk = (i_begin + j) * PK;
+            mbar_arrive_expect_tx(&full[j], x_stage + P_Q_STAGE);
+            tma_load_2d(sx + j * x_stage, &tmap_x, kk, nx0, &full[j]);
+            tma_load_2d(sx + j * x_stage + x_half, &tmap_x, kk + 64, nx0, &full[j]);
+            tma_load_2d(sq + j * P_Q_STAGE, &tmap_q, kk / 2, m0, &full[j]);
+        }
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(P_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    // both CTAs' barriers are initialized and both TMEM allocations done before any remote
+    // arrival or MMA
+    tc_fence_before();
+    __syncthreads();  // thread 0's griddepcontrol.wait, the barrier inits, the TMEM address
+
+    // dequant role (warps 2-17): TMEM lane quarter warp % 4, group (warp - 2) / 4
+    const uint32_t quarter = (uint32_t)(warp & 3);
+    const int group = (warp - 2) >> 2;
+    const int r = (int)quarter * 32 + lane;  // feature row within the CTA == TMEM lane
+    const int grow = m0 + r;
+    const bool row_ok = grow < m;
+    const uint16_t* srow = scales + (size_t)(row_ok ? grow : 0) * nb;
+    const uint32_t lane_base = (quarter * 32u) << 16;
+    const uint32_t afull_leader0 = mapa_shared(smem_u32(&afull[0]), 0);
+    // block `group` of every stage: its scale for stage j (zero past the matrix or past k)
+    auto load_scale = [&](int j) -> uint32_t {
+        const int kb = 4 * (i_begin + j) + group;
+        return (row_ok && j < num_k && kb < nb) ? (uint32_t)__ldg(srow + kb) : 0u;
+    };
+    // scales of stages 0 and 1 in flight during the cluster barrier
+    uint32_t sc0 = 0u, sc1 = 0u;
+    if (warp >= 2) {
+        sc0 = load_scale(0);
+        sc1 = load_scale(1);
+    }
+
+    cluster_sync_relaxed();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            int issued = num_k < stages ? num_k : stages;
+            for (int j = stages; j < num_k; j++) {
+                const int s = j % stages;
+                const uint32_t ph = (uint32_t)(j / stages) & 1u;
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
+                const int kk = (i_begin + j) * PK;
+                mbar_arrive_expect_tx(&full[s], x_stage + P_Q_STAGE);
+                tma_load_2d(sx + s * x_stage, &tmap_x, kk, nx0, &full[s]);
+                tma_load_2d(sx + s * x_stage + x_half, &tmap_x, kk + 64, nx0, &full[s]);
+                tma_load_2d(sq + s * P_Q_STAGE, &tmap_q, kk / 2, m0, &full[s]);
+                issued = j + 1;
+            }
+            // Tail: every issued stage has landed and has been released by the leader's MMA
+            // commits (multicast into this CTA), so no copy or commit still targets this CTA's
+            // shared memory when it leaves.
+            for (int j = (issued > stages ? issued - stages : 0); j < issued; j++) {
+                const int s = j % stages;
+                const uint32_t ph = (uint32_t)(j / stages) & 1u;
+                mbar_wait_bounded(&full[s], ph, err, nullptr);
+                if (!*abort_flag) mbar_wait_bounded(&empty[s], ph, err, abort_flag);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer (CTA 0) ------------------------------
+        if (lane == 0 && crank == 0) {
+            // kind::f16: D f32 (bits 4-5 = 1), A = B = f16, K-major, N >> 3 at 17, M >> 4 at 24
+            const uint32_t idesc =
+                (1u << 4) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)((2 * PM) >> 4) << 24);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int j = 0; j < num_k; j++) {
+                if (!mbar_wait_bounded(&afull[s], ph, err, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t xs = smem_u32(sx + s * x_stage);
+                mma_pair_stage(tmem + acc_col, tmem + (uint32_t)s * P_STAGE_COLS, sw128_desc(xs),
+                               sw128_desc(xs + x_half), idesc, j > 0 ? 1u : 0u);
+                mma_commit_pair(&empty[s]);
+                if (++s == stages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+            mma_commit_pair(done);
+        }
+    } else {
+        // --------------------------- dequant, then epilogue ---------------------------
+        // Every warp dequantizes block `group` of every stage for its 32 rows (16 TMEM columns),
+        // so a stage's four blocks are done by the four groups side by side and the first
+        // stage is ready after one block's work.
+        bool ok = true;
+        for (int j = 0; j < num_k; j++) {
+            const int s = j % stages;
+            const uint32_t ph = (uint32_t)(j / stages) & 1u;
+            const uint32_t sc = sc0;
+            sc0 = sc1;
+            sc1 = load_scale(j + 2);
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], ph, err, abort_flag))) {
+                ok = false;
+                break;
+            }
+            const uint4 qb = *reinterpret_cast<const uint4*>(sq + s * P_Q_STAGE + r * 64 +
+                                                             group * 16);
+            uint32_t cols[16];
+            dequant_block(qb, sc, cols);
+            tmem_st16(tmem + lane_base + (uint32_t)s * P_STAGE_COLS + 16u * (uint32_t)group,
+                      cols);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();  // every lane's stores are complete before the warp's single arrival
+            if (lane == 0) mbar_arrive_remote(afull_leader0 + (uint32_t)s * 8u);
+        }
+        // Epilogue: as in the one-CTA kernel, over this CTA's 128 rows and all bn tokens.
+        // `done` is committed even when this split has no k stages, and is always waited for:
+        // no commit may still be in flight towards this CTA when it leaves
+        const bool have = ok && mbar_wait_bounded(done, 0, err, abort_flag);
+        if (have) tc_fence_after();
+        constexpr int ES = OUT_MODE == 0 ? 2 : 4;
+        const bool issuer = (warp - 2) % 4 == 0 && lane == 0;
+        for (int c0 = group * P_EPI_TOKENS; c0 < bn; c0 += P_DEQ_GROUPS * P_EPI_TOKENS) {
+            uint8_t* tile = sx + (size_t)c0 * PM * ES;
+            if (have) {
+                uint32_t v[32];
+                if (num_k > 0) {
+                    tmem_ld32(tmem + lane_base + acc_col + (uint32_t)c0, v);
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) v[jj] = 0u;
+                }
+                uint8_t* col = tile + (size_t)r * ES;
+#pragma unroll
+                for (int jj = 0; jj < 32; jj++) {
+                    const float f = __uint_as_float(v[jj]);
+                    if (ES == 2)
+                        *reinterpret_cast<__half*>(col + (size_t)jj * PM * ES) = __float2half_rn(f);
+                    else
+                        *reinterpret_cast<float*>(col + (size_t)jj * PM * ES) = f;
+                }
+                fence_proxy_async_smem();
+            }
+            named_barrier_sync(1 + group, 128);
+            if (issuer && have && !*abort_flag && n0 + c0 < n && m0 < m) {
+                const bool whole = c0 + P_EPI_TOKENS <= bn;
+                const CUtensorMap* map = whole ? &tmap_out : &tmap_out16;
+                if (OUT_MODE == 2)
+                    tma_store_3d(map, m0, n0 + c0, (int)blockIdx.z, tile);
+                else
+                    tma_store_2d(map, m0, n0 + c0, tile);
+                bulk_commit();
+            }
+        }
+        if (issuer) bulk_wait_read_all();
+    }
+
+    // Neither CTA frees its TMEM or leaves before both are done with the pair's MMAs, TMEM and
+    // barriers.
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_relaxed();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(P_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+template <int MODE>
+int pair_setup(int device) {
+    static DeviceBits done;
+    if (done.test(device)) return SULIMO_OK;
+    int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_pair_kernel<MODE>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)P_SMEM_LIMIT),
+                        "pair gemm smem attribute");
+    if (!st) done.set(device);
+    return st;
+}
+
+// Launch with a cluster of two CTAs along x and programmatic stream serialization.
+template <typename... Params, typename... Args>
+cudaError_t launch_pair(void (*kernel)(Params...), dim3 grid, size_t smem, cudaStream_t stream,
+                        Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(P_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Pairs that can be resident at once (clusters are placed inside a GPC, so this can be below
+// half the SM count); cached per device.
+int max_active_pairs(int device, int num_sms) {
+    static std::atomic<int> cache[64];
+    int v = cache[device & 63].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms);
+    cfg.blockDim = dim3(P_THREADS);
+    cfg.dynamicSmemBytes = p_smem_bytes(P_BN_MAX, p_ring_stages(P_BN_MAX));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_q4_0_pair_kernel<0>, &cfg) != cudaSuccess ||
+        n <= 0) {
+        cudaGetLastError();
+        n = num_sms / 2;
+    }
+    cache[device & 63].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+}  // namespace
+
+// Tile plan of the pair kernel: token-tile width (a multiple of 32, at most 256) and K splits.
+// The output tiles (256 features x bn tokens) fill the resident pairs by themselves when there
+// are enough; otherwise K is split over more pairs (each split keeping >= 4 stages of 128).
+// SULIMO_PAIR_SPLIT_BN=<w> (a measurement switch) uses w-token tiles for the outputs that
+// split K: narrower tiles need fewer splits for the same fill, so fewer fp32 partials.
+PairPlan gemm_pair_plan(int m, int k, int n, int max_pairs) {
+    PairPlan p;
+    const int pm = (m + 2 * PM - 1) / (2 * PM);
+    const int num_k = (k + PK - 1) / PK;
+    int bn = n >= P_BN_MAX ? P_BN_MAX : ((n + 31) / 32) * 32;
+    int tiles = pm * ((n + bn - 1) / bn);
+    int splits = 1;
+    if (tiles * 2 <= max_pairs) {
+        static const int split_bn = [] {
+            const char* e = getenv("SULIMO_PAIR_SPLIT_BN");
+            const int v = e ? atoi(e) : 0;
+            return (v >= 32 && v <= P_BN_MAX && v % 32 == 0) ? v : 0;
+        }();
+        if (split_bn && split_bn < bn) {
+            bn = split_bn;
+            tiles = pm * ((n + bn - 1) / bn);
+        }
+        splits = max_pairs / tiles;
+        if (splits > num_k / 4) splits = num_k / 4;
+        if (splits < 1) splits = 1;
+    }
+    p.bn = bn;
+    p.splits = splits;
+    p.iters_per_split = (num_k + splits - 1) / splits;
+    p.stages = p_ring_stages(bn);
+    p.smem = p_smem_bytes(bn, p.stages);
+    p.grid_x = 2 * pm;
+    p.grid_y = (n + bn - 1) / bn;
+    return p;
+}
+
+int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
+                     void* out, int m, int k, int n, int out_dtype, int x_row_stride,
+                     int x_row_offset) {
+    const int nb = k / 32;
+    int st;
+    if ((st = pair_setup<0>(ctx->device)) || (st = pair_setup<1>(ctx->device)) ||
+        (st = pair_setup<2>(ctx->device)))
+        return st;
+    const PairPlan p = gemm_pair_plan(m, k, n, max_active_pairs(ctx->device, ctx->num_sms));
+    if (p.grid_y > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
+    const uint8_t* xb =
+        reinterpret_cast<const uint8_t*>(x) + (size_t)x_row_offset * x_row_stride * 2;
+    CUtensorMap tx, tq, to, to16;
+    st = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, (uint64_t)k, (uint64_t)n,
+                   (uint64_t)x_row_stride * 2, 64, (uint32_t)(p.bn / 2),
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16, (uint64_t)m,
+                   (uint64_t)nb * 16, 64, PM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(scales);
+    if (p.splits == 1) {
+        const bool f32 = out_dtype == SULIMO_OUT_F32;
+        const CUtensorMapDataType dt =
+            f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        const uint64_t rowb = (uint64_t)m * (f32 ? 4 : 2);
+        if ((st = encode_2d(&to, dt, out, (uint64_t)m, (uint64_t)n, rowb, PM,
+                            (uint32_t)P_EPI_TOKENS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+            (st = encode_2d(&to16, dt, out, (uint64_t)m, (uint64_t)n, rowb, PM, 16u,
+                            CU_TENSOR_MAP_SWIZZLE_NONE)))
+            return st;
+        const dim3 grid(p.grid_x, p.grid_y, 1);
+        const cudaError_t e =
+            f32 ? launch_pair(gemm_q4_0_pair_kernel<1>, grid, p.smem, ctx->stream, tx, tq, to,
+                              to16, sc, m, k, n, p.bn, nb, p.iters_per_split, p.stages,
+                              ctx->d_error)
+                : launch_pair(gemm_q4_0_pair_kernel<0>, grid, p.smem, ctx->stream, tx, tq, to,
+                              to16, sc, m, k, n, p.bn, nb, p.iters_per_split, p.stages,
+                              ctx->d_error);
+        ctx->launches++;
+        return check_cuda(e, "gemm_q4_0_pair launch");
+    }
+    const size_t nm = (size_t)n * m;
+    if ((st = ensure_workspace(ctx, nm * p.splits * sizeof(float)))) return st;
+    float* ws = reinterpret_cast<float*>(ctx->workspace);
+    {
+        const uint64_t dims[3] = {(uint64_t)m, (uint64_t)n, (uint64_t)p.splits};
+        const uint64_t strides[2] = {(uint64_t)m * 4, (uint64_t)nm * 4};
+        const uint32_t box[3] = {PM, (uint32_t)P_EPI_TOKENS, 1};
+        const uint32_t box16[3] = {PM, 16u, 1};
+        if ((st = encode_tensor_map(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, 3, dims, strides,
+                                    box, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+            (st = encode_tensor_map(&to16, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ws, 3, dims, strides,
+                                    box16, CU_TENSOR_MAP_SWIZZLE_NONE)))
+            return st;
+    }
+    const dim3 grid(p.grid_x, p.grid_y, p.splits);
+    st = check_cuda(launch_pair(gemm_q4_0_pair_kernel<2>, grid, p.smem, ctx->stream, tx, tq, to,
+                                to16, sc, m, k, n, p.bn, nb, p.iters_per_split, p.stages,
+                                ctx->d_error),
+                    "gemm_q4_0_pair split-K launch");
+    if (st) return st;
+    ctx->launches++;
+    return launch_splitk_reduce(ctx, ws, out, nm, p.splits, out_dtype == SULIMO_OUT_F32);
+}
+
+}  // namespace sulimo

@@ -32,6 +32,7 @@
 
 #include "sulimo_common.cuh"
 #include "sulimo_internal.h"
+#include "tc_sm100.cuh"
 
 namespace sulimo {
 namespace {
@@ -67,71 +68,19 @@ __host__ __device__ constexpr uint32_t ring_bytes(int bn, int stages) {
 __host__ __device__ constexpr uint32_t smem_bytes(int bn, int stages) {
     return ring_bytes(bn, stages) + BAR_BYTES + 1024;
 }
+// TMEM columns of one stage's weights: 32 f16x2 columns, or 64 in the exact-weight form
+// (f16 high parts, then f16 low parts).
+__host__ __device__ constexpr uint32_t stage_cols(bool exact) { return exact ? 64u : 32u; }
 // Deepest ring for a token-tile width (>= 2 stages for every bn <= 256).
-__host__ __device__ constexpr int ring_stages(int bn) {
+__host__ __device__ constexpr int ring_stages(int bn, bool exact = false) {
     int s = MAX_STAGES;
-    if ((int)((TMEM_COLS - (uint32_t)bn) / 32) < s) s = (int)((TMEM_COLS - (uint32_t)bn) / 32);
+    const int by_tmem = (int)((TMEM_COLS - (uint32_t)bn) / stage_cols(exact));
+    if (by_tmem < s) s = by_tmem;
     while (s > 2 && smem_bytes(bn, s) > SMEM_LIMIT) s--;
     return s;
 }
 static_assert(ring_stages(BN_MAX) == 6 && smem_bytes(BN_MAX, 6) <= SMEM_LIMIT, "256-token ring");
 static_assert(ring_bytes(BN_MAX, 6) >= BN_MAX * BM * 4, "epilogue staging tile fits the ring");
-
-// ---- tcgen05 / TMA wrappers ----------------------------------------------------------------
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1,
-                                             const void* src) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-            reinterpret_cast<uint64_t>(map)),
-        "r"(c0), "r"(c1), "r"(smem_u32(src))
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int c0, int c1, int c2,
-                                             const void* src) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::
-            "l"(reinterpret_cast<uint64_t>(map)),
-        "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
-        : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit() {
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-// Waits until the committed bulk stores have read their shared-memory sources (the global
-// writes complete on their own before the grid is complete).
-__device__ __forceinline__ void bulk_wait_read_all() {
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-
-// Waits until the committed bulk stores' global writes are complete and visible to this thread.
-__device__ __forceinline__ void bulk_wait_all() {
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
-    d |= (uint64_t)1 << 16;                    // leading byte offset (unused for SW128 K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset
-    d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
-    return d;
-}
 
 // One stage = four K=16 MMAs into the accumulators (the first one overwrites them when
 // `accumulate` is 0), issued in one instruction stream together with a non-blocking test of the
@@ -160,109 +109,27 @@ __device__ __forceinline__ uint32_t mma_stage_and_peek(uint32_t d_tmem, uint32_t
     return ready;
 }
 
+// Four K=16 MMAs accumulating into D (the low-part weights of an exact-form stage).
+__device__ __forceinline__ void mma_stage_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred pt;\n\t"
+        "setp.eq.u32 pt, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %5, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %7, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %9, %3, pt;\n\t}"
+        :
+        : "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(a_tmem + 8u), "l"(b_desc + 2),
+          "r"(a_tmem + 16u), "l"(b_desc + 4), "r"(a_tmem + 24u), "l"(b_desc + 6)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
             smem_u32(bar))
         : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31, %32};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
-        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
-        "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_st_wait() {
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
-// Loads 32 columns of this warp's 32 TMEM lanes and waits for them; the wait carries the
-// registers as operands so no use can be scheduled before it.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
-          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
-          "=r"(v[31])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]),
-                   "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]),
-                   "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]),
-                   "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]),
-                   "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]),
-                   "+r"(v[30]), "+r"(v[31])
-                 :
-                 : "memory");
-}
-
-// 16 quant bytes of one Q4_0 block -> 16 packed f16x2 words (TMEM columns of the block):
-// column c holds weights k = 2c, 2c+1 of the block; weights 0..15 are the low nibbles of
-// bytes 0..15, weights 16..31 the high nibbles (repack.rs:122-129).
-__device__ __forceinline__ void dequant_block(const uint4 q, uint32_t dbits, uint32_t* col) {
-    const __half2 d2 = __halves2half2(__ushort_as_half((uint16_t)dbits),
-                                      __ushort_as_half((uint16_t)dbits));
-    const __half2 k1032 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int w = 0; w < 4; w++) {
-        const uint32_t lo = words[w] & 0x0F0F0F0Fu;
-        const uint32_t hi = (words[w] >> 4) & 0x0F0F0F0Fu;
-        // {0x6400 | nibble} is the f16 value 1024 + nibble; minus 1032 gives nibble - 8 exactly.
-        const uint32_t p[4] = {prmt(lo, 0x64646464u, 0x4140), prmt(lo, 0x64646464u, 0x4342),
-                               prmt(hi, 0x64646464u, 0x4140), prmt(hi, 0x64646464u, 0x4342)};
-        __half2 h[4];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            h[e] = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&p[e]), k1032), d2);
-        }
-        col[2 * w] = *reinterpret_cast<uint32_t*>(&h[0]);
-        col[2 * w + 1] = *reinterpret_cast<uint32_t*>(&h[1]);
-        col[8 + 2 * w] = *reinterpret_cast<uint32_t*>(&h[2]);
-        col[8 + 2 * w + 1] = *reinterpret_cast<uint32_t*>(&h[3]);
-    }
-}
-
-// Partial sums of split-K CTAs go to an fp32 workspace [split][n][m]; this kernel adds the
-// splits in index order (deterministic) and writes f16 or f32 results.  Launched as a
-// programmatic dependent of the GEMM: its CTAs wait for the partials in griddepcontrol.wait.
-template <bool OUT_F32>
-__global__ void __launch_bounds__(256)
-    splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ out, size_t nm,
-                         int splits) {
-    pdl_launch_dependents();
-    pdl_wait_prerequisites();
-    const size_t i4 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    if (i4 >= nm) return;
-    float4 acc = __ldcg(reinterpret_cast<const float4*>(ws + i4));
-    for (int z = 1; z < splits; z++) {
-        const float4 p = __ldcg(reinterpret_cast<const float4*>(ws + (size_t)z * nm + i4));
-        acc.x += p.x;
-        acc.y += p.y;
-        acc.z += p.z;
-        acc.w += p.w;
-    }
-    if (OUT_F32) {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + i4) = acc;
-    } else {
-        __half2 a = __floats2half2_rn(acc.x, acc.y), b = __floats2half2_rn(acc.z, acc.w);
-        uint2 v = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(out) + i4) = v;
-    }
 }
 
 // Row-sharded projection with the all-gather fused into the epilogue: every output chunk is
@@ -303,7 +170,11 @@ __device__ __forceinline__ bool wait_release(const unsigned* word, unsigned epoc
 
 // OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace
 // [split][n][m], 3 / 4 = f16 / f32 to every rank's Y (all by TMA tensor stores).
-template <int OUT_MODE>
+// EXACT: every weight d*(q-8) enters the tensor cores as two f16 parts, hi = f16(d*(q-8)) and
+// lo = f16(d*(q-8) - hi), each multiplied by the same activations (twice the MMAs per stage);
+// hi + lo equals d*(q-8) exactly, so every product is the reference's exact product and only
+// the fp32 accumulation order differs from the reference's scalar sum.
+template <int OUT_MODE, bool EXACT = false>
 __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUtensorMap& tmap_q,
                                           const CUtensorMap& tmap_out,
                                           const CUtensorMap& tmap_out16,
@@ -314,7 +185,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
     const uint32_t x_stage = (uint32_t)bn * 128u;  // a multiple of 1024: SW128 atoms stay aligned
-    const uint32_t acc_col = (uint32_t)stages * 32u;  // accumulators: [acc_col, acc_col + bn)
+    constexpr uint32_t SC = stage_cols(EXACT);
+    const uint32_t acc_col = (uint32_t)stages * SC;  // accumulators: [acc_col, acc_col + bn)
     uint8_t* sx = smem;
     uint8_t* sq = smem + stages * x_stage;
     uint64_t* full = reinterpret_cast<uint64_t*>(sq + stages * Q_STAGE);
@@ -407,10 +279,13 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
                 const uint32_t ph1 = s + 1 == stages ? ph ^ 1u : ph;
                 // K steps advance 32 bytes inside the swizzled 128-byte rows (descriptor +2) and
                 // 8 TMEM columns of the stage's weights
-                ready = mma_stage_and_peek(tmem + acc_col, tmem + A_COL + (uint32_t)s * 32u,
-                                           sw128_desc(smem_u32(sx + s * x_stage)), idesc,
-                                           j > 0 ? 1u : 0u, &afull[s1], ph1) != 0 &&
+                const uint64_t bdesc = sw128_desc(smem_u32(sx + s * x_stage));
+                ready = mma_stage_and_peek(tmem + acc_col, tmem + A_COL + (uint32_t)s * SC, bdesc,
+                                           idesc, j > 0 ? 1u : 0u, &afull[s1], ph1) != 0 &&
                         j + 1 < num_k;
+                if (EXACT)
+                    mma_stage_acc(tmem + acc_col, tmem + A_COL + (uint32_t)s * SC + 32u, bdesc,
+                                  idesc);
                 mma_commit(&empty[s]);
                 if (++s == stages) {
                     s = 0;
@@ -452,9 +327,17 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
             const uint4* qp = reinterpret_cast<const uint4*>(sq + s * Q_STAGE + r * 32);
             const uint4 q0 = qp[0], q1 = qp[1];
             uint32_t cols[32];
-            dequant_block(q0, sa, cols);
-            dequant_block(q1, sb, cols + 16);
-            tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * 32u, cols);
+            if (EXACT) {
+                uint32_t lo[32];
+                dequant_block_exact(q0, sa, cols, lo);
+                dequant_block_exact(q1, sb, cols + 16, lo + 16);
+                tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * SC, cols);
+                tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * SC + 32u, lo);
+            } else {
+                dequant_block(q0, sa, cols);
+                dequant_block(q1, sb, cols + 16);
+                tmem_st32(tmem + lane_base + A_COL + (uint32_t)s * SC, cols);
+            }
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();  // every lane's stores are complete before the warp's single arrival
@@ -548,7 +431,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmap_x, const CUten
     }
 }
 
-template <int OUT_MODE>
+template <int OUT_MODE, bool EXACT>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q4_0_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_q,
@@ -556,8 +439,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const __grid_constant__ CUtensorMap tmap_out16,
                         const uint16_t* __restrict__ scales, int m, int k, int n, int bn, int nb,
                         int iters_per_split, int stages, int* __restrict__ err) {
-    gemm_body<OUT_MODE>(tmap_x, tmap_q, tmap_out, tmap_out16, scales, m, k, n, bn, nb,
-                        iters_per_split, stages, nullptr, err);
+    gemm_body<OUT_MODE, EXACT>(tmap_x, tmap_q, tmap_out, tmap_out16, scales, m, k, n, bn, nb,
+                               iters_per_split, stages, nullptr, err);
 }
 
 template <int OUT_MODE>
@@ -598,27 +481,19 @@ int encode_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int r
     return encode_tensor_map(map, dt, base, rank, dims, strides, box, swz);
 }
 
-int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
-              uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle swz) {
-    const uint64_t dims[2] = {inner, outer};
-    const uint32_t box[2] = {box_inner, box_outer};
-    return encode_map(map, dt, base, 2, dims, &row_bytes, box, swz);
-}
 
-template <int MODE>
+template <int MODE, bool EXACT = false>
 int set_smem_attr(int device) {
     static DeviceBits done;  // the attribute is per device
     if (done.test(device)) return SULIMO_OK;
-    if (MODE >= 3) {
-        int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_allgather_kernel<MODE>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)SMEM_LIMIT),
-                            "gemm smem attribute");
-        if (!st) done.set(device);
-        return st;
-    }
-    int st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<MODE>,
+    int st;
+    if constexpr (MODE >= 3)
+        st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_allgather_kernel<MODE>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)SMEM_LIMIT),
+                        "gemm smem attribute");
+    else
+        st = check_cuda(cudaFuncSetAttribute(gemm_q4_0_tc_kernel<MODE, EXACT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)SMEM_LIMIT),
                         "gemm smem attribute");
@@ -643,12 +518,37 @@ int gemm_splits(int tiles, int num_k, int num_sms) {
     return s < 1 ? 1 : s;
 }
 
+// Form of the GEMM for a shape: the CTA-pair kernel (gemm_q4_0_pair.cu) when the output has
+// more than one 128-feature tile, at least 32 tokens and k >= 128, else this one-CTA kernel
+// (narrow token counts such as the last-token logits, single-tile outputs).  SULIMO_GEMM_FORM=1 selects the
+// one-CTA kernel for every shape (a measurement switch).
+bool gemm_uses_pair(int m, int k, int n) {
+    static const int forced = [] {
+        const char* e = getenv("SULIMO_GEMM_FORM");
+        return e ? atoi(e) : 0;
+    }();
+    return forced != 1 && m > BM && n >= 32 && k >= 128;
+}
+
+namespace {
+
+// The one-CTA kernel of a launch: output mode x weight form.
+template <int MODE>
+auto one_cta_kernel(bool exact) {
+    return exact ? gemm_q4_0_tc_kernel<MODE, true> : gemm_q4_0_tc_kernel<MODE, false>;
+}
+
+}  // namespace
+
 int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                          void* out, int m, int k, int n, int out_dtype, int x_row_stride,
-                         int x_row_offset) {
+                         int x_row_offset, bool exact) {
+    if (!exact && gemm_uses_pair(m, k, n))
+        return launch_gemm_pair(ctx, scales, quants, x, out, m, k, n, out_dtype, x_row_stride,
+                                x_row_offset);
     const int nb = k / 32;
     const int bn = gemm_token_tile(n);
-    const int stages = ring_stages(bn);
+    const int stages = ring_stages(bn, exact);
     const uint32_t smem = smem_bytes(bn, stages);
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(x) + (size_t)x_row_offset * x_row_stride * 2;
     CUtensorMap tx, tq;
@@ -658,8 +558,11 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
     st = encode_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16, (uint64_t)m,
                    (uint64_t)nb * 16, 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    if ((st = set_smem_attr<0>(ctx->device)) || (st = set_smem_attr<1>(ctx->device)) ||
-        (st = set_smem_attr<2>(ctx->device)))
+    if (exact ? ((st = set_smem_attr<0, true>(ctx->device)) ||
+                 (st = set_smem_attr<1, true>(ctx->device)) ||
+                 (st = set_smem_attr<2, true>(ctx->device)))
+              : ((st = set_smem_attr<0>(ctx->device)) || (st = set_smem_attr<1>(ctx->device)) ||
+                 (st = set_smem_attr<2>(ctx->device))))
         return st;
 
     const int mt = (m + BM - 1) / BM, nt = (n + bn - 1) / bn;
@@ -682,9 +585,9 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
         if (st) return st;
         dim3 grid(mt, nt, 1);
         const cudaError_t e =
-            f32 ? launch_pdl(gemm_q4_0_tc_kernel<1>, grid, dim3(THREADS), smem, ctx->stream, tx,
+            f32 ? launch_pdl(one_cta_kernel<1>(exact), grid, dim3(THREADS), smem, ctx->stream, tx,
                              tq, to, to16, sc, m, k, n, bn, nb, ips, stages, ctx->d_error)
-                : launch_pdl(gemm_q4_0_tc_kernel<0>, grid, dim3(THREADS), smem, ctx->stream, tx,
+                : launch_pdl(one_cta_kernel<0>(exact), grid, dim3(THREADS), smem, ctx->stream, tx,
                              tq, to, to16, sc, m, k, n, bn, nb, ips, stages, ctx->d_error);
         ctx->launches++;
         return check_cuda(e, "gemm_q4_0_tc launch");
@@ -707,19 +610,23 @@ int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants
         if (st) return st;
     }
     dim3 grid(mt, nt, splits);
-    st = check_cuda(launch_pdl(gemm_q4_0_tc_kernel<2>, grid, dim3(THREADS), smem, ctx->stream,
+    st = check_cuda(launch_pdl(one_cta_kernel<2>(exact), grid, dim3(THREADS), smem, ctx->stream,
                                tx, tq, to, to16, sc, m, k, n, bn, nb, ips, stages, ctx->d_error),
                     "gemm_q4_0_tc split-K launch");
     if (st) return st;
+    ctx->launches++;
+    return launch_splitk_reduce(ctx, ws, out, nm, splits, out_dtype == SULIMO_OUT_F32);
+}
+
+int launch_splitk_reduce(sulimo_ctx* ctx, const float* ws, void* out, size_t nm, int splits,
+                         bool out_f32) {
     const unsigned rb = (unsigned)((nm / 4 + 255) / 256);  // m % 8 == 0, so nm % 4 == 0
-    const float* wsc = ws;
     const cudaError_t e =
-        out_dtype == SULIMO_OUT_F32
-            ? launch_pdl(splitk_reduce_kernel<true>, dim3(rb), dim3(256), 0, ctx->stream, wsc, out,
-                         nm, splits)
-            : launch_pdl(splitk_reduce_kernel<false>, dim3(rb), dim3(256), 0, ctx->stream, wsc,
-                         out, nm, splits);
-    ctx->launches += 2;
+        out_f32 ? launch_pdl(splitk_reduce_kernel<true>, dim3(rb), dim3(256), 0, ctx->stream, ws,
+                             out, nm, splits)
+                : launch_pdl(splitk_reduce_kernel<false>, dim3(rb), dim3(256), 0, ctx->stream, ws,
+                             out, nm, splits);
+    ctx->launches++;
     return check_cuda(e, "splitk_reduce launch");
 }
 

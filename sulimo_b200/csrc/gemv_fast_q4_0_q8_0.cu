@@ -458,8 +458,35 @@ void fill_group(GrGroup& grp, const GemvMatSrc* src, int count) {
 
 }  // namespace
 
+// The staging buffer of the batched form, grown outside stream capture only (a capture that
+// finds it too small takes the lane-tree form instead).
+static bool ensure_q8_stage(sulimo_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->q8_stage_bytes) return true;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(ctx->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+        return false;
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return false;
+    if (ctx->q8_stage) cudaFree(ctx->q8_stage);
+    ctx->q8_stage = nullptr;
+    ctx->q8_stage_bytes = 0;
+    if (cudaMalloc(&ctx->q8_stage, bytes) != cudaSuccess) {
+        ctx->q8_stage = nullptr;
+        (void)cudaGetLastError();
+        return false;
+    }
+    ctx->q8_stage_bytes = bytes;
+    return true;
+}
+
 int launch_gemv_fast_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const void* x_q8,
                            int cols, int batch, bool static_weights) {
+    // several sequences: restage the Q8_0 blocks, then the tensor-core form
+    if (batch >= GEMV_MMA_MIN_BATCH && gemv_mma_applies(src, count, cols, batch, ctx->num_sms) &&
+        ensure_q8_stage(ctx, q8_staged_bytes(batch, cols))) {
+        const Q8Out xs = q8_staged_view(ctx->q8_stage, batch, cols);
+        const int st = launch_q8_stage(ctx, x_q8, batch, cols, xs);
+        return st ? st : launch_gemv_mma_group(ctx, src, count, xs, cols, batch, static_weights);
+    }
     int nv = 1;
     if (!fast_applies(src, count, cols, batch, &nv)) {
         // the exact kernel satisfies the fast form's contract

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "../../include/sulimo_cuda.h"
+#include "sulimo_internal.h"
 
 // Device error codes written to the context's error word (first writer wins).
 #define SULIMO_DEVERR_WAIT_TIMEOUT 1
@@ -133,21 +134,54 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 
 // ---- Q8_0 ----------------------------------------------------------------------------------
-// Quantizes the 32 values of a block held one per lane and writes the 34-byte Q8_0 block
-// exactly as quantize_f32_to_q8_0 (crates/sulimo-core/src/kv_cache.rs:162-192): d = max|x|/127
-// (IEEE f32), stored as f16 RNE; id = 1/d from the f32 d; q = clamp(roundf(x*id), -128, 127).
-__device__ __forceinline__ void quantize_block_warp(float v, uint8_t* dst, int lane) {
+// Quantizes the 32 values of a block held one per lane exactly as quantize_f32_to_q8_0
+// (crates/sulimo-core/src/kv_cache.rs:162-192): d = max|x|/127 (IEEE f32), stored as f16 RNE;
+// id = 1/d from the f32 d; q = clamp(roundf(x*id), -128, 127).  Returns this lane's code and
+// the f32 d in *d_out (every lane).
+__device__ __forceinline__ int q8_quantize_lane(float v, float* d_out) {
     float a = fabsf(v);  // fmaxf drops NaN like the reference's `a > max_abs` test
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
-    float d = __fdiv_rn(a, 127.0f);
-    float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float d = __fdiv_rn(a, 127.0f);
+    const float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
     float q = roundf(__fmul_rn(v, id));
     if (q != q) q = 0.0f;  // f32 NaN `as i8` == 0
     q = fminf(fmaxf(q, -128.0f), 127.0f);
-    dst[2 + lane] = (uint8_t)(int8_t)(int)q;
+    *d_out = d;
+    return (int)q;
+}
+
+// The 34-byte Q8_0 block [d: f16][32 x i8] of the 32 values held one per lane.
+__device__ __forceinline__ void quantize_block_warp(float v, uint8_t* dst, int lane) {
+    float d;
+    const int q = q8_quantize_lane(v, &d);
+    dst[2 + lane] = (uint8_t)(int8_t)q;
     // the f16 scale as one 2-byte store (blocks are 34 bytes, so dst is 2-byte aligned)
     if (lane == 0) *reinterpret_cast<__half*>(dst) = __float2half_rn(d);
+}
+
+// Writes the block as Q8Out asks: the block array and / or the staged form (the staged
+// aux word needs the block's code sum: one warp reduction).
+__device__ __forceinline__ void q8_store_block(const Q8Out& o, float v, size_t row, int blk,
+                                               int lane) {
+    float d;
+    const int q = q8_quantize_lane(v, &d);
+    const __half dh = __float2half_rn(d);
+    const int nb = o.K / 32;
+    if (o.aos) {
+        uint8_t* dst = o.aos + (row * nb + blk) * 34;
+        dst[2 + lane] = (uint8_t)(int8_t)q;
+        if (lane == 0) *reinterpret_cast<__half*>(dst) = dh;
+    }
+    if (o.codes) {
+        o.codes[row * o.K + (size_t)blk * 32 + lane] = (int8_t)q;
+        int s = q;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (lane == 0)
+            o.aux[((row >> 3) * nb + blk) * 8 + (row & 7)] =
+                make_int2(__float_as_int(__half2float(dh)), 0x4B400000 - 8 * s);
+    }
 }
 
 // ---- misc ------------------------------------------------------------------------------

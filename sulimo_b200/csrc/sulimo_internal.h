@@ -23,6 +23,8 @@ struct sulimo_ctx {
     void* argmax_scratch = nullptr;  // greedy argmax partials + per-row counters (zero at rest)
     size_t argmax_bytes = 0;
     unsigned* attn_counters = nullptr;  // decode attention merge counters (zero at rest)
+    void* q8_stage = nullptr;  // staged activations of the batched fast matvec (C-ABI inputs)
+    size_t q8_stage_bytes = 0;
     std::atomic<uint64_t> launches{0};
 };
 
@@ -77,9 +79,23 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base
                       CUtensorMapSwizzle swz);
 
 // Launchers (return SULIMO_* status; argument checks done by the C-ABI layer).
+// Tile plan of the CTA-pair prefill GEMM (gemm_q4_0_pair.cu).
+struct PairPlan {
+    int bn, splits, iters_per_split, stages, grid_x, grid_y;
+    uint32_t smem;
+};
+PairPlan gemm_pair_plan(int m, int k, int n, int max_pairs);
+bool gemm_uses_pair(int m, int k, int n);
+int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
+                     void* out, int m, int k, int n, int out_dtype, int x_row_stride,
+                     int x_row_offset);
+// Ordered sum of split-K fp32 partials ws[splits][nm] into f16 / f32 out (one launch).
+int launch_splitk_reduce(sulimo_ctx* ctx, const float* ws, void* out, size_t nm, int splits,
+                         bool out_f32);
+// exact: the exact-weight form (hi + lo f16 parts of every weight; one-CTA kernel).
 int launch_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                          void* out, int m, int k, int n, int out_dtype, int x_row_stride,
-                         int x_row_offset);
+                         int x_row_offset, bool exact = false);
 // Row-sharded GEMM with the all-gather in the epilogue (see gemm_q4_0_tc.cu): stores this rank's
 // [n][m_local] result at column col0 of every rank's row-major Y (row pitch f_total elements,
 // out_bases[r] mapped in this process) and adds one per CTA to every rank's counter.
@@ -89,6 +105,23 @@ int launch_gemm_allgather(sulimo_ctx* ctx, const void* scales, const void* quant
                           unsigned* const* flags, unsigned* const* release, int world, int rank,
                           unsigned epoch, unsigned* tiles_out);
 int launch_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned target);
+// Where a decode-step producer writes its Q8_0 activations (row = sequence, K values per row):
+//   aos:   the reference's block array [rows][K/32][34], or null;
+//   codes / aux: the staged form the batched tensor-core matvec reads (gemv_mma_q4_0_q8_0.cu),
+//          or null: codes [rows8][K] i8 (rows8 = rows rounded up to 8) and per block
+//          aux [rows8 / 8][K/32][8] = {d as f32 bits (the f16 value), 0x4B400000 - 8 * sum(q)}
+//          (the second word seeds the matvec's integer accumulator).
+struct Q8Out {
+    uint8_t* aos;
+    int8_t* codes;
+    int2* aux;
+    int K;
+};
+// Bytes of the staged form for `batch` rows of K values, and its two arrays inside `base`.
+size_t q8_staged_bytes(int batch, int K);
+Q8Out q8_staged_view(void* base, int batch, int K);
+// Q8_0 block arrays [batch][K/32][34] -> the staged form (one launch).
+int launch_q8_stage(sulimo_ctx* ctx, const void* x_q8, int batch, int K, const Q8Out& dst);
 int launch_gemv_q4_0_q8_0(sulimo_ctx* ctx, const void* w_scales, const void* w_quants,
                           const void* x_q8, int rows, int cols, int batch, float* out);
 // One matrix of a grouped decode GEMV (all of a group share K and the activations).
@@ -112,6 +145,14 @@ int launch_gemv_static(sulimo_ctx* ctx, const void* w_scales, const void* w_quan
 // kernel when its layout conditions do not hold.
 int launch_gemv_fast_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const void* x_q8,
                            int cols, int batch, bool static_weights);
+// Batched fast-mode matvec on the tensor cores (gemv_mma_q4_0_q8_0.cu) for 1..3 matrices
+// sharing staged activations x (Q8Out codes / aux); gemv_mma_applies tells whether the shape and
+// layout qualify (K a multiple of 256, 16-byte aligned quants and scales).
+bool gemv_mma_applies(const GemvMatSrc* src, int count, int cols, int batch, int num_sms);
+// Sequences from which the fast matvec takes the tensor-core form.
+constexpr int GEMV_MMA_MIN_BATCH = 2;
+int launch_gemv_mma_group(sulimo_ctx* ctx, const GemvMatSrc* src, int count, const Q8Out& x,
+                          int cols, int batch, bool static_weights);
 // Activation producer folded into the fast matvec's prologue (every CTA recomputes the vector
 // from L2 after the launch's dependency wait; the quantization is quantize_f32_to_q8_0):
 //   GEMV_PRO_NORM: v = a + b (b may be null), written to a_out by the CTAs of column 0 when
@@ -153,7 +194,7 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
                            const void* v_ring, size_t seq_stride, size_t capacity,
                            size_t context_len, int head_count, int head_count_kv, int head_dim,
                            int batch, float softcap, float* out, float* partials,
-                           size_t partial_bytes, unsigned* counters, uint8_t* out_q8,
+                           size_t partial_bytes, unsigned* counters, const Q8Out& out_q8,
                            bool* used, size_t static_before = 0);
 size_t attn_decode_mma_partial_bytes(size_t ctx_len, size_t capacity, int H, int Hkv, int HD,
                                      int batch, int num_sms, size_t seq_stride, const void* k,
@@ -161,7 +202,7 @@ size_t attn_decode_mma_partial_bytes(size_t ctx_len, size_t capacity, int H, int
 int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                        size_t seq_stride, size_t capacity, size_t context_len, int head_count,
                        int head_count_kv, int head_dim, int batch, float softcap, float* out,
-                       float* partials, size_t partial_bytes, uint8_t* out_q8 = nullptr,
+                       float* partials, size_t partial_bytes, const Q8Out* out_q8 = nullptr,
                        size_t static_before = 0);
 int launch_unshard_rows(sulimo_ctx* ctx, const void* gathered, void* out, int world,
                         int m_tokens, size_t fs, size_t f, int elem_size);

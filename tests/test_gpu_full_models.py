@@ -89,6 +89,41 @@ def test_config4_llama3b_decode_at_context_4096(ctx):
     decode_positions(ctx, dm, om, 1234, range(cap - 4, cap), "config 4")
 
 
+@pytest.mark.parametrize("batch,check_seqs", [(8, (0, 5, 7)), (32, (0, 19, 31))])
+def test_config4_llama3b_batched_decode(ctx, batch, check_seqs):
+    """Config 4 with 8 and 32 sequences at context 4096 (each sequence its own N(0,1) rings and
+    token): the decode step's batched form (activations staged by their producers, tensor-core
+    matvecs, tensor-core attention).  Three sequences per batch against their own oracle runs."""
+    import torch
+    import sulimo_b200 as sb
+    from sulimo_b200.model import DecodeModel
+    from sulimo_b200.synthetic import LLAMA_3B, make_model_torch
+    cap = 4096
+    w = make_model_torch(dict(LLAMA_3B), seed=0, kv_capacity=cap)
+    dm = DecodeModel(ctx, w, batch=batch)
+    kvd = LLAMA_3B["head_count_kv"] * LLAMA_3B["head_dim"]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(6 + batch)
+    for kr, vr in dm.rings:
+        for r in (kr, vr):
+            x = torch.randn(batch * cap * kvd, device="cuda", generator=gen)
+            sb.quantize_f32_to_q8_0(ctx, x, r)
+    ctx.finish()
+    toks = torch.randint(0, LLAMA_3B["vocab"], (batch,), dtype=torch.int32, device="cuda",
+                         generator=gen)
+    got = dm.forward_token(toks, cap - 1).cpu().numpy().reshape(batch, -1)
+    ctx.finish()
+    hm = host_model(w)
+    slot = kvd // 32 * 34
+    for sq in check_seqs:
+        om = O.OracleModel(hm)
+        for (kr, vr), (ok, ov) in zip(dm.rings, om.rings):
+            ok[:] = kr[sq * cap * slot:(sq + 1) * cap * slot].cpu().numpy()
+            ov[:] = vr[sq * cap * slot:(sq + 1) * cap * slot].cpu().numpy()
+        ref = om.forward_token(int(toks[sq].item()), cap - 1)
+        check(got[sq][:LLAMA_3B["vocab"]], ref, f"config 4 batch {batch} seq {sq}")
+
+
 def test_config3_qwen_decode_after_512_token_prefill(ctx):
     import torch
     from sulimo_b200.model import DecodeModel

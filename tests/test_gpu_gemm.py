@@ -49,6 +49,36 @@ def test_gemm_reference_test_shapes(ctx, n, k, m):
     assert rel_l2(got32, ref32) <= TOL
 
 
+@pytest.mark.parametrize("n,k,m", [(8, 256, 256), (32, 512, 512), (128, 512, 1024),
+                                   (512, 1024, 1024), (512, 1536, 8960), (512, 8960, 1536)])
+def test_gemm_exact_weights_meet_reference_bar(ctx, n, k, m):
+    """The exact-weight form against the reference test's full bar (test_gemm.rs:207-214):
+    max |g - c| / max(|c|, 1) <= 2e-3 and cosine >= 0.9999, on the test's generators (its
+    four shapes) and on benchmark config 2's two shapes."""
+    import torch
+    if (n, k, m) in ((512, 1536, 8960), (512, 8960, 1536)):
+        ws, wq = make_q4_0(m, k, seed=m)
+        x = np.random.default_rng(k).standard_normal(n * k).astype(np.float16)
+    else:
+        ws, wq = make_q4_0_pattern_gemm(m, k)
+        x = make_x_pattern_gemm(n, k)
+    # the scalar reference's f16 result is its fp32 sum rounded to f16
+    ref32 = O.gemm_q4_0_f16_f32out(ws, wq, x.view(np.uint16), m, k, n, threads=8)
+    out = empty(n * m, torch.float16)
+    sb.gemm_q4_0_f16_exact(ctx, dev(ws), dev(wq), dev(x), out, m, k, n, sb.OUT_F16)
+    ctx.finish()
+    g = host(out).astype(np.float32)
+    c = ref32.astype(np.float16).astype(np.float32)
+    mre = max_rel_err(g, c)
+    print(f"exact n={n} k={k} m={m}: max_rel_err={mre:.3e} rel_l2={rel_l2(g, c):.3e}")
+    assert mre <= TOL
+    assert cosine(g, c) >= 0.9999
+    out32 = empty(n * m, torch.float32)
+    sb.gemm_q4_0_f16_exact(ctx, dev(ws), dev(wq), dev(x), out32, m, k, n, sb.OUT_F32)
+    ctx.finish()
+    assert rel_l2(host(out32), ref32) <= 1e-5
+
+
 def torch_reference(ws, wq, x16, m, k, n):
     """fp32 restatement on the GPU: exact f32 dequantized weights, f16 activations widened."""
     import torch
@@ -96,6 +126,11 @@ def test_gemm_config2_full_size(ctx, n, k, m):
     (257, 512, 128),   # two token tiles, the second with one token
     (16, 4096, 128),   # one output tile: K split over 8 CTAs + ordered reduction
     (40, 2080, 64),    # split K with a short last split (33 stages over 4 splits)
+    # CTA-pair form (more than 128 features, >= 32 tokens, k >= 128)
+    (33, 640, 392),    # 64-token pair tile with 33 tokens, second pair half past m
+    (100, 1056, 520),  # K = 33 blocks: the last 128-k stage holds one block
+    (64, 4096, 512),   # two pair tiles: K split into 8 partials + ordered reduction
+    (520, 1536, 384),  # three token tiles, the last one 8 tokens wide
 ])
 def test_gemm_ragged_shapes(ctx, n, k, m):
     ws, wq = make_q4_0(m, k, seed=n + k + m)

@@ -246,3 +246,42 @@ def test_gemv_fast_matches_avx2_within_rounding(ctx, rows, cols, batch):
         got = outs[0][b]
         rel = np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref.astype(np.float64))
         assert rel <= 1e-5, rel
+
+
+# ---- fast mode, several sequences: the tensor-core form (gemv_mma_q4_0_q8_0.cu) ----------------
+
+@pytest.mark.parametrize("rows,cols,batch", [(3072, 3072, 8), (8192, 3072, 32), (3072, 8192, 32),
+                                             (1000, 2048, 13), (16, 256, 2), (257, 512, 17),
+                                             (20000, 3072, 8), (5120, 3072, 40)])
+def test_gemv_fast_batched_tensor_core_form(ctx, rows, cols, batch):
+    """From 2 sequences (K a multiple of 256) the fast entry restages the Q8_0 blocks and runs the
+    tensor-core matvec: exact integer block sums (mma m16n8k32), fp32 accumulation in block order.
+    Each sequence against the AVX2 oracle at rel-L2 <= 1e-5; static / non-static and repeated
+    calls bit-identical.  Shapes: config 4's q/o (8 sequences), gate/up and down (32: one and
+    four 8-sequence groups per CTA), a vocabulary-sized matrix, ragged rows (not a multiple of
+    the 16-row tiles), ragged batches (13, 17, 40: partial 8-sequence tiles and groups), and
+    activations with all-zero and saturated blocks."""
+    import torch
+    ws, wq = make_q4_0(rows, cols, seed=rows + 3 * cols + batch)
+    rng = np.random.default_rng(batch * 31 + rows)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    x[0, :64] = 0.0                      # two all-zero blocks (d = 0)
+    x[-1, 32:64] = 1e4 * np.sign(x[-1, 32:64])   # a saturated block (codes +-127)
+    xq8 = np.concatenate([O.quantize_f32_to_q8_0(x[b]) for b in range(batch)])
+    dws, dwq, dx = dev(ws), dev(wq), dev(xq8)
+    outs = []
+    for static in (False, True, True):
+        out = empty(batch * rows, torch.float32)
+        out.fill_(float("nan"))
+        sb.matvec_q4_0_q8_0_fast(ctx, dws, dwq, dx, rows, cols, out, batch, static)
+        ctx.finish()
+        outs.append(host(out).reshape(batch, rows))
+    for o in outs[1:]:
+        assert np.array_equal(outs[0].view(np.uint32), o.view(np.uint32))
+    nbx = cols // 32 * 34
+    for b in range(batch):
+        ref = O.matvec_q4_0_q8_0_avx2(ws, wq, xq8[b * nbx:(b + 1) * nbx], rows, cols, threads=8)
+        got = outs[0][b]
+        assert np.isfinite(got).all(), b
+        rel = np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref.astype(np.float64))
+        assert rel <= 1e-5, (b, rel)
