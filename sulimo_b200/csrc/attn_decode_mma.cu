@@ -23,10 +23,10 @@
 //       O[head][dim] += P' . V: per 32-dimension block b the A operand is P * d_V[pos][b], again
 //         hi / lo f16 in rows 0-7 / 8-15, B = V's int8 codes; O accumulates in fp32.
 //   merge: the eight warps' (m, l, o) through shared memory into the CTA's partial, written to
-//     the workspace; the last CTA of a (sequence, kv head) (arrival counter, zero at rest)
-//     computes each head's softmax weights over the splits once, then every output dimension
-//     as one weighted sum over the splits, and writes the output (and, for the decode step, its
-//     Q8_0 quantization).  With one split the CTA writes the output directly.
+//     the workspace; attn_decode_merge_kernel, a programmatic dependent launch, then merges the
+//     splits with one warp per (sequence, query head, 32-dimension block) and writes the output
+//     (and, for the decode step, its Q8_0 quantization).  With one split the CTA writes the
+//     output directly.
 // Numerics: products are exact, sums are fp32 in a different order than the reference's
 // sequential loop, and q / P' carry ~22 significant bits: the result matches the reference
 // within fp32-level rounding (the parity tests bound the relative L2 error at 2e-3).
@@ -44,7 +44,7 @@ constexpr int AM_CONSUMERS = 8;                      // consumer warps
 constexpr int AM_THREADS = (AM_CONSUMERS + 1) * 32;  // + one producer warp
 constexpr int AM_SP = 16 * AM_CONSUMERS;             // positions per stage: one tile per warp
 constexpr int AM_MAX_STAGES = 4;
-constexpr int AM_MAX_SPLITS = 32;   // splits per (sequence, kv head): the final merge reads
+constexpr int AM_MAX_SPLITS = 32;   // splits per (sequence, kv head): the merge kernel reads
                                     // each output dimension's partials in one batch
 constexpr size_t AM_SMEM_MAX = 200 * 1024;
 constexpr float AM_LOG2E = 1.4426950408889634f;
@@ -62,7 +62,6 @@ struct AttnMmaArgs {
     float* out;             // [batch][H][HD] or null
     Q8Out q8;               // the output as Q8_0 rows [batch][H * HD] (forms it names)
     float* part;            // [batch][Hkv][splits][G][HD + 2]
-    unsigned* counters;     // [batch][Hkv]
     int* err;
 };
 
@@ -151,7 +150,6 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
     const uint32_t stage_bytes = 2u * AM_SP * rs;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.stages * stage_bytes);
     uint64_t* empty = full + a.stages;
-    int* last_flag = reinterpret_cast<int*>(empty + a.stages);
 
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z, splits = gridDim.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -378,72 +376,55 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
             dst_part[(size_t)gg * HD2 + d] = d < HD ? o : (d == HD ? m : l);
         }
     }
-    if (direct) return;
+}
 
-    // ---- the last CTA of this (sequence, kv head) merges the splits ----
-    __threadfence();  // this thread's partial before the arrival count
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned old = atomicAdd(a.counters + (size_t)seq * a.Hkv + kvh, 1u);
-        *last_flag = old == (unsigned)(splits - 1);
-        __threadfence();
-    }
-    __syncthreads();
-    if (!*last_flag) return;
-    const float* base = a.part + ((size_t)seq * a.Hkv + kvh) * splits * a.G * HD2;
-    // softmax weights of every split per head, w[g][s] = e^(m_s - M) / L: (m, l) of all splits
-    // loaded in one pass, then one warp per head
-    float* wts = reinterpret_cast<float*>(smem);          // [G][splits]
-    float* lsum = wts + (size_t)a.G * AM_MAX_SPLITS;      // [G][splits]
-    for (int i = tid; i < a.G * splits; i += AM_THREADS) {
-        const int gg = i / splits, sp = i % splits;
-        const float* r = base + ((size_t)sp * a.G + gg) * HD2 + HD;
-        wts[i] = __ldcg(r);
-        lsum[i] = __ldcg(r + 1);
-    }
-    __syncthreads();
-    if (warp < a.G) {
-        float* wg = wts + (size_t)warp * splits;
-        const float* lg = lsum + (size_t)warp * splits;
-        float M = -INFINITY;
-        for (int sp = lane; sp < splits; sp += 32) M = fmaxf(M, wg[sp]);
+// Merge of the splits' partials: one warp per (sequence, query head, 32-dimension block), lane =
+// dimension.  The (m, l) of every split and the warp's 32 dimensions of every split's o are
+// loaded in one batch (at most AM_MAX_SPLITS), then O = sum_s o_s e^(m_s - M), L = sum_s l_s
+// e^(m_s - M) and out = O / L; the block is also written as one Q8_0 block when asked (the
+// decode step's o-projection input).  A programmatic dependent of the split kernel: the loads
+// wait in griddepcontrol.wait, the launch and set-up overlap the split kernel's tail.
+template <int HD>
+__global__ void __launch_bounds__(128)
+    attn_decode_merge_kernel(const __grid_constant__ AttnMmaArgs a, int splits) {
+    constexpr int NB = HD / 32, HD2 = HD + 2;
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * 4 + (threadIdx.x >> 5);  // (head, block)
+    const int seq = blockIdx.y;
+    if (item >= a.H * NB) return;
+    const int h = item / NB, b = item % NB;
+    const int kvh = h / a.G, gg = h % a.G;
+    const float* base = a.part + ((size_t)seq * a.Hkv + kvh) * splits * a.G * HD2 +
+                        (size_t)gg * HD2;
+    const size_t sstride = (size_t)a.G * HD2;
+    pdl_wait_prerequisites();
+    float mi[AM_MAX_SPLITS], li[AM_MAX_SPLITS], oi[AM_MAX_SPLITS];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float L = 0.0f;
-        for (int sp = lane; sp < splits; sp += 32) {
-            const float mi = wg[sp];
-            const float e = (mi == -INFINITY) ? 0.0f : exp2f((mi - M) * AM_LOG2E);
-            L = __fmaf_rn(lg[sp], e, L);
-            wg[sp] = e;
+    for (int sp = 0; sp < AM_MAX_SPLITS; sp++) {
+        if (sp < splits) {
+            const float* r = base + (size_t)sp * sstride;
+            mi[sp] = __ldcg(r + HD);
+            li[sp] = __ldcg(r + HD + 1);
+            oi[sp] = __ldcg(r + b * 32 + lane);
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-        __syncwarp();
-        for (int sp = lane; sp < splits; sp += 32) wg[sp] *= inv;
     }
-    __syncthreads();
-    // every output dimension: one weighted sum over the splits, all loads issued first
-    for (int it = tid; it < a.G * HD; it += AM_THREADS) {
-        const int gg = it / HD, d = it % HD;
-        const float* wg = wts + (size_t)gg * splits;
-        const float* col = base + (size_t)gg * HD2 + d;
-        const size_t sstride = (size_t)a.G * HD2;
-        float acc = 0.0f;
-        for (int s0 = 0; s0 < splits; s0 += 32) {
-            float o[32];
+    float M = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 32; j++)
-                o[j] = s0 + j < splits ? __ldcg(col + (size_t)(s0 + j) * sstride) : 0.0f;
+    for (int sp = 0; sp < AM_MAX_SPLITS; sp++)
+        if (sp < splits) M = fmaxf(M, mi[sp]);
+    float L = 0.0f, O = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 32; j++)
-                if (s0 + j < splits) acc = __fmaf_rn(o[j], wg[s0 + j], acc);
+    for (int sp = 0; sp < AM_MAX_SPLITS; sp++) {
+        if (sp < splits && mi[sp] != -INFINITY) {
+            const float e = exp2f((mi[sp] - M) * AM_LOG2E);
+            L = __fmaf_rn(li[sp], e, L);
+            O = __fmaf_rn(oi[sp], e, O);
         }
-        const size_t h = (size_t)kvh * a.G + gg;
-        if (a.out) a.out[((size_t)seq * a.H + h) * HD + d] = acc;
-        if (a.q8.aos || a.q8.codes) q8_store_block(a.q8, acc, (size_t)seq, (int)(h * NB + d / 32), lane);
     }
-    if (tid == 0) a.counters[(size_t)seq * a.Hkv + kvh] = 0u;  // zero at rest for the next call
+    const float val = L > 0.0f ? O / L : 0.0f;
+    if (a.out) a.out[((size_t)seq * a.H + h) * HD + b * 32 + lane] = val;
+    if (a.q8.aos || a.q8.codes) q8_store_block(a.q8, val, (size_t)seq, h * NB + b, lane);
 }
 
 struct MmaPlan {
@@ -489,8 +470,7 @@ bool mma_plan(size_t ctx_len, size_t capacity, int H, int Hkv, int HD, int batch
     size_t chunk = (ctx_len + target - 1) / target;
     chunk = (chunk + 15) / 16 * 16;
     const size_t splits = (ctx_len + chunk - 1) / chunk;
-    if (splits > AM_MAX_SPLITS || G * AM_MAX_SPLITS * 8 > (size_t)pl->stages * stage)
-        return false;
+    if (splits > AM_MAX_SPLITS) return false;
     pl->chunk = (int)chunk;
     pl->splits = (int)splits;
     return true;
@@ -508,12 +488,18 @@ int launch_mma_hd(sulimo_ctx* ctx, const AttnMmaArgs& args, const MmaPlan& pl, i
         if (st) return st;
         attr_done.set(ctx->device);
     }
-    const cudaError_t e =
+    cudaError_t e =
         launch_pdl(attn_decode_mma_kernel<HD>, dim3((unsigned)pl.splits, (unsigned)args.Hkv,
                                                     (unsigned)batch),
                    dim3(AM_THREADS), pl.smem, ctx->stream, args, tk, tv);
     ctx->launches++;
-    return check_cuda(e, "attn_decode_mma launch");
+    if (e != cudaSuccess || pl.splits == 1) return check_cuda(e, "attn_decode_mma launch");
+    constexpr int NB = HD / 32;
+    e = launch_pdl(attn_decode_merge_kernel<HD>,
+                   dim3((unsigned)((args.H * NB + 3) / 4), (unsigned)batch), dim3(128), 0,
+                   ctx->stream, args, pl.splits);
+    ctx->launches++;
+    return check_cuda(e, "attn_decode_merge launch");
 }
 
 }  // namespace
@@ -530,12 +516,11 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
                            const void* v_ring, size_t seq_stride, size_t capacity,
                            size_t context_len, int head_count, int head_count_kv, int head_dim,
                            int batch, float softcap, float* out, float* partials,
-                           size_t partial_bytes, unsigned* counters, const Q8Out& out_q8,
+                           size_t partial_bytes, const Q8Out& out_q8,
                            bool* used, size_t static_before) {
     *used = false;
     MmaPlan pl;
-    if (!counters || (size_t)batch * head_count_kv > ATTN_COUNTERS ||
-        !mma_plan(context_len, capacity, head_count, head_count_kv, head_dim, batch, ctx->num_sms,
+    if (!mma_plan(context_len, capacity, head_count, head_count_kv, head_dim, batch, ctx->num_sms,
                   seq_stride, k_ring, v_ring, &pl))
         return SULIMO_OK;
     const size_t need = (size_t)batch * head_count * pl.splits * (head_dim + 2) * sizeof(float);
@@ -571,7 +556,6 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
     args.out = out;
     args.q8 = out_q8;
     args.part = partials;
-    args.counters = counters;
     args.err = ctx->d_error;
     *used = true;
     return head_dim == 64 ? launch_mma_hd<64>(ctx, args, pl, batch, tk, tv)

@@ -870,7 +870,7 @@ int launch_attn_decode(sulimo_ctx* ctx, const float* q, const void* k_ring, cons
     const int st = launch_attn_decode_mma(ctx, q, k_ring, v_ring, seq_stride, capacity,
                                           context_len, head_count, head_count_kv, head_dim,
                                           batch, softcap, out, partials, partial_bytes,
-                                          ctx->attn_counters, out_q8, &used, static_before);
+                                          out_q8, &used, static_before);
     if (st || used) return st;
     const int splits = attn_decode_splits(context_len, capacity, head_count, head_count_kv,
                                           head_dim, batch, ctx->num_sms, seq_stride, k_ring,

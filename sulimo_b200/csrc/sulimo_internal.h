@@ -194,7 +194,7 @@ int launch_attn_decode_mma(sulimo_ctx* ctx, const float* q, const void* k_ring,
                            const void* v_ring, size_t seq_stride, size_t capacity,
                            size_t context_len, int head_count, int head_count_kv, int head_dim,
                            int batch, float softcap, float* out, float* partials,
-                           size_t partial_bytes, unsigned* counters, const Q8Out& out_q8,
+                           size_t partial_bytes, const Q8Out& out_q8,
                            bool* used, size_t static_before = 0);
 size_t attn_decode_mma_partial_bytes(size_t ctx_len, size_t capacity, int H, int Hkv, int HD,
                                      int batch, int num_sms, size_t seq_stride, const void* k,
