@@ -83,9 +83,12 @@ __device__ __forceinline__ uint32_t s8pair_to_h2(uint32_t w) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// bytes b0 (of x) and b0 (of y) -> f16 pair {x, y}
-__device__ __forceinline__ uint32_t s8two_to_h2(uint32_t x, uint32_t y) {
-    return s8pair_to_h2(prmt(x, y, 0x7740u));
+// bytes 0 and 2 of w (int8 codes) -> the f16 pair {byte0, byte2}, exactly (as s8pair_to_h2;
+// bytes 1 and 3 are ignored): one LOP3 builds 0x64XX with XX = code ^ 0x80.
+__device__ __forceinline__ uint32_t s8sel_to_h2(uint32_t w) {
+    uint32_t t = (w & 0x00FF00FFu) ^ 0x64806480u;
+    __half2 h = __hsub2(*reinterpret_cast<__half2*>(&t), __floats2half2_rn(1152.0f, 1152.0f));
+    return *reinterpret_cast<uint32_t*>(&h);
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -320,11 +323,23 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
                         A[2] = h2_bits(h89);
                         A[3] = h2_bits(__floats2half2_rn(pp[2] - f89.x, pp[3] - f89.y));
                     }
+                    // n-tile n4, column c <-> dimension 32b + 4c + n4: lane group g needs dims
+                    // 4g .. 4g+3 of the block at each of its four positions, one 4-byte word
+                    // per position (two 2-byte loads where the word is 2-byte aligned: the
+                    // codes of even blocks start 2 bytes past a 4-byte boundary)
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const uint8_t* cp =
+                            v0 + (size_t)((i >> 1) * 8 + (i & 1)) * rs + b * 34 + 2 + 4 * g;
+                        w[i] = (b & 1) ? *reinterpret_cast<const uint32_t*>(cp)
+                                       : prmt(lds_u16(cp), lds_u16(cp + 2), 0x5410u);
+                    }
 #pragma unroll
                     for (int n4 = 0; n4 < 4; n4++) {
-                        const uint8_t* col = v0 + b * 34 + 2 + n4 * 8 + g;
-                        const uint32_t b0 = s8two_to_h2(col[0], col[rs]);
-                        const uint32_t b1 = s8two_to_h2(col[(size_t)8 * rs], col[(size_t)9 * rs]);
+                        const uint32_t sel = (uint32_t)n4 | ((uint32_t)(4 + n4) << 8);
+                        const uint32_t b0 = s8sel_to_h2(prmt(w[0], w[1], sel));
+                        const uint32_t b1 = s8sel_to_h2(prmt(w[2], w[3], sel));
                         mma_16816(oc[b * 4 + n4], A, b0, b1);
                     }
                 }
@@ -343,9 +358,9 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
         if (g < a.G) {
             float* row = wpart + ((size_t)warp * a.G + g) * HD2;
 #pragma unroll
-            for (int n = 0; n < NT; n++) {
-                row[n * 8 + 2 * tig] = oc[n][0] + oc[n][2];
-                row[n * 8 + 2 * tig + 1] = oc[n][1] + oc[n][3];
+            for (int n = 0; n < NT; n++) {  // n = 4b + n4: dims 32b + 4c + n4, c = 2tig, +1
+                row[(n >> 2) * 32 + 8 * tig + (n & 3)] = oc[n][0] + oc[n][2];
+                row[(n >> 2) * 32 + 8 * tig + 4 + (n & 3)] = oc[n][1] + oc[n][3];
             }
             if (tig == 0) {
                 row[HD] = m_run;
@@ -379,11 +394,13 @@ __global__ void __launch_bounds__(AM_THREADS, 1)
 }
 
 // Merge of the splits' partials: one warp per (sequence, query head, 32-dimension block), lane =
-// dimension.  The (m, l) of every split and the warp's 32 dimensions of every split's o are
-// loaded in one batch (at most AM_MAX_SPLITS), then O = sum_s o_s e^(m_s - M), L = sum_s l_s
-// e^(m_s - M) and out = O / L; the block is also written as one Q8_0 block when asked (the
-// decode step's o-projection input).  A programmatic dependent of the split kernel: the loads
-// wait in griddepcontrol.wait, the launch and set-up overlap the split kernel's tail.
+// dimension.  Lane s loads split s's (m, l) (splits <= 32) and every lane its dimension of each
+// split's o, all issued before any is used; M is a warp max, split s's weight e_s =
+// e^(m_s - M) is computed once by lane s and broadcast by shuffle, L = sum_s l_s e_s and
+// O = sum_s o_s e_s in split order, out = O / L; the block is also written as one Q8_0 block
+// when asked (the decode step's o-projection input).  A programmatic dependent of the split
+// kernel: the loads wait in griddepcontrol.wait, the launch overlaps the split kernel's tail.
+// The code is kept short (it runs once per launch from a cold instruction cache).
 template <int HD>
 __global__ void __launch_bounds__(128)
     attn_decode_merge_kernel(const __grid_constant__ AttnMmaArgs a, int splits) {
@@ -399,28 +416,25 @@ __global__ void __launch_bounds__(128)
                         (size_t)gg * HD2;
     const size_t sstride = (size_t)a.G * HD2;
     pdl_wait_prerequisites();
-    float mi[AM_MAX_SPLITS], li[AM_MAX_SPLITS], oi[AM_MAX_SPLITS];
-#pragma unroll
-    for (int sp = 0; sp < AM_MAX_SPLITS; sp++) {
-        if (sp < splits) {
-            const float* r = base + (size_t)sp * sstride;
-            mi[sp] = __ldcg(r + HD);
-            li[sp] = __ldcg(r + HD + 1);
-            oi[sp] = __ldcg(r + b * 32 + lane);
-        }
-    }
-    float M = -INFINITY;
+    const bool mine = lane < splits;
+    const float ms = mine ? __ldcg(base + (size_t)lane * sstride + HD) : -INFINITY;
+    const float ls = mine ? __ldcg(base + (size_t)lane * sstride + HD + 1) : 0.0f;
+    float oi[AM_MAX_SPLITS];
 #pragma unroll
     for (int sp = 0; sp < AM_MAX_SPLITS; sp++)
-        if (sp < splits) M = fmaxf(M, mi[sp]);
-    float L = 0.0f, O = 0.0f;
+        oi[sp] = sp < splits ? __ldcg(base + (size_t)sp * sstride + b * 32 + lane) : 0.0f;
+    float M = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float es = (ms == -INFINITY) ? 0.0f : exp2f((ms - M) * AM_LOG2E);
+    float L = ls * es;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    float O = 0.0f;
 #pragma unroll
     for (int sp = 0; sp < AM_MAX_SPLITS; sp++) {
-        if (sp < splits && mi[sp] != -INFINITY) {
-            const float e = exp2f((mi[sp] - M) * AM_LOG2E);
-            L = __fmaf_rn(li[sp], e, L);
-            O = __fmaf_rn(oi[sp], e, O);
-        }
+        const float e = __shfl_sync(0xffffffffu, es, sp);
+        if (sp < splits) O = __fmaf_rn(oi[sp], e, O);
     }
     const float val = L > 0.0f ? O / L : 0.0f;
     if (a.out) a.out[((size_t)seq * a.H + h) * HD + b * 32 + lane] = val;
