@@ -264,28 +264,39 @@ int sulimo_cuda_wait_counter(sulimo_ctx* ctx, const unsigned* flag, unsigned tar
 
 /* ---------------------------------------------------------------------------------------- */
 /* Whole decode position — replaces forward_token                                            */
-/* (crates/sulimo-engine/src/forward_pass.rs:190-417; Llama and Qwen2 branches) for a batch   */
-/* of independent sequences at the same position.  All pointers are device pointers except    */
-/* `layers` (a host array of n_layers entries).  Weights are Q4_0 SoA (scales, quants),       */
-/* norms and biases f32 (biases may be NULL), each sequence has its own Q8_0 K and V ring per  */
-/* layer: sequence s's ring starts kv_seq_stride bytes after sequence s-1's.                   */
+/* (crates/sulimo-engine/src/forward_pass.rs:190-417; its Llama, Qwen2 and Gemma 2 branches)  */
+/* for a batch of independent sequences at the same position.  All pointers are device       */
+/* pointers except `layers` (a host array of n_layers entries).  Weights are Q4_0 SoA (scales, */
+/* quants), norms and biases f32 (biases may be NULL), each sequence has its own Q8_0 K and V  */
+/* ring per layer: sequence s's ring starts kv_seq_stride bytes after sequence s-1's.          */
+/* Gemma 2 (arch = SULIMO_ARCH_GEMMA2): embeddings scaled by sqrt(embd), every RMSNorm        */
+/* weighted by (1 + w) (rmsnorm_gemma), the attention and FFN outputs RMS-normalized by        */
+/* post_attn_norm / post_ffn_norm before their residual adds (layers without them add as the  */
+/* other architectures do), GeGLU instead of SwiGLU, logits soft-capped by final_softcap       */
+/* (<= 0: none); attn_softcap as for every architecture.                                      */
 typedef struct sulimo_layer_desc {
     const void *attn_norm, *ffn_norm, *bq, *bk, *bv;
     const void *wq_scales, *wq_quants, *wk_scales, *wk_quants, *wv_scales, *wv_quants;
     const void *wo_scales, *wo_quants, *wg_scales, *wg_quants, *wu_scales, *wu_quants;
     const void *wd_scales, *wd_quants;
     void *k_ring, *v_ring;
+    const void *post_attn_norm, *post_ffn_norm; /* [embd] f32 (Gemma 2) or NULL */
 } sulimo_layer_desc;
+
+#define SULIMO_ARCH_DEFAULT 0 /* Llama / Qwen2 */
+#define SULIMO_ARCH_GEMMA2 1
 
 typedef struct sulimo_model_desc {
     int n_layers, embd, ffn, head_count, head_count_kv, head_dim, vocab, rope_dim;
-    int rope_mode; /* 0 = Norm (Llama), 1 = Neox (Qwen2) */
+    int rope_mode; /* 0 = Norm (Llama), 1 = Neox (Qwen2, Gemma 2) */
     float eps, rope_base, attn_softcap;
     size_t kv_capacity, kv_seq_stride;
     const void *tok_scales, *tok_quants; /* token_embd [vocab][embd] */
     const void *out_scales, *out_quants; /* output [vocab][embd] (tied: token_embd) */
     const float* out_norm;
     const sulimo_layer_desc* layers;
+    int arch;            /* SULIMO_ARCH_DEFAULT or SULIMO_ARCH_GEMMA2 */
+    float final_softcap; /* final logit soft-capping (Gemma 2); <= 0: none */
 } sulimo_model_desc;
 
 /* Bytes of device scratch sulimo_cuda_forward_token needs for `batch` sequences (the          */
@@ -308,7 +319,9 @@ size_t sulimo_cuda_prefill_scratch_bytes(const sulimo_model_desc* model, int n);
 /* The embeddings are the f16 rows of lookup_token_embedding_f16 (scheduler.rs:329-374), as   */
 /* the reference's engine writes them (engine.rs:249-256).  Unlike the reference's GPU ubatch  */
 /* this one applies the QKV biases (as forward_token does) and keeps the residual stream in    */
-/* fp32; the GEMM activations are f16 like the reference's.                                   */
+/* fp32; the GEMM activations are f16 like the reference's.  Like the reference's GPU ubatch, */
+/* it has no Gemma 2 steps: a Gemma 2 model is rejected (SULIMO_EINVAL) and prefills through  */
+/* sulimo_cuda_forward_token per token, as the reference's CPU prefill does.                   */
 int sulimo_cuda_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model,
                                const int32_t* tokens, int n, size_t start_pos, float* logits,
                                void* scratch, size_t scratch_bytes);

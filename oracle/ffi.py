@@ -46,6 +46,9 @@ def lib():
             "oracle_rope_head_scalar": (None, [vp, sz, sz, f32, i32]),
             "oracle_softmax_scalar": (None, [vp, sz]),
             "oracle_swiglu_scalar": (None, [vp, vp, vp, sz]),
+            "oracle_rmsnorm_gemma_avx2": (None, [vp, vp, sz, f32, vp]),
+            "oracle_geglu_scalar": (None, [vp, vp, vp, sz]),
+            "oracle_logit_softcap_scalar": (None, [vp, sz, f32]),
             "oracle_causal_gqa_decode": (None, [vp, vp, vp, sz, sz, sz, sz, sz, vp, vp, f32]),
             "oracle_rmsnorm_f16": (None, [vp, vp, vp, sz, f32, sz]),
             "oracle_rope_f16": (None, [vp, sz, sz, sz, f32, i32, sz, sz]),
@@ -207,6 +210,31 @@ def rmsnorm_avx2(x, w, eps):
     return out
 
 
+def rmsnorm_gemma_avx2(x, w, eps):
+    """rmsnorm_gemma_avx2 (crates/sulimo-cpu/src/avx2.rs:236-268): (x * scale) * (1 + w)."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm_gemma_avx2(_p(x), _p(w), x.size, eps, _p(out))
+    return out
+
+
+def geglu(gate, up):
+    """geglu_scalar (crates/sulimo-cpu/src/scalar.rs:77-89)."""
+    gate = np.ascontiguousarray(gate, np.float32)
+    up = np.ascontiguousarray(up, np.float32)
+    out = np.empty_like(gate)
+    lib().oracle_geglu_scalar(_p(gate), _p(up), _p(out), gate.size)
+    return out
+
+
+def logit_softcap(v, cap):
+    """logit_softcap_scalar (crates/sulimo-cpu/src/scalar.rs:63-71), on a copy."""
+    v = np.array(v, dtype=np.float32, copy=True)
+    lib().oracle_logit_softcap_scalar(_p(v), v.size, cap)
+    return v
+
+
 def rope_head(vec, pos, rope_dim, freq_base, mode):
     v = np.array(vec, dtype=np.float32, copy=True)
     lib().oracle_rope_head_scalar(_p(v), pos, rope_dim, freq_base, mode)
@@ -244,7 +272,8 @@ def causal_gqa_decode(q, k_ring, v_ring, capacity, context_len, head_count, head
 class _OracleLayer(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in (
         "attn_norm", "ffn_norm", "bq", "bk", "bv", "wq_s", "wq_q", "wk_s", "wk_q", "wv_s", "wv_q",
-        "wo_s", "wo_q", "wg_s", "wg_q", "wu_s", "wu_q", "wd_s", "wd_q", "k_ring", "v_ring")]
+        "wo_s", "wo_q", "wg_s", "wg_q", "wu_s", "wu_q", "wd_s", "wd_q", "k_ring", "v_ring",
+        "post_attn_norm", "post_ffn_norm")]
 
 
 class _OracleModel(C.Structure):
@@ -254,7 +283,8 @@ class _OracleModel(C.Structure):
                 ("eps", C.c_float), ("rope_base", C.c_float), ("attn_softcap", C.c_float),
                 ("kv_capacity", C.c_size_t), ("tok_s", C.c_void_p), ("tok_q", C.c_void_p),
                 ("out_s", C.c_void_p), ("out_q", C.c_void_p), ("out_norm", C.c_void_p),
-                ("layers", C.POINTER(_OracleLayer))]
+                ("layers", C.POINTER(_OracleLayer)), ("arch", C.c_int),
+                ("final_softcap", C.c_float)]
 
 
 class OracleModel:
@@ -272,7 +302,8 @@ class OracleModel:
         layers = (_OracleLayer * cfg["n_layers"])()
         for i, (L, (kr, vr)) in enumerate(zip(w["layers"], self.rings)):
             ent = layers[i]
-            for name in ("attn_norm", "ffn_norm", "bq", "bk", "bv"):
+            for name in ("attn_norm", "ffn_norm", "bq", "bk", "bv", "post_attn_norm",
+                         "post_ffn_norm"):
                 setattr(ent, name, L[name].ctypes.data if L.get(name) is not None else None)
             for name in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
                 setattr(ent, name + "_s", L[name][0].ctypes.data)
@@ -287,6 +318,8 @@ class OracleModel:
         m.out_s, m.out_q = w["out"][0].ctypes.data, w["out"][1].ctypes.data
         m.out_norm = w["out_norm"].ctypes.data
         m.layers = layers
+        m.arch = cfg.get("arch", 0)
+        m.final_softcap = cfg.get("final_softcap", 0.0)
         self.m = m
 
     def forward_token(self, token, pos):

@@ -483,6 +483,48 @@ void oracle_rmsnorm_avx2(const float* x, const float* w, size_t len, float eps, 
     for (size_t i = chunks * 8; i < len; i++) out[i] = x[i] * scale * w[i];
 }
 
+/* rmsnorm_gemma_avx2 — avx2.rs:236-268: the same sum of squares as rmsnorm_avx2, output
+ * (x * scale) * (1 + w) */
+void oracle_rmsnorm_gemma_avx2(const float* x, const float* w, size_t len, float eps, float* out) {
+    size_t chunks = len / 8;
+    __m256 ssv = _mm256_setzero_ps();
+    for (size_t i = 0; i < chunks; i++) {
+        __m256 xv = _mm256_loadu_ps(x + i * 8);
+        ssv = _mm256_fmadd_ps(xv, xv, ssv);
+    }
+    float sum_sq = hsum_256(ssv);
+    for (size_t i = chunks * 8; i < len; i++) sum_sq += x[i] * x[i];
+    float mean = sum_sq / (float)len;
+    float scale = 1.0f / sqrtf(mean + eps);
+    __m256 sv = _mm256_set1_ps(scale);
+    __m256 ones = _mm256_set1_ps(1.0f);
+    for (size_t i = 0; i < chunks; i++) {
+        __m256 xv = _mm256_loadu_ps(x + i * 8);
+        __m256 gw = _mm256_add_ps(ones, _mm256_loadu_ps(w + i * 8));
+        _mm256_storeu_ps(out + i * 8, _mm256_mul_ps(_mm256_mul_ps(xv, sv), gw));
+    }
+    for (size_t i = chunks * 8; i < len; i++) out[i] = x[i] * scale * (1.0f + w[i]);
+}
+
+/* geglu_scalar — scalar.rs:77-89: out = gelu(gate) * up, gelu the tanh form */
+void oracle_geglu_scalar(const float* gate, const float* up, float* out, size_t n) {
+    const float sqrt_2_over_pi = 0.7978846f;
+    for (size_t i = 0; i < n; i++) {
+        float x = gate[i];
+        float cube = x * x * x;
+        float inner = sqrt_2_over_pi * (x + 0.044715f * cube);
+        float gelu_x = 0.5f * x * (1.0f + tanhf(inner));
+        out[i] = gelu_x * up[i];
+    }
+}
+
+/* logit_softcap_scalar — scalar.rs:63-71: v = tanh(v / cap) * cap, in place; cap <= 0: none */
+void oracle_logit_softcap_scalar(float* v, size_t n, float cap) {
+    if (cap <= 0.0f) return;
+    float inv_cap = 1.0f / cap;
+    for (size_t i = 0; i < n; i++) v[i] = tanhf(v[i] * inv_cap) * cap;
+}
+
 /* rope_head_scalar — scalar.rs:92-130 (no freq_factors); mode 0 = Norm, 1 = Neox */
 void oracle_rope_head_scalar(float* vec, size_t pos, size_t rope_dim, float freq_base, int mode) {
     size_t half_dim = rope_dim / 2;
@@ -572,11 +614,20 @@ void oracle_causal_gqa_decode(const float* q, const uint8_t* k_ring, const uint8
  * quantize_f32_to_q8_0 + apply_matvec :509-527 (dispatch_matvec_q4_0_q8_0 -> avx2), add_bias
  * :452-465, rope_head_scalar per head, KvCache::store_key/value, causal_gqa_decode_scalar_ext
  * with context pos+1, swiglu_scalar, residual adds, final norm + output projection. */
+/* apply_rmsnorm — forward_pass.rs:495-507: the Gemma form for ModelArch::Gemma2 */
+static void fwd_rmsnorm(const oracle_model* m, const float* x, const float* w, size_t n, float* out) {
+    if (m->arch == ORACLE_ARCH_GEMMA2)
+        oracle_rmsnorm_gemma_avx2(x, w, n, m->eps, out);
+    else
+        oracle_rmsnorm_avx2(x, w, n, m->eps, out);
+}
+
 void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, float* logits) {
     const size_t E = (size_t)m->embd, F = (size_t)m->ffn, hd = (size_t)m->head_dim;
     const size_t qd = (size_t)m->head_count * hd, kvd = (size_t)m->head_count_kv * hd;
     const size_t nbE = E / 32;
     const size_t ctx = pos + 1;
+    const int gemma = m->arch == ORACLE_ARCH_GEMMA2;
     float* x = (float*)malloc(E * 4);
     float* h = (float*)malloc(E * 4);
     float* q = (float*)malloc(qd * 4);
@@ -593,9 +644,13 @@ void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, flo
     uint8_t* q8 = (uint8_t*)malloc(q8n / 32 * 34);
     oracle_dequantize_q4_0_soa(m->tok_s + (size_t)token * nbE * 2, m->tok_q + (size_t)token * nbE * 16,
                                nbE, x);
+    if (gemma) { /* forward_pass.rs:210-214: x *= sqrt(embd) */
+        const float scale = sqrtf((float)E);
+        for (size_t i = 0; i < E; i++) x[i] *= scale;
+    }
     for (int l = 0; l < m->n_layers; l++) {
         const oracle_layer* L = &m->layers[l];
-        oracle_rmsnorm_avx2(x, L->attn_norm, E, m->eps, h);
+        fwd_rmsnorm(m, x, L->attn_norm, E, h);
         oracle_quantize_f32_to_q8_0(h, E, q8);
         oracle_matvec_q4_0_q8_0_avx2(L->wq_s, L->wq_q, q8, qd, E, q);
         oracle_matvec_q4_0_q8_0_avx2(L->wk_s, L->wk_q, q8, kvd, E, k);
@@ -614,19 +669,33 @@ void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, flo
                                  m->attn_softcap);
         oracle_quantize_f32_to_q8_0(att, qd, q8);
         oracle_matvec_q4_0_q8_0_avx2(L->wo_s, L->wo_q, q8, E, qd, h);
-        for (size_t i = 0; i < E; i++) x[i] += h[i];
-        oracle_rmsnorm_avx2(x, L->ffn_norm, E, m->eps, h);
+        if (L->post_attn_norm) { /* forward_pass.rs:330-336: x += rmsnorm(Wo a) * post_attn_norm */
+            fwd_rmsnorm(m, h, L->post_attn_norm, E, att);
+            for (size_t i = 0; i < E; i++) x[i] += att[i];
+        } else {
+            for (size_t i = 0; i < E; i++) x[i] += h[i];
+        }
+        fwd_rmsnorm(m, x, L->ffn_norm, E, h);
         oracle_quantize_f32_to_q8_0(h, E, q8);
         oracle_matvec_q4_0_q8_0_avx2(L->wg_s, L->wg_q, q8, F, E, g);
         oracle_matvec_q4_0_q8_0_avx2(L->wu_s, L->wu_q, q8, F, E, u);
-        oracle_swiglu_scalar(g, u, sw, F);
+        if (gemma) /* forward_pass.rs:363-368 */
+            oracle_geglu_scalar(g, u, sw, F);
+        else
+            oracle_swiglu_scalar(g, u, sw, F);
         oracle_quantize_f32_to_q8_0(sw, F, q8);
         oracle_matvec_q4_0_q8_0_avx2(L->wd_s, L->wd_q, q8, E, F, dn);
-        for (size_t i = 0; i < E; i++) x[i] += dn[i];
+        if (L->post_ffn_norm) { /* forward_pass.rs:379-385 */
+            fwd_rmsnorm(m, dn, L->post_ffn_norm, E, h);
+            for (size_t i = 0; i < E; i++) x[i] += h[i];
+        } else {
+            for (size_t i = 0; i < E; i++) x[i] += dn[i];
+        }
     }
-    oracle_rmsnorm_avx2(x, m->out_norm, E, m->eps, h);
+    fwd_rmsnorm(m, x, m->out_norm, E, h);
     oracle_quantize_f32_to_q8_0(h, E, q8);
     oracle_matvec_q4_0_q8_0_avx2(m->out_s, m->out_q, q8, (size_t)m->vocab, E, logits);
+    oracle_logit_softcap_scalar(logits, (size_t)m->vocab, m->final_softcap); /* :411-414 */
     free(x); free(h); free(q); free(k); free(v); free(att); free(g); free(u); free(sw);
     free(dn); free(scores); free(q8);
 }

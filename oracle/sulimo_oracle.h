@@ -122,7 +122,7 @@ void oracle_causal_gqa_decode(const float* q, const uint8_t* k_ring, const uint8
                               float* out, float softcap);
 
 /* ---- one decode position through the whole model (forward_token,
- * crates/sulimo-engine/src/forward_pass.rs:190-417), Llama / Qwen2 path: RMSNorm (AVX2),
+ * crates/sulimo-engine/src/forward_pass.rs:190-417), Llama / Qwen2 / Gemma 2 paths: RMSNorm (AVX2),
  * Q8_0 activations, AVX2 matvecs, optional QKV biases, RoPE (Norm / Neox), Q8_0 ring store,
  * causal GQA decode, SwiGLU, residual adds, final norm and the vocab projection. */
 typedef struct oracle_layer {
@@ -131,6 +131,7 @@ typedef struct oracle_layer {
     const uint8_t *wq_s, *wq_q, *wk_s, *wk_q, *wv_s, *wv_q, *wo_s, *wo_q;
     const uint8_t *wg_s, *wg_q, *wu_s, *wu_q, *wd_s, *wd_q;
     uint8_t *k_ring, *v_ring;           /* capacity slots of kv_dim/32 Q8_0 blocks */
+    const float *post_attn_norm, *post_ffn_norm;  /* Gemma 2's post norms, or NULL */
 } oracle_layer;
 
 typedef struct oracle_model {
@@ -141,7 +142,18 @@ typedef struct oracle_model {
     const uint8_t *out_s, *out_q; /* output [vocab][embd] Q4_0 SoA (tied: same pointers) */
     const float* out_norm;
     const oracle_layer* layers;
+    int arch;            /* ORACLE_ARCH_DEFAULT (Llama / Qwen2) or ORACLE_ARCH_GEMMA2 */
+    float final_softcap; /* final logit soft-capping (Gemma 2), <= 0: none */
 } oracle_model;
+
+#define ORACLE_ARCH_DEFAULT 0
+#define ORACLE_ARCH_GEMMA2 1
+
+/* rmsnorm_gemma_avx2 (avx2.rs:236-268), geglu_scalar (scalar.rs:77-89), logit_softcap_scalar
+ * (scalar.rs:63-71) */
+void oracle_rmsnorm_gemma_avx2(const float* x, const float* w, size_t len, float eps, float* out);
+void oracle_geglu_scalar(const float* gate, const float* up, float* out, size_t n);
+void oracle_logit_softcap_scalar(float* v, size_t n, float cap);
 
 /* logits [vocab] for `token` at position `pos` (context pos+1); stores K/V at pos. */
 void oracle_forward_token(const oracle_model* m, uint32_t token, size_t pos, float* logits);

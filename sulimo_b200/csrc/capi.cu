@@ -590,6 +590,8 @@ static int check_model(const sulimo_model_desc* m) {
         m->rope_dim % 2 || m->rope_dim > m->head_dim || (m->rope_mode != 0 && m->rope_mode != 1))
         return set_error(SULIMO_EINVAL, "bad head_dim / rope_dim / rope_mode");
     if (m->kv_capacity == 0) return set_error(SULIMO_EINVAL, "kv_capacity must be positive");
+    if (m->arch != SULIMO_ARCH_DEFAULT && m->arch != SULIMO_ARCH_GEMMA2)
+        return set_error(SULIMO_EINVAL, "arch must be SULIMO_ARCH_DEFAULT or SULIMO_ARCH_GEMMA2");
     if (m->embd * 4 + 33 * 4 > 227 * 1024) return set_error(SULIMO_EINVAL, "embd too large");
     if (!m->tok_scales || !m->tok_quants || !m->out_scales || !m->out_quants || !m->out_norm)
         return set_error(SULIMO_EINVAL, "null embedding / output tensor");
@@ -642,6 +644,9 @@ static int prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* model, const
     int st = check_ctx(ctx);
     if (st) return st;
     if ((st = check_model(model))) return st;
+    if (model->arch != SULIMO_ARCH_DEFAULT)
+        return set_error(SULIMO_EINVAL,
+                         "the prefill ubatch has no Gemma 2 steps: use forward_token per token");
     if (model->head_dim != 64 && model->head_dim != 128)
         return set_error(SULIMO_EINVAL, "prefill supports head_dim 64 and 128");
     if (n <= 0 || n > 65535) return set_error(SULIMO_EINVAL, "n must be in [1, 65535]");
@@ -696,6 +701,9 @@ int sulimo_cuda_repack_context(sulimo_ctx* ctx, const sulimo_model_desc* model,
     int st = check_ctx(ctx);
     if (st) return st;
     if ((st = check_model(model))) return st;
+    if (model->arch != SULIMO_ARCH_DEFAULT)
+        return set_error(SULIMO_EINVAL,
+                         "the re-prefill has no Gemma 2 steps: use forward_token per token");
     if (!new_pos_out) return set_error(SULIMO_EINVAL, "null pointer");
     *new_pos_out = 0;
     if (ubatch <= 0 || ubatch > 65535) return set_error(SULIMO_EINVAL, "ubatch must be in [1, 65535]");

@@ -1,6 +1,7 @@
-// forward.cu — one decode position through a Llama / Qwen2-architecture model on the GPU:
-// the reference's forward_token (crates/sulimo-engine/src/forward_pass.rs:190-417) for a batch
-// of independent sequences that sit at the same position.
+// forward.cu — one decode position through a Llama / Qwen2 / Gemma 2-architecture model on the
+// GPU: the reference's forward_token (crates/sulimo-engine/src/forward_pass.rs:190-417) for a
+// batch of independent sequences that sit at the same position; and the prefill ubatch
+// (execute_prefill_ubatch, crates/sulimo-ocl/src/prefill.rs:337-566) for Llama / Qwen2.
 //
 // Per layer, at one sequence (8 launches on the context's stream, no host synchronisation, each a
 // programmatic dependent of the previous one):
@@ -12,8 +13,9 @@
 //                      (rope_head_scalar, scalar.rs:92-130), K/V quantized into ring slot
 //                      pos % capacity (KvCache::store_key/store_value, kv_cache.rs:93-110)
 //   attention          causal GQA decode over the Q8_0 ring, context pos+1
-//                      (causal_gqa_decode_scalar_ext, scalar.rs:287-359): split-K slots kernel
-//                      + merge, the merge writing the o projection's Q8_0 input -- 2 launches
+//                      (causal_gqa_decode_scalar_ext, scalar.rs:287-359): split-K kernel
+//                      + merge kernel, the merge writing the o projection's Q8_0 input -- 2
+//                      launches
 //   GEMV o             o = Wo . a
 //   GEMV gate,up       one launch; prologue: x += o, RMSNorm (ffn_norm), Q8_0
 //   swiglu_q8          silu(gate)*up -> Q8_0 (swiglu_scalar, scalar.rs:161-170)
@@ -26,6 +28,10 @@
 // stream).  RMSNorm sums squares as a tree (the reference sums eight AVX2 lanes sequentially),
 // and RoPE / SiLU use CUDA's powf / sinf / cosf / expf, so the activations agree with the
 // reference to float rounding, not bit for bit.
+// Gemma 2 (arch SULIMO_ARCH_GEMMA2): the embedding rows are scaled by sqrt(embd), every norm is
+// weighted by (1 + w), the attention and FFN outputs are RMS-normalized by the layer's post norms
+// before their residual adds (inside add_rmsnorm_q8, which always runs as its own launch for
+// this architecture), GeGLU replaces SwiGLU and the logits are soft-capped by one more launch.
 #include "sulimo_common.cuh"
 #include "sulimo_internal.h"
 
@@ -55,11 +61,14 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // One CTA per sequence.  x[seq][E] (+= delta[seq][E] when delta is given, written back), then
 // y = (x * 1/sqrt(mean(x^2) + eps)) * w, quantized to Q8_0 (E/32 blocks) as q8 names (row seq).
 // F16_OUT: y as f16 [seq][E] into y16 (the prefill GEMMs' activations) instead.
+// post_w (Gemma 2's post_attn_norm / post_ffn_norm, forward_pass.rs:330-336, 379-385): delta is
+// RMS-normalized with these weights before it is added.  gemma: every norm weight enters as
+// (1 + w) (rmsnorm_gemma, avx2.rs:236-268).
 template <bool F16_OUT>
 __global__ void __launch_bounds__(NORM_THREADS)
     add_rmsnorm_q8_kernel(float* __restrict__ x, const float* __restrict__ delta,
                           const float* __restrict__ w, int E, float eps, const Q8Out q8,
-                          __half* __restrict__ y16) {
+                          __half* __restrict__ y16, const float* __restrict__ post_w, int gemma) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     extern __shared__ float sx[];  // E floats + 33 reduction slots
@@ -67,11 +76,21 @@ __global__ void __launch_bounds__(NORM_THREADS)
     const int seq = blockIdx.x;
     float* xs = x + (size_t)seq * E;
     const float* ds = delta ? delta + (size_t)seq * E : nullptr;
+    auto weight = [&](const float* wv, int i) { return gemma ? __fadd_rn(1.0f, wv[i]) : wv[i]; };
+    float dscale = 1.0f;
+    if (ds && post_w) {
+        float sd = 0.0f;
+        for (int i = threadIdx.x; i < E; i += blockDim.x) sd = __fmaf_rn(ds[i], ds[i], sd);
+        const float dsum = block_sum(sd, red);
+        dscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(dsum, (float)E), eps)));
+        __syncthreads();  // red is reused below
+    }
     float ss = 0.0f;
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
         float v = xs[i];
         if (ds) {
-            v = __fadd_rn(v, ds[i]);
+            const float d = post_w ? __fmul_rn(__fmul_rn(ds[i], dscale), weight(post_w, i)) : ds[i];
+            v = __fadd_rn(v, d);
             xs[i] = v;
         }
         sx[i] = v;
@@ -83,15 +102,32 @@ __global__ void __launch_bounds__(NORM_THREADS)
     if (F16_OUT) {
         __half* ys = y16 + (size_t)seq * E;
         for (int i = threadIdx.x; i < E; i += blockDim.x)
-            ys[i] = __float2half_rn(__fmul_rn(__fmul_rn(sx[i], scale), w[i]));
+            ys[i] = __float2half_rn(__fmul_rn(__fmul_rn(sx[i], scale), weight(w, i)));
         return;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int b = warp; b < E / 32; b += blockDim.x >> 5) {
         const int i = b * 32 + lane;
-        const float y = __fmul_rn(__fmul_rn(sx[i], scale), w[i]);
+        const float y = __fmul_rn(__fmul_rn(sx[i], scale), weight(w, i));
         q8_store_block(q8, y, (size_t)seq, b, lane);
     }
+}
+
+// x[i] *= s (Gemma 2's embedding scale sqrt(embd), forward_pass.rs:210-214)
+__global__ void __launch_bounds__(256) scale_kernel(float* __restrict__ x, size_t n, float s) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fmul_rn(x[i], s);
+}
+
+// v = tanh(v * inv_cap) * cap (logit_softcap_scalar, scalar.rs:63-71), in place
+__global__ void __launch_bounds__(256)
+    logit_softcap_kernel(float* __restrict__ v, size_t n, float inv_cap, float cap) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) v[i] = __fmul_rn(tanhf(__fmul_rn(v[i], inv_cap)), cap);
 }
 
 // RoPE of one head in place (rope_head_scalar): pair (2i, 2i+1) in Norm mode (0), (i, i+half)
@@ -200,20 +236,28 @@ __global__ void __launch_bounds__(GLUE_THREADS)
     out[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
-// silu(gate) * up -> Q8_0 (rows of F = q8.K values): one warp per 32-value block, all
-// sequences' blocks in one grid.
+// silu(gate) * up (swiglu_scalar) or, for Gemma 2, gelu(gate) * up with the tanh form of
+// geglu_scalar (scalar.rs:77-89) -> Q8_0 (rows of F = q8.K values): one warp per 32-value block,
+// all sequences' blocks in one grid.
 __global__ void __launch_bounds__(GLUE_THREADS)
     swiglu_q8_kernel(const float* __restrict__ gate, const float* __restrict__ up, size_t nblocks,
-                     const Q8Out q8) {
+                     const Q8Out q8, int geglu) {
     pdl_launch_dependents();
     pdl_wait_prerequisites();
     const int lane = threadIdx.x & 31;
     size_t b = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (b >= nblocks) return;
     const float g = gate[b * 32 + lane];
-    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    float act;
+    if (geglu) {
+        const float cube = __fmul_rn(__fmul_rn(g, g), g);
+        const float inner = __fmul_rn(0.7978846f, __fadd_rn(g, __fmul_rn(0.044715f, cube)));
+        act = __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(inner)));
+    } else {
+        act = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    }
     const size_t nb = (size_t)(q8.K / 32);
-    q8_store_block(q8, __fmul_rn(silu, up[b * 32 + lane]), b / nb, (int)(b % nb), lane);
+    q8_store_block(q8, __fmul_rn(act, up[b * 32 + lane]), b / nb, (int)(b % nb), lane);
 }
 
 // First index of the maximum of each row (greedy sampling); NaN never wins.  ARGMAX_CTAS CTAs
@@ -414,7 +458,7 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
         const sulimo_layer_desc& L = m->layers[l];
         (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
                          ctx->stream, s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E,
-                         m->eps, no_q8, h16);
+                         m->eps, no_q8, h16, (const float*)nullptr, 0);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
         if ((st = gemm(L.wq_scales, L.wq_quants, s.h, s.q, qd, E)) ||
@@ -436,7 +480,8 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
             return st;
         (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
                          ctx->stream, s.x, (const float*)s.o,
-                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, no_q8, h16);
+                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, no_q8, h16,
+                         (const float*)nullptr, 0);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
         if ((st = gemm(L.wg_scales, L.wg_quants, s.h, s.g, F, E)) ||
@@ -457,7 +502,7 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
     const size_t last = (size_t)(n - 1) * E;
     (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(1), dim3(NORM_THREADS), norm_smem,
                      ctx->stream, s.x + last, pending + last, m->out_norm, E, m->eps, no_q8,
-                     h16);
+                     h16, (const float*)nullptr, 0);
     ctx->launches++;
     if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
     return launch_gemm_q4_0_f16(ctx, m->out_scales, m->out_quants, s.h, logits, m->vocab, E, 1,
@@ -549,11 +594,14 @@ static int step_gemv(sulimo_ctx* ctx, const GemvMatSrc* g, int count, const Q8Ou
 // sequences that redundant per-CTA work costs more than the launch it saves (measured on
 // config 4: batch 1 1.48 -> 1.40 ms per step, batch 8 5.19 -> 6.41 ms), so the norm kernel
 // updates x in place and writes the activations, then the matvec runs.
+// Gemma 2 (post_w: the delta's post norm; gemma: (1 + w) norm weights) always takes the
+// separate norm kernel.
 static int norm_and_gemv(sulimo_ctx* ctx, const Scratch& s, float*& x, float*& x_other,
                          const float* delta, const float* w, float eps, int E, int batch,
-                         const GemvMatSrc* g, int count, bool keep_x) {
+                         const GemvMatSrc* g, int count, bool keep_x,
+                         const float* post_w = nullptr, int gemma = 0) {
     const GemvPrologue pro = {GEMV_PRO_NORM, x, delta, w, keep_x ? x_other : nullptr, eps};
-    if (batch == 1 && gemv_fast_fused_ok(g, count, E, batch, pro)) {
+    if (batch == 1 && !gemma && !post_w && gemv_fast_fused_ok(g, count, E, batch, pro)) {
         const int st = launch_gemv_fast_fused(ctx, g, count, pro, E, batch, true);
         if (!st && keep_x) {
             float* t = x;
@@ -565,7 +613,7 @@ static int norm_and_gemv(sulimo_ctx* ctx, const Scratch& s, float*& x, float*& x
     const Q8Out form = step_q8_form(ctx, s, g, count, E, batch);
     (void)launch_pdl(add_rmsnorm_q8_kernel<false>, dim3(batch), dim3(NORM_THREADS),
                      (size_t)(E + 33) * sizeof(float), ctx->stream, x, delta, w, E, eps, form,
-                     (__half*)nullptr);
+                     (__half*)nullptr, post_w, gemma);
     ctx->launches++;
     int st = check_cuda(cudaGetLastError(), "add_rmsnorm_q8 launch");
     return st ? st : step_gemv(ctx, g, count, form, E, batch);
@@ -576,11 +624,11 @@ static int norm_and_gemv(sulimo_ctx* ctx, const Scratch& s, float*& x, float*& x
 // step): every CTA of the down projection (hundreds) would recompute all F activations with
 // expf, so this one small kernel runs instead.
 static int swiglu_and_gemv(sulimo_ctx* ctx, const Scratch& s, const float* gate, const float* up,
-                           int F, int batch, const GemvMatSrc& g) {
+                           int F, int batch, const GemvMatSrc& g, int geglu) {
     const size_t nblk = (size_t)batch * F / 32;
     const Q8Out form = step_q8_form(ctx, s, &g, 1, F, batch);
     (void)launch_pdl(swiglu_q8_kernel, dim3((unsigned)((nblk + 7) / 8)), dim3(GLUE_THREADS), 0,
-                     ctx->stream, gate, up, nblk, form);
+                     ctx->stream, gate, up, nblk, form, geglu);
     ctx->launches++;
     int st = check_cuda(cudaGetLastError(), "swiglu_q8 launch");
     return st ? st : step_gemv(ctx, &g, 1, form, F, batch);
@@ -608,9 +656,18 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
     if ((st = launch_dequant_rows(ctx, m->tok_scales, m->tok_quants, E, tokens, batch, s.x,
                                   SULIMO_OUT_F32)))
         return st;
+    const int gemma = m->arch == SULIMO_ARCH_GEMMA2;
+    if (gemma) {  // x *= sqrt(embd) (forward_pass.rs:210-214)
+        const size_t n = (size_t)batch * E;
+        (void)launch_pdl(scale_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                         ctx->stream, s.x, n, sqrtf((float)E));
+        ctx->launches++;
+        if ((st = check_cuda(cudaGetLastError(), "scale launch"))) return st;
+    }
     float* x = s.x;        // the residual stream
     float* x_other = s.x2;
-    const float* pending = nullptr;  // the previous layer's FFN output, added to x next
+    const float* pending = nullptr;       // the previous layer's FFN output, added to x next
+    const float* pending_post = nullptr;  // its post-FFN norm (Gemma 2) or null
     for (int l = 0; l < m->n_layers; l++) {
         const sulimo_layer_desc& L = m->layers[l];
         {  // attention norm, then q, k, v in one launch
@@ -619,7 +676,7 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                                      {L.wv_scales, L.wv_quants, s.v, kvd}};
             if ((st = norm_and_gemv(ctx, s, x, x_other, pending,
                                     reinterpret_cast<const float*>(L.attn_norm), m->eps, E, batch,
-                                    g, 3, true)))
+                                    g, 3, true, pending_post, gemma)))
                 return st;
         }
         (void)launch_pdl(qkv_rope_store_kernel, dim3(H + 2 * Hkv, batch), dim3(128), 0,
@@ -646,17 +703,28 @@ int launch_forward_token(sulimo_ctx* ctx, const sulimo_model_desc* m, const int3
                                      {L.wu_scales, L.wu_quants, s.u, F}};
             if ((st = norm_and_gemv(ctx, s, x, x_other, s.o,
                                     reinterpret_cast<const float*>(L.ffn_norm), m->eps, E, batch,
-                                    g, 2, true)))
+                                    g, 2, true, reinterpret_cast<const float*>(L.post_attn_norm),
+                                    gemma)))
                 return st;
         }
         const GemvMatSrc gd = {L.wd_scales, L.wd_quants, s.o, E};
-        if ((st = swiglu_and_gemv(ctx, s, s.g, s.u, F, batch, gd))) return st;
+        if ((st = swiglu_and_gemv(ctx, s, s.g, s.u, F, batch, gd, gemma))) return st;
         pending = s.o;
+        pending_post = reinterpret_cast<const float*>(L.post_ffn_norm);
     }
     // output norm and the vocab projection (the residual is not needed afterwards)
     const GemvMatSrc gl = {m->out_scales, m->out_quants, logits, m->vocab};
-    return norm_and_gemv(ctx, s, x, x_other, pending, m->out_norm, m->eps, E, batch, &gl, 1,
-                         false);
+    if ((st = norm_and_gemv(ctx, s, x, x_other, pending, m->out_norm, m->eps, E, batch, &gl, 1,
+                            false, pending_post, gemma)))
+        return st;
+    if (m->final_softcap > 0.0f) {  // logit_softcap_scalar (forward_pass.rs:411-414)
+        const size_t n = (size_t)batch * m->vocab;
+        (void)launch_pdl(logit_softcap_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                         ctx->stream, logits, n, 1.0f / m->final_softcap, m->final_softcap);
+        ctx->launches++;
+        st = check_cuda(cudaGetLastError(), "logit_softcap launch");
+    }
+    return st;
 }
 
 }  // namespace sulimo

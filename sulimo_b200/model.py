@@ -16,7 +16,7 @@ class _LayerDesc(C.Structure):
         "attn_norm", "ffn_norm", "bq", "bk", "bv",
         "wq_scales", "wq_quants", "wk_scales", "wk_quants", "wv_scales", "wv_quants",
         "wo_scales", "wo_quants", "wg_scales", "wg_quants", "wu_scales", "wu_quants",
-        "wd_scales", "wd_quants", "k_ring", "v_ring")]
+        "wd_scales", "wd_quants", "k_ring", "v_ring", "post_attn_norm", "post_ffn_norm")]
 
 
 class _ModelDesc(C.Structure):
@@ -27,7 +27,8 @@ class _ModelDesc(C.Structure):
                 ("kv_capacity", C.c_size_t), ("kv_seq_stride", C.c_size_t),
                 ("tok_scales", C.c_void_p), ("tok_quants", C.c_void_p),
                 ("out_scales", C.c_void_p), ("out_quants", C.c_void_p),
-                ("out_norm", C.c_void_p), ("layers", C.POINTER(_LayerDesc))]
+                ("out_norm", C.c_void_p), ("layers", C.POINTER(_LayerDesc)),
+                ("arch", C.c_int), ("final_softcap", C.c_float)]
 
 
 def _p(t):
@@ -52,6 +53,8 @@ class DecodeModel:
             e = layers[i]
             for name in ("attn_norm", "ffn_norm", "bq", "bk", "bv"):
                 setattr(e, name, _p(L[name]))
+            for name in ("post_attn_norm", "post_ffn_norm"):
+                setattr(e, name, _p(L.get(name)))
             for name in _MATS:
                 setattr(e, name + "_scales", _p(L[name][0]))
                 setattr(e, name + "_quants", _p(L[name][1]))
@@ -66,6 +69,8 @@ class DecodeModel:
         d.out_scales, d.out_quants = _p(w["out"][0]), _p(w["out"][1])
         d.out_norm = _p(w["out_norm"])
         d.layers = layers
+        d.arch = cfg.get("arch", 0)
+        d.final_softcap = cfg.get("final_softcap", 0.0)
         self.desc = d
         self._desc_ptr = C.cast(C.pointer(d), C.c_void_p)
         nbytes = capi.load().sulimo_cuda_forward_scratch_bytes(self._desc_ptr, batch)

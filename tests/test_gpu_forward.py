@@ -1,6 +1,8 @@
 """GPU parity of a whole decode position (sulimo_cuda_forward_token) against the oracle's
 restatement of forward_token (crates/sulimo-engine/src/forward_pass.rs:190-417) on small seeded
-models of both supported architectures: Qwen2 (Neox RoPE, QKV biases) and Llama (Norm RoPE).
+models of the supported architectures: Qwen2 (Neox RoPE, QKV biases), Llama (Norm RoPE) and
+Gemma 2 (embedding scale, (1 + w) norms, post-attention / post-FFN norms, GeGLU, attention and
+final logit soft-capping).
 
 Tolerance: the GEMVs are bit-exact with the AVX2 kernel, but RMSNorm's sum of squares is a tree
 (the reference adds eight AVX2 lanes sequentially) and RoPE / SiLU / softmax use CUDA's powf,
@@ -19,6 +21,9 @@ pytestmark = pytest.mark.gpu
 QWEN_SMALL = dict(n_layers=2, embd=256, ffn=512, head_count=4, head_count_kv=2, head_dim=64,
                   vocab=512, rope_dim=64, rope_mode=1, eps=1e-6, rope_base=1e6, attn_softcap=0.0,
                   bias=True)
+GEMMA2_SMALL = dict(n_layers=2, embd=256, ffn=512, head_count=4, head_count_kv=2, head_dim=128,
+                    vocab=640, rope_dim=128, rope_mode=1, eps=1e-6, rope_base=1e4,
+                    attn_softcap=50.0, bias=False, arch=1, final_softcap=30.0)
 LLAMA_SMALL = dict(n_layers=3, embd=384, ffn=1024, head_count=6, head_count_kv=2, head_dim=128,
                    vocab=1000, rope_dim=128, rope_mode=0, eps=1e-5, rope_base=5e5,
                    attn_softcap=0.0, bias=False)
@@ -38,7 +43,8 @@ def check_step(got, ref, where):
         assert int(np.argmax(got)) == int(top[1]), where
 
 
-@pytest.mark.parametrize("cfg", [QWEN_SMALL, LLAMA_SMALL], ids=["qwen2", "llama"])
+@pytest.mark.parametrize("cfg", [QWEN_SMALL, LLAMA_SMALL, GEMMA2_SMALL],
+                         ids=["qwen2", "llama", "gemma2"])
 def test_forward_token_matches_oracle(ctx, cfg):
     import torch
     from sulimo_b200.model import DecodeModel
@@ -60,12 +66,12 @@ def test_forward_token_matches_oracle(ctx, cfg):
             assert rel_l2(g, r) <= 1e-2, (l, which)
 
 
-def test_forward_token_batch_of_sequences(ctx):
+@pytest.mark.parametrize("cfg", [QWEN_SMALL, GEMMA2_SMALL], ids=["qwen2", "gemma2"])
+def test_forward_token_batch_of_sequences(ctx, cfg):
     """Three sequences at once: each matches its own oracle run; greedy argmax on the device."""
     import torch
     from sulimo_b200.model import DecodeModel
     from sulimo_b200.synthetic import make_model_numpy, to_device
-    cfg = QWEN_SMALL
     w = make_model_numpy(cfg, seed=9, kv_capacity=16)
     oms = [O.OracleModel(w) for _ in range(3)]
     dm = DecodeModel(ctx, to_device(w), batch=3)
@@ -92,3 +98,18 @@ def test_forward_token_rejects_context_beyond_ring(ctx):
     with pytest.raises(sb.SulimoError) as e:
         dm.forward_token(tk, 8)   # context 9 > 8 ring slots
     assert e.value.kind == "InvalidArgument"
+
+
+def test_gemma2_prefill_ubatch_rejected(ctx):
+    """The reference's GPU ubatch (prefill.rs:337-566) has no Gemma 2 steps; this one refuses a
+    Gemma 2 model instead of computing something else, and forward_token serves it."""
+    import torch
+    import sulimo_b200 as sb
+    from sulimo_b200.model import DecodeModel
+    from sulimo_b200.synthetic import make_model_numpy, to_device
+    w = make_model_numpy(GEMMA2_SMALL, seed=3, kv_capacity=16)
+    dm = DecodeModel(ctx, to_device(w), batch=1)
+    with pytest.raises(sb.SulimoError) as e:
+        dm.prefill(torch.tensor([1, 2, 3], dtype=torch.int32, device="cuda"))
+    from sulimo_b200 import capi
+    assert e.value.status == capi.EINVAL

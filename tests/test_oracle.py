@@ -152,6 +152,46 @@ def test_rmsnorm_avx2_matches_scalar():
     assert np.max(np.abs(O.rmsnorm_avx2(x, w, 1e-5) - O.rmsnorm_scalar(x, w, 1e-5))) < 1e-5
 
 
+def test_rmsnorm_gemma_with_zero_weight_equals_rmsnorm():
+    """scalar.rs:390-403: (1 + 0) weights give rmsnorm with unit weights (here through the
+    AVX2 restatement, whose tail and vector paths both run at length 4 and 12)."""
+    for n in (4, 12):
+        x = np.arange(1, n + 1, dtype=np.float32)
+        out = O.rmsnorm_gemma_avx2(x, np.zeros(n, np.float32), 1e-5)
+        ref = O.rmsnorm_scalar(x, np.ones(n, np.float32), 1e-5)
+        assert np.max(np.abs(out - ref)) < 1e-6
+
+
+def test_rmsnorm_gemma_avx2_vs_scalar_form():
+    """avx2.rs:399-425: sin / cos inputs of length 64 against the scalar form
+    x * scale * (1 + w) (scalar.rs:43-58), restated here in float32 numpy."""
+    x = np.sin(np.arange(64, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    w = np.cos(np.arange(64, dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    ss = np.float32(0)
+    for v in x:
+        ss = np.float32(ss + v * v)
+    scale = np.float32(1) / np.sqrt(np.float32(ss / np.float32(64)) + np.float32(1e-5))
+    ref = (x * scale * (np.float32(1) + w)).astype(np.float32)
+    assert np.max(np.abs(O.rmsnorm_gemma_avx2(x, w, 1e-5) - ref)) < 1e-5
+
+
+def test_logit_softcap():
+    """scalar.rs:406-416."""
+    out = O.logit_softcap(np.array([1000.0, -1000.0, 0.0, 100.0], np.float32), 50.0)
+    assert 49.99 < out[0] <= 50.0 and -50.0 <= out[1] < -49.99
+    assert out[2] == 0.0 and abs(out[3] - 48.2014) < 1e-3
+    same = np.array([1.0, -2.0], np.float32)
+    assert np.array_equal(O.logit_softcap(same, 0.0), same)  # cap <= 0: untouched
+
+
+def test_geglu():
+    """scalar.rs:419-427, plus the tanh-form value at 1.0."""
+    out = O.geglu(np.array([0.0, 1.0, -1.0], np.float32), np.array([2.0, 3.0, 4.0], np.float32))
+    assert out[0] == 0.0 and out[1] > 0.0 and out[2] < 0.0
+    g1 = 0.5 * (1.0 + np.tanh(0.7978846 * (1.0 + 0.044715)))
+    assert abs(out[1] - 3.0 * g1) < 1e-6
+
+
 def test_softmax_scalar():
     x = O.softmax(np.array([1, 2, 3], np.float32))
     assert abs(float(x.sum()) - 1.0) < 1e-5 and x[2] > x[1] > x[0]
