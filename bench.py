@@ -265,7 +265,7 @@ def run_ours(args, rank, world, local):
     achieved = FLOP_PER_GEMM / (per_launch_ms / 1e3) / 1e12
     roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tf_burst,
             "unit": "TFLOP/s", "frac": round(achieved / tf_burst, 4),
-            "traffic": ncu_traffic("gemm_q4_0_tc_kernel"),
+            "traffic": ncu_traffic("gemm_q4_0_pair_kernel"),
             "peak_source": f"{src} bf16 dense burst (MEASURED_PEAKS.json)"
             if src == "measured" else "fallback 1.59 PFLOP/s"}
 

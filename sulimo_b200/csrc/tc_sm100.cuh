@@ -211,6 +211,9 @@ __device__ __forceinline__ void dequant_block_exact(const uint4 q, uint32_t dbit
 // Partial sums of split-K CTAs go to an fp32 workspace [split][n][m]; this kernel adds the
 // splits in index order (deterministic) and writes f16 or f32 results.  Launched as a
 // programmatic dependent of the GEMM: its CTAs wait for the partials in griddepcontrol.wait.
+// Each thread issues the loads of all its splits (up to SPLITK_BATCH at a time) before the
+// first add, so the partials cost one L2 round trip, not one per split.
+constexpr int SPLITK_BATCH = 8;
 template <bool OUT_F32>
 __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ out, size_t nm,
@@ -219,13 +222,25 @@ __global__ void __launch_bounds__(256)
     pdl_wait_prerequisites();
     const size_t i4 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i4 >= nm) return;
-    float4 acc = __ldcg(reinterpret_cast<const float4*>(ws + i4));
-    for (int z = 1; z < splits; z++) {
-        const float4 p = __ldcg(reinterpret_cast<const float4*>(ws + (size_t)z * nm + i4));
-        acc.x += p.x;
-        acc.y += p.y;
-        acc.z += p.z;
-        acc.w += p.w;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int z0 = 0; z0 < splits; z0 += SPLITK_BATCH) {
+        float4 p[SPLITK_BATCH];
+#pragma unroll
+        for (int j = 0; j < SPLITK_BATCH; j++)
+            if (z0 + j < splits)
+                p[j] = __ldcg(reinterpret_cast<const float4*>(ws + (size_t)(z0 + j) * nm + i4));
+#pragma unroll
+        for (int j = 0; j < SPLITK_BATCH; j++) {
+            if (z0 + j >= splits) break;
+            if (z0 + j == 0) {
+                acc = p[j];
+            } else {
+                acc.x += p[j].x;
+                acc.y += p[j].y;
+                acc.z += p[j].z;
+                acc.w += p[j].w;
+            }
+        }
     }
     if (OUT_F32) {
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + i4) = acc;
