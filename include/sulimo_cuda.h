@@ -125,7 +125,10 @@ int sulimo_cuda_event_free(sulimo_event* ev);
 /* logits_f16_output form, kernels/prefill.cl:269-308).  Requires k % 32 == 0 and            */
 /* m % 8 == 0 (the reference's asserts, gemm.rs:39-40); x, out and quants 16-byte aligned.    */
 /* Tensor cores compute with B operand f16(d*(q-8)) (one RNE rounding per weight) and fp32   */
-/* accumulation.                                                                             */
+/* accumulation.  The weights are read as static: the kernel may start loading scales and    */
+/* quants while the previous kernel of the context's stream still runs, if that kernel lets   */
+/* its dependents launch early (griddepcontrol.launch_dependents); none of this library's     */
+/* kernels that write Q4_0 weights does (sulimo_cuda_repack_q4_0_aos_to_soa).                  */
 /* ---------------------------------------------------------------------------------------- */
 int sulimo_cuda_gemm_q4_0_f16(sulimo_ctx* ctx, const void* scales, const void* quants,
                               const void* x, void* out, int m, int k, int n, int out_dtype);

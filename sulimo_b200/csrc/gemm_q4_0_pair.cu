@@ -55,7 +55,7 @@ constexpr uint32_t P_TMEM_COLS = 512;
 constexpr uint32_t P_STAGE_COLS = PK / 2;   // f16x2 TMEM columns of a stage's weights
 constexpr uint32_t P_Q_STAGE = PM * 64;     // raw nibbles per stage: 128 rows x 4 blocks x 16 B
 constexpr uint32_t P_BAR_BYTES = 512;
-static_assert((3 * P_MAX_STAGES + 1) * 8 + 8 <= P_BAR_BYTES, "barrier block");
+static_assert((4 * P_MAX_STAGES + 1) * 8 + 8 <= P_BAR_BYTES, "barrier block");
 
 // Shared memory per CTA: stages x (activation half: bn/2 rows x 256 bytes, nibbles), barriers,
 // 1024 bytes of alignment slack.
@@ -102,6 +102,18 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 // this side and tcgen05.fence::after_thread_sync after the leader's wait, so the arrival keeps
 // the default CTA-scope release: a cluster-scope release would also wait for this thread's
 // unrelated loads in flight (the next stage's block scales).
+// TMA tensor load into this CTA's shared memory whose completion is signalled on an mbarrier
+// of CTA 0 of the pair (shared::cluster address): both CTAs' activation halves complete on the
+// leader's barrier, the one its MMA issuer waits on.  No multicast.
+__device__ __forceinline__ void tma_load_2d_to_leader(void* dst, const CUtensorMap* map, int c0,
+                                                      int c1, uint32_t leader_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(leader_bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
@@ -158,8 +170,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     const uint32_t acc_col = (uint32_t)stages * P_STAGE_COLS;  // accumulators: bn columns
     uint8_t* sx = smem;
     uint8_t* sq = smem + stages * x_stage;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sq + stages * P_Q_STAGE);
-    uint64_t* empty = full + P_MAX_STAGES;
+    uint64_t* qfull = reinterpret_cast<uint64_t*>(sq + stages * P_Q_STAGE);  // own nibbles
+    uint64_t* xfull = qfull + P_MAX_STAGES;  // CTA 0: both CTAs' activation halves
+    uint64_t* empty = xfull + P_MAX_STAGES;
     uint64_t* afull = empty + P_MAX_STAGES;
     uint64_t* done = afull + P_MAX_STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -177,7 +190,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; s++) {
-            mbar_init(&full[s], 1);
+            mbar_init(&qfull[s], 1);
+            mbar_init(&xfull[s], 1);  // CTA 0's producer arrives with both halves' bytes
             mbar_init(&empty[s], 1);
             mbar_init(&afull[s], 2 * P_DEQ_WARPS);  // every dequant warp of both CTAs
         }
@@ -188,14 +202,12 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         prefetch_tensormap(&tmap_q);
         prefetch_tensormap(&tmap_out);
         pdl_launch_dependents();
-        pdl_wait_prerequisites();
-        // the first ring pass needs no empty-slot waits
+        // The weights are static (no kernel that writes them lets its dependents start early):
+        // the first ring pass of nibbles streams, and is dequantized, while this grid still
+        // waits for the previous kernel; the activations follow the programmatic wait below.
         for (int j = 0; j < num_k && j < stages; j++) {
-            const int kk = (i_begin + j) * PK;
-            mbar_arrive_expect_tx(&full[j], x_stage + P_Q_STAGE);
-            tma_load_2d(sx + j * x_stage, &tmap_x, kk, nx0, &full[j]);
-            tma_load_2d(sx + j * x_stage + x_half, &tmap_x, kk + 64, nx0, &full[j]);
-            tma_load_2d(sq + j * P_Q_STAGE, &tmap_q, kk / 2, m0, &full[j]);
+            mbar_arrive_expect_tx(&qfull[j], P_Q_STAGE);
+            tma_load_2d(sq + j * P_Q_STAGE, &tmap_q, (i_begin + j) * PK / 2, m0, &qfull[j]);
         }
     }
     if (warp == 1) {
@@ -208,7 +220,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     // both CTAs' barriers are initialized and both TMEM allocations done before any remote
     // arrival or MMA
     tc_fence_before();
-    __syncthreads();  // thread 0's griddepcontrol.wait, the barrier inits, the TMEM address
+    __syncthreads();  // the barrier inits and the TMEM address
 
     // dequant role (warps 2-17): TMEM lane quarter warp % 4, group (warp - 2) / 4
     const uint32_t quarter = (uint32_t)(warp & 3);
@@ -238,25 +250,37 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
+            // the activations are the previous kernel's output
+            pdl_wait_prerequisites();
+            const uint32_t xbar0 = mapa_shared(smem_u32(&xfull[0]), 0);
+            // stage j's activation halves; CTA 0 arrives with both CTAs' bytes (the peer's may
+            // complete first: the phase still waits for this arrival)
+            auto load_x = [&](int j, int s) {
+                const int kk = (i_begin + j) * PK;
+                if (crank == 0) mbar_arrive_expect_tx(&xfull[s], 2u * x_stage);
+                tma_load_2d_to_leader(sx + s * x_stage, &tmap_x, kk, nx0, xbar0 + 8u * s);
+                tma_load_2d_to_leader(sx + s * x_stage + x_half, &tmap_x, kk + 64, nx0,
+                                      xbar0 + 8u * s);
+            };
+            for (int j = 0; j < num_k && j < stages; j++) load_x(j, j);
             int issued = num_k < stages ? num_k : stages;
             for (int j = stages; j < num_k; j++) {
                 const int s = j % stages;
                 const uint32_t ph = (uint32_t)(j / stages) & 1u;
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
-                const int kk = (i_begin + j) * PK;
-                mbar_arrive_expect_tx(&full[s], x_stage + P_Q_STAGE);
-                tma_load_2d(sx + s * x_stage, &tmap_x, kk, nx0, &full[s]);
-                tma_load_2d(sx + s * x_stage + x_half, &tmap_x, kk + 64, nx0, &full[s]);
-                tma_load_2d(sq + s * P_Q_STAGE, &tmap_q, kk / 2, m0, &full[s]);
+                mbar_arrive_expect_tx(&qfull[s], P_Q_STAGE);
+                tma_load_2d(sq + s * P_Q_STAGE, &tmap_q, (i_begin + j) * PK / 2, m0, &qfull[s]);
+                load_x(j, s);
                 issued = j + 1;
             }
             // Tail: every issued stage has landed and has been released by the leader's MMA
-            // commits (multicast into this CTA), so no copy or commit still targets this CTA's
-            // shared memory when it leaves.
+            // commits (multicast into this CTA; a release implies both activation halves had
+            // landed), so no copy or commit still targets this CTA's shared memory when it
+            // leaves.
             for (int j = (issued > stages ? issued - stages : 0); j < issued; j++) {
                 const int s = j % stages;
                 const uint32_t ph = (uint32_t)(j / stages) & 1u;
-                mbar_wait_bounded(&full[s], ph, err, nullptr);
+                mbar_wait_bounded(&qfull[s], ph, err, nullptr);
                 if (!*abort_flag) mbar_wait_bounded(&empty[s], ph, err, abort_flag);
             }
         }
@@ -269,7 +293,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             int s = 0;
             uint32_t ph = 0;
             for (int j = 0; j < num_k; j++) {
-                if (!mbar_wait_bounded(&afull[s], ph, err, abort_flag)) break;
+                if (!mbar_wait_bounded(&xfull[s], ph, err, abort_flag) ||
+                    !mbar_wait_bounded(&afull[s], ph, err, abort_flag))
+                    break;
                 tc_fence_after();
                 const uint32_t xs = smem_u32(sx + s * x_stage);
                 mma_pair_stage(tmem + acc_col, tmem + (uint32_t)s * P_STAGE_COLS, sw128_desc(xs),
@@ -294,7 +320,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             const uint32_t sc = sc0;
             sc0 = sc1;
             sc1 = load_scale(j + 2);
-            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], ph, err, abort_flag))) {
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(&qfull[s], ph, err, abort_flag))) {
                 ok = false;
                 break;
             }

@@ -21,7 +21,9 @@ constexpr int RP_BYTES = RP_THREADS * 18;
 __global__ void __launch_bounds__(RP_THREADS)
     repack_q4_0_kernel(const uint8_t* __restrict__ src, size_t nblocks, bool src16,
                        uint16_t* __restrict__ scales, uint8_t* __restrict__ quants) {
-    pdl_launch_dependents();
+    // No griddepcontrol.launch_dependents: the GEMMs and matvecs read their weights before
+    // their own programmatic wait, so the kernel that writes weights lets its dependents start
+    // only when it has completed.
     pdl_wait_prerequisites();
     __shared__ __align__(16) uint8_t tile[RP_BYTES];
     const size_t b0 = (size_t)blockIdx.x * RP_THREADS;
