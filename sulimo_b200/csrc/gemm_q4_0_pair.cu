@@ -342,20 +342,33 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         if (have) tc_fence_after();
         constexpr int ES = OUT_MODE == 0 ? 2 : 4;
         const bool issuer = (warp - 2) % 4 == 0 && lane == 0;
-        for (int c0 = group * P_EPI_TOKENS; c0 < bn; c0 += P_DEQ_GROUPS * P_EPI_TOKENS) {
+        // the group's chunks are c0 = 32 * (group + 4 * ci); all their TMEM loads are in flight
+        // before the first wait (warp-uniform: TMEM loads are warp-collective)
+        constexpr int CH = P_BN_MAX / (P_DEQ_GROUPS * P_EPI_TOKENS);
+        uint32_t v[CH][32];
+        const bool ld = __all_sync(0xffffffffu, have) && num_k > 0;
+#pragma unroll
+        for (int ci = 0; ci < CH; ci++) {
+            const int c0 = (group + ci * P_DEQ_GROUPS) * P_EPI_TOKENS;
+            if (ld && c0 < bn) {
+                tmem_ld32_issue(tmem + lane_base + acc_col + (uint32_t)c0, v[ci]);
+            } else {
+#pragma unroll
+                for (int jj = 0; jj < 32; jj++) v[ci][jj] = 0u;
+            }
+        }
+#pragma unroll
+        for (int ci = 0; ci < CH; ci++) tmem_ld_wait_carry(v[ci]);
+#pragma unroll
+        for (int ci = 0; ci < CH; ci++) {
+            const int c0 = (group + ci * P_DEQ_GROUPS) * P_EPI_TOKENS;
+            if (c0 >= bn) break;
             uint8_t* tile = sx + (size_t)c0 * PM * ES;
             if (have) {
-                uint32_t v[32];
-                if (num_k > 0) {
-                    tmem_ld32(tmem + lane_base + acc_col + (uint32_t)c0, v);
-                } else {
-#pragma unroll
-                    for (int jj = 0; jj < 32; jj++) v[jj] = 0u;
-                }
                 uint8_t* col = tile + (size_t)r * ES;
 #pragma unroll
                 for (int jj = 0; jj < 32; jj++) {
-                    const float f = __uint_as_float(v[jj]);
+                    const float f = __uint_as_float(v[ci][jj]);
                     if (ES == 2)
                         *reinterpret_cast<__half*>(col + (size_t)jj * PM * ES) = __float2half_rn(f);
                     else
