@@ -30,6 +30,7 @@ SOURCES = [
     "shard.cu",
     "forward.cu",
     "attn_prefill_q8_0.cu",
+    "attn_prefill_tc.cu",
 ]
 
 NVCC_FLAGS = [

@@ -5,6 +5,8 @@
 // Token n of the ubatch sits at position start_pos + n and attends to positions
 // 0 .. start_pos + n (ring slot p % capacity), query head h to kv head h / (H / Hkv).
 //
+// This file: the mma.sync form (rings or buffers outside the tcgen05 form's layout conditions);
+// the tcgen05 form is attn_prefill_tc.cu.
 // Flash-attention form on tensor cores (mma.sync m16n8k16, f16 in, f32 accumulate): one CTA
 // per (64-token tile, query head), 4 warps x 16 tokens.  Keys come in chunks of 64: the chunk's
 // Q8_0 integers are staged in shared memory as f16 (exact: |q| <= 128) -- K as [key][dim], V
@@ -14,6 +16,9 @@
 // softmax in f32 with the causal mask; P V per 32-dimension output block uses P scaled by
 // d_v(key, b) (f16 operand).  The reference accumulates the output in f16 in global memory
 // (prefill.cl:233); here it stays f32 in registers and is written once as f16.
+#include <stdlib.h>
+#include <string.h>
+
 #include "sulimo_common.cuh"
 #include "sulimo_internal.h"
 
@@ -236,9 +241,19 @@ __global__ void __launch_bounds__(PF_THREADS)
 
 }  // namespace
 
+// The tcgen05 form (attn_prefill_tc.cu) where its layout conditions hold (16-byte aligned q,
+// out and rings, 16-byte multiple slot pitch), else this mma.sync form; SULIMO_PREFILL_ATTN=mma
+// selects this form always (a measurement switch).
 int launch_attn_prefill(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                         size_t start_pos, size_t capacity, int n_tok, int H, int Hkv, int hd,
                         void* out) {
+    static const bool force_mma = [] {
+        const char* e = getenv("SULIMO_PREFILL_ATTN");
+        return e && strcmp(e, "mma") == 0;
+    }();
+    if (!force_mma && attn_prefill_tc_applies(q, k_ring, v_ring, capacity, Hkv, hd, out))
+        return launch_attn_prefill_tc(ctx, q, k_ring, v_ring, start_pos, capacity, n_tok, H, Hkv,
+                                      hd, out);
     dim3 grid((unsigned)((n_tok + PF_TOK - 1) / PF_TOK), (unsigned)H);
     const float scale = 1.0f / sqrtf((float)hd);
     const uint8_t* k = reinterpret_cast<const uint8_t*>(k_ring);

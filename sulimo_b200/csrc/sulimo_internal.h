@@ -223,6 +223,12 @@ int launch_repack_context(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
                           void* scratch, size_t* new_pos);
 int launch_repack_q4_0(sulimo_ctx* ctx, const void* src_aos, size_t nblocks, void* dst_scales,
                        void* dst_quants);
+// tcgen05 form of the prefill attention (attn_prefill_tc.cu) and whether it applies.
+bool attn_prefill_tc_applies(const float* q, const void* k_ring, const void* v_ring,
+                             size_t capacity, int Hkv, int hd, const void* out);
+int launch_attn_prefill_tc(sulimo_ctx* ctx, const float* q, const void* k_ring,
+                           const void* v_ring, size_t start_pos, size_t capacity, int n_tok,
+                           int H, int Hkv, int hd, void* out);
 int launch_attn_prefill(sulimo_ctx* ctx, const float* q, const void* k_ring, const void* v_ring,
                         size_t start_pos, size_t capacity, int n_tok, int H, int Hkv, int hd,
                         void* out);

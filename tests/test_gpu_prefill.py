@@ -44,6 +44,9 @@ def make_ring(rng, cap, hkv, hd):
     (70, 130, 12, 2, 128, 256),   # second ubatch: earlier positions come from the ring
     (64, 0, 24, 8, 128, 64),      # Llama geometry, exactly one tile, full ring
     (33, 7, 8, 8, 64, 48),        # MHA, head_dim 64
+    (300, 200, 12, 2, 128, 512),  # three 128-token tiles, eight 64-key chunks per tile
+    (512, 1024, 12, 2, 128, 1536),  # config-3 sized ubatch late in the prompt: 24 chunks
+    (257, 0, 4, 4, 64, 300),      # head_dim 64, a one-token last tile
 ])
 def test_prefill_attention_matches_oracle(ctx, n, start, H, Hkv, hd, cap):
     import torch
