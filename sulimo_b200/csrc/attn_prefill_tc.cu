@@ -202,18 +202,34 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------ converters ------------------------------
         const int ct = threadIdx.x - 128;
-        for (int it = ct; it < AT_TQ * (HD / 8); it += 128) {
-            const int row = it / (HD / 8), kc = it % (HD / 8);
-            const int t = t0 + row;
-            uint4 w = make_uint4(0u, 0u, 0u, 0u);
-            if (t < a.n) {
-                const float4* src =
-                    reinterpret_cast<const float4*>(a.q + ((size_t)t * a.H + h) * HD + kc * 8);
-                const float4 x0f = __ldg(src), x1f = __ldg(src + 1);
-                w = make_uint4(h2(x0f.x, x0f.y), h2(x0f.z, x0f.w), h2(x1f.x, x1f.y),
+        // the queries: batches of QB items per thread, all of a batch's loads issued before any
+        // is converted (one L2 round trip per batch, not per item)
+        constexpr int QITEMS = AT_TQ * (HD / 8) / 128, QB = 8;
+        for (int i0 = 0; i0 < QITEMS; i0 += QB) {
+            float4 xv[QB][2];
+#pragma unroll
+            for (int i = 0; i < QB; i++) {
+                const int it = ct + (i0 + i) * 128;
+                const int row = it / (HD / 8), kc = it % (HD / 8);
+                const int t = t0 + row;
+                if (t < a.n) {
+                    const float4* src = reinterpret_cast<const float4*>(
+                        a.q + ((size_t)t * a.H + h) * HD + kc * 8);
+                    xv[i][0] = __ldg(src);
+                    xv[i][1] = __ldg(src + 1);
+                } else {
+                    xv[i][0] = xv[i][1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < QB; i++) {
+                const int it = ct + (i0 + i) * 128;
+                const int row = it / (HD / 8), kc = it % (HD / 8);
+                const float4 x0f = xv[i][0], x1f = xv[i][1];
+                *reinterpret_cast<uint4*>(sQ + sw128_off(row, kc, AT_TQ)) =
+                    make_uint4(h2(x0f.x, x0f.y), h2(x0f.z, x0f.w), h2(x1f.x, x1f.y),
                                h2(x1f.z, x1f.w));
             }
-            *reinterpret_cast<uint4*>(sQ + sw128_off(row, kc, AT_TQ)) = w;
         }
         fence_proxy_async_smem();
         __syncwarp();
