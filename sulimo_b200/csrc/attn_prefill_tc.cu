@@ -11,12 +11,14 @@
 //     V ring rows of the kv head (a box of 64 slots starting at the 16-byte boundary at or below
 //     the head's first byte), two chunks in flight;
 //   warps 4-7 (converters): the CTA's queries once, as f16, into a 128-byte-swizzled K-major
-//     tile; then per chunk the raw Q8_0 rows dequantized to f16(d * q) — K as [key][dim], V
-//     transposed as [dim][key], both swizzled K-major B tiles (keys past the CTA's range: 0);
+//     tile; then per chunk one thread per (tensor, key): the key's staged ring row read with
+//     16-byte loads, each Q8_0 block dequantized to f16(d * q) by byte permutes and exact half
+//     arithmetic, written as [key][dim] into a 128-byte-swizzled tile — K-major B for S = Q K^T,
+//     MN-major B for O += P V (keys past the CTA's range: 0);
 //   warp 8, one thread (MMA): S = Q K^T (tcgen05.mma kind::f16, A and B from shared memory,
 //     M = 128, N = 64, fp32 in TMEM, two S buffers so S of the next chunk overlaps the softmax
-//     of this one), then O += P V (A = P from TMEM, B = V^T from shared memory, N = hd, O in
-//     TMEM for the whole key range);
+//     of this one), then O += P V (A = P from TMEM, B = V from shared memory read MN-major,
+//     N = hd, O in TMEM for the whole key range);
 //   warps 0-3 (softmax, thread = query row = TMEM lane): tcgen05.ld of the row's 64 scores,
 //     scale by 1/sqrt(hd), causal mask, online softmax in fp32 with a lazily raised running
 //     maximum (O and l are rescaled only when the row maximum grows by more than 8 in log2
@@ -47,18 +49,19 @@ constexpr uint32_t AT_O_COL = 256;   // O: [256, 256 + hd)
 constexpr float AT_LOG2E = 1.4426950408889634f;
 constexpr float AT_RESCALE = 8.0f;   // log2 of the largest P before O is rescaled
 constexpr uint32_t AT_BOXW_MAX = 160;  // bytes of a staged ring row (hd 128: 136 + lead-in)
+constexpr int AT_KV_ST = 3;            // K/V tile stages (the converters run ahead of P V)
 
 template <int HD>
 struct AtGeom {
     static constexpr int HB = HD / 32 * 34;                 // ring bytes of one kv head
     static constexpr uint32_t Q_BYTES = AT_TQ * HD * 2;     // Q tile, f16
     static constexpr uint32_t K_BYTES = AT_CK * HD * 2;     // K tile [64 keys][hd]
-    static constexpr uint32_t V_BYTES = HD * AT_CK * 2;     // V^T tile [hd][64 keys]
+    static constexpr uint32_t V_BYTES = AT_CK * HD * 2;     // V tile [64 keys][hd]
     static constexpr uint32_t RAW_BYTES = AT_CK * AT_BOXW_MAX;  // one tensor's staged rows
-    // layout: Q | K0 | K1 | V0 | V1 | raw K0, V0, K1, V1 | barriers
+    // layout: Q | K tiles | V tiles | raw K0, V0, K1, V1 | barriers
     static constexpr uint32_t OFF_K = Q_BYTES;
-    static constexpr uint32_t OFF_V = OFF_K + 2 * K_BYTES;
-    static constexpr uint32_t OFF_RAW = OFF_V + 2 * V_BYTES;
+    static constexpr uint32_t OFF_V = OFF_K + AT_KV_ST * K_BYTES;
+    static constexpr uint32_t OFF_RAW = OFF_V + AT_KV_ST * V_BYTES;
     static constexpr uint32_t OFF_BAR = OFF_RAW + 4 * RAW_BYTES;
     static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // + barriers + alignment slack
 };
@@ -76,6 +79,96 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int kc, int rows) {
 __device__ __forceinline__ uint32_t h2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Shared-memory descriptor of an MN-major operand with the 128-byte swizzle: 128-byte rows of
+// 64 f16 along MN, 8 rows (K) per 1024-byte atom; `lbo` bytes between the atoms of successive
+// 64-element MN blocks, 1024 bytes between successive 8-row K groups.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// One key's staged ring row of one kv head (the head's first byte at LEAD, the row 16-byte
+// aligned) dequantized to f16(d * q) into row `key` of a [64 keys][HD] tile with the 128-byte
+// swizzle.  A code byte q becomes f16 by a byte permute: (q ^ 0x80) is the low byte of the
+// f16 1024 + (q + 128), from which 1152 is subtracted exactly; the product with the block's
+// f16 scale is rounded once (mul.rn, no contraction), as f16(float(d) * q) is: the two agree
+// bit for bit.  A dead key (past the CTA's range) is written as zeros.
+template <int HD, int LEAD>
+__device__ __forceinline__ void convert_key_row(const uint8_t* row, uint8_t* tile, int key,
+                                                bool live) {
+    constexpr int NB = HD / 32;
+    constexpr int NW = (LEAD + NB * 34 + 15) / 16 * 4;  // 32-bit words staged for the head
+    uint32_t w[NW];
+#pragma unroll
+    for (int i = 0; i < NW / 4; i++) {
+        const uint4 x = reinterpret_cast<const uint4*>(row)[i];
+        w[4 * i] = x.x;
+        w[4 * i + 1] = x.y;
+        w[4 * i + 2] = x.z;
+        w[4 * i + 3] = x.w;
+    }
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480u));  // 1152
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        const int so = LEAD + 34 * b;  // the block's scale; its 32 codes follow
+        const uint32_t sbits = (so & 2) ? (w[so >> 2] >> 16) : (w[so >> 2] & 0xFFFFu);
+        uint32_t d2u = __byte_perm(sbits, 0u, 0x1010);
+        if (!live) d2u = 0u;
+        const __half2 d2 = *reinterpret_cast<const __half2*>(&d2u);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; c8++) {
+            uint32_t out[4];
+#pragma unroll
+            for (int jj = 0; jj < 2; jj++) {
+                const int o = so + 2 + 8 * c8 + 4 * jj;  // byte offset of 4 codes
+                uint32_t x = (o & 3) ? __byte_perm(w[o >> 2], w[(o >> 2) + 1], 0x5432) : w[o >> 2];
+                x ^= 0x80808080u;
+                uint32_t lo = __byte_perm(x, 0x64646464u, 0x5140);
+                uint32_t hi = __byte_perm(x, 0x64646464u, 0x7362);
+                __half2 hl = __hmul2_rn(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), d2);
+                __half2 hh = __hmul2_rn(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), d2);
+                out[2 * jj] = *reinterpret_cast<uint32_t*>(&hl);
+                out[2 * jj + 1] = *reinterpret_cast<uint32_t*>(&hh);
+            }
+            *reinterpret_cast<uint4*>(tile + sw128_off(key, b * 4 + c8, AT_CK)) =
+                make_uint4(out[0], out[1], out[2], out[3]);
+        }
+    }
+}
+
+template <int HD>
+__device__ __forceinline__ void convert_key_row_any(int lead, const uint8_t* row, uint8_t* tile,
+                                                    int key, bool live) {
+    if (lead == 0) {
+        convert_key_row<HD, 0>(row, tile, key, live);
+    } else if (lead == 8) {
+        convert_key_row<HD, 8>(row, tile, key, live);
+    } else if constexpr (HD == 64) {
+        if (lead == 4)
+            convert_key_row<HD, 4>(row, tile, key, live);
+        else
+            convert_key_row<HD, 12>(row, tile, key, live);
+    }
+}
+
+__device__ __forceinline__ float fmax3(float x, float y, float z) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+    return r;
+}
+
+// 2^x by the special-function unit's approximation (ex2.approx; -inf -> +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
 }
 
 // SS-form MMA: A and B from shared-memory descriptors.
@@ -110,20 +203,53 @@ __device__ __forceinline__ void commit_to(uint64_t* bar) {
 struct AtArgs {
     const float* q;        // [n][H][hd] fp32 (after RoPE)
     __half* out;           // [n][H][hd] f16
+    float* part;           // split tiles: [work][H][128 rows][hd] fp32 O / l
+    float* part_lse;       // split tiles: [work][H][128 rows] m + log2(l), log2 units
     size_t start_pos;
     int n, H, Hkv;
     int boxw;              // bytes of a staged ring row (16-byte multiple)
+    int per_cta;           // key-chunk budget of a CTA: a tile of c chunks runs as ceil(c / per_cta)
     float scale_log2;      // log2(e) / sqrt(hd)
     int* err;
 };
+
+// Key chunks of the 128-token tile x: positions 0 .. start_pos + the tile's last token.
+__host__ __device__ __forceinline__ int at_tile_chunks(size_t start_pos, int n, int x) {
+    const long last = (long)(x + 1) * AT_TQ < (long)n ? (long)(x + 1) * AT_TQ : (long)n;
+    return (int)(((long)start_pos + last + AT_CK - 1) / AT_CK);
+}
+
+// The CTA `w` of a launch: tile, its chunk range (the tile's chunks divided evenly among its
+// splits), the tile's split count and the work index of its first split.
+struct AtWork {
+    int tile, c_begin, c_end, splits, first;
+};
+
+__device__ __forceinline__ AtWork at_work(const AtArgs& a, int w) {
+    const int tiles = (a.n + AT_TQ - 1) / AT_TQ;
+    if (a.per_cta >= at_tile_chunks(a.start_pos, a.n, tiles - 1))  // no tile is split
+        return {w, 0, at_tile_chunks(a.start_pos, a.n, w), 1, w};
+    int first = 0;
+    for (int x = 0; x < tiles; x++) {
+        const int nch = at_tile_chunks(a.start_pos, a.n, x);
+        const int gx = (nch + a.per_cta - 1) / a.per_cta;
+        if (w < first + gx) {
+            const int g = w - first;
+            return {x, g * nch / gx, (g + 1) * nch / gx, gx, first};
+        }
+        first += gx;
+    }
+    return {tiles, 0, 0, 0, first};
+}
 
 template <int HD>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ AtArgs a,
                            const __grid_constant__ CUtensorMap tmap_k,
-                           const __grid_constant__ CUtensorMap tmap_v) {
+                           const __grid_constant__ CUtensorMap tmap_v,
+                           const __grid_constant__ CUtensorMap tmap_o,
+                           const __grid_constant__ CUtensorMap tmap_p) {
     using G = AtGeom<HD>;
-    constexpr int NB = HD / 32;
     constexpr unsigned FULL = 0xffffffffu;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -132,24 +258,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint8_t* sV = smem + G::OFF_V;
     uint8_t* sRaw = smem + G::OFF_RAW;  // stage s: K at 2s, V at 2s + 1 (RAW_BYTES each)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::OFF_BAR);
-    uint64_t* q_full = bars;        // converters: the query tile is in place
+    uint64_t* q_full = bars;        // softmax warps: the query tile is in place
     uint64_t* raw_full = bars + 1;  // [2] producer: the chunk's ring rows landed
     uint64_t* raw_free = bars + 3;  // [2] converters: done reading the chunk's ring rows
-    uint64_t* kv_full = bars + 5;   // [2] converters: the chunk's K and V tiles in place
-    uint64_t* kv_free = bars + 7;   // [2] MMA: the chunk's P V done, its tiles may be refilled
-    uint64_t* s_full = bars + 9;    // [2] MMA: S of the chunk in TMEM
-    uint64_t* p_full = bars + 11;   // [2] softmax: P of the chunk in TMEM, O rescaled
-    uint64_t* pv_done = bars + 13;  // MMA: P V of the chunk done (one phase per chunk)
-    uint64_t* drained = bars + 14;  // MMA: everything it issued has completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    uint64_t* kv_full = bars + 5;   // [3] converters: the chunk's K and V tiles in place
+    uint64_t* kv_free = bars + 8;   // [3] MMA: the chunk's P V done, its tiles may be refilled
+    uint64_t* s_full = bars + 11;   // [2] MMA: S of the chunk in TMEM
+    uint64_t* p_full = bars + 13;   // [2] softmax: P of the chunk in TMEM, O rescaled
+    uint64_t* pv_done = bars + 15;  // [2] MMA: P V of the chunk done (per P buffer)
+    uint64_t* drained = bars + 17;  // MMA: everything it issued has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t0 = blockIdx.x * AT_TQ, h = blockIdx.y;
+    const AtWork wk = at_work(a, blockIdx.x);
+    const int t0 = wk.tile * AT_TQ, h = blockIdx.y;
     const int kvh = h / (a.H / a.Hkv);
     const long last_tok = min((long)a.n - 1, (long)t0 + AT_TQ - 1);
-    const long key_end = (long)a.start_pos + last_tok + 1;  // keys [0, key_end) for this CTA
-    const int nch = (int)((key_end + AT_CK - 1) / AT_CK);
+    const long key_end = (long)a.start_pos + last_tok + 1;  // keys [0, key_end) for the tile
+    const int cb = wk.c_begin, nloc = wk.c_end - wk.c_begin;  // this CTA's chunks
+    if (wk.tile >= (a.n + AT_TQ - 1) / AT_TQ || nloc <= 0) return;  // (not for a planned grid)
     const int x0 = (kvh * G::HB) & ~15;  // TMA x coordinate: 16-byte aligned
     const int lead = kvh * G::HB - x0;   // the head's first byte inside a staged row
 
@@ -158,17 +286,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         for (int s = 0; s < 2; s++) {
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_free[s], 4);
-            mbar_init(&kv_full[s], 4);
-            mbar_init(&kv_free[s], 1);
             mbar_init(&s_full[s], 1);
             mbar_init(&p_full[s], 4);
+            mbar_init(&pv_done[s], 1);
         }
-        mbar_init(pv_done, 1);
+        for (int s = 0; s < AT_KV_ST; s++) {
+            mbar_init(&kv_full[s], 4);
+            mbar_init(&kv_free[s], 1);
+        }
         mbar_init(drained, 1);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmap_k);
         prefetch_tensormap(&tmap_v);
+        prefetch_tensormap(wk.splits > 1 ? &tmap_p : &tmap_o);
     }
     if (warp == 8) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -184,32 +315,17 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 9) {
-        // ------------------------------ producer ------------------------------
-        if (lane == 0) {
-            const uint32_t bytes = 2u * AT_CK * (uint32_t)a.boxw;
-            for (int c = 0; c < nch; c++) {
-                const int s = c & 1;
-                if (c >= 2 &&
-                    !mbar_wait_bounded(&raw_free[s], ((c >> 1) - 1) & 1, a.err, abort_flag))
-                    break;
-                mbar_arrive_expect_tx(&raw_full[s], bytes);
-                tma_load_2d(sRaw + (2 * s) * G::RAW_BYTES, &tmap_k, x0, c * AT_CK, &raw_full[s]);
-                tma_load_2d(sRaw + (2 * s + 1) * G::RAW_BYTES, &tmap_v, x0, c * AT_CK,
-                            &raw_full[s]);
-            }
-        }
-    } else if (warp >= 4 && warp < 8) {
-        // ------------------------------ converters ------------------------------
-        const int ct = threadIdx.x - 128;
-        // the queries: batches of QB items per thread, all of a batch's loads issued before any
-        // is converted (one L2 round trip per batch, not per item)
+    if (warp < 4) {
+        // the queries (softmax warps, while the converters start on the first chunk), f16 into
+        // the swizzled K-major tile: batches of QB items per thread, all of a batch's loads
+        // issued before any is converted
         constexpr int QITEMS = AT_TQ * (HD / 8) / 128, QB = 8;
+#pragma unroll
         for (int i0 = 0; i0 < QITEMS; i0 += QB) {
             float4 xv[QB][2];
 #pragma unroll
             for (int i = 0; i < QB; i++) {
-                const int it = ct + (i0 + i) * 128;
+                const int it = threadIdx.x + (i0 + i) * 128;
                 const int row = it / (HD / 8), kc = it % (HD / 8);
                 const int t = t0 + row;
                 if (t < a.n) {
@@ -223,7 +339,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
 #pragma unroll
             for (int i = 0; i < QB; i++) {
-                const int it = ct + (i0 + i) * 128;
+                const int it = threadIdx.x + (i0 + i) * 128;
                 const int row = it / (HD / 8), kc = it % (HD / 8);
                 const float4 x0f = xv[i][0], x1f = xv[i][1];
                 *reinterpret_cast<uint4*>(sQ + sw128_off(row, kc, AT_TQ)) =
@@ -234,78 +350,64 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(q_full);
-        for (int c = 0; c < nch; c++) {
-            const int s = c & 1;
-            if (!__all_sync(FULL, mbar_wait_bounded(&raw_full[s], (c >> 1) & 1, a.err,
+    }
+
+    if (warp == 9) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            const uint32_t bytes = 2u * AT_CK * (uint32_t)a.boxw;
+            for (int i = 0; i < nloc; i++) {
+                const int s = i & 1, c = cb + i;
+                if (i >= 2 &&
+                    !mbar_wait_bounded(&raw_free[s], ((i >> 1) - 1) & 1, a.err, abort_flag))
+                    break;
+                mbar_arrive_expect_tx(&raw_full[s], bytes);
+                tma_load_2d(sRaw + (2 * s) * G::RAW_BYTES, &tmap_k, x0, c * AT_CK, &raw_full[s]);
+                tma_load_2d(sRaw + (2 * s + 1) * G::RAW_BYTES, &tmap_v, x0, c * AT_CK,
+                            &raw_full[s]);
+            }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------ converters ------------------------------
+        const int ct = threadIdx.x - 128;
+        for (int i = 0; i < nloc; i++) {
+            const int s = i & 1, c = cb + i;
+            if (!__all_sync(FULL, mbar_wait_bounded(&raw_full[s], (i >> 1) & 1, a.err,
                                                     abort_flag)))
                 break;
-            if (c >= 2 && !__all_sync(FULL, mbar_wait_bounded(&kv_free[s], ((c >> 1) - 1) & 1,
-                                                               a.err, abort_flag)))
+            const int ks = i % AT_KV_ST;
+            if (i >= AT_KV_ST &&
+                !__all_sync(FULL, mbar_wait_bounded(&kv_free[ks], (i / AT_KV_ST - 1) & 1, a.err,
+                                                    abort_flag)))
                 break;
-            const long k0 = (long)c * AT_CK;
-            const uint8_t* rk = sRaw + (2 * s) * G::RAW_BYTES + lead;
-            const uint8_t* rv = sRaw + (2 * s + 1) * G::RAW_BYTES + lead;
-            // K tile [key][dim]: f16(d * q), one (key, Q8_0 block) per item
-            uint8_t* kt = sK + s * G::K_BYTES;
-            for (int it = ct; it < AT_CK * NB; it += 128) {
-                const int key = it / NB, b = it % NB;
-                const bool live = k0 + key < key_end;
-                const uint8_t* blk = rk + key * a.boxw + b * 34;
-                const float d = live ? __half2float(*reinterpret_cast<const __half*>(blk)) : 0.0f;
-#pragma unroll
-                for (int c8 = 0; c8 < 4; c8++) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const uint32_t pr =
-                            live ? *reinterpret_cast<const uint16_t*>(blk + 2 + c8 * 8 + 2 * e) : 0u;
-                        w[e] = h2(d * (float)(int8_t)(pr & 0xFFu), d * (float)(int8_t)(pr >> 8));
-                    }
-                    *reinterpret_cast<uint4*>(kt + sw128_off(key, b * 4 + c8, AT_CK)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
-                }
-            }
-            // V^T tile [dim][key]: one (dimension, 8 keys) per item
-            uint8_t* vt = sV + s * G::V_BYTES;
-            for (int it = ct; it < HD * (AT_CK / 8); it += 128) {
-                const int dm = it % HD, o = it / HD;
-                const int b = dm >> 5, e = dm & 31;
-                uint32_t w[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int key = o * 8 + 2 * i;
-                    const uint8_t* r0 = rv + key * a.boxw + b * 34;
-                    const uint8_t* r1 = r0 + a.boxw;
-                    const bool l0 = k0 + key < key_end, l1 = k0 + key + 1 < key_end;
-                    const float d0 = l0 ? __half2float(*reinterpret_cast<const __half*>(r0)) : 0.0f;
-                    const float d1 = l1 ? __half2float(*reinterpret_cast<const __half*>(r1)) : 0.0f;
-                    const int c0 = l0 ? (int)(int8_t)r0[2 + e] : 0;
-                    const int c1 = l1 ? (int)(int8_t)r1[2 + e] : 0;
-                    w[i] = h2(d0 * (float)c0, d1 * (float)c1);
-                }
-                *reinterpret_cast<uint4*>(vt + sw128_off(dm, o, HD)) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
-            }
+            // thread ct: tensor ct / 64 (K, V), key ct % 64 of the chunk
+            const int tsel = ct >> 6, key = ct & 63;
+            const bool live = (long)c * AT_CK + key < key_end;
+            convert_key_row_any<HD>(lead, sRaw + (2 * s + tsel) * G::RAW_BYTES + key * a.boxw,
+                                    (tsel ? sV + ks * G::V_BYTES : sK + ks * G::K_BYTES), key,
+                                    live);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&kv_full[s]);
+                mbar_arrive(&kv_full[ks]);
                 mbar_arrive(&raw_free[s]);
             }
         }
     } else if (warp == 8) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
-            // kind::f16, D f32, A = B = f16 K-major; N >> 3 at bit 17, M >> 4 at bit 24
+            // kind::f16, D f32, A = B = f16; N >> 3 at bit 17, M >> 4 at bit 24
             const uint32_t idesc_s =
                 (1u << 4) | ((uint32_t)(AT_CK >> 3) << 17) | ((uint32_t)(AT_TQ >> 4) << 24);
-            const uint32_t idesc_o =
-                (1u << 4) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(AT_TQ >> 4) << 24);
-            auto issue_s = [&](int c) -> bool {
-                const int s = c & 1;
-                if (!mbar_wait_bounded(&kv_full[s], (c >> 1) & 1, a.err, abort_flag)) return false;
+            // O += P V: B = V read MN-major (bit 16)
+            const uint32_t idesc_o = (1u << 4) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) |
+                                     ((uint32_t)(AT_TQ >> 4) << 24);
+            auto issue_s = [&](int i) -> bool {
+                const int s = i & 1, ks = i % AT_KV_ST;
+                if (!mbar_wait_bounded(&kv_full[ks], (i / AT_KV_ST) & 1, a.err, abort_flag))
+                    return false;
                 tc_fence_after();
-                const uint32_t qa = smem_u32(sQ), kb = smem_u32(sK + s * G::K_BYTES);
+                const uint32_t qa = smem_u32(sQ), kb = smem_u32(sK + ks * G::K_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; kk++) {
                     const uint64_t ad =
@@ -318,21 +420,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 return true;
             };
             bool ok = mbar_wait_bounded(q_full, 0, a.err, abort_flag) && issue_s(0);
-            for (int c = 0; ok && c < nch; c++) {
-                const int s = c & 1;
+            for (int i = 0; ok && i < nloc; i++) {
+                const int s = i & 1;
                 // S of the next chunk overlaps this chunk's softmax (its buffer was read by the
-                // softmax of chunk c - 1, whose P this loop already waited for)
-                if (c + 1 < nch && !issue_s(c + 1)) break;
-                if (!mbar_wait_bounded(&p_full[s], (c >> 1) & 1, a.err, abort_flag)) break;
+                // softmax of chunk i - 1, whose P this loop already waited for)
+                if (i + 1 < nloc && !issue_s(i + 1)) break;
+                if (!mbar_wait_bounded(&p_full[s], (i >> 1) & 1, a.err, abort_flag)) break;
                 tc_fence_after();
-                const uint32_t vb = smem_u32(sV + s * G::V_BYTES);
+                const uint32_t vb = smem_u32(sV + (i % AT_KV_ST) * G::V_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < AT_CK / 16; kk++)
                     mma_ts(tmem + AT_O_COL, tmem + AT_P_COL + (uint32_t)s * 32u + (uint32_t)kk * 8u,
-                           sw128_desc(vb) + (uint64_t)(kk * 2), idesc_o,
-                           (c > 0 || kk > 0) ? 1u : 0u);
-                commit_to(pv_done);
-                commit_to(&kv_free[s]);
+                           sw128_mn_desc(vb + (uint32_t)kk * 2048u, 64u * 128u), idesc_o,
+                           (i > 0 || kk > 0) ? 1u : 0u);
+                commit_to(&pv_done[s]);
+                commit_to(&kv_free[i % AT_KV_ST]);
             }
             commit_to(drained);
             mbar_wait_bounded(drained, 0, a.err, nullptr);
@@ -343,11 +445,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const int t = t0 + row;
         const long pos = (long)a.start_pos + t;
         const uint32_t lane_base = ((uint32_t)(warp * 32)) << 16;
+        const long pos_first = (long)a.start_pos + t0;  // the tile's first query position
+        const float sc = a.scale_log2;
+        // running maximum in log2 units (-inf while no key of the CTA's range is visible to
+        // the row: possible in a split other than the tile's first), row sum
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (int c = 0; c < nch; c++) {
-            const int s = c & 1;
-            if (!__all_sync(FULL, mbar_wait_bounded(&s_full[s], (c >> 1) & 1, a.err, abort_flag))) {
+        for (int i = 0; i < nloc; i++) {
+            const int s = i & 1;
+            if (!__all_sync(FULL, mbar_wait_bounded(&s_full[s], (i >> 1) & 1, a.err, abort_flag))) {
                 ok = false;
                 break;
             }
@@ -357,28 +463,39 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             tmem_ld32_issue(tmem + lane_base + AT_S_COL + (uint32_t)s * 64u + 32u, v[1]);
             tmem_ld_wait_carry(v[0]);
             tmem_ld_wait_carry(v[1]);
-            const long k0 = (long)c * AT_CK;
-            float mx = -INFINITY;
+            const long k0 = (long)(cb + i) * AT_CK;
+            if (k0 + AT_CK - 1 > pos_first) {  // the chunk reaches past some row's position
 #pragma unroll
-            for (int j = 0; j < AT_CK; j++) {
-                const float x = (k0 + j <= pos) ? __uint_as_float(v[j >> 5][j & 31]) * a.scale_log2
-                                                : -INFINITY;
-                v[j >> 5][j & 31] = __float_as_uint(x);
-                mx = fmaxf(mx, x);
+                for (int j = 0; j < AT_CK; j++)
+                    if (k0 + j > pos) v[j >> 5][j & 31] = __float_as_uint(-INFINITY);
             }
-            // O and this chunk's P buffer are free once P V of chunk c - 1 has completed
-            if (c > 0 && !__all_sync(FULL, mbar_wait_bounded(pv_done, (uint32_t)(c - 1) & 1u,
-                                                             a.err, abort_flag))) {
-                ok = false;
-                break;
+            // row maximum of the raw scores (the scale is positive): eight independent chains
+            float mx8[8];
+#pragma unroll
+            for (int q8 = 0; q8 < 8; q8++) {
+                const uint32_t* u = &v[q8 >> 2][(q8 & 3) * 8];
+                mx8[q8] = fmax3(fmax3(__uint_as_float(u[0]), __uint_as_float(u[1]),
+                                      __uint_as_float(u[2])),
+                                fmax3(__uint_as_float(u[3]), __uint_as_float(u[4]),
+                                      __uint_as_float(u[5])),
+                                fmaxf(__uint_as_float(u[6]), __uint_as_float(u[7])));
             }
-            tc_fence_after();
-            const float m_new = fmaxf(m_used, mx);
-            if (c == 0) {
-                m_used = m_new;  // key 0 is visible to every row: finite
+            const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                                   fmaxf(mx8[6], mx8[7]));
+            const float m_new = fmaxf(m_used, mx * sc);
+            if (i == 0) {
+                m_used = m_new;
             } else if (__any_sync(FULL, m_new > m_used + AT_RESCALE)) {
+                // O holds P V up to the previous chunk: wait for it before scaling
+                if (!__all_sync(FULL, mbar_wait_bounded(&pv_done[(i - 1) & 1],
+                                                        (uint32_t)((i - 1) >> 1) & 1u, a.err,
+                                                        abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
                 const bool mine = m_new > m_used + AT_RESCALE;
-                const float alpha = mine ? exp2f(m_used - m_new) : 1.0f;
+                const float alpha = mine ? ex2_approx(m_used - m_new) : 1.0f;
                 if (mine) {
                     l *= alpha;
                     m_used = m_new;
@@ -393,23 +510,39 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     tmem_st32(tmem + lane_base + AT_O_COL + (uint32_t)c0, o);
                 }
             }
+            // this P buffer was last read by P V two chunks back
+            if (i >= 2 && !__all_sync(FULL, mbar_wait_bounded(&pv_done[s],
+                                                              (uint32_t)((i >> 1) - 1) & 1u,
+                                                              a.err, abort_flag))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
             uint32_t pw[32];
-            float psum = 0.0f;
+            float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float nm = m_used == -INFINITY ? 0.0f : -m_used;
 #pragma unroll
             for (int j = 0; j < AT_CK; j += 2) {
-                const float p0 = exp2f(__uint_as_float(v[j >> 5][j & 31]) - m_used);
-                const float p1 = exp2f(__uint_as_float(v[(j + 1) >> 5][(j + 1) & 31]) - m_used);
-                psum += p0 + p1;
+                const float p0 = ex2_approx(fmaf(__uint_as_float(v[j >> 5][j & 31]), sc, nm));
+                const float p1 =
+                    ex2_approx(fmaf(__uint_as_float(v[(j + 1) >> 5][(j + 1) & 31]), sc, nm));
+                ps[(j >> 1) & 3] += p0 + p1;
                 pw[j >> 1] = h2(p0, p1);
             }
-            l += psum;
+            l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
             tmem_st32(tmem + lane_base + AT_P_COL + (uint32_t)s * 32u, pw);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[s]);
         }
-        if (ok && __all_sync(FULL, mbar_wait_bounded(pv_done, (uint32_t)(nch - 1) & 1u, a.err,
+        // epilogue: O / l staged in the (now unused) K/V tiles as 128-byte-swizzled boxes of
+        // 128 rows, then stored by TMA — f16 into out for a tile of one CTA, fp32 partials
+        // (+ the row's lse) for a split tile
+        const bool split = wk.splits > 1;
+        uint8_t* stg = sK;
+        if (ok && __all_sync(FULL, mbar_wait_bounded(&pv_done[(nloc - 1) & 1],
+                                                    (uint32_t)((nloc - 1) >> 1) & 1u, a.err,
                                                     abort_flag))) {
             tc_fence_after();
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
@@ -417,17 +550,44 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             for (int c0 = 0; c0 < HD; c0 += 32) {
                 uint32_t o[32];
                 tmem_ld32(tmem + lane_base + AT_O_COL + (uint32_t)c0, o);
-                if (t < a.n) {
-                    __half* dst = a.out + ((size_t)t * a.H + h) * HD + c0;
+                const float* f = reinterpret_cast<const float*>(o);
+                if (split) {
+                    uint8_t* bx = stg + (c0 / 32) * (AT_TQ * 128) + row * 128;
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; q4++) {
-                        const float* f = reinterpret_cast<const float*>(o + q4 * 8);
-                        *reinterpret_cast<uint4*>(dst + q4 * 8) =
-                            make_uint4(h2(f[0] * inv, f[1] * inv), h2(f[2] * inv, f[3] * inv),
-                                       h2(f[4] * inv, f[5] * inv), h2(f[6] * inv, f[7] * inv));
+                    for (int k = 0; k < 8; k++)
+                        *reinterpret_cast<float4*>(bx + ((k ^ (row & 7)) << 4)) =
+                            make_float4(f[4 * k] * inv, f[4 * k + 1] * inv, f[4 * k + 2] * inv,
+                                        f[4 * k + 3] * inv);
+                } else {
+                    uint8_t* bx = stg + (c0 / 64) * (AT_TQ * 128) + row * 128;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int kc = (c0 % 64) / 8 + k;
+                        *reinterpret_cast<uint4*>(bx + ((kc ^ (row & 7)) << 4)) =
+                            make_uint4(h2(f[8 * k] * inv, f[8 * k + 1] * inv),
+                                       h2(f[8 * k + 2] * inv, f[8 * k + 3] * inv),
+                                       h2(f[8 * k + 4] * inv, f[8 * k + 5] * inv),
+                                       h2(f[8 * k + 6] * inv, f[8 * k + 7] * inv));
                     }
                 }
             }
+            if (split && t < a.n)
+                a.part_lse[((size_t)blockIdx.x * a.H + h) * AT_TQ + row] =
+                    l > 0.0f ? m_used + __log2f(l) : -INFINITY;
+        }
+        fence_proxy_async_smem();
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 0 && *abort_flag == 0) {
+            if (split) {
+                for (int j = 0; j < HD / 32; j++)
+                    tma_store_2d(&tmap_p, j * 32, (blockIdx.x * a.H + h) * AT_TQ,
+                                 stg + j * (AT_TQ * 128));
+            } else {
+                for (int j = 0; j < HD / 64; j++)
+                    tma_store_3d(&tmap_o, j * 64, h, t0, stg + j * (AT_TQ * 128));
+            }
+            bulk_commit();
+            bulk_wait_read_all();
         }
     }
 
@@ -441,8 +601,53 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     }
 }
 
+// Merges the splits of each split tile: out = sum_g 2^(lse_g - m) (O/l)_g / sum_g 2^(lse_g - m)
+// as f16, combined online over the splits (split 0 holds key 0, so its lse is finite).
+// Grid (tiles x 128 / RPB, H): a block is RPB rows of one tile, a thread 4 dimensions of a row;
+// blocks of tiles with one split return at once.
 template <int HD>
-int launch_hd_tc(sulimo_ctx* ctx, const AtArgs& a, const CUtensorMap& tk, const CUtensorMap& tv) {
+__global__ void __launch_bounds__(256) attn_prefill_merge_kernel(const __grid_constant__ AtArgs a) {
+    pdl_launch_dependents();
+    constexpr int TPR = HD / 4;     // threads per row
+    constexpr int RPB = 256 / TPR;  // rows per block
+    const int x = blockIdx.x / (AT_TQ / RPB), h = blockIdx.y;
+    const int row = (blockIdx.x % (AT_TQ / RPB)) * RPB + threadIdx.x / TPR;
+    const int sub = threadIdx.x % TPR;
+    int first = 0, gx = 0;
+    for (int xx = 0; xx <= x; xx++) {
+        const int g = (at_tile_chunks(a.start_pos, a.n, xx) + a.per_cta - 1) / a.per_cta;
+        if (xx == x)
+            gx = g;
+        else
+            first += g;
+    }
+    const int t = x * AT_TQ + row;
+    if (gx <= 1 || t >= a.n) return;
+    pdl_wait_prerequisites();
+    size_t u = ((size_t)first * a.H + h) * AT_TQ + row;
+    const size_t ustep = (size_t)a.H * AT_TQ;
+    float m = a.part_lse[u], wsum = 1.0f;
+    float4 acc = *reinterpret_cast<const float4*>(a.part + u * HD + sub * 4);
+#pragma unroll 4
+    for (int g = 1; g < gx; g++) {
+        u += ustep;
+        const float lg = a.part_lse[u];
+        const float4 p = *reinterpret_cast<const float4*>(a.part + u * HD + sub * 4);
+        const float mn = fmaxf(m, lg);
+        const float so = ex2_approx(m - mn), w = ex2_approx(lg - mn);
+        acc = make_float4(fmaf(w, p.x, acc.x * so), fmaf(w, p.y, acc.y * so),
+                          fmaf(w, p.z, acc.z * so), fmaf(w, p.w, acc.w * so));
+        wsum = fmaf(wsum, so, w);
+        m = mn;
+    }
+    const float inv = 1.0f / wsum;
+    *reinterpret_cast<uint2*>(a.out + ((size_t)t * a.H + h) * HD + sub * 4) =
+        make_uint2(h2(acc.x * inv, acc.y * inv), h2(acc.z * inv, acc.w * inv));
+}
+
+template <int HD>
+int launch_hd_tc(sulimo_ctx* ctx, const AtArgs& a, int nwork, const CUtensorMap& tk,
+                 const CUtensorMap& tv, const CUtensorMap& to, const CUtensorMap& tp) {
     static DeviceBits attr;
     if (!attr.test(ctx->device)) {
         int st = check_cuda(cudaFuncSetAttribute(attn_prefill_tc_kernel<HD>,
@@ -452,11 +657,42 @@ int launch_hd_tc(sulimo_ctx* ctx, const AtArgs& a, const CUtensorMap& tk, const 
         if (st) return st;
         attr.set(ctx->device);
     }
-    const dim3 grid((unsigned)((a.n + AT_TQ - 1) / AT_TQ), (unsigned)a.H);
-    const cudaError_t e = launch_pdl(attn_prefill_tc_kernel<HD>, grid, dim3(AT_THREADS),
-                                     (size_t)AtGeom<HD>::SMEM, ctx->stream, a, tk, tv);
+    const int tiles = (a.n + AT_TQ - 1) / AT_TQ;
+    cudaError_t e = launch_pdl(attn_prefill_tc_kernel<HD>, dim3((unsigned)nwork, (unsigned)a.H),
+                               dim3(AT_THREADS), (size_t)AtGeom<HD>::SMEM, ctx->stream, a, tk,
+                               tv, to, tp);
     ctx->launches++;
-    return check_cuda(e, "attn_prefill_tc launch");
+    int st = check_cuda(e, "attn_prefill_tc launch");
+    if (st || nwork == tiles) return st;
+    constexpr int rpb = 256 / (HD / 4);
+    e = launch_pdl(attn_prefill_merge_kernel<HD>,
+                   dim3((unsigned)(tiles * (AT_TQ / rpb)), (unsigned)a.H), dim3(256), 0,
+                   ctx->stream, a);
+    ctx->launches++;
+    return check_cuda(e, "attn_prefill_merge launch");
+}
+
+// The chunk budget of a CTA: the smallest (at least two chunks) whose CTAs, over all tiles
+// and heads, fit in one wave of one CTA per SM.  Returns the number of CTAs per head.
+int plan_splits(size_t start_pos, int n, int H, int num_sms, int* per_cta) {
+    const int tiles = (n + AT_TQ - 1) / AT_TQ;
+    const int per_head = std::max(1, (num_sms > 0 ? num_sms : 148) / H);
+    int total = 0, most = 1;
+    for (int x = 0; x < tiles; x++) {
+        const int c = at_tile_chunks(start_pos, n, x);
+        total += c;
+        most = std::max(most, c);
+    }
+    auto ctas = [&](int per) {
+        int w = 0;
+        for (int x = 0; x < tiles; x++) w += (at_tile_chunks(start_pos, n, x) + per - 1) / per;
+        return w;
+    };
+    int per = tiles >= per_head ? most : std::max(2, (total + per_head - 1) / per_head);
+    while (per < most && ctas(per) > per_head) per++;
+    per = std::min(per, most);
+    *per_cta = per;
+    return ctas(per);
 }
 
 }  // namespace
@@ -490,6 +726,17 @@ int launch_attn_prefill_tc(sulimo_ctx* ctx, const float* q, const void* k_ring,
     a.boxw = (int)((lead + hb + 15) / 16 * 16);
     a.scale_log2 = AT_LOG2E / sqrtf((float)hd);
     a.err = ctx->d_error;
+    a.part = nullptr;
+    a.part_lse = nullptr;
+    const int nwork = plan_splits(start_pos, n_tok, H, ctx->num_sms, &a.per_cta);
+    if (nwork > (n_tok + AT_TQ - 1) / AT_TQ) {
+        // split partials: O / l then lse, per (CTA, head, row)
+        const size_t rows = (size_t)nwork * H * AT_TQ;
+        int st = ensure_workspace(ctx, rows * ((size_t)hd + 1) * sizeof(float));
+        if (st) return st;
+        a.part = reinterpret_cast<float*>(ctx->workspace);
+        a.part_lse = a.part + rows * hd;
+    }
     CUtensorMap tk, tv;
     memset(&tk, 0, sizeof(tk));
     memset(&tv, 0, sizeof(tv));
@@ -501,7 +748,24 @@ int launch_attn_prefill_tc(sulimo_ctx* ctx, const float* q, const void* k_ring,
                        (uint64_t)capacity, (uint64_t)bpp, (uint32_t)a.boxw, (uint32_t)AT_CK,
                        CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    return hd == 64 ? launch_hd_tc<64>(ctx, a, tk, tv) : launch_hd_tc<128>(ctx, a, tk, tv);
+    // the output as [n][H][hd] f16 and the split partials as [rows][hd] fp32, both stored in
+    // boxes of 128 rows x 128 bytes with the 128-byte swizzle
+    CUtensorMap to, tp;
+    memset(&to, 0, sizeof(to));
+    memset(&tp, 0, sizeof(tp));
+    const uint64_t odims[3] = {(uint64_t)hd, (uint64_t)H, (uint64_t)n_tok};
+    const uint64_t ostr[2] = {(uint64_t)hd * 2, (uint64_t)H * hd * 2};
+    const uint32_t obox[3] = {64, 1, (uint32_t)AT_TQ};
+    if ((st = encode_tensor_map(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out, 3, odims, ostr, obox,
+                                CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    if (a.part &&
+        (st = encode_2d(&tp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.part, (uint64_t)hd,
+                        (uint64_t)nwork * H * AT_TQ, (uint64_t)hd * 4, 32, (uint32_t)AT_TQ,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    return hd == 64 ? launch_hd_tc<64>(ctx, a, nwork, tk, tv, to, tp)
+                    : launch_hd_tc<128>(ctx, a, nwork, tk, tv, to, tp);
 }
 
 }  // namespace sulimo
