@@ -191,6 +191,77 @@ __global__ void __launch_bounds__(128)
         quantize_block_warp(sv[b * 32 + lane], ring + b * 34, lane);
 }
 
+// A prefill ubatch's q / k / v from the stacked GEMM: its fp32 split-K partials
+// [splits][n][qd + 2 kvd] summed in split order, then per token what qkv_rope_store_kernel does
+// (bias, RoPE of the q and k heads, q written as f32, k and v quantized into the ring at slot
+// pos % capacity).  One CTA per token: the row in shared memory, the angles of each rotary
+// frequency computed once and used by every head.
+__global__ void __launch_bounds__(256)
+    qkv_reduce_rope_store_kernel(const float* __restrict__ part, int splits, int n,
+                                 const float* __restrict__ bq, const float* __restrict__ bk,
+                                 const float* __restrict__ bv, int H, int Hkv, int hd,
+                                 int rope_dim, int mode, float base, size_t pos0,
+                                 float* __restrict__ q, uint8_t* __restrict__ k_ring,
+                                 uint8_t* __restrict__ v_ring, size_t capacity) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
+    extern __shared__ float qkv_row[];  // [qd + 2 kvd], then cos and sin [rope_dim / 2] each
+    const int qd = H * hd, kvd = Hkv * hd, mt = qd + 2 * kvd, half = rope_dim / 2;
+    const int t = blockIdx.x;
+    const size_t pos = pos0 + (size_t)t;
+    float* cs = qkv_row + mt;
+    float* sn = cs + half;
+    const size_t nm = (size_t)n * mt;
+    const float* src = part + (size_t)t * mt;
+    for (int j = threadIdx.x * 4; j < mt; j += blockDim.x * 4) {
+        float4 acc = __ldcg(reinterpret_cast<const float4*>(src + j));
+        for (int z = 1; z < splits; z++) {
+            const float4 p = __ldcg(reinterpret_cast<const float4*>(src + (size_t)z * nm + j));
+            acc.x += p.x;
+            acc.y += p.y;
+            acc.z += p.z;
+            acc.w += p.w;
+        }
+        // qd and kvd are multiples of 4: a group of four lies in one of q, k, v
+        const float* b = j < qd ? (bq ? bq + j : nullptr)
+                                : (j < qd + kvd ? (bk ? bk + (j - qd) : nullptr)
+                                                : (bv ? bv + (j - qd - kvd) : nullptr));
+        if (b) {
+            acc.x = __fadd_rn(acc.x, b[0]);
+            acc.y = __fadd_rn(acc.y, b[1]);
+            acc.z = __fadd_rn(acc.z, b[2]);
+            acc.w = __fadd_rn(acc.w, b[3]);
+        }
+        *reinterpret_cast<float4*>(qkv_row + j) = acc;
+    }
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float freq =
+            __fdiv_rn(1.0f, powf(base, __fdiv_rn((float)(2 * i), (float)rope_dim)));
+        const float theta = __fmul_rn((float)pos, freq);
+        cs[i] = cosf(theta);
+        sn[i] = sinf(theta);
+    }
+    __syncthreads();
+    // the q heads then the k heads lie back to back: head hh at hh * hd
+    for (int w = threadIdx.x; w < (H + Hkv) * half; w += blockDim.x) {
+        const int hh = w / half, i = w % half;
+        rope_pair(qkv_row + hh * hd, i, half, mode, cs[i], sn[i]);
+    }
+    __syncthreads();
+    float* qdst = q + (size_t)t * qd;
+    for (int j = threadIdx.x * 4; j < qd; j += blockDim.x * 4)
+        *reinterpret_cast<float4*>(qdst + j) = *reinterpret_cast<const float4*>(qkv_row + j);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kb = kvd / 32;  // Q8_0 blocks of one tensor per slot
+    const size_t slot = (pos % capacity) * (size_t)kb * 34;
+    for (int b = warp; b < 2 * kb; b += blockDim.x >> 5) {
+        const bool isv = b >= kb;
+        const int bb = isv ? b - kb : b;
+        quantize_block_warp(qkv_row[qd + (isv ? kvd : 0) + bb * 32 + lane],
+                            (isv ? v_ring : k_ring) + slot + (size_t)bb * 34, lane);
+    }
+}
+
 // silu(gate) * up -> f16 (the prefill down-projection GEMM's activations), 4 elements per
 // thread: 16-byte loads and an 8-byte store (n4 = n / 4; the buffers are 16-byte aligned).
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -453,6 +524,16 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
     auto gemm = [&](const void* sc, const void* qu, const void* x, float* out, int rows, int k) {
         return launch_gemm_q4_0_f16(ctx, sc, qu, x, out, rows, k, n, SULIMO_OUT_F32, k, 0);
     };
+    // q, k and v as one stacked GEMM (split-K partials summed by the RoPE / ring-store kernel)
+    // where the shapes allow; three GEMMs and qkv_rope_store_kernel otherwise
+    const size_t qkv_smem = (size_t)(qd + 2 * kvd + m->rope_dim) * sizeof(float);
+    bool stacked_qkv = qkv_smem <= 48 * 1024;
+    if (stacked_qkv) {
+        const GemmSeg probe[3] = {{m->layers[0].wq_scales, m->layers[0].wq_quants, qd},
+                                  {m->layers[0].wk_scales, m->layers[0].wk_quants, kvd},
+                                  {m->layers[0].wv_scales, m->layers[0].wv_quants, kvd}};
+        stacked_qkv = gemm_stacked_applies(probe, 3, E, n);
+    }
     const float* pending = nullptr;
     for (int l = 0; l < m->n_layers; l++) {
         const sulimo_layer_desc& L = m->layers[l];
@@ -461,17 +542,35 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
                          m->eps, no_q8, h16, (const float*)nullptr, 0);
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
-        if ((st = gemm(L.wq_scales, L.wq_quants, s.h, s.q, qd, E)) ||
-            (st = gemm(L.wk_scales, L.wk_quants, s.h, s.k, kvd, E)) ||
-            (st = gemm(L.wv_scales, L.wv_quants, s.h, s.v, kvd, E)))
-            return st;
-        (void)launch_pdl(qkv_rope_store_kernel, dim3(H + 2 * Hkv, n), dim3(128), 0, ctx->stream,
-                         s.q, (const float*)s.k, (const float*)s.v,
-                         reinterpret_cast<const float*>(L.bq), reinterpret_cast<const float*>(L.bk),
-                         reinterpret_cast<const float*>(L.bv), H, Hkv, hd, m->rope_dim,
-                         m->rope_mode, m->rope_base, start_pos, (size_t)1,
-                         reinterpret_cast<uint8_t*>(L.k_ring), reinterpret_cast<uint8_t*>(L.v_ring),
-                         m->kv_capacity, (size_t)0);
+        if (stacked_qkv) {
+            const GemmSeg qkv[3] = {{L.wq_scales, L.wq_quants, qd},
+                                    {L.wk_scales, L.wk_quants, kvd},
+                                    {L.wv_scales, L.wv_quants, kvd}};
+            const float* part = nullptr;
+            int splits = 0;
+            if ((st = launch_gemm_pair_stacked(ctx, qkv, 3, s.h, E, n, &part, &splits)))
+                return st;
+            (void)launch_pdl(qkv_reduce_rope_store_kernel, dim3(n), dim3(256), qkv_smem,
+                             ctx->stream, part, splits, n, reinterpret_cast<const float*>(L.bq),
+                             reinterpret_cast<const float*>(L.bk),
+                             reinterpret_cast<const float*>(L.bv), H, Hkv, hd, m->rope_dim,
+                             m->rope_mode, m->rope_base, start_pos, s.q,
+                             reinterpret_cast<uint8_t*>(L.k_ring),
+                             reinterpret_cast<uint8_t*>(L.v_ring), m->kv_capacity);
+        } else {
+            if ((st = gemm(L.wq_scales, L.wq_quants, s.h, s.q, qd, E)) ||
+                (st = gemm(L.wk_scales, L.wk_quants, s.h, s.k, kvd, E)) ||
+                (st = gemm(L.wv_scales, L.wv_quants, s.h, s.v, kvd, E)))
+                return st;
+            (void)launch_pdl(qkv_rope_store_kernel, dim3(H + 2 * Hkv, n), dim3(128), 0,
+                             ctx->stream, s.q, (const float*)s.k, (const float*)s.v,
+                             reinterpret_cast<const float*>(L.bq),
+                             reinterpret_cast<const float*>(L.bk),
+                             reinterpret_cast<const float*>(L.bv), H, Hkv, hd, m->rope_dim,
+                             m->rope_mode, m->rope_base, start_pos, (size_t)1,
+                             reinterpret_cast<uint8_t*>(L.k_ring),
+                             reinterpret_cast<uint8_t*>(L.v_ring), m->kv_capacity, (size_t)0);
+        }
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
         if ((st = launch_attn_prefill(ctx, s.q, L.k_ring, L.v_ring, start_pos, m->kv_capacity, n,

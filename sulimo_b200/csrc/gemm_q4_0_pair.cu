@@ -154,13 +154,18 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
 }
 
 // OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace [split][n][m].
+// The m weight rows may be up to three matrices stacked (segment g from row start[g], a
+// multiple of 128, so that every CTA's 128 rows lie in one matrix): nibbles through
+// tmap_q / tmap_q1 / tmap_q2, block scales from scales[g], rows[g] rows each.
 template <int OUT_MODE>
 __global__ void __launch_bounds__(P_THREADS, 1)
     gemm_q4_0_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                           const __grid_constant__ CUtensorMap tmap_q,
+                          const __grid_constant__ CUtensorMap tmap_q1,
+                          const __grid_constant__ CUtensorMap tmap_q2,
                           const __grid_constant__ CUtensorMap tmap_out,
                           const __grid_constant__ CUtensorMap tmap_out16,
-                          const uint16_t* __restrict__ scales, int m, int k, int n, int bn, int nb,
+                          const __grid_constant__ PairSegs sg, int m, int k, int n, int bn, int nb,
                           int iters_per_split, int stages, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     // the same offset in both CTAs: the leader's B descriptors address both SMs' stages
@@ -181,6 +186,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t crank = cluster_ctarank();
     const int m0 = (blockIdx.x >> 1) * (2 * PM) + (int)crank * PM;
+    const int seg = m0 >= sg.start[2] ? 2 : (m0 >= sg.start[1] ? 1 : 0);
+    const CUtensorMap* qmap = seg == 0 ? &tmap_q : (seg == 1 ? &tmap_q1 : &tmap_q2);
+    const int lm0 = m0 - sg.start[seg];  // the CTA's first row within its matrix
     const int n0 = blockIdx.y * bn;
     const int nx0 = n0 + (int)crank * (bn / 2);  // this CTA's activation rows
     const int num_k_total = (k + PK - 1) / PK;
@@ -199,7 +207,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmap_x);
-        prefetch_tensormap(&tmap_q);
+        prefetch_tensormap(qmap);
         prefetch_tensormap(&tmap_out);
         pdl_launch_dependents();
         // The weights are static (no kernel that writes them lets its dependents start early):
@@ -207,7 +215,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         // waits for the previous kernel; the activations follow the programmatic wait below.
         for (int j = 0; j < num_k && j < stages; j++) {
             mbar_arrive_expect_tx(&qfull[j], P_Q_STAGE);
-            tma_load_2d(sq + j * P_Q_STAGE, &tmap_q, (i_begin + j) * PK / 2, m0, &qfull[j]);
+            tma_load_2d(sq + j * P_Q_STAGE, qmap, (i_begin + j) * PK / 2, lm0, &qfull[j]);
         }
     }
     if (warp == 1) {
@@ -226,9 +234,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     const uint32_t quarter = (uint32_t)(warp & 3);
     const int group = (warp - 2) >> 2;
     const int r = (int)quarter * 32 + lane;  // feature row within the CTA == TMEM lane
-    const int grow = m0 + r;
-    const bool row_ok = grow < m;
-    const uint16_t* srow = scales + (size_t)(row_ok ? grow : 0) * nb;
+    const int lrow = lm0 + r;
+    const bool row_ok = lrow < sg.rows[seg] && m0 + r < m;
+    const uint16_t* srow = sg.scales[seg] + (size_t)(row_ok ? lrow : 0) * nb;
     const uint32_t lane_base = (quarter * 32u) << 16;
     const uint32_t afull_leader0 = mapa_shared(smem_u32(&afull[0]), 0);
     // block `group` of every stage: its scale for stage j (zero past the matrix or past k)
@@ -269,7 +277,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                 const uint32_t ph = (uint32_t)(j / stages) & 1u;
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
                 mbar_arrive_expect_tx(&qfull[s], P_Q_STAGE);
-                tma_load_2d(sq + s * P_Q_STAGE, &tmap_q, (i_begin + j) * PK / 2, m0, &qfull[s]);
+                tma_load_2d(sq + s * P_Q_STAGE, qmap, (i_begin + j) * PK / 2, lm0, &qfull[s]);
                 load_x(j, s);
                 issued = j + 1;
             }
@@ -501,28 +509,53 @@ PairPlan gemm_pair_plan(int m, int k, int n, int max_pairs) {
     return p;
 }
 
-int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
-                     void* out, int m, int k, int n, int out_dtype, int x_row_stride,
-                     int x_row_offset) {
+namespace {
+
+// Encodes the nibble map of one matrix (rows x nb*16 bytes, boxes of 128 rows x 64 bytes).
+int encode_nibbles(CUtensorMap* map, const void* quants, int rows, int nb) {
+    return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16,
+                     (uint64_t)(rows > 0 ? rows : 1), (uint64_t)nb * 16, 64, PM,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// The pair GEMM over `nseg` stacked matrices.  partials != null: fp32 split-K partials into the
+// workspace whatever the split count, left for the caller; otherwise `out` (f16 / f32), a
+// split plan reduced by splitk_reduce.
+int launch_pair_impl(sulimo_ctx* ctx, const GemmSeg* segs, int nseg, const void* x, void* out,
+                     int k, int n, int out_dtype, int x_row_stride, int x_row_offset,
+                     const float** partials, int* splits_out) {
     const int nb = k / 32;
     int st;
     if ((st = pair_setup<0>(ctx->device)) || (st = pair_setup<1>(ctx->device)) ||
         (st = pair_setup<2>(ctx->device)))
         return st;
+    PairSegs sg;
+    int m = 0;
+    for (int g = 0; g < 3; g++) {
+        const bool have = g < nseg;
+        sg.scales[g] = reinterpret_cast<const uint16_t*>(have ? segs[g].scales : segs[0].scales);
+        sg.start[g] = m;
+        sg.rows[g] = have ? segs[g].rows : 0;
+        m += sg.rows[g];
+    }
+    for (int g = nseg; g < 3; g++) sg.start[g] = m;
     const PairPlan p = gemm_pair_plan(m, k, n, max_active_pairs(ctx->device, ctx->num_sms));
     if (p.grid_y > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
     const uint8_t* xb =
         reinterpret_cast<const uint8_t*>(x) + (size_t)x_row_offset * x_row_stride * 2;
-    CUtensorMap tx, tq, to, to16;
+    CUtensorMap tx, tq[3], to, to16;
     st = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, (uint64_t)k, (uint64_t)n,
                    (uint64_t)x_row_stride * 2, 64, (uint32_t)(p.bn / 2),
                    CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    st = encode_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16, (uint64_t)m,
-                   (uint64_t)nb * 16, 64, PM, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st) return st;
-    const uint16_t* sc = reinterpret_cast<const uint16_t*>(scales);
-    if (p.splits == 1) {
+    for (int g = 0; g < 3; g++) {
+        if (g < nseg) {
+            if ((st = encode_nibbles(&tq[g], segs[g].quants, segs[g].rows, nb))) return st;
+        } else {
+            tq[g] = tq[0];
+        }
+    }
+    if (p.splits == 1 && !partials) {
         const bool f32 = out_dtype == SULIMO_OUT_F32;
         const CUtensorMapDataType dt =
             f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -534,12 +567,12 @@ int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, co
             return st;
         const dim3 grid(p.grid_x, p.grid_y, 1);
         const cudaError_t e =
-            f32 ? launch_pair(gemm_q4_0_pair_kernel<1>, grid, p.smem, ctx->stream, tx, tq, to,
-                              to16, sc, m, k, n, p.bn, nb, p.iters_per_split, p.stages,
-                              ctx->d_error)
-                : launch_pair(gemm_q4_0_pair_kernel<0>, grid, p.smem, ctx->stream, tx, tq, to,
-                              to16, sc, m, k, n, p.bn, nb, p.iters_per_split, p.stages,
-                              ctx->d_error);
+            f32 ? launch_pair(gemm_q4_0_pair_kernel<1>, grid, p.smem, ctx->stream, tx, tq[0],
+                              tq[1], tq[2], to, to16, sg, m, k, n, p.bn, nb, p.iters_per_split,
+                              p.stages, ctx->d_error)
+                : launch_pair(gemm_q4_0_pair_kernel<0>, grid, p.smem, ctx->stream, tx, tq[0],
+                              tq[1], tq[2], to, to16, sg, m, k, n, p.bn, nb, p.iters_per_split,
+                              p.stages, ctx->d_error);
         ctx->launches++;
         return check_cuda(e, "gemm_q4_0_pair launch");
     }
@@ -558,13 +591,44 @@ int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, co
             return st;
     }
     const dim3 grid(p.grid_x, p.grid_y, p.splits);
-    st = check_cuda(launch_pair(gemm_q4_0_pair_kernel<2>, grid, p.smem, ctx->stream, tx, tq, to,
-                                to16, sc, m, k, n, p.bn, nb, p.iters_per_split, p.stages,
-                                ctx->d_error),
+    st = check_cuda(launch_pair(gemm_q4_0_pair_kernel<2>, grid, p.smem, ctx->stream, tx, tq[0],
+                                tq[1], tq[2], to, to16, sg, m, k, n, p.bn, nb, p.iters_per_split,
+                                p.stages, ctx->d_error),
                     "gemm_q4_0_pair split-K launch");
     if (st) return st;
     ctx->launches++;
+    if (partials) {
+        *partials = ws;
+        *splits_out = p.splits;
+        return SULIMO_OK;
+    }
     return launch_splitk_reduce(ctx, ws, out, nm, p.splits, out_dtype == SULIMO_OUT_F32);
+}
+
+}  // namespace
+
+int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
+                     void* out, int m, int k, int n, int out_dtype, int x_row_stride,
+                     int x_row_offset) {
+    const GemmSeg seg{scales, quants, m};
+    return launch_pair_impl(ctx, &seg, 1, x, out, k, n, out_dtype, x_row_stride, x_row_offset,
+                            nullptr, nullptr);
+}
+
+bool gemm_stacked_applies(const GemmSeg* segs, int nseg, int k, int n) {
+    if (nseg < 1 || nseg > 3) return false;
+    int m = 0;
+    for (int g = 0; g < nseg; g++) {
+        if (segs[g].rows <= 0 || (g + 1 < nseg && segs[g].rows % PM)) return false;
+        m += segs[g].rows;
+    }
+    return gemm_uses_pair(m, k, n) && k % 32 == 0;
+}
+
+int launch_gemm_pair_stacked(sulimo_ctx* ctx, const GemmSeg* segs, int nseg, const void* x, int k,
+                             int n, const float** partials, int* splits) {
+    return launch_pair_impl(ctx, segs, nseg, x, nullptr, k, n, SULIMO_OUT_F32, k, 0, partials,
+                            splits);
 }
 
 }  // namespace sulimo

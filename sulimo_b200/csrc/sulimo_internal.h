@@ -85,6 +85,26 @@ struct PairPlan {
     uint32_t smem;
 };
 PairPlan gemm_pair_plan(int m, int k, int n, int max_pairs);
+// Weight matrices stacked along M for one pair GEMM: matrix g from row start[g] (a multiple of
+// 128), rows[g] rows, block scales scales[g].
+struct PairSegs {
+    const uint16_t* scales[3];
+    int start[3];
+    int rows[3];
+};
+// One matrix of a stacked GEMM: Q4_0 SoA weights of `rows` rows.
+struct GemmSeg {
+    const void* scales;
+    const void* quants;
+    int rows;
+};
+// Whether the pair GEMM takes these matrices stacked (every one but the last a multiple of 128
+// rows, the stack wide enough for the pair kernel).
+bool gemm_stacked_applies(const GemmSeg* segs, int nseg, int k, int n);
+// The pair GEMM of f16 activations x [n][k] against the stacked matrices, as fp32 split-K
+// partials [*splits][n][sum of rows] in ctx->workspace (*partials); the caller sums them.
+int launch_gemm_pair_stacked(sulimo_ctx* ctx, const GemmSeg* segs, int nseg, const void* x, int k,
+                             int n, const float** partials, int* splits);
 bool gemm_uses_pair(int m, int k, int n);
 int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                      void* out, int m, int k, int n, int out_dtype, int x_row_stride,
