@@ -113,6 +113,60 @@ __global__ void __launch_bounds__(NORM_THREADS)
     }
 }
 
+// A prefill ubatch's residual step after a split-K projection (o or down): x += the ordered
+// sum of the projection's fp32 partials (split z of token row t at part + z * split_stride +
+// t * E), then RMSNorm(x) * w as f16 — the split-K reduce and add_rmsnorm_q8_kernel<true> in
+// one pass.  One CTA per token, four consecutive values per thread (E a multiple of 4).
+__global__ void __launch_bounds__(256)
+    reduce_add_rmsnorm_f16_kernel(float* __restrict__ x, const float* __restrict__ part,
+                                  size_t split_stride, int splits, int E,
+                                  const float* __restrict__ w, float eps,
+                                  __half* __restrict__ y16) {
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();
+    extern __shared__ float sx[];  // E floats + 33 reduction slots
+    float* red = sx + E;
+    const int t = blockIdx.x;
+    float* xs = x + (size_t)t * E;
+    const float* ps = part + (size_t)t * E;
+    float ss = 0.0f;
+    for (int i = threadIdx.x * 4; i < E; i += blockDim.x * 4) {
+        float4 d = __ldcg(reinterpret_cast<const float4*>(ps + i));
+        for (int z = 1; z < splits; z++) {
+            const float4 p =
+                __ldcg(reinterpret_cast<const float4*>(ps + (size_t)z * split_stride + i));
+            d.x += p.x;
+            d.y += p.y;
+            d.z += p.z;
+            d.w += p.w;
+        }
+        float4 v = *reinterpret_cast<const float4*>(xs + i);
+        v.x = __fadd_rn(v.x, d.x);
+        v.y = __fadd_rn(v.y, d.y);
+        v.z = __fadd_rn(v.z, d.z);
+        v.w = __fadd_rn(v.w, d.w);
+        *reinterpret_cast<float4*>(xs + i) = v;
+        *reinterpret_cast<float4*>(sx + i) = v;
+        ss = __fmaf_rn(v.x, v.x, ss);
+        ss = __fmaf_rn(v.y, v.y, ss);
+        ss = __fmaf_rn(v.z, v.z, ss);
+        ss = __fmaf_rn(v.w, v.w, ss);
+    }
+    const float sum_sq = block_sum(ss, red);
+    const float mean = __fdiv_rn(sum_sq, (float)E);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    __half* ys = y16 + (size_t)t * E;
+    for (int i = threadIdx.x * 4; i < E; i += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(sx + i);
+        const __half2 lo = __floats2half2_rn(__fmul_rn(__fmul_rn(v.x, scale), w[i]),
+                                             __fmul_rn(__fmul_rn(v.y, scale), w[i + 1]));
+        const __half2 hi = __floats2half2_rn(__fmul_rn(__fmul_rn(v.z, scale), w[i + 2]),
+                                             __fmul_rn(__fmul_rn(v.w, scale), w[i + 3]));
+        *reinterpret_cast<uint2*>(ys + i) = make_uint2(*reinterpret_cast<const uint32_t*>(&lo),
+                                                       *reinterpret_cast<const uint32_t*>(&hi));
+    }
+}
+
 // x[i] *= s (Gemma 2's embedding scale sqrt(embd), forward_pass.rs:210-214)
 __global__ void __launch_bounds__(256) scale_kernel(float* __restrict__ x, size_t n, float s) {
     pdl_launch_dependents();
@@ -445,6 +499,11 @@ int ensure_norm_attr(sulimo_ctx* ctx) {
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              227 * 1024),
                         "rmsnorm smem attribute");
+    if (!st)
+        st = check_cuda(cudaFuncSetAttribute(reduce_add_rmsnorm_f16_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024),
+                        "rmsnorm smem attribute");
     if (!st) done.set(ctx->device);
     return st;
 }
@@ -534,14 +593,31 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
                                   {m->layers[0].wv_scales, m->layers[0].wv_quants, kvd}};
         stacked_qkv = gemm_stacked_applies(probe, 3, E, n);
     }
+    // the o and down projections as split-K partials summed by the residual + RMSNorm kernel
+    // that follows each, where the pair GEMM takes their shapes
+    const GemmSeg o_shape{nullptr, nullptr, E};
+    const bool fused_o = E % 4 == 0 && gemm_stacked_applies(&o_shape, 1, qd, n);
+    const bool fused_d = E % 4 == 0 && gemm_stacked_applies(&o_shape, 1, F, n);
+    // the residual update still to apply: a projection's dense output, or its partials
     const float* pending = nullptr;
+    const float* pend_part = nullptr;
+    int pend_splits = 0;
+    auto residual_norm = [&](float* x, const float* dense, const float* part, int splits,
+                             const void* w, int rows) -> int {
+        if (part)
+            (void)launch_pdl(reduce_add_rmsnorm_f16_kernel, dim3(rows), dim3(256), norm_smem,
+                             ctx->stream, x, part, (size_t)n * E, splits, E,
+                             reinterpret_cast<const float*>(w), m->eps, h16);
+        else
+            (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(rows), dim3(NORM_THREADS),
+                             norm_smem, ctx->stream, x, dense, reinterpret_cast<const float*>(w),
+                             E, m->eps, no_q8, h16, (const float*)nullptr, 0);
+        ctx->launches++;
+        return check_cuda(cudaGetLastError(), "residual norm launch");
+    };
     for (int l = 0; l < m->n_layers; l++) {
         const sulimo_layer_desc& L = m->layers[l];
-        (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
-                         ctx->stream, s.x, pending, reinterpret_cast<const float*>(L.attn_norm), E,
-                         m->eps, no_q8, h16, (const float*)nullptr, 0);
-        ctx->launches++;
-        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
+        if ((st = residual_norm(s.x, pending, pend_part, pend_splits, L.attn_norm, n))) return st;
         if (stacked_qkv) {
             const GemmSeg qkv[3] = {{L.wq_scales, L.wq_quants, qd},
                                     {L.wk_scales, L.wk_quants, kvd},
@@ -574,15 +650,19 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "qkv_rope_store launch"))) return st;
         if ((st = launch_attn_prefill(ctx, s.q, L.k_ring, L.v_ring, start_pos, m->kv_capacity, n,
-                                      H, Hkv, hd, s.h)) ||
-            (st = gemm(L.wo_scales, L.wo_quants, s.h, s.o, E, qd)))
+                                      H, Hkv, hd, s.h)))
             return st;
-        (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(n), dim3(NORM_THREADS), norm_smem,
-                         ctx->stream, s.x, (const float*)s.o,
-                         reinterpret_cast<const float*>(L.ffn_norm), E, m->eps, no_q8, h16,
-                         (const float*)nullptr, 0);
-        ctx->launches++;
-        if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
+        if (fused_o) {
+            const GemmSeg wo{L.wo_scales, L.wo_quants, E};
+            const float* part = nullptr;
+            int splits = 0;
+            if ((st = launch_gemm_pair_stacked(ctx, &wo, 1, s.h, qd, n, &part, &splits)) ||
+                (st = residual_norm(s.x, nullptr, part, splits, L.ffn_norm, n)))
+                return st;
+        } else if ((st = gemm(L.wo_scales, L.wo_quants, s.h, s.o, E, qd)) ||
+                   (st = residual_norm(s.x, s.o, nullptr, 0, L.ffn_norm, n))) {
+            return st;
+        }
         if ((st = gemm(L.wg_scales, L.wg_quants, s.h, s.g, F, E)) ||
             (st = gemm(L.wu_scales, L.wu_quants, s.h, s.u, F, E)))
             return st;
@@ -594,16 +674,22 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
                          nf4, reinterpret_cast<uint2*>(s.h));
         ctx->launches++;
         if ((st = check_cuda(cudaGetLastError(), "swiglu_f16 launch"))) return st;
-        if ((st = gemm(L.wd_scales, L.wd_quants, s.h, s.o, E, F))) return st;
-        pending = s.o;
+        if (fused_d) {
+            const GemmSeg wd{L.wd_scales, L.wd_quants, E};
+            if ((st = launch_gemm_pair_stacked(ctx, &wd, 1, s.h, F, n, &pend_part, &pend_splits)))
+                return st;
+            pending = nullptr;
+        } else {
+            if ((st = gemm(L.wd_scales, L.wd_quants, s.h, s.o, E, F))) return st;
+            pending = s.o;
+            pend_part = nullptr;
+        }
     }
     // the last token only: residual, final norm, vocab projection (fp32 logits)
     const size_t last = (size_t)(n - 1) * E;
-    (void)launch_pdl(add_rmsnorm_q8_kernel<true>, dim3(1), dim3(NORM_THREADS), norm_smem,
-                     ctx->stream, s.x + last, pending + last, m->out_norm, E, m->eps, no_q8,
-                     h16, (const float*)nullptr, 0);
-    ctx->launches++;
-    if ((st = check_cuda(cudaGetLastError(), "add_rmsnorm launch"))) return st;
+    if ((st = residual_norm(s.x + last, pending ? pending + last : nullptr,
+                            pend_part ? pend_part + last : nullptr, pend_splits, m->out_norm, 1)))
+        return st;
     return launch_gemm_q4_0_f16(ctx, m->out_scales, m->out_quants, s.h, logits, m->vocab, E, 1,
                                 SULIMO_OUT_F32, E, 0);
 }
