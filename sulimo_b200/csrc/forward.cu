@@ -113,6 +113,32 @@ __global__ void __launch_bounds__(NORM_THREADS)
     }
 }
 
+// The ordered sum p[0] + p[1] + ... of `splits` float4 partials `stride` floats apart, every
+// load of a batch of eight issued before the first add.
+__device__ __forceinline__ float4 sum_splits4(const float* p, size_t stride, int splits) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int z0 = 0; z0 < splits; z0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (z0 + j < splits)
+                v[j] = __ldcg(reinterpret_cast<const float4*>(p + (size_t)(z0 + j) * stride));
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (z0 + j >= splits) break;
+            if (z0 + j == 0) {
+                acc = v[j];
+            } else {
+                acc.x += v[j].x;
+                acc.y += v[j].y;
+                acc.z += v[j].z;
+                acc.w += v[j].w;
+            }
+        }
+    }
+    return acc;
+}
+
 // A prefill ubatch's residual step after a split-K projection (o or down): x += the ordered
 // sum of the projection's fp32 partials (split z of token row t at part + z * split_stride +
 // t * E), then RMSNorm(x) * w as f16 — the split-K reduce and add_rmsnorm_q8_kernel<true> in
@@ -131,15 +157,7 @@ __global__ void __launch_bounds__(256)
     const float* ps = part + (size_t)t * E;
     float ss = 0.0f;
     for (int i = threadIdx.x * 4; i < E; i += blockDim.x * 4) {
-        float4 d = __ldcg(reinterpret_cast<const float4*>(ps + i));
-        for (int z = 1; z < splits; z++) {
-            const float4 p =
-                __ldcg(reinterpret_cast<const float4*>(ps + (size_t)z * split_stride + i));
-            d.x += p.x;
-            d.y += p.y;
-            d.z += p.z;
-            d.w += p.w;
-        }
+        const float4 d = sum_splits4(ps + i, split_stride, splits);
         float4 v = *reinterpret_cast<const float4*>(xs + i);
         v.x = __fadd_rn(v.x, d.x);
         v.y = __fadd_rn(v.y, d.y);
@@ -268,14 +286,7 @@ __global__ void __launch_bounds__(256)
     const size_t nm = (size_t)n * mt;
     const float* src = part + (size_t)t * mt;
     for (int j = threadIdx.x * 4; j < mt; j += blockDim.x * 4) {
-        float4 acc = __ldcg(reinterpret_cast<const float4*>(src + j));
-        for (int z = 1; z < splits; z++) {
-            const float4 p = __ldcg(reinterpret_cast<const float4*>(src + (size_t)z * nm + j));
-            acc.x += p.x;
-            acc.y += p.y;
-            acc.z += p.z;
-            acc.w += p.w;
-        }
+        float4 acc = sum_splits4(src + j, nm, splits);
         // qd and kvd are multiples of 4: a group of four lies in one of q, k, v
         const float* b = j < qd ? (bq ? bq + j : nullptr)
                                 : (j < qd + kvd ? (bk ? bk + (j - qd) : nullptr)
@@ -598,6 +609,8 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
     const GemmSeg o_shape{nullptr, nullptr, E};
     const bool fused_o = E % 4 == 0 && gemm_stacked_applies(&o_shape, 1, qd, n);
     const bool fused_d = E % 4 == 0 && gemm_stacked_applies(&o_shape, 1, F, n);
+    // gate and up as one gated pair GEMM writing silu(gate) * up as f16 where it applies
+    const bool gated = gemm_gated_applies(F, E, n);
     // the residual update still to apply: a projection's dense output, or its partials
     const float* pending = nullptr;
     const float* pend_part = nullptr;
@@ -663,24 +676,35 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
                    (st = residual_norm(s.x, s.o, nullptr, 0, L.ffn_norm, n))) {
             return st;
         }
-        if ((st = gemm(L.wg_scales, L.wg_quants, s.h, s.g, F, E)) ||
-            (st = gemm(L.wu_scales, L.wu_quants, s.h, s.u, F, E)))
-            return st;
-        const size_t nf4 = (size_t)n * F / 4;  // F is a multiple of 32
-        (void)launch_pdl(swiglu_f16_kernel,
-                         dim3((unsigned)((nf4 + GLUE_THREADS - 1) / GLUE_THREADS)),
-                         dim3(GLUE_THREADS), 0, ctx->stream,
-                         reinterpret_cast<const float4*>(s.g), reinterpret_cast<const float4*>(s.u),
-                         nf4, reinterpret_cast<uint2*>(s.h));
-        ctx->launches++;
-        if ((st = check_cuda(cudaGetLastError(), "swiglu_f16 launch"))) return st;
+        if (gated) {
+            // f16 [n][F] into s.g: other CTAs may still be reading the activations in s.h
+            if ((st = launch_gemm_pair_gated(ctx, GemmSeg{L.wg_scales, L.wg_quants, F},
+                                             GemmSeg{L.wu_scales, L.wu_quants, F}, s.h, E, n,
+                                             s.g)))
+                return st;
+        } else {
+            if ((st = gemm(L.wg_scales, L.wg_quants, s.h, s.g, F, E)) ||
+                (st = gemm(L.wu_scales, L.wu_quants, s.h, s.u, F, E)))
+                return st;
+            const size_t nf4 = (size_t)n * F / 4;  // F is a multiple of 32
+            (void)launch_pdl(swiglu_f16_kernel,
+                             dim3((unsigned)((nf4 + GLUE_THREADS - 1) / GLUE_THREADS)),
+                             dim3(GLUE_THREADS), 0, ctx->stream,
+                             reinterpret_cast<const float4*>(s.g),
+                             reinterpret_cast<const float4*>(s.u), nf4,
+                             reinterpret_cast<uint2*>(s.h));
+            ctx->launches++;
+            if ((st = check_cuda(cudaGetLastError(), "swiglu_f16 launch"))) return st;
+        }
+        const void* ffn_act = gated ? static_cast<const void*>(s.g) : static_cast<const void*>(s.h);
         if (fused_d) {
             const GemmSeg wd{L.wd_scales, L.wd_quants, E};
-            if ((st = launch_gemm_pair_stacked(ctx, &wd, 1, s.h, F, n, &pend_part, &pend_splits)))
+            if ((st = launch_gemm_pair_stacked(ctx, &wd, 1, ffn_act, F, n, &pend_part,
+                                               &pend_splits)))
                 return st;
             pending = nullptr;
         } else {
-            if ((st = gemm(L.wd_scales, L.wd_quants, s.h, s.o, E, F))) return st;
+            if ((st = gemm(L.wd_scales, L.wd_quants, ffn_act, s.o, E, F))) return st;
             pending = s.o;
             pend_part = nullptr;
         }

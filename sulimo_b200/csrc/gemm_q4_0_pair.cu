@@ -55,7 +55,7 @@ constexpr uint32_t P_TMEM_COLS = 512;
 constexpr uint32_t P_STAGE_COLS = PK / 2;   // f16x2 TMEM columns of a stage's weights
 constexpr uint32_t P_Q_STAGE = PM * 64;     // raw nibbles per stage: 128 rows x 4 blocks x 16 B
 constexpr uint32_t P_BAR_BYTES = 512;
-static_assert((4 * P_MAX_STAGES + 1) * 8 + 8 <= P_BAR_BYTES, "barrier block");
+static_assert((4 * P_MAX_STAGES + 2) * 8 + 8 <= P_BAR_BYTES, "barrier block");
 
 // Shared memory per CTA: stages x (activation half: bn/2 rows x 256 bytes, nibbles), barriers,
 // 1024 bytes of alignment slack.
@@ -88,6 +88,64 @@ __device__ __forceinline__ void cluster_sync_relaxed() {
     asm volatile(
         "barrier.cluster.arrive.relaxed.aligned;\n\t"
         "barrier.cluster.wait.aligned;" ::: "memory");
+}
+
+// Gated epilogue (OUT_MODE 3): the token chunks of 32 that CTA 0 finishes are the first
+// ceil(chunks / 2), CTA 1 the rest; the other CTA's accumulators for them arrive, token-major
+// ([token][feature row], so that a warp's stores are contiguous), in an exchange buffer after
+// the f16 staging tiles of the whole token tile.
+__host__ __device__ constexpr int p_gate_split(int bn) { return (bn / 32 + 1) / 2; }
+__host__ __device__ constexpr uint32_t p_gate_xch_off(int bn) { return (uint32_t)bn * PM * 2u; }
+__host__ __device__ constexpr uint32_t p_gate_xch_bytes(int bn) {
+    return (uint32_t)p_gate_split(bn) * 32u * PM * 4u;
+}
+static_assert(p_gate_xch_off(256) + p_gate_xch_bytes(256) <=
+                  4u * (p_x_stage(256) + P_Q_STAGE), "gated exchange fits (256)");
+
+// Arrival on the other CTA's mbarrier, releasing this thread's prior writes (its DSMEM stores
+// included) at cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote_release(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                     cluster_addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (for arrivals that publish DSMEM stores).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity,
+                                                          int* err, volatile int* abort_flag) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if ((++spins & 63u) == 0) {
+            if (abort_flag && *abort_flag) return false;
+            if (globaltimer_ns() - t0 > SULIMO_WAIT_LIMIT_NS) {
+                record_device_error(err, SULIMO_DEVERR_WAIT_TIMEOUT);
+                if (abort_flag) *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ float silu_times(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
 // Shared-memory address of the same variable in CTA `rank` of the cluster.
@@ -153,8 +211,10 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
         : "memory");
 }
 
-// OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace [split][n][m].
-// The m weight rows may be up to three matrices stacked (segment g from row start[g], a
+// OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace [split][n][m],
+// 3 = gated: CTA 0 of a pair computes 128 rows of matrix 0 (gate), CTA 1 the same rows of
+// matrix 1 (up), and the pair writes silu(gate) * up as f16 [n][m] (m = rows per matrix).
+// Otherwise the m weight rows may be up to three matrices stacked (segment g from row start[g], a
 // multiple of 128, so that every CTA's 128 rows lie in one matrix): nibbles through
 // tmap_q / tmap_q1 / tmap_q2, block scales from scales[g], rows[g] rows each.
 template <int OUT_MODE>
@@ -180,15 +240,18 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     uint64_t* empty = xfull + P_MAX_STAGES;
     uint64_t* afull = empty + P_MAX_STAGES;
     uint64_t* done = afull + P_MAX_STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* xchg = done + 1;  // gated epilogue: the other CTA's accumulators have arrived
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t crank = cluster_ctarank();
-    const int m0 = (blockIdx.x >> 1) * (2 * PM) + (int)crank * PM;
-    const int seg = m0 >= sg.start[2] ? 2 : (m0 >= sg.start[1] ? 1 : 0);
+    const int m0 = OUT_MODE == 3 ? (blockIdx.x >> 1) * PM
+                                 : (blockIdx.x >> 1) * (2 * PM) + (int)crank * PM;
+    const int seg = OUT_MODE == 3 ? (int)crank
+                                  : (m0 >= sg.start[2] ? 2 : (m0 >= sg.start[1] ? 1 : 0));
     const CUtensorMap* qmap = seg == 0 ? &tmap_q : (seg == 1 ? &tmap_q1 : &tmap_q2);
-    const int lm0 = m0 - sg.start[seg];  // the CTA's first row within its matrix
+    const int lm0 = OUT_MODE == 3 ? m0 : m0 - sg.start[seg];  // first row within its matrix
     const int n0 = blockIdx.y * bn;
     const int nx0 = n0 + (int)crank * (bn / 2);  // this CTA's activation rows
     const int num_k_total = (k + PK - 1) / PK;
@@ -204,6 +267,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             mbar_init(&afull[s], 2 * P_DEQ_WARPS);  // every dequant warp of both CTAs
         }
         mbar_init(done, 1);
+        mbar_init(xchg, P_DEQ_WARPS);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmap_x);
@@ -367,10 +431,58 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         }
 #pragma unroll
         for (int ci = 0; ci < CH; ci++) tmem_ld_wait_carry(v[ci]);
+        if (OUT_MODE == 3) {
+            // send the other CTA the accumulators of the chunks it finishes, then finish ours
+            const int hsplit = p_gate_split(bn);
+            uint8_t* xch = sx + p_gate_xch_off(bn);  // [owner's token][feature row] fp32
+            const uint32_t xch_peer = mapa_shared(smem_u32(xch), crank ^ 1u);
+#pragma unroll
+            for (int ci = 0; ci < CH; ci++) {
+                const int c0 = (group + ci * P_DEQ_GROUPS) * P_EPI_TOKENS;
+                const uint32_t owner = c0 / P_EPI_TOKENS < hsplit ? 0u : 1u;
+                if (c0 >= bn || owner == crank || !have) continue;
+                const int base = owner == 0 ? 0 : hsplit * P_EPI_TOKENS;
+#pragma unroll
+                for (int jj = 0; jj < 32; jj++)
+                    st_cluster_f32(xch_peer + (uint32_t)(((c0 + jj - base) * PM + r) * 4),
+                                   __uint_as_float(v[ci][jj]));
+            }
+            asm volatile("fence.acq_rel.cluster;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote_release(mapa_shared(smem_u32(xchg), crank ^ 1u));
+            const bool got = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(xchg, 0, err,
+                                                                                abort_flag));
+#pragma unroll
+            for (int ci = 0; ci < CH; ci++) {
+                const int c0 = (group + ci * P_DEQ_GROUPS) * P_EPI_TOKENS;
+                const uint32_t owner = c0 / P_EPI_TOKENS < hsplit ? 0u : 1u;
+                if (c0 >= bn || owner != crank) continue;
+                const int base = owner == 0 ? 0 : hsplit * P_EPI_TOKENS;
+                uint8_t* tile = sx + (size_t)c0 * PM * 2;
+                if (have && got) {
+                    const float* other = reinterpret_cast<const float*>(xch);
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) {
+                        const float mine = __uint_as_float(v[ci][jj]);
+                        const float peer = other[(c0 + jj - base) * PM + r];
+                        const float y = crank == 0 ? silu_times(mine, peer) : silu_times(peer, mine);
+                        *reinterpret_cast<__half*>(tile + (size_t)(jj * PM + r) * 2) =
+                            __float2half_rn(y);
+                    }
+                    fence_proxy_async_smem();
+                }
+                named_barrier_sync(1 + group, 128);
+                if (issuer && have && got && !*abort_flag && n0 + c0 < n && m0 < m) {
+                    const bool whole = c0 + P_EPI_TOKENS <= bn;
+                    tma_store_2d(whole ? &tmap_out : &tmap_out16, m0, n0 + c0, tile);
+                    bulk_commit();
+                }
+            }
+        }
 #pragma unroll
         for (int ci = 0; ci < CH; ci++) {
             const int c0 = (group + ci * P_DEQ_GROUPS) * P_EPI_TOKENS;
-            if (c0 >= bn) break;
+            if (OUT_MODE == 3 || c0 >= bn) break;
             uint8_t* tile = sx + (size_t)c0 * PM * ES;
             if (have) {
                 uint8_t* col = tile + (size_t)r * ES;
@@ -613,6 +725,49 @@ int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, co
     const GemmSeg seg{scales, quants, m};
     return launch_pair_impl(ctx, &seg, 1, x, out, k, n, out_dtype, x_row_stride, x_row_offset,
                             nullptr, nullptr);
+}
+
+bool gemm_gated_applies(int rows, int k, int n) {
+    if (!gemm_uses_pair(2 * rows, k, n) || k % 32) return false;
+    const PairPlan p = gemm_pair_plan(2 * rows, k, n, 74);
+    return p_gate_xch_off(p.bn) + p_gate_xch_bytes(p.bn) <=
+           (uint32_t)p.stages * (p_x_stage(p.bn) + P_Q_STAGE);
+}
+
+int launch_gemm_pair_gated(sulimo_ctx* ctx, const GemmSeg& gate, const GemmSeg& up,
+                           const void* x, int k, int n, void* out) {
+    const int rows = gate.rows, nb = k / 32;
+    int st = pair_setup<3>(ctx->device);
+    if (st) return st;
+    PairPlan p = gemm_pair_plan(2 * rows, k, n, max_active_pairs(ctx->device, ctx->num_sms));
+    if (p.grid_y > 65535) return set_error(SULIMO_EINVAL, "too many token tiles");
+    p.splits = 1;  // silu is not linear: no split-K
+    p.iters_per_split = (k + PK - 1) / PK;
+    PairSegs sg;
+    sg.scales[0] = reinterpret_cast<const uint16_t*>(gate.scales);
+    sg.scales[1] = reinterpret_cast<const uint16_t*>(up.scales);
+    sg.scales[2] = sg.scales[0];
+    for (int g = 0; g < 3; g++) {
+        sg.start[g] = 0;
+        sg.rows[g] = rows;
+    }
+    CUtensorMap tx, tg, tu, to, to16;
+    if ((st = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, (uint64_t)k, (uint64_t)n,
+                        (uint64_t)k * 2, 64, (uint32_t)(p.bn / 2), CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (st = encode_nibbles(&tg, gate.quants, rows, nb)) ||
+        (st = encode_nibbles(&tu, up.quants, rows, nb)) ||
+        (st = encode_2d(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out, (uint64_t)rows, (uint64_t)n,
+                        (uint64_t)rows * 2, PM, (uint32_t)P_EPI_TOKENS,
+                        CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+        (st = encode_2d(&to16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out, (uint64_t)rows, (uint64_t)n,
+                        (uint64_t)rows * 2, PM, 16u, CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return st;
+    const dim3 grid(2 * ((rows + PM - 1) / PM), p.grid_y, 1);
+    const cudaError_t e = launch_pair(gemm_q4_0_pair_kernel<3>, grid, p.smem, ctx->stream, tx, tg,
+                                      tu, tg, to, to16, sg, rows, k, n, p.bn, nb,
+                                      p.iters_per_split, p.stages, ctx->d_error);
+    ctx->launches++;
+    return check_cuda(e, "gemm_q4_0_pair gated launch");
 }
 
 bool gemm_stacked_applies(const GemmSeg* segs, int nseg, int k, int n) {

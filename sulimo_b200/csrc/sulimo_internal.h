@@ -105,6 +105,12 @@ bool gemm_stacked_applies(const GemmSeg* segs, int nseg, int k, int n);
 // partials [*splits][n][sum of rows] in ctx->workspace (*partials); the caller sums them.
 int launch_gemm_pair_stacked(sulimo_ctx* ctx, const GemmSeg* segs, int nseg, const void* x, int k,
                              int n, const float** partials, int* splits);
+// Whether the gated pair GEMM takes rows x k weights and n tokens.
+bool gemm_gated_applies(int rows, int k, int n);
+// silu(x W_gate^T) * (x W_up^T) as f16 out [n][rows] in one pair GEMM (no split-K): CTA 0 of a
+// pair computes the gate rows, CTA 1 the same up rows, and they exchange halves of the tile.
+int launch_gemm_pair_gated(sulimo_ctx* ctx, const GemmSeg& gate, const GemmSeg& up,
+                           const void* x, int k, int n, void* out);
 bool gemm_uses_pair(int m, int k, int n);
 int launch_gemm_pair(sulimo_ctx* ctx, const void* scales, const void* quants, const void* x,
                      void* out, int m, int k, int n, int out_dtype, int x_row_stride,
