@@ -558,13 +558,17 @@ size_t prefill_scratch_bytes(const sulimo_model_desc* m, int n) {
 }
 
 // One prefill ubatch of n tokens at positions start_pos .. start_pos+n-1 of one sequence
-// (execute_prefill_ubatch, crates/sulimo-ocl/src/prefill.rs:337-566): per layer RMSNorm -> f16,
-// q/k/v GEMMs (fp32 out), biases + RoPE + K/V ring store for every token, causal prefill
-// attention (f16 out), o GEMM, residual + RMSNorm, gate/up GEMMs, SwiGLU (f16), down GEMM,
-// residual; then the last token's final norm and the vocab projection (enqueue_logits_final,
-// prefill.rs:300-330) into logits[vocab].  The reference's GPU ubatch skips the QKV biases and
-// keeps activations in f16; this one adds the biases (as forward_token does) and keeps the
-// residual stream in fp32.
+// (execute_prefill_ubatch, crates/sulimo-ocl/src/prefill.rs:337-566): per layer residual +
+// RMSNorm -> f16, q/k/v projections, biases + RoPE + K/V ring store for every token, causal
+// prefill attention (f16 out), o projection, residual + RMSNorm, gate/up projections with
+// SwiGLU (f16), down projection; then the last token's residual, final norm and the vocab
+// projection (enqueue_logits_final, prefill.rs:300-330) into logits[vocab].  Where the CTA-pair
+// GEMM takes the shapes, q/k/v are one stacked GEMM whose split-K partials the RoPE / ring-store
+// kernel sums, the o and down partials are summed by the residual + RMSNorm kernel that follows
+// them, and gate/up run as one gated GEMM that writes silu(gate)*up; otherwise each projection
+// is its own GEMM with its own reduce.  The reference's GPU ubatch skips the QKV biases and keeps
+// activations in f16; this one adds the biases (as forward_token does) and keeps the residual
+// stream in fp32.
 int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int32_t* tokens,
                           const void* x_f16, int n, size_t start_pos, float* logits,
                           void* scratch) {
