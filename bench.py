@@ -795,6 +795,9 @@ def run_probe(args, local):
                             --probe-batch sequences (the tensor-core form from 2);
       attn                  decode attention, Llama-3.2-3B geometry (24 / 8 heads, hd 128),
                             context 4096, batch 1, random Q8_0 rings;
+      attn_prefill          prefill attention, Qwen2.5-1.5B geometry (12 / 2 heads, hd 128),
+                            a 512-token ubatch at positions 1536..2047 (--probe-start to move
+                            it), random Q8_0 rings of 4096 slots;
       decode_step           one config-4 forward_token at context 4096 for --probe-batch
                             sequences."""
     import numpy as np
@@ -856,6 +859,21 @@ def run_probe(args, local):
 
         def launch(s):
             sb.causal_gqa_decode(ctx, s[0], s[1], s[2], cap, cap, H, Hkv, hd, s[3])
+    elif kern == "attn_prefill":
+        H, Hkv, hd, cap, n = 12, 2, 128, 4096, 512
+        start = args.probe_start
+        for _ in range(4):
+            ring = lambda: torch.randint(-127, 128, (cap * Hkv * hd // 32, 34), device="cuda",  # noqa: E731
+                                         dtype=torch.int32, generator=g).to(torch.int8)
+            kr, vr = ring(), ring()
+            for r in (kr, vr):
+                r[:, 0:2] = torch.tensor([0.02], dtype=torch.float16).view(torch.int8).cuda()
+            sets.append((torch.randn(n * H * hd, device="cuda", generator=g), kr, vr,
+                         torch.empty(n * H * hd, device="cuda", dtype=torch.float16)))
+
+        def launch(s):
+            sb.causal_gqa_attention_prefill(ctx, s[0], s[1], s[2], start, cap, n, H, Hkv, hd,
+                                            s[3])
     elif kern == "decode_step":
         from sulimo_b200.model import DecodeModel
         from sulimo_b200.synthetic import LLAMA_3B, make_model_torch
@@ -903,7 +921,9 @@ def main():
                     help="sequences per launch for --mode probe (gemv_batched: 8 if 1)")
     ap.add_argument("--kernel", default="attn",
                     help="--mode probe: gemm_up, gemm_down, gemv_fast, gemv_exact, "
-                         "gemv_batched, attn, decode_step")
+                         "gemv_batched, attn, attn_prefill, decode_step")
+    ap.add_argument("--probe-start", type=int, default=1536,
+                    help="--mode probe --kernel attn_prefill: the ubatch's first position")
     ap.add_argument("--mode", default="headline",
                     choices=["headline", "sharded", "decode", "generate", "probe", "secondary"],
                     help="headline: the contract line (config 2); sharded: the row-sharded "

@@ -7,23 +7,24 @@
 // head h / (H / Hkv).
 //
 // One CTA per (128 query tokens, query head), flash-attention form with the accumulators in TMEM:
-//   warp 9, one thread (producer): per chunk of 64 keys, one TMA tensor copy each of the K and
+//   warp 13, one thread (producer): per chunk of 64 keys, one TMA tensor copy each of the K and
 //     V ring rows of the kv head (a box of 64 slots starting at the 16-byte boundary at or below
 //     the head's first byte), two chunks in flight;
-//   warps 4-7 (converters): the CTA's queries once, as f16, into a 128-byte-swizzled K-major
-//     tile; then per chunk one thread per (tensor, key): the key's staged ring row read with
+//   warps 8-11 (converters): per chunk one thread per (tensor, key): the key's staged ring row read with
 //     16-byte loads, each Q8_0 block dequantized to f16(d * q) by byte permutes and exact half
 //     arithmetic, written as [key][dim] into a 128-byte-swizzled tile — K-major B for S = Q K^T,
 //     MN-major B for O += P V (keys past the CTA's range: 0);
-//   warp 8, one thread (MMA): S = Q K^T (tcgen05.mma kind::f16, A and B from shared memory,
+//   warp 12, one thread (MMA): S = Q K^T (tcgen05.mma kind::f16, A and B from shared memory,
 //     M = 128, N = 64, fp32 in TMEM, two S buffers so S of the next chunk overlaps the softmax
 //     of this one), then O += P V (A = P from TMEM, B = V from shared memory read MN-major,
 //     N = hd, O in TMEM for the whole key range);
-//   warps 0-3 (softmax, thread = query row = TMEM lane): tcgen05.ld of the row's 64 scores,
-//     scale by 1/sqrt(hd), causal mask, online softmax in fp32 with a lazily raised running
-//     maximum (O and l are rescaled only when the row maximum grows by more than 8 in log2
-//     units, so P <= 256 stays well inside f16), P as f16 into TMEM with tcgen05.st; at the end
-//     O / l as f16 to the output row.
+//   warps 0-7 (softmax): the CTA's queries once, as f16, into a 128-byte-swizzled K-major tile;
+//     then thread = (query row = TMEM lane, half of the chunk): tcgen05.ld of the row's 32
+//     scores, causal mask, the row maximum shared with the other half's warp through shared
+//     memory, online softmax in fp32 with a lazily raised running maximum (O and l are rescaled
+//     only when the row maximum grows by more than 8 in log2 units, so P <= 256 stays well
+//     inside f16), P as f16 into TMEM with tcgen05.st; each half keeps its own row sum and
+//     rescales its half of O; at the end O / l (the halves' sums added) to the output row.
 // The reference keeps q, the dequantized K/V and the accumulated output in f16 (prefill.cl
 // works on half); here K and V enter the tensor cores as f16(d * q) (one rounding), P as f16,
 // and every sum is fp32.  Every mbarrier wait is bounded by %globaltimer (device error, abort,
@@ -41,7 +42,7 @@ namespace {
 
 constexpr int AT_TQ = 128;       // query tokens per CTA = MMA M = TMEM lanes
 constexpr int AT_CK = 64;        // keys per chunk = S's N
-constexpr int AT_THREADS = 320;  // softmax 0-3, converters 4-7, MMA 8, producer 9
+constexpr int AT_THREADS = 448;  // softmax 0-7, converters 8-11, MMA 12, producer 13
 constexpr uint32_t AT_TMEM_COLS = 512;
 constexpr uint32_t AT_S_COL = 0;     // S buffers: [0, 64), [64, 128)
 constexpr uint32_t AT_P_COL = 128;   // P buffers: [128, 160), [160, 192) (f16 pairs)
@@ -63,7 +64,8 @@ struct AtGeom {
     static constexpr uint32_t OFF_V = OFF_K + AT_KV_ST * K_BYTES;
     static constexpr uint32_t OFF_RAW = OFF_V + AT_KV_ST * V_BYTES;
     static constexpr uint32_t OFF_BAR = OFF_RAW + 4 * RAW_BYTES;
-    static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;  // + barriers + alignment slack
+    static constexpr uint32_t OFF_RED = OFF_BAR + 256;  // softmax pairs: row maxima, row sums
+    static constexpr uint32_t SMEM = OFF_RED + 3 * 2 * AT_TQ * 4 + 1024;  // + alignment slack
 };
 static_assert(AtGeom<128>::SMEM <= 232448, "prefill attention smem (hd 128)");
 
@@ -269,6 +271,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint64_t* drained = bars + 17;  // MMA: everything it issued has completed
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(smem + G::OFF_RED);  // [3][2][128]: max (2 slots), l
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AtWork wk = at_work(a, blockIdx.x);
@@ -282,12 +285,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     const int lead = kvh * G::HB - x0;   // the head's first byte inside a staged row
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 4);
+        mbar_init(q_full, 8);
         for (int s = 0; s < 2; s++) {
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_free[s], 4);
             mbar_init(&s_full[s], 1);
-            mbar_init(&p_full[s], 4);
+            mbar_init(&p_full[s], 8);
             mbar_init(&pv_done[s], 1);
         }
         for (int s = 0; s < AT_KV_ST; s++) {
@@ -301,7 +304,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         prefetch_tensormap(&tmap_v);
         prefetch_tensormap(wk.splits > 1 ? &tmap_p : &tmap_o);
     }
-    if (warp == 8) {
+    if (warp == 12) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
                      "r"(AT_TMEM_COLS)
@@ -315,17 +318,17 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {
+    if (warp < 8) {
         // the queries (softmax warps, while the converters start on the first chunk), f16 into
         // the swizzled K-major tile: batches of QB items per thread, all of a batch's loads
         // issued before any is converted
-        constexpr int QITEMS = AT_TQ * (HD / 8) / 128, QB = 8;
+        constexpr int QITEMS = AT_TQ * (HD / 8) / 256, QB = QITEMS < 8 ? QITEMS : 8;
 #pragma unroll
         for (int i0 = 0; i0 < QITEMS; i0 += QB) {
             float4 xv[QB][2];
 #pragma unroll
             for (int i = 0; i < QB; i++) {
-                const int it = threadIdx.x + (i0 + i) * 128;
+                const int it = threadIdx.x + (i0 + i) * 256;
                 const int row = it / (HD / 8), kc = it % (HD / 8);
                 const int t = t0 + row;
                 if (t < a.n) {
@@ -339,7 +342,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
 #pragma unroll
             for (int i = 0; i < QB; i++) {
-                const int it = threadIdx.x + (i0 + i) * 128;
+                const int it = threadIdx.x + (i0 + i) * 256;
                 const int row = it / (HD / 8), kc = it % (HD / 8);
                 const float4 x0f = xv[i][0], x1f = xv[i][1];
                 *reinterpret_cast<uint4*>(sQ + sw128_off(row, kc, AT_TQ)) =
@@ -352,7 +355,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         if (lane == 0) mbar_arrive(q_full);
     }
 
-    if (warp == 9) {
+    if (warp == 13) {
         // ------------------------------ producer ------------------------------
         if (lane == 0) {
             const uint32_t bytes = 2u * AT_CK * (uint32_t)a.boxw;
@@ -367,9 +370,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                             &raw_full[s]);
             }
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 8 && warp < 12) {
         // ------------------------------ converters ------------------------------
-        const int ct = threadIdx.x - 128;
+        const int ct = threadIdx.x - 256;
         for (int i = 0; i < nloc; i++) {
             const int s = i & 1, c = cb + i;
             if (!__all_sync(FULL, mbar_wait_bounded(&raw_full[s], (i >> 1) & 1, a.err,
@@ -393,7 +396,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 mbar_arrive(&raw_free[s]);
             }
         }
-    } else if (warp == 8) {
+    } else if (warp == 12) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
             // kind::f16, D f32, A = B = f16; N >> 3 at bit 17, M >> 4 at bit 24
@@ -440,58 +443,68 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             mbar_wait_bounded(drained, 0, a.err, nullptr);
         }
     } else {
-        // ------------------------------ softmax (warps 0-3) ------------------------------
-        const int row = warp * 32 + lane;  // TMEM lane
+        // ------------------------------ softmax (warps 0-7) ------------------------------
+        // warp w: TMEM lanes 32 (w % 4) .. (rows), half w / 4 of every chunk's 64 keys and of O's
+        // columns; the two warps of a row quarter share each chunk's row maximum through `red`
+        // behind a 64-thread named barrier.  Neither leaves the loop early (a missing partner
+        // would hold the other at the barrier): after a failed wait a warp only keeps meeting
+        // the barriers.
+        const int rq = warp & 3, hf = warp >> 2;
+        const int row = rq * 32 + lane;  // TMEM lane
         const int t = t0 + row;
         const long pos = (long)a.start_pos + t;
-        const uint32_t lane_base = ((uint32_t)(warp * 32)) << 16;
+        const uint32_t lane_base = ((uint32_t)(rq * 32)) << 16;
         const long pos_first = (long)a.start_pos + t0;  // the tile's first query position
         const float sc = a.scale_log2;
+        float* red_max = red;              // [2 chunk slots][2 halves][128 rows]
+        float* red_l = red + 4 * AT_TQ;    // [2 halves][128 rows]
         // running maximum in log2 units (-inf while no key of the CTA's range is visible to
-        // the row: possible in a split other than the tile's first), row sum
+        // the row: possible in a split other than the tile's first), this half's row sum
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int i = 0; i < nloc; i++) {
             const int s = i & 1;
-            if (!__all_sync(FULL, mbar_wait_bounded(&s_full[s], (i >> 1) & 1, a.err, abort_flag))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t v[2][32];
-            tmem_ld32_issue(tmem + lane_base + AT_S_COL + (uint32_t)s * 64u, v[0]);
-            tmem_ld32_issue(tmem + lane_base + AT_S_COL + (uint32_t)s * 64u + 32u, v[1]);
-            tmem_ld_wait_carry(v[0]);
-            tmem_ld_wait_carry(v[1]);
-            const long k0 = (long)(cb + i) * AT_CK;
-            if (k0 + AT_CK - 1 > pos_first) {  // the chunk reaches past some row's position
+            ok = ok && __all_sync(FULL, mbar_wait_bounded(&s_full[s], (i >> 1) & 1, a.err,
+                                                          abort_flag));
+            uint32_t v[32];
+            float mxh = -INFINITY;
+            if (ok) {
+                tc_fence_after();
+                tmem_ld32(tmem + lane_base + AT_S_COL + (uint32_t)s * 64u + (uint32_t)hf * 32u, v);
+                const long k0 = (long)(cb + i) * AT_CK + hf * 32;
+                if (k0 + 31 > pos_first) {  // the half reaches past some row's position
 #pragma unroll
-                for (int j = 0; j < AT_CK; j++)
-                    if (k0 + j > pos) v[j >> 5][j & 31] = __float_as_uint(-INFINITY);
-            }
-            // row maximum of the raw scores (the scale is positive): eight independent chains
-            float mx8[8];
+                    for (int j = 0; j < 32; j++)
+                        if (k0 + j > pos) v[j] = __float_as_uint(-INFINITY);
+                }
+                // the half's maximum of the raw scores (the scale is positive)
+                float mx4[4];
 #pragma unroll
-            for (int q8 = 0; q8 < 8; q8++) {
-                const uint32_t* u = &v[q8 >> 2][(q8 & 3) * 8];
-                mx8[q8] = fmax3(fmax3(__uint_as_float(u[0]), __uint_as_float(u[1]),
-                                      __uint_as_float(u[2])),
-                                fmax3(__uint_as_float(u[3]), __uint_as_float(u[4]),
-                                      __uint_as_float(u[5])),
-                                fmaxf(__uint_as_float(u[6]), __uint_as_float(u[7])));
+                for (int q8 = 0; q8 < 4; q8++) {
+                    const uint32_t* u = &v[q8 * 8];
+                    mx4[q8] = fmax3(fmax3(__uint_as_float(u[0]), __uint_as_float(u[1]),
+                                          __uint_as_float(u[2])),
+                                    fmax3(__uint_as_float(u[3]), __uint_as_float(u[4]),
+                                          __uint_as_float(u[5])),
+                                    fmaxf(__uint_as_float(u[6]), __uint_as_float(u[7])));
+                }
+                mxh = fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
             }
-            const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
-                                   fmaxf(mx8[6], mx8[7]));
+            // slot i % 2: the partner read slot i % 2 of chunk i - 2 before the barrier of i - 1
+            red_max[((i & 1) * 2 + hf) * AT_TQ + row] = mxh;
+            named_barrier_sync(2 + rq, 64);
+            const float mx = fmaxf(mxh, red_max[((i & 1) * 2 + (hf ^ 1)) * AT_TQ + row]);
+            if (!ok) continue;
             const float m_new = fmaxf(m_used, mx * sc);
             if (i == 0) {
                 m_used = m_new;
             } else if (__any_sync(FULL, m_new > m_used + AT_RESCALE)) {
-                // O holds P V up to the previous chunk: wait for it before scaling
+                // O holds P V up to the previous chunk: wait for it before scaling this half
                 if (!__all_sync(FULL, mbar_wait_bounded(&pv_done[(i - 1) & 1],
                                                         (uint32_t)((i - 1) >> 1) & 1u, a.err,
                                                         abort_flag))) {
                     ok = false;
-                    break;
+                    continue;
                 }
                 tc_fence_after();
                 const bool mine = m_new > m_used + AT_RESCALE;
@@ -501,7 +514,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     m_used = m_new;
                 }
 #pragma unroll
-                for (int c0 = 0; c0 < HD; c0 += 32) {
+                for (int c0 = hf * (HD / 2); c0 < (hf + 1) * (HD / 2); c0 += 32) {
                     uint32_t o[32];
                     tmem_ld32(tmem + lane_base + AT_O_COL + (uint32_t)c0, o);
 #pragma unroll
@@ -515,39 +528,42 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                                                               (uint32_t)((i >> 1) - 1) & 1u,
                                                               a.err, abort_flag))) {
                 ok = false;
-                break;
+                continue;
             }
             tc_fence_after();
-            uint32_t pw[32];
+            uint32_t pw[16];
             float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             const float nm = m_used == -INFINITY ? 0.0f : -m_used;
 #pragma unroll
-            for (int j = 0; j < AT_CK; j += 2) {
-                const float p0 = ex2_approx(fmaf(__uint_as_float(v[j >> 5][j & 31]), sc, nm));
-                const float p1 =
-                    ex2_approx(fmaf(__uint_as_float(v[(j + 1) >> 5][(j + 1) & 31]), sc, nm));
+            for (int j = 0; j < 32; j += 2) {
+                const float p0 = ex2_approx(fmaf(__uint_as_float(v[j]), sc, nm));
+                const float p1 = ex2_approx(fmaf(__uint_as_float(v[j + 1]), sc, nm));
                 ps[(j >> 1) & 3] += p0 + p1;
                 pw[j >> 1] = h2(p0, p1);
             }
             l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-            tmem_st32(tmem + lane_base + AT_P_COL + (uint32_t)s * 32u, pw);
+            tmem_st16(tmem + lane_base + AT_P_COL + (uint32_t)s * 32u + (uint32_t)hf * 16u, pw);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[s]);
         }
-        // epilogue: O / l staged in the (now unused) K/V tiles as 128-byte-swizzled boxes of
-        // 128 rows, then stored by TMA — f16 into out for a tile of one CTA, fp32 partials
-        // (+ the row's lse) for a split tile
+        // epilogue: the row sum of both halves; O / l staged in the (now unused) K/V tiles as
+        // 128-byte-swizzled boxes of 128 rows, each half its columns, then stored by TMA — f16
+        // into out for a tile of one CTA, fp32 partials (+ the row's lse) for a split tile
+        const bool fin = ok && __all_sync(FULL, mbar_wait_bounded(&pv_done[(nloc - 1) & 1],
+                                                                  (uint32_t)((nloc - 1) >> 1) & 1u,
+                                                                  a.err, abort_flag));
+        red_l[hf * AT_TQ + row] = l;
+        named_barrier_sync(2 + rq, 64);
+        const float lt = red_l[row] + red_l[AT_TQ + row];
         const bool split = wk.splits > 1;
         uint8_t* stg = sK;
-        if (ok && __all_sync(FULL, mbar_wait_bounded(&pv_done[(nloc - 1) & 1],
-                                                    (uint32_t)((nloc - 1) >> 1) & 1u, a.err,
-                                                    abort_flag))) {
+        if (fin) {
             tc_fence_after();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
 #pragma unroll
-            for (int c0 = 0; c0 < HD; c0 += 32) {
+            for (int c0 = hf * (HD / 2); c0 < (hf + 1) * (HD / 2); c0 += 32) {
                 uint32_t o[32];
                 tmem_ld32(tmem + lane_base + AT_O_COL + (uint32_t)c0, o);
                 const float* f = reinterpret_cast<const float*>(o);
@@ -571,12 +587,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     }
                 }
             }
-            if (split && t < a.n)
+            if (split && hf == 0 && t < a.n)
                 a.part_lse[((size_t)blockIdx.x * a.H + h) * AT_TQ + row] =
-                    l > 0.0f ? m_used + __log2f(l) : -INFINITY;
+                    lt > 0.0f ? m_used + __log2f(lt) : -INFINITY;
         }
         fence_proxy_async_smem();
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, 256);
         if (threadIdx.x == 0 && *abort_flag == 0) {
             if (split) {
                 for (int j = 0; j < HD / 32; j++)
@@ -593,7 +609,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == 12) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(AT_TMEM_COLS)
