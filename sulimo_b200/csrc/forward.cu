@@ -142,8 +142,9 @@ __device__ __forceinline__ float4 sum_splits4(const float* p, size_t stride, int
 // A prefill ubatch's residual step after a split-K projection (o or down): x += the ordered
 // sum of the projection's fp32 partials (split z of token row t at part + z * split_stride +
 // t * E), then RMSNorm(x) * w as f16 — the split-K reduce and add_rmsnorm_q8_kernel<true> in
-// one pass.  One CTA per token, four consecutive values per thread (E a multiple of 4).
-__global__ void __launch_bounds__(256)
+// one pass.  One CTA per token, four consecutive values per thread (E a multiple of 4): the
+// block has E / 4 threads (at most 1024), so every partial of the row is requested at once.
+__global__ void __launch_bounds__(1024)
     reduce_add_rmsnorm_f16_kernel(float* __restrict__ x, const float* __restrict__ part,
                                   size_t split_stride, int splits, int E,
                                   const float* __restrict__ w, float eps,
@@ -267,8 +268,9 @@ __global__ void __launch_bounds__(128)
 // [splits][n][qd + 2 kvd] summed in split order, then per token what qkv_rope_store_kernel does
 // (bias, RoPE of the q and k heads, q written as f32, k and v quantized into the ring at slot
 // pos % capacity).  One CTA per token: the row in shared memory, the angles of each rotary
-// frequency computed once and used by every head.
-__global__ void __launch_bounds__(256)
+// frequency computed once and used by every head; (qd + 2 kvd) / 4 threads (at most 1024), so
+// every partial of the row is requested at once.
+__global__ void __launch_bounds__(1024)
     qkv_reduce_rope_store_kernel(const float* __restrict__ part, int splits, int n,
                                  const float* __restrict__ bq, const float* __restrict__ bk,
                                  const float* __restrict__ bv, int H, int Hkv, int hd,
@@ -519,6 +521,13 @@ int ensure_norm_attr(sulimo_ctx* ctx) {
     return st;
 }
 
+// Threads of a one-row-per-CTA kernel over `width` floats, four per thread: a multiple of 32,
+// at most 1024.
+unsigned row_threads(int width) {
+    const int t = (width / 4 + 31) / 32 * 32;
+    return (unsigned)(t < 32 ? 32 : (t > 1024 ? 1024 : t));
+}
+
 // Prefill scratch: x, q, k, v, o, gate, up (f32 [n][dim]) and one f16 activation buffer
 // [n][max(embd, q dim, ffn)] shared by the norm, attention and SwiGLU outputs.
 struct PrefillScratch {
@@ -622,7 +631,8 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
     auto residual_norm = [&](float* x, const float* dense, const float* part, int splits,
                              const void* w, int rows) -> int {
         if (part)
-            (void)launch_pdl(reduce_add_rmsnorm_f16_kernel, dim3(rows), dim3(256), norm_smem,
+            (void)launch_pdl(reduce_add_rmsnorm_f16_kernel, dim3(rows), dim3(row_threads(E)),
+                             norm_smem,
                              ctx->stream, x, part, (size_t)n * E, splits, E,
                              reinterpret_cast<const float*>(w), m->eps, h16);
         else
@@ -643,7 +653,8 @@ int launch_prefill_ubatch(sulimo_ctx* ctx, const sulimo_model_desc* m, const int
             int splits = 0;
             if ((st = launch_gemm_pair_stacked(ctx, qkv, 3, s.h, E, n, &part, &splits)))
                 return st;
-            (void)launch_pdl(qkv_reduce_rope_store_kernel, dim3(n), dim3(256), qkv_smem,
+            (void)launch_pdl(qkv_reduce_rope_store_kernel, dim3(n),
+                             dim3(row_threads(qd + 2 * kvd)), qkv_smem,
                              ctx->stream, part, splits, n, reinterpret_cast<const float*>(L.bq),
                              reinterpret_cast<const float*>(L.bk),
                              reinterpret_cast<const float*>(L.bv), H, Hkv, hd, m->rope_dim,
