@@ -370,6 +370,13 @@ bool gm_plan(const int* rows, int count, int K, int batch, int num_sms, GmPlan* 
             if (fixed + 2 * G.stage > GM_SMEM_MAX) continue;
             int stages = (int)((GM_SMEM_MAX - fixed) / G.stage);
             if (stages > GM_MAX_STAGES) stages = GM_MAX_STAGES;
+            // two CTAs per SM (twice the consumer warps to hide the latency of each block's
+            // MMA and scale steps) when a ring of two stages or more fits in half the SM
+            const size_t half = 114u * 1024u - 1024u;
+            if (fixed + 2 * G.stage <= half) {
+                const int s2 = (int)((half - fixed) / G.stage);
+                if (s2 < stages) stages = s2;
+            }
             p->nt = nt;
             p->rw = rw;
             p->kc = kc;
