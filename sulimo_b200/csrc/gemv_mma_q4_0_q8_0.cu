@@ -349,50 +349,54 @@ int count_bands(const int* rows, int count, int bh) {
     return n > 0x7fffffffL ? 0x7fffffff : (int)n;
 }
 
+// Pass 0 looks for a plan that admits two CTAs per SM (twice the consumer warps to hide the
+// latency of each block's MMA and scale steps; with several 8-sequence tiles, groups of at
+// least two tiles and stages of at least 32 blocks), its ring cut to what fits in half the SM;
+// pass 1 takes the largest group and the deepest ring that fit one CTA.
 bool gm_plan(const int* rows, int count, int K, int batch, int num_sms, GmPlan* p) {
     const int nb = K / 32, tiles = (batch + 7) / 8;
-    for (int nt = 4; nt >= 1; nt >>= 1) {
-        if (nt > 1 && nt > tiles) continue;
-        const int groups = (tiles + nt - 1) / nt;
-        // the tallest band that still gives every SM a band
-        int rw = 1;
-        for (int c = GM_CONSUMERS; c > 1; c >>= 1)
-            if ((long)count_bands(rows, count, 16 * c) * groups >= num_sms) {
-                rw = c;
-                break;
+    const size_t half = 114u * 1024u - 1024u;
+    for (int pass = 0; pass < 2; pass++) {
+        for (int nt = 4; nt >= 1; nt >>= 1) {
+            if (nt > 1 && nt > tiles) continue;
+            if (pass == 0 && tiles > 1 && nt < 2) continue;
+            const int groups = (tiles + nt - 1) / nt;
+            // the tallest band that still gives every SM a band
+            int rw = 1;
+            for (int c = GM_CONSUMERS; c > 1; c >>= 1)
+                if ((long)count_bands(rows, count, 16 * c) * groups >= num_sms) {
+                    rw = c;
+                    break;
+                }
+            for (int rb = 2048; rb >= 512; rb >>= 1) {  // row-blocks per stage
+                int kc = rb / (16 * rw) / 8 * 8;
+                if (kc < 8) kc = 8;
+                if (kc > nb) kc = nb;
+                const GmGeom G = gm_geom(nt, K, rw, kc);
+                const size_t fixed = 1024 + G.act_codes + G.act_aux + G.red + 256;
+                const size_t limit = pass == 0 ? half : GM_SMEM_MAX;
+                if (fixed + 2 * G.stage > limit) continue;
+                // (pass 0 with several tiles: stages of at least 32 blocks, or the one-CTA plan)
+                if (pass == 0 && tiles > 1 && kc < 32 && kc < nb) continue;
+                int stages = (int)((limit - fixed) / G.stage);
+                if (stages > GM_MAX_STAGES) stages = GM_MAX_STAGES;
+                p->nt = nt;
+                p->rw = rw;
+                p->kc = kc;
+                p->stages = stages;
+                p->bands = count_bands(rows, count, G.BH);
+                p->groups = groups;
+                p->smem = fixed + (size_t)stages * G.stage;
+                // CTAs per SM the shared memory admits (228 KB per SM, 1 KB reserved per CTA)
+                int occ = (int)((228u * 1024u) / (p->smem + 1024));
+                if (occ < 1) occ = 1;
+                if (occ > 2) occ = 2;
+                long ctas = ((long)num_sms * occ + groups - 1) / groups;
+                if (ctas > p->bands) ctas = p->bands;
+                if (ctas < 1) ctas = 1;
+                p->ctas = (int)ctas;
+                return true;
             }
-        for (int rb = 2048; rb >= 512; rb >>= 1) {  // row-blocks per stage
-            int kc = rb / (16 * rw) / 8 * 8;
-            if (kc < 8) kc = 8;
-            if (kc > nb) kc = nb;
-            const GmGeom G = gm_geom(nt, K, rw, kc);
-            const size_t fixed = 1024 + G.act_codes + G.act_aux + G.red + 256;
-            if (fixed + 2 * G.stage > GM_SMEM_MAX) continue;
-            int stages = (int)((GM_SMEM_MAX - fixed) / G.stage);
-            if (stages > GM_MAX_STAGES) stages = GM_MAX_STAGES;
-            // two CTAs per SM (twice the consumer warps to hide the latency of each block's
-            // MMA and scale steps) when a ring of two stages or more fits in half the SM
-            const size_t half = 114u * 1024u - 1024u;
-            if (fixed + 2 * G.stage <= half) {
-                const int s2 = (int)((half - fixed) / G.stage);
-                if (s2 < stages) stages = s2;
-            }
-            p->nt = nt;
-            p->rw = rw;
-            p->kc = kc;
-            p->stages = stages;
-            p->bands = count_bands(rows, count, G.BH);
-            p->groups = groups;
-            p->smem = fixed + (size_t)stages * G.stage;
-            // CTAs per SM the shared memory admits (228 KB per SM, 1 KB reserved per CTA)
-            int occ = (int)((228u * 1024u) / (p->smem + 1024));
-            if (occ < 1) occ = 1;
-            if (occ > 2) occ = 2;
-            long ctas = ((long)num_sms * occ + groups - 1) / groups;
-            if (ctas > p->bands) ctas = p->bands;
-            if (ctas < 1) ctas = 1;
-            p->ctas = (int)ctas;
-            return true;
         }
     }
     return false;
