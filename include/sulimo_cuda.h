@@ -366,7 +366,10 @@ int sulimo_cuda_repack_q4_0_aos_to_soa(sulimo_ctx* ctx, const void* src_aos, siz
 /* causal_gqa_attention_prefill (kernels/prefill.cl:120-237, enqueue_attention_prefill):       */
 /* q [n][head_count][head_dim] fp32 (after RoPE; the reference passes f16), token t at         */
 /* position start_pos + t attends to positions 0 .. start_pos + t (slot p % capacity);         */
-/* out [n][head_count][head_dim] f16.  head_dim 64 or 128.                                    */
+/* out [n][head_count][head_dim] f16.  head_dim 64 or 128.  When the (128-token tile, head)    */
+/* pairs are fewer than the SMs, a tile's keys are split over several CTAs whose partials      */
+/* live in the context workspace (grown, after a stream synchronisation, on first need) and    */
+/* are combined by a second kernel.                                                           */
 int sulimo_cuda_attn_prefill_q8_0(sulimo_ctx* ctx, const float* q, const void* k_ring,
                                   const void* v_ring, size_t start_pos, size_t capacity, int n,
                                   int head_count, int head_count_kv, int head_dim, void* out);
