@@ -587,7 +587,8 @@ int max_active_pairs(int device, int num_sms) {
 
 // Tile plan of the pair kernel: token-tile width (a multiple of 32, at most 256) and K splits.
 // The output tiles (256 features x bn tokens) fill the resident pairs by themselves when there
-// are enough; otherwise K is split over more pairs (each split keeping >= 4 stages of 128).
+// are enough; otherwise K is split over more pairs (each split keeping >= 4 stages of 128),
+// with 128-token tiles when K is at most 16 stages.
 // SULIMO_PAIR_SPLIT_BN=<w> (a measurement switch) uses w-token tiles for the outputs that
 // split K: narrower tiles need fewer splits for the same fill, so fewer fp32 partials.
 PairPlan gemm_pair_plan(int m, int k, int n, int max_pairs) {
@@ -605,6 +606,11 @@ PairPlan gemm_pair_plan(int m, int k, int n, int max_pairs) {
         }();
         if (split_bn && split_bn < bn) {
             bn = split_bn;
+            tiles = pm * ((n + bn - 1) / bn);
+        } else if (num_k <= 16 && bn > 128) {
+            // short K: the split CTAs' fixed costs (prologue, fp32 partial epilogue) outweigh
+            // their few stages; 128-token tiles need fewer splits and halve each CTA's partials
+            bn = 128;
             tiles = pm * ((n + bn - 1) / bn);
         }
         splits = max_pairs / tiles;
