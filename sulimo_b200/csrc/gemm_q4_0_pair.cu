@@ -55,7 +55,7 @@ constexpr uint32_t P_TMEM_COLS = 512;
 constexpr uint32_t P_STAGE_COLS = PK / 2;   // f16x2 TMEM columns of a stage's weights
 constexpr uint32_t P_Q_STAGE = PM * 64;     // raw nibbles per stage: 128 rows x 4 blocks x 16 B
 constexpr uint32_t P_BAR_BYTES = 512;
-static_assert((4 * P_MAX_STAGES + 2) * 8 + 8 <= P_BAR_BYTES, "barrier block");
+static_assert((4 * P_MAX_STAGES + 1) * 8 + 8 <= P_BAR_BYTES, "barrier block");
 
 // Shared memory per CTA: stages x (activation half: bn/2 rows x 256 bytes, nibbles), barriers,
 // 1024 bytes of alignment slack.
@@ -90,59 +90,14 @@ __device__ __forceinline__ void cluster_sync_relaxed() {
         "barrier.cluster.wait.aligned;" ::: "memory");
 }
 
-// Gated epilogue (OUT_MODE 3): the token chunks of 32 that CTA 0 finishes are the first
-// ceil(chunks / 2), CTA 1 the rest; the other CTA's accumulators for them arrive, token-major
-// ([token][feature row], so that a warp's stores are contiguous), in an exchange buffer after
-// the f16 staging tiles of the whole token tile.
-__host__ __device__ constexpr int p_gate_split(int bn) { return (bn / 32 + 1) / 2; }
-__host__ __device__ constexpr uint32_t p_gate_xch_off(int bn) { return (uint32_t)bn * PM * 2u; }
-__host__ __device__ constexpr uint32_t p_gate_xch_bytes(int bn) {
-    return (uint32_t)p_gate_split(bn) * 32u * PM * 4u;
-}
+// Gated epilogue (OUT_MODE 3): a CTA's TMEM lanes 0-63 hold 64 rows of the gate matrix, lanes
+// 64-127 the same 64 rows of the up matrix; per 32-token chunk the up lanes hand their
+// accumulators to the gate lanes through an exchange area ([token][64] fp32) placed after the
+// f16 staging tiles ([token][64]) of the whole token tile.
+__host__ __device__ constexpr uint32_t p_gate_xch_off(int bn) { return (uint32_t)bn * 64u * 2u; }
+__host__ __device__ constexpr uint32_t p_gate_xch_bytes(int bn) { return (uint32_t)bn * 64u * 4u; }
 static_assert(p_gate_xch_off(256) + p_gate_xch_bytes(256) <=
                   4u * (p_x_stage(256) + P_Q_STAGE), "gated exchange fits (256)");
-
-// Arrival on the other CTA's mbarrier, releasing this thread's prior writes (its DSMEM stores
-// included) at cluster scope.
-__device__ __forceinline__ void mbar_arrive_remote_release(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-                     cluster_addr)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait with cluster-scope acquire (for arrivals that publish DSMEM stores).
-__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity,
-                                                          int* err, volatile int* abort_flag) {
-    const uint64_t t0 = globaltimer_ns();
-    uint32_t spins = 0;
-    while (!mbar_try_wait_cluster(bar, parity)) {
-        if ((++spins & 63u) == 0) {
-            if (abort_flag && *abort_flag) return false;
-            if (globaltimer_ns() - t0 > SULIMO_WAIT_LIMIT_NS) {
-                record_device_error(err, SULIMO_DEVERR_WAIT_TIMEOUT);
-                if (abort_flag) *abort_flag = 1;
-                return false;
-            }
-        }
-    }
-    return true;
-}
-
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
 
 __device__ __forceinline__ float silu_times(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
@@ -212,8 +167,9 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
 }
 
 // OUT_MODE: 0 = f16 out, 1 = f32 out, 2 = fp32 split-K partial to the workspace [split][n][m],
-// 3 = gated: CTA 0 of a pair computes 128 rows of matrix 0 (gate), CTA 1 the same rows of
-// matrix 1 (up), and the pair writes silu(gate) * up as f16 [n][m] (m = rows per matrix).
+// 3 = gated: CTA r of pair p computes rows p*128 + 64r .. + 63 of matrix 0 (gate) in its TMEM
+// lanes 0-63 and the same rows of matrix 1 (up) in lanes 64-127, and writes silu(gate) * up for
+// those 64 features as f16 [n][m] (m = rows per matrix; nibble maps of 64-row boxes).
 // Otherwise the m weight rows may be up to three matrices stacked (segment g from row start[g], a
 // multiple of 128, so that every CTA's 128 rows lie in one matrix): nibbles through
 // tmap_q / tmap_q1 / tmap_q2, block scales from scales[g], rows[g] rows each.
@@ -240,18 +196,26 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     uint64_t* empty = xfull + P_MAX_STAGES;
     uint64_t* afull = empty + P_MAX_STAGES;
     uint64_t* done = afull + P_MAX_STAGES;
-    uint64_t* xchg = done + 1;  // gated epilogue: the other CTA's accumulators have arrived
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t crank = cluster_ctarank();
-    const int m0 = OUT_MODE == 3 ? (blockIdx.x >> 1) * PM
+    // gated: m0 = the CTA's first output feature (64 per CTA); otherwise its first row (128)
+    const int m0 = OUT_MODE == 3 ? (blockIdx.x >> 1) * PM + (int)crank * (PM / 2)
                                  : (blockIdx.x >> 1) * (2 * PM) + (int)crank * PM;
-    const int seg = OUT_MODE == 3 ? (int)crank
-                                  : (m0 >= sg.start[2] ? 2 : (m0 >= sg.start[1] ? 1 : 0));
+    const int seg = OUT_MODE == 3 ? 0 : (m0 >= sg.start[2] ? 2 : (m0 >= sg.start[1] ? 1 : 0));
     const CUtensorMap* qmap = seg == 0 ? &tmap_q : (seg == 1 ? &tmap_q1 : &tmap_q2);
     const int lm0 = OUT_MODE == 3 ? m0 : m0 - sg.start[seg];  // first row within its matrix
+    // one stage's nibbles: the CTA's 128 rows, or (gated) 64 gate rows then the same 64 up rows
+    auto load_q = [&](uint8_t* dst, int kx, uint64_t* bar) {
+        if (OUT_MODE == 3) {
+            tma_load_2d(dst, &tmap_q, kx, m0, bar);
+            tma_load_2d(dst + P_Q_STAGE / 2, &tmap_q1, kx, m0, bar);
+        } else {
+            tma_load_2d(dst, qmap, kx, lm0, bar);
+        }
+    };
     const int n0 = blockIdx.y * bn;
     const int nx0 = n0 + (int)crank * (bn / 2);  // this CTA's activation rows
     const int num_k_total = (k + PK - 1) / PK;
@@ -267,11 +231,11 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             mbar_init(&afull[s], 2 * P_DEQ_WARPS);  // every dequant warp of both CTAs
         }
         mbar_init(done, 1);
-        mbar_init(xchg, P_DEQ_WARPS);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmap_x);
         prefetch_tensormap(qmap);
+        if (OUT_MODE == 3) prefetch_tensormap(&tmap_q1);
         prefetch_tensormap(&tmap_out);
         pdl_launch_dependents();
         // The weights are static (no kernel that writes them lets its dependents start early):
@@ -279,7 +243,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         // waits for the previous kernel; the activations follow the programmatic wait below.
         for (int j = 0; j < num_k && j < stages; j++) {
             mbar_arrive_expect_tx(&qfull[j], P_Q_STAGE);
-            tma_load_2d(sq + j * P_Q_STAGE, qmap, (i_begin + j) * PK / 2, lm0, &qfull[j]);
+            load_q(sq + j * P_Q_STAGE, (i_begin + j) * PK / 2, &qfull[j]);
         }
     }
     if (warp == 1) {
@@ -298,9 +262,11 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     const uint32_t quarter = (uint32_t)(warp & 3);
     const int group = (warp - 2) >> 2;
     const int r = (int)quarter * 32 + lane;  // feature row within the CTA == TMEM lane
-    const int lrow = lm0 + r;
-    const bool row_ok = lrow < sg.rows[seg] && m0 + r < m;
-    const uint16_t* srow = sg.scales[seg] + (size_t)(row_ok ? lrow : 0) * nb;
+    // (gated: lanes 0-63 gate rows, 64-127 the same up rows)
+    const int lrow = OUT_MODE == 3 ? m0 + (r & 63) : lm0 + r;
+    const int rseg = OUT_MODE == 3 ? (r >> 6) : seg;
+    const bool row_ok = OUT_MODE == 3 ? lrow < m : (lrow < sg.rows[seg] && m0 + r < m);
+    const uint16_t* srow = sg.scales[rseg] + (size_t)(row_ok ? lrow : 0) * nb;
     const uint32_t lane_base = (quarter * 32u) << 16;
     const uint32_t afull_leader0 = mapa_shared(smem_u32(&afull[0]), 0);
     // block `group` of every stage: its scale for stage j (zero past the matrix or past k)
@@ -341,7 +307,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                 const uint32_t ph = (uint32_t)(j / stages) & 1u;
                 if (!mbar_wait_bounded(&empty[s], ph ^ 1u, err, abort_flag)) break;
                 mbar_arrive_expect_tx(&qfull[s], P_Q_STAGE);
-                tma_load_2d(sq + s * P_Q_STAGE, qmap, (i_begin + j) * PK / 2, lm0, &qfull[s]);
+                load_q(sq + s * P_Q_STAGE, (i_begin + j) * PK / 2, &qfull[s]);
                 load_x(j, s);
                 issued = j + 1;
             }
@@ -432,47 +398,32 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 #pragma unroll
         for (int ci = 0; ci < CH; ci++) tmem_ld_wait_carry(v[ci]);
         if (OUT_MODE == 3) {
-            // send the other CTA the accumulators of the chunks it finishes, then finish ours
-            const int hsplit = p_gate_split(bn);
-            uint8_t* xch = sx + p_gate_xch_off(bn);  // [owner's token][feature row] fp32
-            const uint32_t xch_peer = mapa_shared(smem_u32(xch), crank ^ 1u);
+            // per chunk: the up lanes (quarters 2, 3) leave their accumulators in the exchange
+            // area, the gate lanes (quarters 0, 1) write silu(gate) * up as f16, and one thread
+            // of the group stores the 64-feature x 32-token box
+            float* xch = reinterpret_cast<float*>(sx + p_gate_xch_off(bn));
+            const bool up_lane = quarter >= 2;
+            const int f = r & 63;
 #pragma unroll
             for (int ci = 0; ci < CH; ci++) {
                 const int c0 = (group + ci * P_DEQ_GROUPS) * P_EPI_TOKENS;
-                const uint32_t owner = c0 / P_EPI_TOKENS < hsplit ? 0u : 1u;
-                if (c0 >= bn || owner == crank || !have) continue;
-                const int base = owner == 0 ? 0 : hsplit * P_EPI_TOKENS;
+                if (c0 >= bn) break;
+                float* xc = xch + (size_t)c0 * 64;
+                uint8_t* tile = sx + (size_t)c0 * 64 * 2;
+                if (up_lane && have) {
 #pragma unroll
-                for (int jj = 0; jj < 32; jj++)
-                    st_cluster_f32(xch_peer + (uint32_t)(((c0 + jj - base) * PM + r) * 4),
-                                   __uint_as_float(v[ci][jj]));
-            }
-            asm volatile("fence.acq_rel.cluster;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote_release(mapa_shared(smem_u32(xchg), crank ^ 1u));
-            const bool got = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(xchg, 0, err,
-                                                                                abort_flag));
+                    for (int jj = 0; jj < 32; jj++) xc[jj * 64 + f] = __uint_as_float(v[ci][jj]);
+                }
+                named_barrier_sync(1 + group, 128);
+                if (!up_lane && have) {
 #pragma unroll
-            for (int ci = 0; ci < CH; ci++) {
-                const int c0 = (group + ci * P_DEQ_GROUPS) * P_EPI_TOKENS;
-                const uint32_t owner = c0 / P_EPI_TOKENS < hsplit ? 0u : 1u;
-                if (c0 >= bn || owner != crank) continue;
-                const int base = owner == 0 ? 0 : hsplit * P_EPI_TOKENS;
-                uint8_t* tile = sx + (size_t)c0 * PM * 2;
-                if (have && got) {
-                    const float* other = reinterpret_cast<const float*>(xch);
-#pragma unroll
-                    for (int jj = 0; jj < 32; jj++) {
-                        const float mine = __uint_as_float(v[ci][jj]);
-                        const float peer = other[(c0 + jj - base) * PM + r];
-                        const float y = crank == 0 ? silu_times(mine, peer) : silu_times(peer, mine);
-                        *reinterpret_cast<__half*>(tile + (size_t)(jj * PM + r) * 2) =
-                            __float2half_rn(y);
-                    }
+                    for (int jj = 0; jj < 32; jj++)
+                        *reinterpret_cast<__half*>(tile + (size_t)(jj * 64 + f) * 2) =
+                            __float2half_rn(silu_times(__uint_as_float(v[ci][jj]), xc[jj * 64 + f]));
                     fence_proxy_async_smem();
                 }
                 named_barrier_sync(1 + group, 128);
-                if (issuer && have && got && !*abort_flag && n0 + c0 < n && m0 < m) {
+                if (issuer && have && !*abort_flag && n0 + c0 < n && m0 < m) {
                     const bool whole = c0 + P_EPI_TOKENS <= bn;
                     tma_store_2d(whole ? &tmap_out : &tmap_out16, m0, n0 + c0, tile);
                     bulk_commit();
@@ -629,10 +580,10 @@ PairPlan gemm_pair_plan(int m, int k, int n, int max_pairs) {
 
 namespace {
 
-// Encodes the nibble map of one matrix (rows x nb*16 bytes, boxes of 128 rows x 64 bytes).
-int encode_nibbles(CUtensorMap* map, const void* quants, int rows, int nb) {
+// Encodes the nibble map of one matrix (rows x nb*16 bytes, boxes of box_rows rows x 64 bytes).
+int encode_nibbles(CUtensorMap* map, const void* quants, int rows, int nb, int box_rows = PM) {
     return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, quants, (uint64_t)nb * 16,
-                     (uint64_t)(rows > 0 ? rows : 1), (uint64_t)nb * 16, 64, PM,
+                     (uint64_t)(rows > 0 ? rows : 1), (uint64_t)nb * 16, 64, (uint32_t)box_rows,
                      CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
@@ -760,13 +711,13 @@ int launch_gemm_pair_gated(sulimo_ctx* ctx, const GemmSeg& gate, const GemmSeg& 
     CUtensorMap tx, tg, tu, to, to16;
     if ((st = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, (uint64_t)k, (uint64_t)n,
                         (uint64_t)k * 2, 64, (uint32_t)(p.bn / 2), CU_TENSOR_MAP_SWIZZLE_128B)) ||
-        (st = encode_nibbles(&tg, gate.quants, rows, nb)) ||
-        (st = encode_nibbles(&tu, up.quants, rows, nb)) ||
+        (st = encode_nibbles(&tg, gate.quants, rows, nb, PM / 2)) ||
+        (st = encode_nibbles(&tu, up.quants, rows, nb, PM / 2)) ||
         (st = encode_2d(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out, (uint64_t)rows, (uint64_t)n,
-                        (uint64_t)rows * 2, PM, (uint32_t)P_EPI_TOKENS,
+                        (uint64_t)rows * 2, PM / 2, (uint32_t)P_EPI_TOKENS,
                         CU_TENSOR_MAP_SWIZZLE_NONE)) ||
         (st = encode_2d(&to16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out, (uint64_t)rows, (uint64_t)n,
-                        (uint64_t)rows * 2, PM, 16u, CU_TENSOR_MAP_SWIZZLE_NONE)))
+                        (uint64_t)rows * 2, PM / 2, 16u, CU_TENSOR_MAP_SWIZZLE_NONE)))
         return st;
     const dim3 grid(2 * ((rows + PM - 1) / PM), p.grid_y, 1);
     const cudaError_t e = launch_pair(gemm_q4_0_pair_kernel<3>, grid, p.smem, ctx->stream, tx, tg,
