@@ -99,8 +99,12 @@ __host__ __device__ constexpr uint32_t p_gate_xch_bytes(int bn) { return (uint32
 static_assert(p_gate_xch_off(256) + p_gate_xch_bytes(256) <=
                   4u * (p_x_stage(256) + P_Q_STAGE), "gated exchange fits (256)");
 
+// silu(g) * u = g * u / (1 + e^-g) with the special-function unit's exponential and reciprocal
+// (relative error ~1e-6, far inside the f16 rounding of the result; e^-g = inf -> 0)
 __device__ __forceinline__ float silu_times(float g, float u) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, __expf(-g))));
+    return __fmul_rn(__fmul_rn(g, r), u);
 }
 
 // Shared-memory address of the same variable in CTA `rank` of the cluster.
