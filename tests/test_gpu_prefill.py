@@ -180,8 +180,17 @@ def check_logits(got, ref, where):
         assert int(np.argmax(got)) == int(top[1]), where
 
 
-@pytest.mark.parametrize("cfg,splits", [(QWEN_SMALL, [37]), (LLAMA_SMALL, [20, 45])],
-                         ids=["qwen2-one-ubatch", "llama-two-ubatches"])
+# ragged for the prefill's fused projections: ffn 576 leaves the gated gate/up GEMM's last CTA
+# pair half empty, embd 320 the o / down tiles ragged, q width 320 (not a multiple of 128) keeps
+# q/k/v on separate GEMMs next to the fused o / down / gate-up paths
+QWEN_RAGGED = dict(n_layers=2, embd=320, ffn=576, head_count=5, head_count_kv=1, head_dim=64,
+                   vocab=304, rope_dim=64, rope_mode=1, eps=1e-6, rope_base=1e6, attn_softcap=0.0,
+                   bias=True)
+
+
+@pytest.mark.parametrize("cfg,splits", [(QWEN_SMALL, [37]), (LLAMA_SMALL, [20, 45]),
+                                        (QWEN_RAGGED, [45, 70])],
+                         ids=["qwen2-one-ubatch", "llama-two-ubatches", "ragged-two-ubatches"])
 def test_prefill_ubatch_then_decode_matches_cpu_prefill(ctx, cfg, splits):
     import torch
     from sulimo_b200.model import DecodeModel
