@@ -6,14 +6,17 @@
 // 0 .. start_pos + t (ring slot = position: start_pos + n <= capacity), query head h to kv
 // head h / (H / Hkv).
 //
-// One CTA per (128 query tokens, query head), flash-attention form with the accumulators in TMEM:
+// One CTA per (128 query tokens, query head, key range), flash-attention form with the
+// accumulators in TMEM (when the (tile, head) pairs are fewer than the SMs, a tile's key chunks
+// are divided among several CTAs, which write O / l and the row's log2-sum-exp for
+// attn_prefill_merge_kernel to combine):
 //   warp 13, one thread (producer): per chunk of 64 keys, one TMA tensor copy each of the K and
 //     V ring rows of the kv head (a box of 64 slots starting at the 16-byte boundary at or below
 //     the head's first byte), two chunks in flight;
-//   warps 8-11 (converters): per chunk one thread per (tensor, key): the key's staged ring row read with
-//     16-byte loads, each Q8_0 block dequantized to f16(d * q) by byte permutes and exact half
-//     arithmetic, written as [key][dim] into a 128-byte-swizzled tile — K-major B for S = Q K^T,
-//     MN-major B for O += P V (keys past the CTA's range: 0);
+//   warps 8-11 (converters): per chunk one thread per (tensor, key): the key's staged ring row
+//     read with 16-byte loads, each Q8_0 block dequantized to f16(d * q) by byte permutes and
+//     exact half arithmetic, written as [key][dim] into a 128-byte-swizzled tile — K-major B for
+//     S = Q K^T, MN-major B for O += P V (keys past the CTA's range: 0), three stages;
 //   warp 12, one thread (MMA): S = Q K^T (tcgen05.mma kind::f16, A and B from shared memory,
 //     M = 128, N = 64, fp32 in TMEM, two S buffers so S of the next chunk overlaps the softmax
 //     of this one), then O += P V (A = P from TMEM, B = V from shared memory read MN-major,
@@ -24,7 +27,8 @@
 //     memory, online softmax in fp32 with a lazily raised running maximum (O and l are rescaled
 //     only when the row maximum grows by more than 8 in log2 units, so P <= 256 stays well
 //     inside f16), P as f16 into TMEM with tcgen05.st; each half keeps its own row sum and
-//     rescales its half of O; at the end O / l (the halves' sums added) to the output row.
+//     rescales its half of O; at the end O / l (the halves' sums added) staged in the free K/V
+//     tiles and stored by TMA.
 // The reference keeps q, the dequantized K/V and the accumulated output in f16 (prefill.cl
 // works on half); here K and V enter the tensor cores as f16(d * q) (one rounding), P as f16,
 // and every sum is fp32.  Every mbarrier wait is bounded by %globaltimer (device error, abort,
@@ -210,7 +214,7 @@ struct AtArgs {
     size_t start_pos;
     int n, H, Hkv;
     int boxw;              // bytes of a staged ring row (16-byte multiple)
-    int per_cta;           // key-chunk budget of a CTA: a tile of c chunks runs as ceil(c / per_cta)
+    int per_cta;           // key-chunk budget of a CTA: c chunks run as ceil(c / per_cta) CTAs
     float scale_log2;      // log2(e) / sqrt(hd)
     int* err;
 };

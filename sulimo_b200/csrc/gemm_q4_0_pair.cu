@@ -421,9 +421,11 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                 named_barrier_sync(1 + group, 128);
                 if (!up_lane && have) {
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj++)
+                    for (int jj = 0; jj < 32; jj++) {
+                        const float y = silu_times(__uint_as_float(v[ci][jj]), xc[jj * 64 + f]);
                         *reinterpret_cast<__half*>(tile + (size_t)(jj * 64 + f) * 2) =
-                            __float2half_rn(silu_times(__uint_as_float(v[ci][jj]), xc[jj * 64 + f]));
+                            __float2half_rn(y);
+                    }
                     fence_proxy_async_smem();
                 }
                 named_barrier_sync(1 + group, 128);
